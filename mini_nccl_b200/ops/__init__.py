@@ -1,0 +1,1 @@
+"""Compute ops: hand-written sm_100a kernels and their autograd wrappers."""

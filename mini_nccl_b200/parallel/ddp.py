@@ -1,0 +1,310 @@
+"""Data parallelism: bucketed, overlapped gradient averaging.
+
+Semantics of the reference DDP (mini_nccl/ddp.py:113-247): rank 0's weights
+are broadcast at construction; parameters are bucketed in *reverse*
+registration order up to ``bucket_cap_mb`` (a dtype change starts a new
+bucket); each ``param.grad`` is a view into its bucket's flat buffer so
+autograd accumulates straight into the communication buffer; a
+post-accumulate-grad hook marks readiness; buckets are always reduced in
+index order so every rank issues the same collective sequence; ``no_sync()``
+suppresses communication for gradient accumulation; ``sync()`` waits.
+
+Two engines:
+
+* **CUDA parameters.**  Bucket buffers are allocated in the group's
+  *symmetric* device memory, so the all-reduce kernel reads every peer's
+  bucket over NVLink with no copy-in.  There is no communication thread: the
+  hook that completes bucket ``i`` records a CUDA event on the compute stream,
+  the communication stream waits on it and the fused all-reduce kernel (sum in
+  fp32, ``1/W`` scale, bf16 or fp32 in and out) is launched there, while
+  backward keeps running on the compute stream.  ``sync()`` only makes the
+  compute stream wait on the communication stream; the host never blocks.
+* **CPU parameters.**  A one-thread executor runs the host collectives while
+  autograd continues, exactly as the reference does.
+"""
+
+from __future__ import annotations
+
+import threading
+import time
+from concurrent.futures import Future, ThreadPoolExecutor
+from contextlib import contextmanager
+
+import torch
+from torch import nn
+
+from .. import collectives
+from ..communicator import Communicator
+
+
+def average_gradients(pg: Communicator, params, algorithm: str = "ring") -> int:
+    """Average ``params``' gradients over ``pg``; returns the bytes reduced.
+
+    The explicit form of DDP's reduction, for pipelines (once after the
+    schedule drains, not per microbatch) and for reducing along one mesh
+    dimension only (mini_nccl/ddp.py:53-79).  CUDA gradients are reduced by
+    one fused multi-tensor kernel per dtype: the kernel gathers the gradient
+    pointers itself, so there is no flatten/unflatten copy, and the ``1/W``
+    scale is applied in its epilogue.
+    """
+    if pg.world_size == 1:
+        return 0
+    grads = [p.grad for p in params if p.grad is not None]
+    if not grads:
+        return 0
+    total = 0
+    if grads[0].is_cuda and hasattr(pg, "device_comm"):
+        dc = pg.device_comm()
+        by_dtype: dict[torch.dtype, list[torch.Tensor]] = {}
+        for g in grads:
+            by_dtype.setdefault(g.dtype, []).append(g)
+        for group in by_dtype.values():
+            total += dc.all_reduce_multi(group, scale=1.0 / pg.world_size)
+        return total
+    flat = torch.cat([g.reshape(-1) for g in grads])
+    collectives.all_reduce(pg, flat, algorithm=algorithm)
+    flat.div_(pg.world_size)
+    offset = 0
+    for g in grads:
+        n = g.numel()
+        g.copy_(flat[offset : offset + n].view_as(g))
+        offset += n
+    return flat.numel() * flat.element_size()
+
+
+class _Bucket:
+    """A flat gradient buffer shared by a run of parameters."""
+
+    def __init__(self, index: int, params: list[nn.Parameter], buffer: torch.Tensor) -> None:
+        self.index = index
+        self.params = params
+        self.buffer = buffer
+        self.views: list[torch.Tensor] = []
+        offset = 0
+        for p in params:
+            n = p.numel()
+            self.views.append(buffer[offset : offset + n].view(p.shape))
+            offset += n
+        self.pending = len(params)
+        self.ready = threading.Event()
+        self.lock = threading.Lock()
+        self.launched = False
+
+    def attach_grads(self) -> None:
+        for p, v in zip(self.params, self.views, strict=True):
+            p.grad = v
+
+    def mark_ready(self) -> bool:
+        """Count one parameter in; True when the bucket just became complete."""
+        with self.lock:
+            self.pending -= 1
+            done = self.pending == 0
+        if done:
+            self.ready.set()
+        return done
+
+    def reset(self) -> None:
+        with self.lock:
+            self.pending = len(self.params)
+            self.ready.clear()
+            self.launched = False
+
+    @property
+    def nbytes(self) -> int:
+        return self.buffer.numel() * self.buffer.element_size()
+
+
+class DistributedDataParallel(nn.Module):
+    """Bucketed data parallelism over ``pg`` (see module docstring)."""
+
+    def __init__(
+        self,
+        module: nn.Module,
+        pg: Communicator,
+        bucket_cap_mb: float = 1.0,
+        overlap: bool = True,
+        algorithm: str = "ring",
+        broadcast_buffers: bool = True,
+    ) -> None:
+        super().__init__()
+        self.module = module
+        self.pg = pg
+        self.algorithm = algorithm
+        self._overlap = overlap and pg.world_size > 1
+        self._buckets: list[_Bucket] = []
+        self._accumulating = False
+        self._future: Future | None = None
+        #: ``perf_counter_ns`` at which this iteration's first reduction was
+        #: dispatched (None until then) -- lets tests check overlap mechanically.
+        self.reduce_submitted_ns: int | None = None
+        params = [p for p in module.parameters()]
+        self._cuda = bool(params) and params[0].is_cuda
+
+        if pg.world_size > 1:
+            with torch.no_grad():
+                for p in module.parameters():
+                    collectives.broadcast(pg, p.data if p.data.is_contiguous() else p.data.contiguous(), src=0)
+                if broadcast_buffers:
+                    for b in module.buffers():
+                        if b.is_contiguous():
+                            collectives.broadcast(pg, b.data, src=0)
+            self._build_buckets(bucket_cap_mb)
+            for bucket in self._buckets:
+                bucket.attach_grads()
+                for p in bucket.params:
+                    p.register_post_accumulate_grad_hook(self._make_hook(bucket))
+            if self._cuda:
+                self._dc = pg.device_comm()
+                self._comm_stream = torch.cuda.Stream(device=params[0].device)
+                self._next_launch = 0
+                self._last_done: torch.cuda.Event | None = None
+            else:
+                self._comm = ThreadPoolExecutor(max_workers=1, thread_name_prefix="mnb-ddp")
+
+    # ---- buckets --------------------------------------------------------------
+
+    def _build_buckets(self, cap_mb: float) -> None:
+        cap = int(cap_mb * 1024 * 1024)
+        groups: list[list[nn.Parameter]] = []
+        run: list[nn.Parameter] = []
+        run_bytes = 0
+        for p in reversed(list(self.module.parameters())):
+            if not p.requires_grad:
+                continue
+            nb = p.numel() * p.element_size()
+            if run and (run_bytes + nb > cap or p.dtype != run[0].dtype):
+                groups.append(run)
+                run, run_bytes = [], 0
+            run.append(p)
+            run_bytes += nb
+        if run:
+            groups.append(run)
+        for i, ps in enumerate(groups):
+            numel = sum(p.numel() for p in ps)
+            if self._cuda:
+                buf = self.pg.device_comm().symmetric_zeros(numel, ps[0].dtype)
+            else:
+                buf = torch.zeros(numel, dtype=ps[0].dtype, device=ps[0].device)
+            self._buckets.append(_Bucket(i, ps, buf))
+
+    def _make_hook(self, bucket: _Bucket):
+        def hook(_param: nn.Parameter) -> None:
+            if self._accumulating:
+                return  # inside no_sync(): keep summing into the buckets, no traffic
+            complete = bucket.mark_ready()
+            if not self._overlap:
+                return
+            if self._cuda:
+                if complete:
+                    self._launch_ready_prefix()
+            elif self._future is None:
+                self.reduce_submitted_ns = time.perf_counter_ns()
+                self._future = self._comm.submit(self._reduce_all_host)
+
+        return hook
+
+    # ---- CUDA engine ------------------------------------------------------------
+
+    def _launch(self, bucket: _Bucket) -> None:
+        if self.reduce_submitted_ns is None:
+            self.reduce_submitted_ns = time.perf_counter_ns()
+        produced = torch.cuda.Event()
+        produced.record(torch.cuda.current_stream(bucket.buffer.device))
+        ev = self.pg.recorder.start(
+            f"ddp_bucket{bucket.index}", self.algorithm, channel=-1,
+            nbytes=bucket.nbytes, params=len(bucket.params),
+        )
+        try:
+            with torch.cuda.stream(self._comm_stream):
+                self._comm_stream.wait_event(produced)
+                self._dc.all_reduce(
+                    bucket.buffer, op="sum", algorithm="auto", scale=1.0 / self.pg.world_size
+                )
+                done = torch.cuda.Event()
+                done.record(self._comm_stream)
+                self._last_done = done
+        finally:
+            self.pg.recorder.finish(ev)
+        bucket.launched = True
+
+    def _launch_ready_prefix(self) -> None:
+        """Launch, in index order, every bucket whose predecessors are launched."""
+        while self._next_launch < len(self._buckets):
+            b = self._buckets[self._next_launch]
+            if not b.ready.is_set():
+                return
+            self._launch(b)
+            self._next_launch += 1
+
+    def _sync_cuda(self) -> None:
+        while self._next_launch < len(self._buckets):
+            self._launch(self._buckets[self._next_launch])  # unused params: reduce anyway
+            self._next_launch += 1
+        if self._last_done is not None:
+            torch.cuda.current_stream(self._buckets[0].buffer.device).wait_event(self._last_done)
+        self._next_launch = 0
+        self._last_done = None
+
+    # ---- host engine -------------------------------------------------------------
+
+    def _reduce_all_host(self) -> None:
+        for bucket in self._buckets:
+            bucket.ready.wait()
+            ev = self.pg.recorder.start(
+                f"ddp_bucket{bucket.index}", self.algorithm, channel=-1,
+                nbytes=bucket.nbytes, params=len(bucket.params),
+            )
+            try:
+                collectives.all_reduce(self.pg, bucket.buffer, algorithm=self.algorithm)
+                bucket.buffer.div_(self.pg.world_size)
+            finally:
+                self.pg.recorder.finish(ev)
+
+    # ---- public ---------------------------------------------------------------------
+
+    @contextmanager
+    def no_sync(self):
+        """Accumulate into the buckets without communicating (don't zero_grad inside)."""
+        before = self._accumulating
+        self._accumulating = True
+        try:
+            yield
+        finally:
+            self._accumulating = before
+
+    def forward(self, *args, **kwargs):
+        return self.module(*args, **kwargs)
+
+    def sync(self) -> None:
+        """Finish gradient averaging; call after ``backward()``."""
+        if self.pg.world_size == 1:
+            return
+        if self._cuda:
+            if not self._overlap:
+                for b in self._buckets:
+                    b.ready.set()
+            self._sync_cuda()
+        elif self._overlap:
+            if self._future is not None:
+                self._future.result()
+                self._future = None
+        else:
+            for b in self._buckets:
+                b.ready.set()
+            self._reduce_all_host()
+        for b in self._buckets:
+            b.reset()
+        self.reduce_submitted_ns = None
+
+    def zero_grad(self, set_to_none: bool = False) -> None:
+        """Zero the buckets in place (grads must stay views, so never ``None``)."""
+        if self.pg.world_size == 1:
+            self.module.zero_grad(set_to_none=False)
+            return
+        for b in self._buckets:
+            b.buffer.zero_()
+            b.attach_grads()
+
+    def grad_buffers(self) -> list[torch.Tensor]:
+        """The flat bucket buffers, in bucket order (for fused optimizers)."""
+        return [b.buffer for b in self._buckets]

@@ -1,0 +1,381 @@
+"""Fully sharded data parallelism (ZeRO-3 style).
+
+Semantics of the reference FSDP (mini_nccl/fsdp.py:1-389): every child module
+matching ``unit_cls`` (or listed in ``units``) becomes a *unit* whose
+parameters are flattened, padded to a multiple of the world size and split so
+rank ``r`` keeps shard ``r`` as its only persistent copy.  Forward gathers
+the full flat parameters, runs the unit without building a graph and drops
+them again; backward gathers again, **recomputes** the unit's forward with the
+CPU and CUDA generator states rewound (so dropout replays the same mask),
+takes gradients, reduce-scatters them and divides by ``W``.  Parameters
+outside any unit stay replicated and are averaged in ``sync()``.  The
+optimizer sees shards and replicated parameters only, so parameters,
+gradients and optimizer state all scale as ``1/W``.
+
+On CUDA the shards live in the group's symmetric device memory: the gather is
+one peer-memory kernel that *pulls* every rank's shard straight into the
+destination buffer (no staging copy), and the gradient reduce-scatter reads
+peers' gradient buffers directly and applies the ``1/W`` scale in its
+epilogue.  ``prefetch=True`` issues the next unit's gather on a side stream
+while the current unit computes.
+"""
+
+from __future__ import annotations
+
+from collections.abc import Iterator
+
+import torch
+from torch import nn
+
+from .. import collectives
+from ..communicator import Communicator
+from .ddp import average_gradients
+
+_RELEASED = torch.empty(0)
+
+
+class _Unit:
+    """One module whose parameters are sharded across ranks."""
+
+    def __init__(self, module: nn.Module, pg: Communicator, name: str) -> None:
+        self.module = module
+        self.pg = pg
+        self.name = name
+        self.owner: FullyShardedDataParallel | None = None
+        # (owning submodule, attribute, shape, numel); a tied parameter appears once.
+        self.entries: list[tuple[nn.Module, str, torch.Size, int]] = []
+        self.params: list[nn.Parameter] = []
+        seen: set[int] = set()
+        for sub in module.modules():
+            for attr, p in list(sub.named_parameters(recurse=False)):
+                if id(p) in seen:
+                    continue
+                seen.add(id(p))
+                self.entries.append((sub, attr, p.shape, p.numel()))
+                self.params.append(p)
+        dtypes = {p.dtype for p in self.params}
+        if len(dtypes) > 1:
+            raise ValueError(f"unit {name!r} mixes dtypes {dtypes}; shard them separately")
+        self.dtype = self.params[0].dtype if self.params else torch.float32
+        self.device = self.params[0].device if self.params else torch.device("cpu")
+        W = pg.world_size
+        self.total_numel = sum(e[3] for e in self.entries)
+        self.padded_numel = -(-self.total_numel // W) * W
+        self.shard_numel = self.padded_numel // W
+
+        flat = torch.zeros(self.padded_numel, dtype=self.dtype, device=self.device)
+        at = 0
+        for p, (_, _, _, n) in zip(self.params, self.entries, strict=True):
+            flat[at : at + n].copy_(p.detach().reshape(-1))
+            at += n
+        mine = flat[pg.rank * self.shard_numel : (pg.rank + 1) * self.shard_numel]
+        if self.device.type == "cuda" and W > 1:
+            store = pg.device_comm().symmetric_zeros(self.shard_numel, self.dtype)
+            store.copy_(mine)
+            self.shard = nn.Parameter(store)
+        else:
+            self.shard = nn.Parameter(mine.clone())
+        self.release()
+
+    @property
+    def full_bytes(self) -> int:
+        return self.padded_numel * self.shard.element_size()
+
+    def _gather(self, shard: torch.Tensor) -> torch.Tensor:
+        if self.pg.world_size == 1:
+            return shard.detach().reshape(-1)
+        out = torch.empty(self.padded_numel, dtype=self.dtype, device=shard.device)
+        return collectives.all_gather_into(self.pg, out, shard.detach())
+
+    def _bind(self, flat: torch.Tensor) -> None:
+        at = 0
+        for sub, attr, shape, n in self.entries:
+            param = sub._parameters[attr]
+            assert param is not None
+            param.data = flat[at : at + n].view(shape)
+            at += n
+
+    def materialize(self, shard: torch.Tensor, flat: torch.Tensor | None = None) -> torch.Tensor:
+        """Gather (unless ``flat`` was prefetched) and point the params at it."""
+        if flat is None:
+            flat = self._gather(shard)
+        self._bind(flat)
+        if self.owner is not None:
+            self.owner._note_materialized(self.full_bytes)
+        return flat
+
+    def release(self) -> None:
+        for sub, attr, _, _ in self.entries:
+            param = sub._parameters[attr]
+            assert param is not None
+            param.data = _RELEASED
+        if self.owner is not None:
+            self.owner._note_released(self.full_bytes)
+
+    def reduce_scatter_grads(self, grads: tuple[torch.Tensor | None, ...]) -> torch.Tensor:
+        """Flatten the unit's gradients, keep this rank's averaged slice."""
+        W = self.pg.world_size
+        if self.device.type == "cuda" and W > 1:
+            flat = self.pg.device_comm().scratch_zeros(self.padded_numel, self.dtype)
+        else:
+            flat = torch.zeros(self.padded_numel, dtype=self.dtype, device=self.device)
+        at = 0
+        for g, (_, _, _, n) in zip(grads, self.entries, strict=True):
+            if g is not None:
+                flat[at : at + n].copy_(g.reshape(-1))
+            at += n
+        if W == 1:
+            return flat
+        if flat.is_cuda:
+            return self.pg.device_comm().reduce_scatter(flat, op="sum", scale=1.0 / W)
+        return collectives.reduce_scatter(self.pg, flat, op="sum").div_(W)
+
+    def gather_full_flat(self) -> torch.Tensor:
+        return self._gather(self.shard)
+
+
+class _ShardedForward(torch.autograd.Function):
+    """Unit forward with gathered parameters; backward recomputes (RNG rewound).
+
+    Replaying the generator state is what keeps a unit with dropout correct:
+    without it the recompute draws a new mask and the shard gradients are
+    taken against a graph that never produced the loss, while everything
+    downstream of the unit still looks fine (mini_nccl/fsdp.py:162-217).
+    """
+
+    @staticmethod
+    def forward(ctx, unit: _Unit, shard: torch.Tensor, x: torch.Tensor):
+        ctx.unit = unit
+        ctx.save_for_backward(x, shard)
+        ctx.cpu_rng = torch.get_rng_state()
+        ctx.cuda_dev = x.device if x.is_cuda else None
+        if ctx.cuda_dev is not None:
+            ctx.cuda_rng = torch.cuda.get_rng_state(ctx.cuda_dev)
+        owner = unit.owner
+        flat = owner._take_prefetched(unit) if owner is not None else None
+        with torch.no_grad():
+            unit.materialize(shard, flat)
+            if owner is not None:
+                owner._prefetch_after(unit)
+            try:
+                y = unit.module(x)
+            finally:
+                unit.release()
+        return y
+
+    @staticmethod
+    def backward(ctx, grad_y: torch.Tensor):
+        x, shard = ctx.saved_tensors
+        unit: _Unit = ctx.unit
+        unit.materialize(shard)
+        try:
+            devices = [] if ctx.cuda_dev is None else [ctx.cuda_dev]
+            x_in = x.detach().requires_grad_(True)
+            with torch.random.fork_rng(devices=devices, enabled=True):
+                torch.set_rng_state(ctx.cpu_rng)
+                if ctx.cuda_dev is not None:
+                    torch.cuda.set_rng_state(ctx.cuda_rng, ctx.cuda_dev)
+                with torch.enable_grad():
+                    y = unit.module(x_in)
+            grads = torch.autograd.grad(y, [x_in, *unit.params], grad_outputs=grad_y, allow_unused=True)
+            shard_grad = unit.reduce_scatter_grads(grads[1:])
+        finally:
+            unit.release()
+        return None, shard_grad, grads[0] if ctx.needs_input_grad[2] else None
+
+
+class _UnitWrapper(nn.Module):
+    """Stands in for a sharded module inside the model tree."""
+
+    def __init__(self, unit: _Unit) -> None:
+        super().__init__()
+        self.unit = unit
+        self.wrapped = unit.module
+        self.shard = unit.shard
+
+    def forward(self, x: torch.Tensor) -> torch.Tensor:
+        return _ShardedForward.apply(self.unit, self.shard, x)
+
+
+class FullyShardedDataParallel(nn.Module):
+    """Shard every ``unit_cls`` child (or each module in ``units``) across ``pg``."""
+
+    def __init__(
+        self,
+        module: nn.Module,
+        pg: Communicator,
+        unit_cls: type | tuple[type, ...] | None = None,
+        units: list[nn.Module] | None = None,
+        prefetch: bool = False,
+    ) -> None:
+        super().__init__()
+        if unit_cls is None and units is None:
+            raise ValueError("pass unit_cls or units to say what should be sharded")
+        self.pg = pg
+        self.units: list[_Unit] = []
+        self._live_bytes = 0
+        self.peak_materialized_bytes = 0
+        self.prefetch = prefetch
+        self._prefetched: dict[int, tuple[torch.Tensor, torch.cuda.Event]] = {}
+        self._param_names = {id(p): name for name, p in module.named_parameters()}
+
+        if pg.world_size > 1:
+            with torch.no_grad():
+                for p in module.parameters():
+                    collectives.broadcast(pg, p.data, src=0)
+                for b in module.buffers():
+                    collectives.broadcast(pg, b.data, src=0)
+
+        chosen = {id(m) for m in (units or [])}
+        for parent in list(module.modules()):
+            for key, child in list(parent._modules.items()):
+                if child is None:
+                    continue
+                hit = id(child) in chosen or (unit_cls is not None and isinstance(child, unit_cls))
+                if not hit or not any(True for _ in child.parameters()):
+                    continue
+                unit = _Unit(child, pg, name=f"{type(child).__name__.lower()}{len(self.units)}")
+                unit.owner = self
+                self.units.append(unit)
+                parent._modules[key] = _UnitWrapper(unit)
+        if not self.units:
+            raise ValueError("no modules matched unit_cls/units, so nothing would be sharded")
+
+        self.module = module
+        unit_ids = {id(p) for u in self.units for p in u.params}
+        shard_ids = {id(u.shard) for u in self.units}
+        self._replicated = [
+            p for p in module.parameters() if id(p) not in unit_ids and id(p) not in shard_ids
+        ]
+        self._index = {id(u): i for i, u in enumerate(self.units)}
+        self._side = None
+
+    # ---- prefetch (CUDA) -----------------------------------------------------------
+
+    def _prefetch_after(self, unit: _Unit) -> None:
+        if not self.prefetch or unit.device.type != "cuda" or self.pg.world_size == 1:
+            return
+        i = self._index[id(unit)] + 1
+        if i >= len(self.units) or i in self._prefetched:
+            return
+        nxt = self.units[i]
+        if self._side is None:
+            self._side = torch.cuda.Stream(device=unit.device)
+        cur = torch.cuda.current_stream(unit.device)
+        self._side.wait_stream(cur)
+        with torch.cuda.stream(self._side):
+            flat = nxt._gather(nxt.shard)
+            done = torch.cuda.Event()
+            done.record(self._side)
+        flat.record_stream(cur)
+        self._prefetched[i] = (flat, done)
+
+    def _take_prefetched(self, unit: _Unit):
+        hit = self._prefetched.pop(self._index[id(unit)], None)
+        if hit is None:
+            return None
+        flat, done = hit
+        torch.cuda.current_stream(unit.device).wait_event(done)
+        return flat
+
+    # ---- what the optimizer sees ------------------------------------------------------
+
+    def shard_parameters(self) -> list[nn.Parameter]:
+        return [u.shard for u in self.units]
+
+    def parameters(self, recurse: bool = True):
+        """Shards and replicated parameters only (never the transient full ones)."""
+        return iter(self.shard_parameters() + self._replicated)
+
+    def named_parameters(
+        self, prefix: str = "", recurse: bool = True, remove_duplicate: bool = True
+    ) -> Iterator[tuple[str, nn.Parameter]]:
+        for u in self.units:
+            yield f"{prefix}{u.name}.shard", u.shard
+        for p in self._replicated:
+            yield prefix + self._param_names.get(id(p), "replicated"), p
+
+    # ---- memory accounting --------------------------------------------------------------
+
+    def _note_materialized(self, nbytes: int) -> None:
+        self._live_bytes += nbytes
+        self.peak_materialized_bytes = max(self.peak_materialized_bytes, self._live_bytes)
+
+    def _note_released(self, nbytes: int) -> None:
+        self._live_bytes = max(0, self._live_bytes - nbytes)
+
+    def memory_report(self) -> dict[str, int]:
+        """Measured bytes of parameter storage per rank."""
+        item = self.units[0].shard.element_size()
+        full = sum(u.padded_numel for u in self.units) * item
+        resident = sum(u.shard_numel for u in self.units) * item
+        replicated = sum(p.numel() * p.element_size() for p in self._replicated)
+        return {
+            "sharded_params_full": full,
+            "sharded_params_resident": resident,
+            "replicated_params": replicated,
+            "peak_transient": self.peak_materialized_bytes,
+            "ddp_equivalent": full + replicated,
+            "fsdp_peak": resident + replicated + self.peak_materialized_bytes,
+        }
+
+    # ---- training ----------------------------------------------------------------------------
+
+    def forward(self, *args, **kwargs):
+        return self.module(*args, **kwargs)
+
+    def sync(self) -> None:
+        """Average the replicated gradients (sharded ones were done in backward)."""
+        if self.pg.world_size == 1 or not self._replicated:
+            return
+        average_gradients(self.pg, self._replicated)
+
+    def zero_grad(self, set_to_none: bool = True) -> None:
+        for p in self.parameters():
+            if set_to_none:
+                p.grad = None
+            elif p.grad is not None:
+                p.grad.zero_()
+
+    # ---- checkpointing -------------------------------------------------------------------------
+
+    def full_state_dict(self) -> dict[str, torch.Tensor]:
+        """The unsharded model under its original parameter names."""
+        state: dict[str, torch.Tensor] = {}
+        for u in self.units:
+            flat = u.gather_full_flat()
+            at = 0
+            for p, (_, _, shape, n) in zip(u.params, u.entries, strict=True):
+                name = self._param_names.get(id(p), f"{u.name}.{at}")
+                state[name] = flat[at : at + n].view(shape).clone()
+                at += n
+        for p in self._replicated:
+            name = self._param_names.get(id(p))
+            if name is not None:
+                state[name] = p.detach().clone()
+        for name, b in self.module.named_buffers():
+            state[name] = b.detach().clone()
+        return state
+
+    def sharded_state_dict(self) -> dict[str, object]:
+        """This rank's shards plus the metadata to re-assemble them (per-rank file)."""
+        return {
+            "rank": self.pg.rank,
+            "world_size": self.pg.world_size,
+            "shards": {u.name: u.shard.detach().clone() for u in self.units},
+            "replicated": {
+                self._param_names.get(id(p), f"replicated{i}"): p.detach().clone()
+                for i, p in enumerate(self._replicated)
+            },
+        }
+
+    def load_sharded_state_dict(self, state: dict[str, object]) -> None:
+        if state["world_size"] != self.pg.world_size or state["rank"] != self.pg.rank:
+            raise ValueError("sharded checkpoint was written by a different rank layout")
+        shards = state["shards"]
+        replicated = state["replicated"]
+        with torch.no_grad():
+            for u in self.units:
+                u.shard.copy_(shards[u.name])  # type: ignore[index]
+            for i, p in enumerate(self._replicated):
+                p.copy_(replicated[self._param_names.get(id(p), f"replicated{i}")])  # type: ignore[index]
