@@ -1,0 +1,482 @@
+#!/usr/bin/env python
+"""Headline benchmark: GPT training tokens/s per box (DDP).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference|torch]
+
+Model: decoder-only GPT, 12 layers, d_model 768, 12 heads, vocab 50304,
+sequence 1024, learned positions, MLP 4x, tied head (124M parameters),
+random init.  Data: synthetic uniform token ids.  Micro-batch 16 sequences
+per GPU, data parallel over N GPUs with 25 MB gradient buckets, AdamW
+(0.9, 0.95, wd 0.1), bf16 compute with fp32 master weights.
+
+For N > 1 launch with torchrun (one process per GPU):
+
+    python -m torch.distributed.run --nnodes=1 --nproc-per-node N \\
+        --master-addr 127.0.0.1 --master-port P bench.py --gpus N
+
+Two timed phases, each of exactly K steps after W warm-up steps, bracketed
+by a barrier and torch.cuda.synchronize() on both sides, max over ranks:
+
+1. ``value``: device time (CUDA events) of K training steps whose batches
+   are already resident on the device;
+2. ``e2e``: wall time of K steps through the public API where every step
+   copies that step's inputs from pinned host memory and reads the loss back
+   to the host.
+
+Arms: ``ours`` (this library: sm_100a kernels, peer-memory DDP all-reduce),
+``reference`` (the unmodified reference package from baseline/_ref with its
+own example GPT; gradients averaged with its GPU entry point
+``mini_nccl.device.all_reduce_staged``), ``torch`` (torch DDP over NCCL with
+the same model in autocast -- the NCCL+cuBLAS baseline).
+"""
+
+from __future__ import annotations
+
+import argparse
+import importlib.util
+import json
+import os
+import statistics
+import sys
+import threading
+import time
+from datetime import timedelta
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+REF_ROOT = ROOT / "baseline" / "_ref"
+
+VOCAB, SEQ, LAYERS, HEADS, EMBD = 50304, 1024, 12, 12, 768
+MICRO_BATCH = 16
+BUCKET_MB = 25.0
+METRIC = "GPT tok/s/box (DDP)"
+
+
+def parse_args():
+    ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference", "torch"], default="ours")
+    ap.add_argument("--micro-batch", type=int, default=MICRO_BATCH)
+    ap.add_argument("--no-e2e", action="store_true", help="skip the end-to-end phase")
+    return ap.parse_args()
+
+
+# ---------------------------------------------------------------------------
+# clocks: NVML sampled in a thread during the timed region
+# ---------------------------------------------------------------------------
+class ClockSampler:
+    REASONS = {
+        "gpu_idle": 0x1, "applications_clocks_setting": 0x2, "sw_power_cap": 0x4, "hw_slowdown": 0x8,
+        "sync_boost": 0x10, "sw_thermal_slowdown": 0x20, "hw_thermal_slowdown": 0x40,
+        "hw_power_brake_slowdown": 0x80, "display_clock_setting": 0x100,
+    }
+
+    def __init__(self, index: int) -> None:
+        self.samples: list[tuple[int, int]] = []
+        self.max_mhz = None
+        self._stop = threading.Event()
+        self._thread = None
+        try:
+            import pynvml
+
+            pynvml.nvmlInit()
+            self._nvml = pynvml
+            self._h = pynvml.nvmlDeviceGetHandleByIndex(index)
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self._h, pynvml.NVML_CLOCK_SM)
+        except Exception:
+            self._nvml = None
+
+    def _run(self) -> None:
+        nv = self._nvml
+        while not self._stop.is_set():
+            try:
+                mhz = nv.nvmlDeviceGetClockInfo(self._h, nv.NVML_CLOCK_SM)
+                reasons = nv.nvmlDeviceGetCurrentClocksEventReasons(self._h)
+                self.samples.append((mhz, reasons))
+            except Exception:
+                pass
+            self._stop.wait(0.1)
+
+    def __enter__(self):
+        if self._nvml is not None:
+            self._thread = threading.Thread(target=self._run, daemon=True)
+            self._thread.start()
+        return self
+
+    def __exit__(self, *exc):
+        self._stop.set()
+        if self._thread is not None:
+            self._thread.join(2.0)
+
+    def summary(self) -> dict:
+        if not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": self.max_mhz, "reasons": ["unavailable"]}
+        mhz = [s for s, _ in self.samples]
+        seen = 0
+        for _, r in self.samples:
+            seen |= r
+        names = sorted(n for n, bit in self.REASONS.items() if seen & bit and n != "gpu_idle")
+        return {"sm_mhz": statistics.median(mhz), "sm_max_mhz": self.max_mhz, "reasons": names,
+                "samples": len(mhz)}
+
+
+# ---------------------------------------------------------------------------
+# shared harness
+# ---------------------------------------------------------------------------
+def env_rank():
+    return (int(os.environ.get("RANK", "0")), int(os.environ.get("WORLD_SIZE", "1")),
+            int(os.environ.get("LOCAL_RANK", "0")))
+
+
+def batches_on_device(torch, n, B, dev, seed):
+    g = torch.Generator().manual_seed(seed)
+    xs = [torch.randint(0, VOCAB, (B, SEQ), generator=g).to(dev) for _ in range(n)]
+    ys = [torch.randint(0, VOCAB, (B, SEQ), generator=g).to(dev) for _ in range(n)]
+    return xs, ys
+
+
+def run_phases(torch, args, step_fn, barrier, reduce_max, dev, clocks: ClockSampler, e2e_step=None):
+    """Warm-up, device-timed phase, optional e2e phase.  Returns (ms, e2e_ms, launches)."""
+    from mini_nccl_b200.utils import launches
+
+    for i in range(args.warmup):
+        step_fn(i)
+    barrier()
+    torch.cuda.synchronize()
+    launches.reset()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with clocks:
+        barrier()
+        torch.cuda.synchronize()
+        start.record()
+        for i in range(args.steps):
+            step_fn(i)
+        end.record()
+        torch.cuda.synchronize()
+        barrier()
+    n_launch = launches.count()
+    ms = reduce_max(start.elapsed_time(end))
+    e2e_ms = None
+    if e2e_step is not None and not args.no_e2e:
+        barrier()
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        for i in range(args.steps):
+            e2e_step(i)
+        torch.cuda.synchronize()
+        barrier()
+        e2e_ms = reduce_max((time.perf_counter() - t0) * 1e3)
+    return ms, e2e_ms, n_launch
+
+
+def emit(args, world, impl, ms, e2e_ms, clocks, launches, extra=None):
+    tokens = world * args.micro_batch * SEQ * args.steps
+    value = tokens / (ms / 1e3)
+    line = {
+        "metric": METRIC,
+        "value": round(value, 1),
+        "unit": "tokens/s",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": round(ms / args.steps, 3),
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "bf16",
+        "data": "synthetic uniform token ids, random-init weights",
+        "config": {
+            "model": f"GPT {LAYERS}L/{EMBD}/{HEADS}H V{VOCAB} T{SEQ} (124M, tied head)",
+            "global_batch": world * args.micro_batch,
+            "micro_batch_per_gpu": args.micro_batch,
+            "seq_len": SEQ,
+            "parallelism": f"dp{world}",
+            "bucket_mb": BUCKET_MB,
+            "optimizer": "AdamW(0.9,0.95,wd0.1), fp32 master",
+            "l2": "no flush: per-step working set (activations, 124M params, grads, Adam state) >> 126 MB L2",
+        },
+        "clocks": clocks.summary(),
+        "impl": impl,
+    }
+    if e2e_ms is not None:
+        line["e2e"] = {
+            "value": round(tokens / (e2e_ms / 1e3), 1),
+            "unit": "tokens/s",
+            "h2d_bytes_per_step": 2 * args.micro_batch * SEQ * 8,
+            "d2h_bytes_per_step": 4,
+            "ms_per_step": round(e2e_ms / args.steps, 3),
+        }
+    if launches is not None:
+        line["gpu_launches"] = launches
+    if extra:
+        line.update(extra)
+    print(json.dumps(line), flush=True)
+
+
+# ---------------------------------------------------------------------------
+# ours
+# ---------------------------------------------------------------------------
+def run_ours(args):
+    import torch
+
+    sys.path.insert(0, str(ROOT))
+    import mini_nccl_b200 as mn
+    from mini_nccl_b200.models.gpt import GPT
+    from mini_nccl_b200.ops.kernels import FusedAdamW
+
+    rank, world, local = env_rank()
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    if world > 1:
+        pg = mn.init_process_group(rank, world, device=dev, op_timeout=120.0)
+    else:
+        pg = mn.ProcessGroup(0, 1, device=dev)
+    torch.manual_seed(0)
+    model = GPT(VOCAB, SEQ, LAYERS, HEADS, EMBD).to(dev, torch.bfloat16)
+    ddp = mn.DistributedDataParallel(model, pg, bucket_cap_mb=BUCKET_MB, overlap=True, algorithm="auto")
+    opt = FusedAdamW(model.parameters(), lr=3e-4, betas=(0.9, 0.95), weight_decay=0.1)
+    B = args.micro_batch
+    xs, ys = batches_on_device(torch, 4, B, dev, seed=1000 + rank)
+
+    def step(i):
+        ddp.zero_grad()
+        _, loss = ddp(xs[i % 4], ys[i % 4])
+        loss.backward()
+        ddp.sync()
+        opt.step()
+        return loss
+
+    hx = torch.empty((B, SEQ), dtype=torch.int64).pin_memory()
+    hy = torch.empty((B, SEQ), dtype=torch.int64).pin_memory()
+    gen = torch.Generator().manual_seed(77 + rank)
+    losses = []
+
+    def e2e_step(i):
+        torch.randint(0, VOCAB, (B, SEQ), generator=gen, out=hx)
+        torch.randint(0, VOCAB, (B, SEQ), generator=gen, out=hy)
+        x = hx.to(dev, non_blocking=True)
+        y = hy.to(dev, non_blocking=True)
+        ddp.zero_grad()
+        _, loss = ddp(x, y)
+        loss.backward()
+        ddp.sync()
+        opt.step()
+        losses.append(loss.item())
+
+    def barrier():
+        if world > 1:
+            mn.collectives.barrier(pg)
+
+    def reduce_max(v):
+        if world == 1:
+            return v
+        t = torch.tensor([v], dtype=torch.float64)
+        mn.collectives.all_reduce(pg, t, op="max")
+        return float(t.item())
+
+    clocks = ClockSampler(dev.index)
+    ms, e2e_ms, n_launch = run_phases(torch, args, step, barrier, reduce_max, dev, clocks, e2e_step)
+    if world > 1:
+        pg.device_comm().synchronize()
+    if rank == 0:
+        emit(args, world, "ours", ms, e2e_ms, clocks, n_launch,
+             {"final_loss": round(losses[-1], 4) if losses else None})
+    pg.close()
+
+
+# ---------------------------------------------------------------------------
+# reference arm
+# ---------------------------------------------------------------------------
+def _store_addrs(torch, rank, world):
+    import torch.distributed as dist
+
+    sys.path.insert(0, str(ROOT))
+    from mini_nccl_b200.launcher import _free_ports
+
+    store = dist.TCPStore(os.environ.get("MASTER_ADDR", "127.0.0.1"), int(os.environ["MASTER_PORT"]), world,
+                          is_master=False, timeout=timedelta(seconds=300))
+    run_id = os.environ.get("TORCHELASTIC_RUN_ID", "bench")
+    store.set(f"ref/{run_id}/{rank}", str(_free_ports(1)[0]))
+    ports = []
+    for r in range(world):
+        store.wait([f"ref/{run_id}/{r}"])
+        ports.append(int(store.get(f"ref/{run_id}/{r}")))
+    return [("127.0.0.1", p) for p in ports]
+
+
+def run_reference(args):
+    rank, world, local = env_rank()
+    if not (REF_ROOT / "mini_nccl" / "__init__.py").exists() or not (REF_ROOT / "examples" / "model.py").exists():
+        if rank == 0:
+            print(json.dumps({"impl": "reference", "unavailable":
+                              "baseline/_ref not installed (pip install --target baseline/_ref of the reference)"}))
+        return
+    import torch
+
+    sys.path.insert(0, str(REF_ROOT))
+    import mini_nccl as rmn
+    from mini_nccl import device as rdev
+
+    spec = importlib.util.spec_from_file_location("ref_example_model", REF_ROOT / "examples" / "model.py")
+    mod = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(mod)
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    pg = None
+    if world > 1:
+        pg = rmn.ProcessGroup(rank, world, addrs=_store_addrs(torch, rank, world))
+    torch.manual_seed(0)
+    model = mod.GPT(vocab_size=VOCAB, block_size=SEQ, n_layer=LAYERS, n_head=HEADS, n_embd=EMBD).to(dev)
+    opt = torch.optim.AdamW(model.parameters(), lr=3e-4, betas=(0.9, 0.95), weight_decay=0.1)
+    B = args.micro_batch
+    xs, ys = batches_on_device(torch, 4, B, dev, seed=1000 + rank)
+    params = [p for p in model.parameters()]
+
+    def train(x, y):
+        opt.zero_grad(set_to_none=False)
+        with torch.autocast("cuda", dtype=torch.bfloat16):
+            _, loss = model(x, y)
+        loss.backward()
+        if world > 1:
+            grads = [p.grad for p in params if p.grad is not None]
+            flat = torch.cat([g.reshape(-1) for g in grads])
+            rdev.all_reduce_staged(pg, flat)
+            flat.div_(world)
+            at = 0
+            for g in grads:
+                g.copy_(flat[at : at + g.numel()].view_as(g))
+                at += g.numel()
+        opt.step()
+        return loss
+
+    def step(i):
+        return train(xs[i % 4], ys[i % 4])
+
+    hx = torch.empty((B, SEQ), dtype=torch.int64).pin_memory()
+    hy = torch.empty((B, SEQ), dtype=torch.int64).pin_memory()
+    gen = torch.Generator().manual_seed(77 + rank)
+
+    def e2e_step(i):
+        torch.randint(0, VOCAB, (B, SEQ), generator=gen, out=hx)
+        torch.randint(0, VOCAB, (B, SEQ), generator=gen, out=hy)
+        train(hx.to(dev, non_blocking=True), hy.to(dev, non_blocking=True)).item()
+
+    def barrier():
+        if pg is not None:
+            rmn.collectives.barrier(pg)
+
+    def reduce_max(v):
+        if pg is None:
+            return v
+        t = torch.tensor([v], dtype=torch.float64)
+        rmn.collectives.all_reduce(pg, t, op="max")
+        return float(t.item())
+
+    clocks = ClockSampler(dev.index)
+    sys.path.insert(0, str(ROOT))
+    ms, e2e_ms, _ = run_phases(torch, args, step, barrier, reduce_max, dev, clocks, e2e_step)
+    if rank == 0:
+        emit(args, world, "reference", ms, e2e_ms, clocks, None,
+             {"reference_path": "examples/model.py GPT + torch.optim.AdamW; grads via mini_nccl.device.all_reduce_staged"})
+    if pg is not None:
+        pg.close()
+
+
+# ---------------------------------------------------------------------------
+# torch DDP + NCCL baseline
+# ---------------------------------------------------------------------------
+def run_torch(args):
+    import torch
+    import torch.distributed as dist
+
+    sys.path.insert(0, str(ROOT))
+    from mini_nccl_b200.models.gpt import GPT
+
+    rank, world, local = env_rank()
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    if world > 1:
+        dist.init_process_group("nccl", device_id=dev, timeout=timedelta(seconds=120))
+    torch.manual_seed(0)
+    model = GPT(VOCAB, SEQ, LAYERS, HEADS, EMBD).to(dev)  # fp32 params, autocast bf16 compute
+    B = args.micro_batch
+    xs, ys = batches_on_device(torch, 4, B, dev, seed=1000 + rank)
+    import torch.nn.functional as F
+
+    class StockGPT(torch.nn.Module):
+        """The same parameters run through stock torch ops only (cuBLAS, SDPA)."""
+
+        def __init__(self, m):
+            super().__init__()
+            self.m = m
+
+        def forward(self, x, y):
+            m = self.m
+            T = x.shape[1]
+            h = m.tok_emb(x) + m.pos_emb[:, :T]
+            for blk in m.blocks:
+                C = h.shape[-1]
+                q, k, v = blk.qkv(blk.ln1(h)).split(C, dim=-1)
+                q, k, v = (t.view(x.shape[0], T, blk.n_head, C // blk.n_head).transpose(1, 2) for t in (q, k, v))
+                a = F.scaled_dot_product_attention(q, k, v, is_causal=True)
+                h = h + blk.proj(a.transpose(1, 2).reshape(x.shape[0], T, C))
+                h = h + blk.mlp(blk.ln2(h))
+            logits = m.head(m.ln_f(h))
+            return F.cross_entropy(logits.view(-1, logits.shape[-1]).float(), y.view(-1))
+
+    net = StockGPT(model)
+    if world > 1:
+        net = torch.nn.parallel.DistributedDataParallel(net, bucket_cap_mb=BUCKET_MB)
+    opt = torch.optim.AdamW(model.parameters(), lr=3e-4, betas=(0.9, 0.95), weight_decay=0.1, fused=True)
+
+    def train(x, y):
+        opt.zero_grad(set_to_none=True)
+        with torch.autocast("cuda", dtype=torch.bfloat16):
+            loss = net(x, y)
+        loss.backward()
+        opt.step()
+        return loss
+
+    def step(i):
+        return train(xs[i % 4], ys[i % 4])
+
+    hx = torch.empty((B, SEQ), dtype=torch.int64).pin_memory()
+    hy = torch.empty((B, SEQ), dtype=torch.int64).pin_memory()
+    gen = torch.Generator().manual_seed(77 + rank)
+
+    def e2e_step(i):
+        torch.randint(0, VOCAB, (B, SEQ), generator=gen, out=hx)
+        torch.randint(0, VOCAB, (B, SEQ), generator=gen, out=hy)
+        train(hx.to(dev, non_blocking=True), hy.to(dev, non_blocking=True)).item()
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    def reduce_max(v):
+        if world == 1:
+            return v
+        t = torch.tensor([v], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    clocks = ClockSampler(dev.index)
+    ms, e2e_ms, _ = run_phases(torch, args, step, barrier, reduce_max, dev, clocks, e2e_step)
+    if rank == 0:
+        emit(args, world, "torch", ms, e2e_ms, clocks, None)
+    if world > 1:
+        dist.destroy_process_group()
+
+
+def main():
+    args = parse_args()
+    _, world, _ = env_rank()
+    if args.gpus != world:
+        raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={world}: launch N>1 with torch.distributed.run")
+    {"ours": run_ours, "reference": run_reference, "torch": run_torch}[args.impl](args)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,723 @@
+// Memory-bound kernels of the GPT training step, all bf16 in/out with fp32 math:
+// LayerNorm forward/backward, GELU, token+position embedding forward/backward,
+// softmax cross-entropy (loss and logit gradient in one pass), column sums for
+// bias gradients, and a multi-tensor AdamW with fp32 master weights.
+//
+// Row kernels use one warp per row with 16-byte vector accesses; reductions
+// over rows (LayerNorm weight grads, bias grads) write per-block fp32 partials
+// that a second small kernel folds, so results do not depend on atomics.
+#include <ATen/cuda/CUDAContext.h>
+#include <c10/cuda/CUDAGuard.h>
+#include <torch/extension.h>
+
+#include "common.cuh"
+
+namespace mnb {
+
+namespace {
+
+constexpr int kRowWarps = 8;  // rows per block in the warp-per-row kernels
+
+MNB_DEVICE void load8(const __nv_bfloat16* p, float* f) {
+  uint4 w = ld_v4(p);
+  uint32_t ws[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    float2 t = unpack_bf16x2(ws[j]);
+    f[2 * j] = t.x;
+    f[2 * j + 1] = t.y;
+  }
+}
+MNB_DEVICE void store8(__nv_bfloat16* p, const float* f) {
+  st_v4(p, make_uint4(pack_bf16x2(f[0], f[1]), pack_bf16x2(f[2], f[3]), pack_bf16x2(f[4], f[5]),
+                      pack_bf16x2(f[6], f[7])));
+}
+
+}  // namespace
+
+// ---------------------------------------------------------------------------
+// LayerNorm
+// ---------------------------------------------------------------------------
+__global__ void layernorm_fwd_kernel(const __nv_bfloat16* __restrict__ x, const __nv_bfloat16* __restrict__ w,
+                                     const __nv_bfloat16* __restrict__ b, __nv_bfloat16* __restrict__ y,
+                                     float* __restrict__ mean_out, float* __restrict__ rstd_out, int rows, int C,
+                                     float eps) {
+  const int row = blockIdx.x * kRowWarps + threadIdx.x / 32;
+  const int lane = threadIdx.x % 32;
+  if (row >= rows) return;
+  const __nv_bfloat16* xr = x + static_cast<long long>(row) * C;
+  float s = 0.f;
+  for (int c = lane * 8; c < C; c += 256) {
+    float f[8];
+    load8(xr + c, f);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) s += f[j];
+  }
+  const float mean = warp_sum(s) / C;
+  float ss = 0.f;
+  for (int c = lane * 8; c < C; c += 256) {
+    float f[8];
+    load8(xr + c, f);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      float d = f[j] - mean;
+      ss += d * d;
+    }
+  }
+  const float rstd = rsqrtf(warp_sum(ss) / C + eps);
+  __nv_bfloat16* yr = y + static_cast<long long>(row) * C;
+  for (int c = lane * 8; c < C; c += 256) {
+    float f[8], g[8], h[8];
+    load8(xr + c, f);
+    load8(w + c, g);
+    load8(b + c, h);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) f[j] = (f[j] - mean) * rstd * g[j] + h[j];
+    store8(yr + c, f);
+  }
+  if (lane == 0) {
+    mean_out[row] = mean;
+    rstd_out[row] = rstd;
+  }
+}
+
+// dx per row; per-block fp32 partials of dgamma/dbeta in `part` [gridDim.x, 2, C].
+// NCH > 0: the row (C = NCH*256 wide) stays in registers, one global read,
+// and each lane accumulates the weight gradients of its own columns in
+// registers across all rows it visits.  NCH == 0: any C, shared-memory atomics.
+template <int NCH>
+__global__ void layernorm_bwd_kernel(const __nv_bfloat16* __restrict__ dy, const __nv_bfloat16* __restrict__ x,
+                                     const __nv_bfloat16* __restrict__ w, const float* __restrict__ mean,
+                                     const float* __restrict__ rstd, __nv_bfloat16* __restrict__ dx,
+                                     float* __restrict__ part, int rows, int C) {
+  extern __shared__ float sacc[];  // [2][C]
+  for (int i = threadIdx.x; i < 2 * C; i += blockDim.x) sacc[i] = 0.f;
+  __syncthreads();
+  const int lane = threadIdx.x % 32;
+  const int warp = threadIdx.x / 32;
+  if constexpr (NCH > 0) {
+    float dg[NCH][8], dbb[NCH][8], ww[NCH][8];
+#pragma unroll
+    for (int k = 0; k < NCH; ++k) {
+      load8(w + k * 256 + lane * 8, ww[k]);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) dg[k][j] = dbb[k][j] = 0.f;
+    }
+    for (int row = blockIdx.x * kRowWarps + warp; row < rows; row += gridDim.x * kRowWarps) {
+      const __nv_bfloat16* xr = x + static_cast<long long>(row) * C;
+      const __nv_bfloat16* gr = dy + static_cast<long long>(row) * C;
+      const float mu = mean[row], rs = rstd[row];
+      float xh[NCH][8], g[NCH][8];
+      float a = 0.f, bsum = 0.f;
+#pragma unroll
+      for (int k = 0; k < NCH; ++k) {
+        load8(xr + k * 256 + lane * 8, xh[k]);
+        load8(gr + k * 256 + lane * 8, g[k]);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          xh[k][j] = (xh[k][j] - mu) * rs;
+          const float d = g[k][j] * ww[k][j];
+          a += d;
+          bsum += d * xh[k][j];
+          dg[k][j] += g[k][j] * xh[k][j];
+          dbb[k][j] += g[k][j];
+        }
+      }
+      a = warp_sum(a) / C;
+      bsum = warp_sum(bsum) / C;
+      __nv_bfloat16* dr = dx + static_cast<long long>(row) * C;
+#pragma unroll
+      for (int k = 0; k < NCH; ++k) {
+        float o[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) o[j] = rs * (g[k][j] * ww[k][j] - a - xh[k][j] * bsum);
+        store8(dr + k * 256 + lane * 8, o);
+      }
+    }
+#pragma unroll
+    for (int k = 0; k < NCH; ++k)
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        atomicAdd(&sacc[k * 256 + lane * 8 + j], dg[k][j]);
+        atomicAdd(&sacc[C + k * 256 + lane * 8 + j], dbb[k][j]);
+      }
+  } else {
+    for (int row = blockIdx.x * kRowWarps + warp; row < rows; row += gridDim.x * kRowWarps) {
+      const __nv_bfloat16* xr = x + static_cast<long long>(row) * C;
+      const __nv_bfloat16* gr = dy + static_cast<long long>(row) * C;
+      const float mu = mean[row], rs = rstd[row];
+      float a = 0.f, bsum = 0.f;
+      for (int c = lane * 8; c < C; c += 256) {
+        float f[8], g[8], wv[8];
+        load8(xr + c, f);
+        load8(gr + c, g);
+        load8(w + c, wv);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          float xhv = (f[j] - mu) * rs;
+          float d = g[j] * wv[j];
+          a += d;
+          bsum += d * xhv;
+          atomicAdd(&sacc[c + j], g[j] * xhv);
+          atomicAdd(&sacc[C + c + j], g[j]);
+        }
+      }
+      a = warp_sum(a) / C;
+      bsum = warp_sum(bsum) / C;
+      __nv_bfloat16* dr = dx + static_cast<long long>(row) * C;
+      for (int c = lane * 8; c < C; c += 256) {
+        float f[8], g[8], wv[8], o[8];
+        load8(xr + c, f);
+        load8(gr + c, g);
+        load8(w + c, wv);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          float xhv = (f[j] - mu) * rs;
+          o[j] = rs * (g[j] * wv[j] - a - xhv * bsum);
+        }
+        store8(dr + c, o);
+      }
+    }
+  }
+  __syncthreads();
+  float* mine = part + static_cast<long long>(blockIdx.x) * 2 * C;
+  for (int i = threadIdx.x; i < 2 * C; i += blockDim.x) mine[i] = sacc[i];
+}
+
+// out[c] (+)= sum over `nparts` rows of part[:, c]; bf16 or fp32 destination.
+__global__ void fold_partials_kernel(const float* __restrict__ part, int nparts, long long stride, int C,
+                                     void* out, int out_f32, int accumulate) {
+  const int c = blockIdx.x * blockDim.x + threadIdx.x;
+  if (c >= C) return;
+  float s = 0.f;
+  for (int p = 0; p < nparts; ++p) s += part[p * stride + c];
+  if (out_f32) {
+    float* o = reinterpret_cast<float*>(out);
+    o[c] = accumulate ? o[c] + s : s;
+  } else {
+    __nv_bfloat16* o = reinterpret_cast<__nv_bfloat16*>(out);
+    o[c] = f32_to_bf16(accumulate ? bf16_to_f32(o[c]) + s : s);
+  }
+}
+
+// Column sums of a [rows, C] bf16 matrix into per-block partials [gridDim.y, C].
+// A block covers 256 columns x kColRows rows: each warp walks every 8th row
+// with 16-byte loads into register accumulators, then the 8 warps are summed
+// through shared memory.
+constexpr int kColRows = 128;
+__global__ void __launch_bounds__(256) colsum_partial_kernel(const __nv_bfloat16* __restrict__ g,
+                                                             float* __restrict__ part, int rows, int C) {
+  __shared__ float red[8][256];
+  const int lane = threadIdx.x % 32, warp = threadIdx.x / 32;
+  const int c0 = blockIdx.x * 256 + lane * 8;
+  const int r0 = blockIdx.y * kColRows;
+  const int r1 = min(rows, r0 + kColRows);
+  float s[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+  if (c0 < C) {
+#pragma unroll 4
+    for (int r = r0 + warp; r < r1; r += 8) {
+      float f[8];
+      load8(g + static_cast<long long>(r) * C + c0, f);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) s[j] += f[j];
+    }
+  }
+#pragma unroll
+  for (int j = 0; j < 8; ++j) red[warp][lane * 8 + j] = s[j];
+  __syncthreads();
+  float t = 0.f;
+#pragma unroll
+  for (int w = 0; w < 8; ++w) t += red[w][threadIdx.x];
+  const int c = blockIdx.x * 256 + threadIdx.x;
+  if (c < C) part[static_cast<long long>(blockIdx.y) * C + c] = t;
+}
+
+// ---------------------------------------------------------------------------
+// GELU (standalone; the MLP path fuses it into the GEMM epilogues)
+// ---------------------------------------------------------------------------
+__global__ void gelu_fwd_kernel(const __nv_bfloat16* __restrict__ x, __nv_bfloat16* __restrict__ y, long long n8) {
+  for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < n8;
+       i += static_cast<long long>(gridDim.x) * blockDim.x) {
+    float f[8];
+    load8(x + 8 * i, f);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) f[j] = gelu_exact(f[j]);
+    store8(y + 8 * i, f);
+  }
+}
+__global__ void gelu_bwd_kernel(const __nv_bfloat16* __restrict__ x, const __nv_bfloat16* __restrict__ dy,
+                                __nv_bfloat16* __restrict__ dx, long long n8) {
+  for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < n8;
+       i += static_cast<long long>(gridDim.x) * blockDim.x) {
+    float f[8], g[8];
+    load8(x + 8 * i, f);
+    load8(dy + 8 * i, g);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) f[j] = g[j] * gelu_grad(f[j]);
+    store8(dx + 8 * i, f);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Embedding: y[b, t] = wte[idx[b, t]] + wpe[t]
+// ---------------------------------------------------------------------------
+__global__ void embed_fwd_kernel(const int64_t* __restrict__ idx, const __nv_bfloat16* __restrict__ wte,
+                                 const __nv_bfloat16* __restrict__ wpe, __nv_bfloat16* __restrict__ y, int tokens,
+                                 int T, int C) {
+  const int row = blockIdx.x * kRowWarps + threadIdx.x / 32;
+  const int lane = threadIdx.x % 32;
+  if (row >= tokens) return;
+  const long long tok = idx[row];
+  const int t = row % T;
+  for (int c = lane * 8; c < C; c += 256) {
+    float a[8], p[8];
+    load8(wte + tok * C + c, a);
+    load8(wpe + static_cast<long long>(t) * C + c, p);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) a[j] += p[j];
+    store8(y + static_cast<long long>(row) * C + c, a);
+  }
+}
+
+// dwte[idx] += dy (bf16x2 atomics, collisions are rare for real token streams);
+__global__ void embed_bwd_tok_kernel(const int64_t* __restrict__ idx, const __nv_bfloat16* __restrict__ dy,
+                                     __nv_bfloat16* __restrict__ dwte, int tokens, int C) {
+  const int row = blockIdx.x * kRowWarps + threadIdx.x / 32;
+  const int lane = threadIdx.x % 32;
+  if (row >= tokens) return;
+  const long long tok = idx[row];
+  for (int c = lane * 2; c < C; c += 64) {
+    __nv_bfloat162 g = *reinterpret_cast<const __nv_bfloat162*>(dy + static_cast<long long>(row) * C + c);
+    atomicAdd(reinterpret_cast<__nv_bfloat162*>(dwte + tok * C + c), g);
+  }
+}
+
+// dwpe[t] (+)= sum_b dy[b, t]
+__global__ void embed_bwd_pos_kernel(const __nv_bfloat16* __restrict__ dy, __nv_bfloat16* __restrict__ dwpe, int B,
+                                     int T, int C, int accumulate) {
+  const int t = blockIdx.x;
+  for (int c = threadIdx.x * 8; c < C; c += blockDim.x * 8) {
+    float s[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+    for (int b = 0; b < B; ++b) {
+      float f[8];
+      load8(dy + (static_cast<long long>(b) * T + t) * C + c, f);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) s[j] += f[j];
+    }
+    if (accumulate) {
+      float o[8];
+      load8(dwpe + static_cast<long long>(t) * C + c, o);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) s[j] += o[j];
+    }
+    store8(dwpe + static_cast<long long>(t) * C + c, s);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Cross-entropy: per row, loss = logsumexp(z) - z[target]; the logits are
+// overwritten in place with (softmax(z) - onehot) * grad_scale.
+// ---------------------------------------------------------------------------
+constexpr int kXentThreads = 512;
+
+__global__ void __launch_bounds__(kXentThreads) xent_fwd_bwd_kernel(__nv_bfloat16* __restrict__ logits,
+                                                                    const int64_t* __restrict__ targets,
+                                                                    float* __restrict__ loss, int V, long long ld,
+                                                                    float grad_scale, int ignore_index) {
+  __shared__ float sm[32], ss[32];
+  const int row = blockIdx.x;
+  __nv_bfloat16* z = logits + static_cast<long long>(row) * ld;
+  // Online max / sum of exp per thread, then merged across the block.
+  float m = -INFINITY, s = 0.f;
+  for (int c = threadIdx.x * 8; c < V; c += kXentThreads * 8) {
+    float f[8];
+    if (c + 8 <= V) {
+      load8(z + c, f);
+    } else {
+      for (int j = 0; j < 8; ++j) f[j] = (c + j < V) ? bf16_to_f32(z[c + j]) : -INFINITY;
+    }
+    float lm = f[0];
+#pragma unroll
+    for (int j = 1; j < 8; ++j) lm = fmaxf(lm, f[j]);
+    float nm = fmaxf(m, lm);
+    float acc = (m == -INFINITY) ? 0.f : s * __expf(m - nm);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) acc += (f[j] == -INFINITY) ? 0.f : __expf(f[j] - nm);
+    m = nm;
+    s = acc;
+  }
+  // warp merge
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    float om = __shfl_xor_sync(0xffffffffu, m, o);
+    float os = __shfl_xor_sync(0xffffffffu, s, o);
+    float nm = fmaxf(m, om);
+    s = (m == -INFINITY ? 0.f : s * __expf(m - nm)) + (om == -INFINITY ? 0.f : os * __expf(om - nm));
+    m = nm;
+  }
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  if (lane == 0) {
+    sm[warp] = m;
+    ss[warp] = s;
+  }
+  __syncthreads();
+  if (warp == 0) {
+    m = lane < kXentThreads / 32 ? sm[lane] : -INFINITY;
+    s = lane < kXentThreads / 32 ? ss[lane] : 0.f;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      float om = __shfl_xor_sync(0xffffffffu, m, o);
+      float os = __shfl_xor_sync(0xffffffffu, s, o);
+      float nm = fmaxf(m, om);
+      s = (m == -INFINITY ? 0.f : s * __expf(m - nm)) + (om == -INFINITY ? 0.f : os * __expf(om - nm));
+      m = nm;
+    }
+    if (lane == 0) {
+      sm[0] = m;
+      ss[0] = s;
+    }
+  }
+  __syncthreads();
+  const float rmax = sm[0];
+  const float inv = 1.f / ss[0];
+  const int64_t tgt = targets[row];
+  const bool ignored = tgt == ignore_index;
+  if (threadIdx.x == 0) {
+    loss[row] = ignored ? 0.f : (rmax + logf(ss[0]) - bf16_to_f32(z[tgt]));
+  }
+  __syncthreads();  // everyone read z[tgt] above before it is overwritten
+  const float gs = ignored ? 0.f : grad_scale;
+  for (int c = threadIdx.x * 8; c < V; c += kXentThreads * 8) {
+    if (c + 8 <= V) {
+      float f[8];
+      load8(z + c, f);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        float p = __expf(f[j] - rmax) * inv;
+        f[j] = (p - ((c + j) == tgt ? 1.f : 0.f)) * gs;
+      }
+      store8(z + c, f);
+    } else {
+      for (int j = 0; j < 8 && c + j < V; ++j) {
+        float p = __expf(bf16_to_f32(z[c + j]) - rmax) * inv;
+        z[c + j] = f32_to_bf16((p - ((c + j) == tgt ? 1.f : 0.f)) * gs);
+      }
+    }
+  }
+}
+
+// Single-read variant: the whole row is staged in shared memory (V*2 bytes)
+// while the online max/sum runs, so the logits are read from HBM once.
+__global__ void __launch_bounds__(kXentThreads) xent_smem_kernel(__nv_bfloat16* __restrict__ logits,
+                                                                 const int64_t* __restrict__ targets,
+                                                                 float* __restrict__ loss, int V, long long ld,
+                                                                 float grad_scale, int ignore_index) {
+  extern __shared__ __align__(16) uint8_t xs_raw[];
+  __nv_bfloat16* row_s = reinterpret_cast<__nv_bfloat16*>(xs_raw);
+  __shared__ float sm[32], ss[32];
+  const int row = blockIdx.x;
+  __nv_bfloat16* z = logits + static_cast<long long>(row) * ld;
+  float m = -INFINITY, s = 0.f;
+  for (int c = threadIdx.x * 8; c < V; c += kXentThreads * 8) {
+    uint4 raw = ld_v4(z + c);
+    st_v4(row_s + c, raw);
+    float f[8];
+    const uint32_t ws[4] = {raw.x, raw.y, raw.z, raw.w};
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      float2 t = unpack_bf16x2(ws[j]);
+      f[2 * j] = t.x;
+      f[2 * j + 1] = t.y;
+    }
+    float lm = f[0];
+#pragma unroll
+    for (int j = 1; j < 8; ++j) lm = fmaxf(lm, f[j]);
+    const float nm = fmaxf(m, lm);
+    float acc = (m == -INFINITY) ? 0.f : s * __expf(m - nm);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) acc += __expf(f[j] - nm);
+    m = nm;
+    s = acc;
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    float om = __shfl_xor_sync(0xffffffffu, m, o);
+    float os = __shfl_xor_sync(0xffffffffu, s, o);
+    float nm = fmaxf(m, om);
+    s = (m == -INFINITY ? 0.f : s * __expf(m - nm)) + (om == -INFINITY ? 0.f : os * __expf(om - nm));
+    m = nm;
+  }
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  if (lane == 0) {
+    sm[warp] = m;
+    ss[warp] = s;
+  }
+  __syncthreads();
+  if (warp == 0) {
+    m = lane < kXentThreads / 32 ? sm[lane] : -INFINITY;
+    s = lane < kXentThreads / 32 ? ss[lane] : 0.f;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      float om = __shfl_xor_sync(0xffffffffu, m, o);
+      float os = __shfl_xor_sync(0xffffffffu, s, o);
+      float nm = fmaxf(m, om);
+      s = (m == -INFINITY ? 0.f : s * __expf(m - nm)) + (om == -INFINITY ? 0.f : os * __expf(om - nm));
+      m = nm;
+    }
+    if (lane == 0) {
+      sm[0] = m;
+      ss[0] = s;
+    }
+  }
+  __syncthreads();
+  const float rmax = sm[0];
+  const float inv = 1.f / ss[0];
+  const int64_t tgt = targets[row];
+  const bool ignored = tgt == ignore_index;
+  if (threadIdx.x == 0) loss[row] = ignored ? 0.f : (rmax + logf(ss[0]) - bf16_to_f32(row_s[tgt]));
+  const float gs = ignored ? 0.f : grad_scale;
+  for (int c = threadIdx.x * 8; c < V; c += kXentThreads * 8) {
+    float f[8];
+    load8(row_s + c, f);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const float p = __expf(f[j] - rmax) * inv;
+      f[j] = (p - ((c + j) == tgt ? 1.f : 0.f)) * gs;
+    }
+    store8(z + c, f);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Multi-tensor AdamW with fp32 master weights.
+//   table rows: {param(bf16 or fp32), grad(bf16 or fp32), master(fp32 or null), m, v, numel}
+// ---------------------------------------------------------------------------
+struct AdamEntry {
+  void* param;
+  const void* grad;
+  float* master;
+  float* m;
+  float* v;
+  long long numel;
+};
+
+struct AdamChunk {
+  long long entry;
+  long long start;
+  long long len;
+};
+
+// One chunk (<= 64K contiguous elements of one tensor) per block iteration:
+// no per-element search, fully coalesced accesses.
+__global__ void __launch_bounds__(512) adamw_kernel(const AdamEntry* __restrict__ table,
+                                                    const AdamChunk* __restrict__ chunks, int n_chunks,
+                                                    int param_bf16, int grad_bf16, float lr, float beta1, float beta2,
+                                                    float eps, float wd, float bc1, float bc2, float grad_scale) {
+  const float c1 = 1.f / bc1;
+  const float c2 = 1.f / bc2;
+  for (int ci = blockIdx.x; ci < n_chunks; ci += gridDim.x) {
+    const AdamChunk ch = chunks[ci];
+    const AdamEntry e = table[ch.entry];
+    const long long end = ch.start + ch.len;
+    for (long long k = ch.start + threadIdx.x; k < end; k += blockDim.x) {
+      float g = grad_bf16 ? bf16_to_f32(reinterpret_cast<const __nv_bfloat16*>(e.grad)[k])
+                          : reinterpret_cast<const float*>(e.grad)[k];
+      g *= grad_scale;
+      float w = e.master ? e.master[k]
+                         : (param_bf16 ? bf16_to_f32(reinterpret_cast<__nv_bfloat16*>(e.param)[k])
+                                       : reinterpret_cast<float*>(e.param)[k]);
+      const float m = beta1 * e.m[k] + (1.f - beta1) * g;
+      const float v = beta2 * e.v[k] + (1.f - beta2) * g * g;
+      e.m[k] = m;
+      e.v[k] = v;
+      w -= lr * wd * w;
+      w -= lr * (m * c1) / (sqrtf(v * c2) + eps);
+      if (e.master) e.master[k] = w;
+      if (param_bf16) reinterpret_cast<__nv_bfloat16*>(e.param)[k] = f32_to_bf16(w);
+      else reinterpret_cast<float*>(e.param)[k] = w;
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
+// host wrappers
+// ---------------------------------------------------------------------------
+static void check_bf16(const torch::Tensor& t, const char* n) {
+  TORCH_CHECK(t.is_cuda() && t.scalar_type() == at::kBFloat16 && t.is_contiguous(), n,
+              " must be a contiguous CUDA bf16 tensor");
+}
+
+void layernorm_fwd(torch::Tensor x, torch::Tensor w, torch::Tensor b, torch::Tensor y, torch::Tensor mean,
+                   torch::Tensor rstd, double eps) {
+  check_bf16(x, "x");
+  check_bf16(w, "weight");
+  check_bf16(b, "bias");
+  check_bf16(y, "y");
+  const int C = static_cast<int>(x.size(-1));
+  TORCH_CHECK(C % 8 == 0, "LayerNorm width must be a multiple of 8");
+  const int rows = static_cast<int>(x.numel() / C);
+  c10::cuda::CUDAGuard g(x.device());
+  layernorm_fwd_kernel<<<(rows + kRowWarps - 1) / kRowWarps, kRowWarps * 32, 0, at::cuda::getCurrentCUDAStream()>>>(
+      reinterpret_cast<const __nv_bfloat16*>(x.data_ptr()), reinterpret_cast<const __nv_bfloat16*>(w.data_ptr()),
+      reinterpret_cast<const __nv_bfloat16*>(b.data_ptr()), reinterpret_cast<__nv_bfloat16*>(y.data_ptr()),
+      mean.data_ptr<float>(), rstd.data_ptr<float>(), rows, C, static_cast<float>(eps));
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+int ln_bwd_blocks(int rows) { return std::max(1, std::min(148 * 2, (rows + kRowWarps - 1) / kRowWarps)); }
+
+void layernorm_bwd(torch::Tensor dy, torch::Tensor x, torch::Tensor w, torch::Tensor mean, torch::Tensor rstd,
+                   torch::Tensor dx, torch::Tensor dw, torch::Tensor db, torch::Tensor partials, bool accumulate) {
+  check_bf16(dy, "dy");
+  check_bf16(x, "x");
+  check_bf16(dx, "dx");
+  const int C = static_cast<int>(x.size(-1));
+  const int rows = static_cast<int>(x.numel() / C);
+  const int blocks = ln_bwd_blocks(rows);
+  TORCH_CHECK(partials.numel() >= static_cast<int64_t>(blocks) * 2 * C && partials.scalar_type() == at::kFloat,
+              "partials workspace too small");
+  c10::cuda::CUDAGuard g(x.device());
+  auto stream = at::cuda::getCurrentCUDAStream();
+  const size_t smem = 2 * C * sizeof(float);
+  auto launch = [&](auto kern) {
+    if (smem > 48 * 1024)
+      C10_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+    kern<<<blocks, kRowWarps * 32, smem, stream>>>(
+        reinterpret_cast<const __nv_bfloat16*>(dy.data_ptr()), reinterpret_cast<const __nv_bfloat16*>(x.data_ptr()),
+        reinterpret_cast<const __nv_bfloat16*>(w.data_ptr()), mean.data_ptr<float>(), rstd.data_ptr<float>(),
+        reinterpret_cast<__nv_bfloat16*>(dx.data_ptr()), partials.data_ptr<float>(), rows, C);
+  };
+  if (C == 256) launch(layernorm_bwd_kernel<1>);
+  else if (C == 512) launch(layernorm_bwd_kernel<2>);
+  else if (C == 768) launch(layernorm_bwd_kernel<3>);
+  else if (C == 1024) launch(layernorm_bwd_kernel<4>);
+  else launch(layernorm_bwd_kernel<0>);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+  const bool f32 = dw.scalar_type() == at::kFloat;
+  fold_partials_kernel<<<(C + 255) / 256, 256, 0, stream>>>(partials.data_ptr<float>(), blocks, 2LL * C, C,
+                                                             dw.data_ptr(), f32, accumulate);
+  fold_partials_kernel<<<(C + 255) / 256, 256, 0, stream>>>(partials.data_ptr<float>() + C, blocks, 2LL * C, C,
+                                                             db.data_ptr(), f32, accumulate);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+int colsum_row_blocks(int rows) { return std::max(1, (rows + kColRows - 1) / kColRows); }
+
+void bias_grad(torch::Tensor g, torch::Tensor out, torch::Tensor partials, bool accumulate) {
+  check_bf16(g, "grad");
+  const int C = static_cast<int>(g.size(-1));
+  TORCH_CHECK(C % 8 == 0, "bias width must be a multiple of 8");
+  const int rows = static_cast<int>(g.numel() / C);
+  const int yb = colsum_row_blocks(rows);
+  TORCH_CHECK(partials.numel() >= static_cast<int64_t>(yb) * C, "partials workspace too small");
+  c10::cuda::CUDAGuard guard(g.device());
+  auto stream = at::cuda::getCurrentCUDAStream();
+  colsum_partial_kernel<<<dim3((C + 255) / 256, yb), 256, 0, stream>>>(
+      reinterpret_cast<const __nv_bfloat16*>(g.data_ptr()), partials.data_ptr<float>(), rows, C);
+  fold_partials_kernel<<<(C + 255) / 256, 256, 0, stream>>>(partials.data_ptr<float>(), yb, C, C, out.data_ptr(),
+                                                             out.scalar_type() == at::kFloat, accumulate);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+static int elementwise_blocks(long long n8) {
+  return static_cast<int>(std::max(1LL, std::min((n8 + 255) / 256, 148LL * 16)));
+}
+
+void gelu_fwd(torch::Tensor x, torch::Tensor y) {
+  check_bf16(x, "x");
+  TORCH_CHECK(x.numel() % 8 == 0, "numel must be a multiple of 8");
+  const long long n8 = x.numel() / 8;
+  c10::cuda::CUDAGuard g(x.device());
+  gelu_fwd_kernel<<<elementwise_blocks(n8), 256, 0, at::cuda::getCurrentCUDAStream()>>>(
+      reinterpret_cast<const __nv_bfloat16*>(x.data_ptr()), reinterpret_cast<__nv_bfloat16*>(y.data_ptr()), n8);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+void gelu_bwd(torch::Tensor x, torch::Tensor dy, torch::Tensor dx) {
+  check_bf16(x, "x");
+  const long long n8 = x.numel() / 8;
+  c10::cuda::CUDAGuard g(x.device());
+  gelu_bwd_kernel<<<elementwise_blocks(n8), 256, 0, at::cuda::getCurrentCUDAStream()>>>(
+      reinterpret_cast<const __nv_bfloat16*>(x.data_ptr()), reinterpret_cast<const __nv_bfloat16*>(dy.data_ptr()),
+      reinterpret_cast<__nv_bfloat16*>(dx.data_ptr()), n8);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+void embed_fwd(torch::Tensor idx, torch::Tensor wte, torch::Tensor wpe, torch::Tensor y) {
+  check_bf16(wte, "wte");
+  check_bf16(wpe, "wpe");
+  TORCH_CHECK(idx.scalar_type() == at::kLong && idx.is_contiguous(), "idx must be int64");
+  const int T = static_cast<int>(idx.size(-1));
+  const int C = static_cast<int>(wte.size(1));
+  const int tokens = static_cast<int>(idx.numel());
+  c10::cuda::CUDAGuard g(wte.device());
+  embed_fwd_kernel<<<(tokens + kRowWarps - 1) / kRowWarps, kRowWarps * 32, 0, at::cuda::getCurrentCUDAStream()>>>(
+      idx.data_ptr<int64_t>(), reinterpret_cast<const __nv_bfloat16*>(wte.data_ptr()),
+      reinterpret_cast<const __nv_bfloat16*>(wpe.data_ptr()), reinterpret_cast<__nv_bfloat16*>(y.data_ptr()), tokens,
+      T, C);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+void embed_bwd(torch::Tensor idx, torch::Tensor dy, torch::Tensor dwte, torch::Tensor dwpe, bool accumulate_pos) {
+  check_bf16(dy, "dy");
+  const int B = static_cast<int>(idx.size(0));
+  const int T = static_cast<int>(idx.size(1));
+  const int C = static_cast<int>(dwte.size(1));
+  const int tokens = B * T;
+  c10::cuda::CUDAGuard g(dy.device());
+  auto stream = at::cuda::getCurrentCUDAStream();
+  embed_bwd_tok_kernel<<<(tokens + kRowWarps - 1) / kRowWarps, kRowWarps * 32, 0, stream>>>(
+      idx.data_ptr<int64_t>(), reinterpret_cast<const __nv_bfloat16*>(dy.data_ptr()),
+      reinterpret_cast<__nv_bfloat16*>(dwte.data_ptr()), tokens, C);
+  embed_bwd_pos_kernel<<<T, 128, 0, stream>>>(reinterpret_cast<const __nv_bfloat16*>(dy.data_ptr()),
+                                             reinterpret_cast<__nv_bfloat16*>(dwpe.data_ptr()), B, T, C,
+                                             accumulate_pos ? 1 : 0);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+void xent_fwd_bwd(torch::Tensor logits, torch::Tensor targets, torch::Tensor loss, double grad_scale,
+                  int64_t ignore_index) {
+  TORCH_CHECK(logits.is_cuda() && logits.scalar_type() == at::kBFloat16 && logits.stride(1) == 1,
+              "logits must be row-major bf16");
+  TORCH_CHECK(targets.scalar_type() == at::kLong, "targets must be int64");
+  const int rows = static_cast<int>(logits.size(0));
+  const int V = static_cast<int>(logits.size(1));
+  TORCH_CHECK(logits.stride(0) % 8 == 0, "logits row stride must be a multiple of 8");
+  c10::cuda::CUDAGuard g(logits.device());
+  const size_t row_bytes = static_cast<size_t>(V) * 2;
+  if (V % 8 == 0 && row_bytes <= 200 * 1024) {
+    static size_t configured = 0;
+    if (row_bytes > configured) {
+      C10_CUDA_CHECK(cudaFuncSetAttribute(xent_smem_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                          static_cast<int>(row_bytes)));
+      configured = row_bytes;
+    }
+    xent_smem_kernel<<<rows, kXentThreads, row_bytes, at::cuda::getCurrentCUDAStream()>>>(
+        reinterpret_cast<__nv_bfloat16*>(logits.data_ptr()), targets.data_ptr<int64_t>(), loss.data_ptr<float>(), V,
+        logits.stride(0), static_cast<float>(grad_scale), static_cast<int>(ignore_index));
+    C10_CUDA_KERNEL_LAUNCH_CHECK();
+    return;
+  }
+  xent_fwd_bwd_kernel<<<rows, kXentThreads, 0, at::cuda::getCurrentCUDAStream()>>>(
+      reinterpret_cast<__nv_bfloat16*>(logits.data_ptr()), targets.data_ptr<int64_t>(), loss.data_ptr<float>(), V,
+      logits.stride(0), static_cast<float>(grad_scale), static_cast<int>(ignore_index));
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+// table: int64 [n, 6] {param, grad, master, m, v, numel}; chunks: int64 [c, 3] {entry, start, len}.
+void adamw_step(torch::Tensor table, torch::Tensor chunks, bool param_bf16, bool grad_bf16, double lr, double beta1,
+                double beta2, double eps, double wd, double bc1, double bc2, double grad_scale) {
+  TORCH_CHECK(table.is_cuda() && table.scalar_type() == at::kLong && table.size(1) == 6, "bad AdamW table");
+  TORCH_CHECK(chunks.is_cuda() && chunks.scalar_type() == at::kLong && chunks.size(1) == 3, "bad AdamW chunks");
+  c10::cuda::CUDAGuard g(table.device());
+  const int n_chunks = static_cast<int>(chunks.size(0));
+  const int blocks = std::max(1, std::min(n_chunks, 148 * 8));
+  adamw_kernel<<<blocks, 512, 0, at::cuda::getCurrentCUDAStream()>>>(
+      reinterpret_cast<const AdamEntry*>(table.data_ptr()), reinterpret_cast<const AdamChunk*>(chunks.data_ptr()),
+      n_chunks, param_bf16, grad_bf16, static_cast<float>(lr), static_cast<float>(beta1), static_cast<float>(beta2),
+      static_cast<float>(eps), static_cast<float>(wd), static_cast<float>(bc1), static_cast<float>(bc2),
+      static_cast<float>(grad_scale));
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+}  // namespace mnb

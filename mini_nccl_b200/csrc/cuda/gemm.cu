@@ -1,0 +1,540 @@
+// tcgen05 GEMM for sm_100a: D = A * B^T with fused epilogues.
+//
+// Layout (M, N, K logical):
+//   A is [M, K] K-major (row-major, K contiguous), or with a_mn [K, M] (M contiguous)
+//   B is [N, K] K-major, or with b_mn [K, N] (N contiguous)
+// which covers every GEMM of a linear layer:
+//   forward   Y  = X  W^T : A = X  (K-major), B = W (K-major)
+//   data grad dX = dY W   : A = dY (K-major), B = W stored [N_out, K_in] -> MN-major
+//   weight    dW = dY^T X : A = dY stored [tokens, N] -> MN-major,
+//                           B = X  stored [tokens, K] -> MN-major
+//
+// Kernel structure (one CTA per SM, persistent over output tiles):
+//   warp 0      TMA producer: one elected lane streams 128x64 A and BNx64 B
+//               tiles (128-byte swizzle) into a STAGES-deep ring of shared
+//               memory, each slot guarded by a full/empty mbarrier pair.
+//   warp 1      owns the TMEM allocation (2 x BN fp32 columns: double-buffered
+//               accumulators) and one lane issues tcgen05.mma (M=128, N=BN,
+//               K=16 per instruction) and tcgen05.commit to release smem slots
+//               and to publish a finished accumulator.
+//   warps 2..5  epilogue: tcgen05.ld the accumulator (each thread owns one row),
+//               apply bias / GELU / residual / accumulate, convert, store.
+//               While they drain accumulator i the MMA warp fills accumulator
+//               i^1 for the next tile.
+// TMA loads are per-CTA (no cluster multicast).  Every wait is bounded and
+// reports through args.status instead of hanging.
+#include <ATen/cuda/CUDAContext.h>
+#include <c10/cuda/CUDAGuard.h>
+#include <cudaTypedefs.h>
+#include <torch/extension.h>
+
+#include <mutex>
+
+#include "common.cuh"
+
+namespace mnb {
+
+enum : int {
+  kEpiNone = 0,
+  kEpiBias = 1,       // + bias[col]
+  kEpiGelu = 2,       // out = gelu(acc + bias), aux = acc + bias (pre-activation)
+  kEpiResid = 4,      // + resid[row, col]
+  kEpiGeluGrad = 8,   // out = acc * gelu'(aux[row, col])
+  kEpiAccum = 16,     // out += acc (read-modify-write of the existing output)
+  kEpiOutF32 = 32,    // fp32 output instead of bf16
+};
+
+struct GemmArgs {
+  int M, N, K;
+  int k_blocks_per_split;
+  int splits;
+  void* out;
+  long long ldo;
+  long long split_stride;  // elements between split-K partial outputs (fp32 workspace)
+  const __nv_bfloat16* bias;
+  __nv_bfloat16* aux;
+  long long ldaux;
+  const __nv_bfloat16* resid;
+  long long ldr;
+  int epi;
+  int* status;
+};
+
+constexpr int kBM = 128;
+constexpr int kBK = 64;
+constexpr int kGemmThreads = 192;
+
+template <int BN, int STAGES>
+struct GemmSmem {
+  static constexpr uint32_t a_bytes = kBM * kBK * 2;
+  static constexpr uint32_t b_bytes = BN * kBK * 2;
+  static constexpr uint32_t ring = STAGES * (a_bytes + b_bytes);
+  static constexpr uint32_t bars = (2 * STAGES + 4) * 8;
+  static constexpr uint32_t total = ring + bars + 16 + 1024;  // + tmem slot + alignment slack
+};
+
+MNB_DEVICE void epilogue_store(const GemmArgs& a, int row, int col0, float* v) {
+  const int N = a.N;
+  if (row >= a.M) return;
+  const bool full = col0 + 32 <= N;
+  if (a.epi & kEpiBias) {
+#pragma unroll
+    for (int i = 0; i < 32; ++i) {
+      int c = col0 + i;
+      v[i] += (c < N) ? bf16_to_f32(a.bias[c]) : 0.f;
+    }
+  }
+  if (a.epi & kEpiGelu) {
+    __nv_bfloat16* ap = a.aux + static_cast<long long>(row) * a.ldaux + col0;
+    if (full) {
+      uint32_t pk[16];
+#pragma unroll
+      for (int i = 0; i < 16; ++i) pk[i] = pack_bf16x2(v[2 * i], v[2 * i + 1]);
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+        st_v4(ap + 8 * i, make_uint4(pk[4 * i], pk[4 * i + 1], pk[4 * i + 2], pk[4 * i + 3]));
+    } else {
+      for (int i = 0; i < 32 && col0 + i < N; ++i) ap[i] = f32_to_bf16(v[i]);
+    }
+#pragma unroll
+    for (int i = 0; i < 32; ++i) v[i] = gelu_exact(v[i]);
+  }
+  if (a.epi & kEpiGeluGrad) {
+    const __nv_bfloat16* ap = a.aux + static_cast<long long>(row) * a.ldaux + col0;
+    if (full) {
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        uint4 w = ld_v4(ap + 8 * i);
+        uint32_t ws[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          float2 f = unpack_bf16x2(ws[j]);
+          v[8 * i + 2 * j] *= gelu_grad(f.x);
+          v[8 * i + 2 * j + 1] *= gelu_grad(f.y);
+        }
+      }
+    } else {
+      for (int i = 0; i < 32 && col0 + i < N; ++i) v[i] *= gelu_grad(bf16_to_f32(ap[i]));
+    }
+  }
+  if (a.epi & kEpiResid) {
+    const __nv_bfloat16* rp = a.resid + static_cast<long long>(row) * a.ldr + col0;
+    if (full) {
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        uint4 w = ld_v4(rp + 8 * i);
+        uint32_t ws[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          float2 f = unpack_bf16x2(ws[j]);
+          v[8 * i + 2 * j] += f.x;
+          v[8 * i + 2 * j + 1] += f.y;
+        }
+      }
+    } else {
+      for (int i = 0; i < 32 && col0 + i < N; ++i) v[i] += bf16_to_f32(rp[i]);
+    }
+  }
+  if (a.epi & kEpiOutF32) {
+    float* op = reinterpret_cast<float*>(a.out) + static_cast<long long>(row) * a.ldo + col0;
+    if (full) {
+      if (a.epi & kEpiAccum) {
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          float4 o = reinterpret_cast<float4*>(op)[i];
+          v[4 * i] += o.x; v[4 * i + 1] += o.y; v[4 * i + 2] += o.z; v[4 * i + 3] += o.w;
+        }
+      }
+#pragma unroll
+      for (int i = 0; i < 8; ++i)
+        reinterpret_cast<float4*>(op)[i] = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
+    } else {
+      for (int i = 0; i < 32 && col0 + i < N; ++i) op[i] = (a.epi & kEpiAccum) ? op[i] + v[i] : v[i];
+    }
+    return;
+  }
+  __nv_bfloat16* op = reinterpret_cast<__nv_bfloat16*>(a.out) + static_cast<long long>(row) * a.ldo + col0;
+  if (full) {
+    if (a.epi & kEpiAccum) {
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        uint4 w = ld_v4(op + 8 * i);
+        uint32_t ws[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          float2 f = unpack_bf16x2(ws[j]);
+          v[8 * i + 2 * j] += f.x;
+          v[8 * i + 2 * j + 1] += f.y;
+        }
+      }
+    }
+    uint32_t pk[16];
+#pragma unroll
+    for (int i = 0; i < 16; ++i) pk[i] = pack_bf16x2(v[2 * i], v[2 * i + 1]);
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+      st_v4(op + 8 * i, make_uint4(pk[4 * i], pk[4 * i + 1], pk[4 * i + 2], pk[4 * i + 3]));
+  } else {
+    for (int i = 0; i < 32 && col0 + i < N; ++i) {
+      float x = v[i];
+      if (a.epi & kEpiAccum) x += bf16_to_f32(op[i]);
+      op[i] = f32_to_bf16(x);
+    }
+  }
+}
+
+template <int BN, bool A_MN, bool B_MN, int STAGES>
+__global__ void __launch_bounds__(kGemmThreads, 1)
+    gemm_tcgen05_kernel(const __grid_constant__ CUtensorMap map_a,
+                        const __grid_constant__ CUtensorMap map_b, const GemmArgs args) {
+  using S = GemmSmem<BN, STAGES>;
+  constexpr uint32_t kIdesc = idesc_bf16(kBM, BN, A_MN, B_MN);
+  constexpr uint32_t kTmemCols = 2 * BN;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  uint8_t* ring_a = smem;
+  uint8_t* ring_b = smem + STAGES * S::a_bytes;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + S::ring);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * STAGES + 4);
+  const uint32_t full0 = smem_u32(bars);
+  const uint32_t empty0 = smem_u32(bars + STAGES);
+  const uint32_t tfull0 = smem_u32(bars + 2 * STAGES);
+  const uint32_t tempty0 = smem_u32(bars + 2 * STAGES + 2);
+
+  const int warp = threadIdx.x / 32;
+  const int lane = threadIdx.x % 32;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(full0 + 8 * s, 1);
+      mbar_init(empty0 + 8 * s, 1);
+    }
+    for (int s = 0; s < 2; ++s) {
+      mbar_init(tfull0 + 8 * s, 1);
+      mbar_init(tempty0 + 8 * s, 128);
+    }
+    fence_mbar_init();
+    tma_prefetch_desc(&map_a);
+    tma_prefetch_desc(&map_b);
+  }
+  if (warp == 1) {
+    tmem_alloc(smem_u32(tmem_slot), kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  const int m_tiles = (args.M + kBM - 1) / kBM;
+  const int n_tiles = (args.N + BN - 1) / BN;
+  const int k_blocks = (args.K + kBK - 1) / kBK;
+  const int units = m_tiles * n_tiles * args.splits;
+  int* status = args.status;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      for (int u = blockIdx.x; u < units; u += gridDim.x) {
+        const int split = u / (m_tiles * n_tiles);
+        const int t = u % (m_tiles * n_tiles);
+        const int mb = t % m_tiles, nb = t / m_tiles;
+        const int kb0 = split * args.k_blocks_per_split;
+        const int kb1 = min(k_blocks, kb0 + args.k_blocks_per_split);
+        bool ok = true;
+        for (int kb = kb0; kb < kb1; ++kb) {
+          if (!mbar_wait(empty0 + 8 * stage, phase ^ 1, status)) { ok = false; break; }
+          const uint32_t full = full0 + 8 * stage;
+          mbar_arrive_expect_tx(full, S::a_bytes + S::b_bytes);
+          const uint32_t sa = smem_u32(ring_a + stage * S::a_bytes);
+          const uint32_t sb = smem_u32(ring_b + stage * S::b_bytes);
+          const int k0 = kb * kBK;
+          if (!A_MN) {
+            tma_load_2d(sa, &map_a, k0, mb * kBM, full);
+          } else {
+#pragma unroll
+            for (int j = 0; j < kBM / 64; ++j) tma_load_2d(sa + j * 8192, &map_a, mb * kBM + 64 * j, k0, full);
+          }
+          if (!B_MN) {
+            tma_load_2d(sb, &map_b, k0, nb * BN, full);
+          } else {
+#pragma unroll
+            for (int j = 0; j < BN / 64; ++j) tma_load_2d(sb + j * 8192, &map_b, nb * BN + 64 * j, k0, full);
+          }
+          if (++stage == STAGES) { stage = 0; phase ^= 1; }
+        }
+        if (!ok) break;
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      int acc = 0;
+      uint32_t acc_phase = 0;
+      for (int u = blockIdx.x; u < units; u += gridDim.x) {
+        const int split = u / (m_tiles * n_tiles);
+        const int kb0 = split * args.k_blocks_per_split;
+        const int kb1 = min(k_blocks, kb0 + args.k_blocks_per_split);
+        if (!mbar_wait(tempty0 + 8 * acc, acc_phase ^ 1, status)) break;
+        tc_fence_after();
+        const uint32_t d = tmem_base + static_cast<uint32_t>(acc * BN);
+        bool ok = true;
+        for (int kb = kb0; kb < kb1; ++kb) {
+          if (!mbar_wait(full0 + 8 * stage, phase, status)) { ok = false; break; }
+          tc_fence_after();
+          const uint32_t sa = smem_u32(ring_a + stage * S::a_bytes);
+          const uint32_t sb = smem_u32(ring_b + stage * S::b_bytes);
+#pragma unroll
+          for (int k = 0; k < kBK / 16; ++k) {
+            const uint64_t ad = A_MN ? smem_desc_sw128(sa + k * 2048, 8192, 1024)
+                                     : smem_desc_sw128(sa + k * 32, 16, 1024);
+            const uint64_t bd = B_MN ? smem_desc_sw128(sb + k * 2048, 8192, 1024)
+                                     : smem_desc_sw128(sb + k * 32, 16, 1024);
+            tc_mma(d, ad, bd, kIdesc, (kb > kb0 || k > 0) ? 1u : 0u);
+          }
+          tc_commit(empty0 + 8 * stage);  // slot free once these MMAs have read it
+          if (++stage == STAGES) { stage = 0; phase ^= 1; }
+        }
+        if (!ok) break;
+        tc_commit(tfull0 + 8 * acc);  // accumulator ready for the epilogue
+        acc ^= 1;
+        if (acc == 0) acc_phase ^= 1;
+      }
+    }
+  } else {
+    // Epilogue warps 2..5: warp w may only touch TMEM lanes 32*(w%4) .. +31.
+    const int q = warp & 3;
+    const int row_in_tile = q * 32 + lane;
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    for (int u = blockIdx.x; u < units; u += gridDim.x) {
+      const int split = u / (m_tiles * n_tiles);
+      const int t = u % (m_tiles * n_tiles);
+      const int mb = t % m_tiles, nb = t / m_tiles;
+      bool ok = mbar_wait(tfull0 + 8 * acc, acc_phase, status);
+      if (!__all_sync(0xffffffffu, ok)) break;
+      tc_fence_after();
+      GemmArgs a = args;
+      if (args.splits > 1)
+        a.out = reinterpret_cast<float*>(args.out) + static_cast<long long>(split) * args.split_stride;
+      const int row = mb * kBM + row_in_tile;
+      const uint32_t lane_addr = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + acc * BN;
+#pragma unroll 1
+      for (int c = 0; c < BN / 32; ++c) {
+        float v[32];
+        tmem_ld_32(lane_addr + c * 32, v);
+        const int col0 = nb * BN + c * 32;
+        if (col0 < a.N) epilogue_store(a, row, col0, v);
+      }
+      tc_fence_before();
+      mbar_arrive(tempty0 + 8 * acc);
+      acc ^= 1;
+      if (acc == 0) acc_phase ^= 1;
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, kTmemCols);
+  }
+}
+
+// Sum split-K fp32 partials into the final output (bf16 or fp32), optionally
+// accumulating into what is already there.
+__global__ void splitk_reduce_kernel(const float* __restrict__ ws, int splits, long long split_stride,
+                                     int M, int N, void* out, long long ldo, int out_f32, int accumulate) {
+  const long long total4 = static_cast<long long>(M) * N / 4;
+  for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < total4;
+       i += static_cast<long long>(gridDim.x) * blockDim.x) {
+    const long long e = 4 * i;
+    const int row = static_cast<int>(e / N), col = static_cast<int>(e % N);
+    float4 s = reinterpret_cast<const float4*>(ws)[i];
+    for (int k = 1; k < splits; ++k) {
+      float4 p = reinterpret_cast<const float4*>(ws + k * split_stride)[i];
+      s.x += p.x; s.y += p.y; s.z += p.z; s.w += p.w;
+    }
+    if (out_f32) {
+      float* o = reinterpret_cast<float*>(out) + row * ldo + col;
+      if (accumulate) { s.x += o[0]; s.y += o[1]; s.z += o[2]; s.w += o[3]; }
+      *reinterpret_cast<float4*>(o) = s;
+    } else {
+      __nv_bfloat16* o = reinterpret_cast<__nv_bfloat16*>(out) + row * ldo + col;
+      if (accumulate) {
+        uint2 w = *reinterpret_cast<uint2*>(o);
+        float2 a = unpack_bf16x2(w.x), b = unpack_bf16x2(w.y);
+        s.x += a.x; s.y += a.y; s.z += b.x; s.w += b.y;
+      }
+      *reinterpret_cast<uint2*>(o) = make_uint2(pack_bf16x2(s.x, s.y), pack_bf16x2(s.z, s.w));
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
+// host side
+// ---------------------------------------------------------------------------
+namespace {
+
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    cudaDriverEntryPointQueryResult q;
+    void* p = nullptr;
+    cudaError_t e = cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q);
+    TORCH_CHECK(e == cudaSuccess && q == cudaDriverEntryPointSuccess && p != nullptr,
+                "cuTensorMapEncodeTiled unavailable");
+    fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  });
+  return fn;
+}
+
+}  // namespace
+
+CUtensorMap make_tma_2d_bf16(const void* base, uint64_t inner, uint64_t outer, uint64_t row_stride_elems,
+                             uint32_t box_inner, uint32_t box_outer) {
+  TORCH_CHECK(reinterpret_cast<uintptr_t>(base) % 16 == 0, "TMA base address must be 16-byte aligned");
+  TORCH_CHECK((row_stride_elems * 2) % 16 == 0, "TMA row stride must be a multiple of 16 bytes");
+  CUtensorMap map;
+  cuuint64_t dims[2] = {inner, outer};
+  cuuint64_t strides[1] = {row_stride_elems * 2};
+  cuuint32_t box[2] = {box_inner, box_outer};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = encode_fn()(&map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides,
+                           box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                           CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  TORCH_CHECK(r == CUDA_SUCCESS, "cuTensorMapEncodeTiled failed: ", static_cast<int>(r));
+  return map;
+}
+
+int num_sms() {
+  static int n = [] {
+    int dev = 0, v = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev);
+    return v;
+  }();
+  return n;
+}
+
+template <int BN, bool A_MN, bool B_MN, int STAGES>
+void launch_gemm(const CUtensorMap& ma, const CUtensorMap& mb, const GemmArgs& args, int units,
+                 cudaStream_t stream) {
+  using S = GemmSmem<BN, STAGES>;
+  auto kern = gemm_tcgen05_kernel<BN, A_MN, B_MN, STAGES>;
+  static bool configured = false;
+  if (!configured) {
+    C10_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, S::total));
+    configured = true;
+  }
+  const int grid = std::min(units, num_sms());
+  kern<<<grid, kGemmThreads, S::total, stream>>>(ma, mb, args);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+// Inner-dim contiguity + 16-byte row strides are what TMA needs.
+static int64_t row_stride(const torch::Tensor& t, const char* name) {
+  TORCH_CHECK(t.dim() == 2, name, " must be 2-D");
+  TORCH_CHECK(t.stride(1) == 1, name, " must be contiguous in its last dimension");
+  TORCH_CHECK(t.scalar_type() == at::kBFloat16, name, " must be bfloat16");
+  TORCH_CHECK((t.stride(0) * 2) % 16 == 0, name, " row stride must be a multiple of 8 elements");
+  return t.stride(0);
+}
+
+// Public entry: out = epi(A * B^T) with the layouts described at the top.
+void gemm(torch::Tensor a, torch::Tensor b, torch::Tensor out, bool a_mn, bool b_mn,
+          c10::optional<torch::Tensor> bias, c10::optional<torch::Tensor> aux,
+          c10::optional<torch::Tensor> resid, int64_t epi, int64_t splits,
+          c10::optional<torch::Tensor> workspace, torch::Tensor status) {
+  c10::cuda::CUDAGuard guard(a.device());
+  const int64_t lda = row_stride(a, "A");
+  const int64_t ldb = row_stride(b, "B");
+  const int M = static_cast<int>(a_mn ? a.size(1) : a.size(0));
+  const int K = static_cast<int>(a_mn ? a.size(0) : a.size(1));
+  const int N = static_cast<int>(b_mn ? b.size(1) : b.size(0));
+  TORCH_CHECK((b_mn ? b.size(0) : b.size(1)) == K, "A and B disagree on K");
+  TORCH_CHECK(out.dim() == 2 && out.size(0) == M && out.size(1) == N && out.stride(1) == 1, "bad output shape");
+  TORCH_CHECK(N % 8 == 0 && K % 8 == 0, "N and K must be multiples of 8");
+  const bool out_f32 = out.scalar_type() == at::kFloat;
+  TORCH_CHECK(out_f32 || out.scalar_type() == at::kBFloat16, "output must be bf16 or fp32");
+  GemmArgs args{};
+  args.M = M;
+  args.N = N;
+  args.K = K;
+  args.epi = static_cast<int>(epi) | (out_f32 ? kEpiOutF32 : 0);
+  args.status = status.data_ptr<int>();
+  if (bias) {
+    TORCH_CHECK(bias->scalar_type() == at::kBFloat16 && bias->numel() == N, "bias must be bf16 [N]");
+    args.bias = reinterpret_cast<const __nv_bfloat16*>(bias->data_ptr());
+    args.epi |= kEpiBias;
+  }
+  if (aux) {
+    TORCH_CHECK(aux->scalar_type() == at::kBFloat16 && aux->stride(1) == 1, "aux must be bf16 row-major");
+    args.aux = reinterpret_cast<__nv_bfloat16*>(aux->data_ptr());
+    args.ldaux = aux->stride(0);
+  }
+  if (resid) {
+    TORCH_CHECK(resid->scalar_type() == at::kBFloat16 && resid->stride(1) == 1, "resid must be bf16 row-major");
+    args.resid = reinterpret_cast<const __nv_bfloat16*>(resid->data_ptr());
+    args.ldr = resid->stride(0);
+    args.epi |= kEpiResid;
+  }
+  const int k_blocks = (K + kBK - 1) / kBK;
+  splits = std::max<int64_t>(1, std::min<int64_t>(splits, k_blocks));
+  const int per = static_cast<int>((k_blocks + splits - 1) / splits);
+  splits = (k_blocks + per - 1) / per;  // no empty splits
+  args.k_blocks_per_split = per;
+  args.splits = static_cast<int>(splits);
+  if (splits > 1) {
+    TORCH_CHECK(workspace.has_value() && workspace->scalar_type() == at::kFloat &&
+                    workspace->numel() >= splits * static_cast<int64_t>(M) * N,
+                "split-K needs an fp32 workspace of splits*M*N");
+    TORCH_CHECK(!(args.epi & ~(kEpiAccum | kEpiOutF32)), "split-K supports plain/accumulate epilogues only");
+    args.out = workspace->data_ptr();
+    args.ldo = N;
+    args.split_stride = static_cast<long long>(M) * N;
+    args.epi = kEpiOutF32;
+  } else {
+    args.out = out.data_ptr();
+    args.ldo = out.stride(0);
+  }
+  const bool wide = N >= 256;
+  const int BN = wide ? 256 : 128;
+  const int m_tiles = (M + kBM - 1) / kBM;
+  const int n_tiles = (N + BN - 1) / BN;
+  const int units = m_tiles * n_tiles * static_cast<int>(splits);
+  CUtensorMap ma = a_mn ? make_tma_2d_bf16(a.data_ptr(), M, K, lda, 64, 64)
+                        : make_tma_2d_bf16(a.data_ptr(), K, M, lda, 64, kBM);
+  CUtensorMap mb = b_mn ? make_tma_2d_bf16(b.data_ptr(), N, K, ldb, 64, 64)
+                        : make_tma_2d_bf16(b.data_ptr(), K, N, ldb, 64, BN);
+  cudaStream_t stream = at::cuda::getCurrentCUDAStream();
+#define MNB_GEMM_CASE(BNV, AM, BMJ, ST)                                   \
+  if (BN == BNV && a_mn == AM && b_mn == BMJ) {                            \
+    launch_gemm<BNV, AM, BMJ, ST>(ma, mb, args, units, stream);            \
+  } else
+  MNB_GEMM_CASE(256, false, false, 4)
+  MNB_GEMM_CASE(256, false, true, 4)
+  MNB_GEMM_CASE(256, true, false, 4)
+  MNB_GEMM_CASE(256, true, true, 4)
+  MNB_GEMM_CASE(128, false, false, 6)
+  MNB_GEMM_CASE(128, false, true, 6)
+  MNB_GEMM_CASE(128, true, false, 6)
+  MNB_GEMM_CASE(128, true, true, 6) { TORCH_CHECK(false, "unsupported GEMM configuration"); }
+#undef MNB_GEMM_CASE
+  if (splits > 1) {
+    const long long total4 = static_cast<long long>(M) * N / 4;
+    const int threads = 256;
+    const int blocks = static_cast<int>(std::min<long long>((total4 + threads - 1) / threads, 148LL * 8));
+    splitk_reduce_kernel<<<blocks, threads, 0, stream>>>(
+        reinterpret_cast<const float*>(workspace->data_ptr()), static_cast<int>(splits),
+        static_cast<long long>(M) * N, M, N, out.data_ptr(), out.stride(0), out_f32 ? 1 : 0,
+        (epi & kEpiAccum) ? 1 : 0);
+    C10_CUDA_KERNEL_LAUNCH_CHECK();
+  }
+}
+
+}  // namespace mnb

@@ -30,17 +30,17 @@ def linear(x: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor | None = No
 
 
 def gelu(x: torch.Tensor) -> torch.Tensor:
-    """tanh-approximated GELU (the GPT-2 form)."""
+    """Exact (erf) GELU, as ``nn.GELU()``."""
     if x.is_cuda:
         return _kernels().Gelu.apply(x)
-    return F.gelu(x, approximate="tanh")
+    return F.gelu(x)
 
 
 def linear_gelu(x: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor | None) -> torch.Tensor:
     """``gelu(x @ weight.T + bias)``; one GEMM with a fused GELU epilogue on CUDA."""
     if x.is_cuda and _kernels().supports_gemm(x, weight):
         return _kernels().LinearGelu.apply(x, weight, bias)
-    return F.gelu(F.linear(x, weight, bias), approximate="tanh")
+    return F.gelu(F.linear(x, weight, bias))
 
 
 def layer_norm(x: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor, eps: float = 1e-5) -> torch.Tensor:
@@ -49,13 +49,15 @@ def layer_norm(x: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor, eps: f
     return F.layer_norm(x, (x.shape[-1],), weight, bias, eps)
 
 
-def causal_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, n_head: int) -> torch.Tensor:
-    """Causal softmax attention.  ``q, k, v`` are ``[B, T, H*D]`` (views allowed);
-    returns ``[B, T, H, D]``."""
-    B, T, C = q.shape
+def causal_attention(qkv: torch.Tensor, n_head: int) -> torch.Tensor:
+    """Causal softmax attention on a fused ``[B, T, 3*H*D]`` tensor laid out
+    ``[q | k | v]``; returns ``[B, T, H, D]``."""
+    B, T, C3 = qkv.shape
+    C = C3 // 3
     D = C // n_head
-    if q.is_cuda:
-        return _kernels().FlashAttention.apply(q, k, v, n_head)
+    if qkv.is_cuda:
+        return _kernels().FlashAttention.apply(qkv, n_head)
+    q, k, v = qkv.split(C, dim=-1)
     qh, kh, vh = (t.reshape(B, T, n_head, D).transpose(1, 2) for t in (q, k, v))
     y = F.scaled_dot_product_attention(qh, kh, vh, is_causal=True)
     return y.transpose(1, 2)

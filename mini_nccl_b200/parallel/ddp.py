@@ -299,7 +299,9 @@ class DistributedDataParallel(nn.Module):
     def zero_grad(self, set_to_none: bool = False) -> None:
         """Zero the buckets in place (grads must stay views, so never ``None``)."""
         if self.pg.world_size == 1:
-            self.module.zero_grad(set_to_none=False)
+            # Nothing to bucket: dropping the grads lets autograd hand each
+            # parameter its freshly computed gradient instead of a fill + add.
+            self.module.zero_grad(set_to_none=True)
             return
         for b in self._buckets:
             b.buffer.zero_()

@@ -305,8 +305,7 @@ class ParallelSelfAttention(nn.Module):
     def _attend(self, qkv: torch.Tensor) -> torch.Tensor:
         B, T, _ = qkv.shape
         w = self.local_heads * self.head_dim
-        q, k, v = qkv.split(w, dim=-1)
-        return OF.causal_attention(q, k, v, self.local_heads).reshape(B, T, w)
+        return OF.causal_attention(qkv, self.local_heads).reshape(B, T, w)
 
 
 __all__ = [

@@ -1,0 +1,182 @@
+"""Device (peer-memory) collectives across real GPUs, one process per GPU.
+
+Every rank recomputes every rank's input from seeds and checks the exact
+expected result, as the host battery does.  Needs >= 2 GPUs; on a 1-GPU box
+these tests skip (kernels that wait on each other never share one GPU).
+"""
+
+from __future__ import annotations
+
+import os
+
+import pytest
+import torch
+
+pytestmark = [pytest.mark.gpu, pytest.mark.multigpu]
+
+from mini_nccl_b200 import collectives as C  # noqa: E402
+from mini_nccl_b200.launcher import run  # noqa: E402
+
+
+def n_gpus() -> int:
+    return torch.cuda.device_count() if torch.cuda.is_available() else 0
+
+
+needs2 = pytest.mark.skipif(n_gpus() < 2, reason="needs at least 2 GPUs")
+
+
+def seeded(rank: int, numel: int, dtype: torch.dtype, dev) -> torch.Tensor:
+    g = torch.Generator().manual_seed(9000 + rank)
+    if dtype.is_floating_point:
+        return torch.randn(numel, generator=g).to(dtype).to(dev)
+    return torch.randint(-40, 40, (numel,), generator=g, dtype=dtype).to(dev)
+
+
+def expected(world: int, numel: int, dtype, op: str, dev) -> torch.Tensor:
+    parts = [seeded(r, numel, dtype, "cpu").double() if dtype.is_floating_point else seeded(r, numel, dtype, "cpu")
+             for r in range(world)]
+    out = parts[0].clone()
+    for p in parts[1:]:
+        out = {"sum": out + p, "prod": out * p, "max": torch.maximum(out, p), "min": torch.minimum(out, p)}[op]
+    return out.to(dev)
+
+
+def _battery(pg) -> None:
+    dev = torch.device("cuda", torch.cuda.current_device())
+    W, r = pg.world_size, pg.rank
+    tol = {torch.float32: 1e-5, torch.bfloat16: 2e-2, torch.int64: 0}
+    for algorithm in ("one_shot", "two_shot", "ring", "tree", "halving", "naive"):
+        for dtype in (torch.float32, torch.bfloat16, torch.int64):
+            for op in ("sum", "max", "min"):
+                for numel in (1, 3, 1000, 262_147):
+                    t = seeded(r, numel, dtype, dev)
+                    C.all_reduce(pg, t, op=op, algorithm=algorithm)
+                    want = expected(W, numel, dtype, op, dev)
+                    if dtype == torch.int64:
+                        assert torch.equal(t, want), (algorithm, op, numel)
+                    else:
+                        err = (t.double() - want).abs().max().item()
+                        assert err <= tol[dtype] * (want.abs().max().item() + 1), (algorithm, dtype, op, numel, err)
+    # identical bits on every rank (fixed reduction order)
+    t = seeded(r, 4096, torch.float32, dev)
+    C.all_reduce(pg, t, algorithm="two_shot")
+    everyone = C.all_gather(pg, t)
+    for other in everyone:
+        assert torch.equal(other, everyone[0])
+    # scale fused into the kernel (DDP averaging) and symmetric in-place path
+    dc = pg.device_comm()
+    sym = dc.symmetric_zeros(1 << 20, torch.bfloat16)
+    sym.copy_(seeded(r, 1 << 20, torch.bfloat16, dev))
+    dc.all_reduce(sym, algorithm="two_shot", scale=1.0 / W)
+    want = expected(W, 1 << 20, torch.bfloat16, "sum", dev) / W
+    assert (sym.double() - want).abs().max().item() < 3e-2
+    # narrow wire: fp32 tensor, bf16 on the wire, fp32 accumulation
+    t = seeded(r, 100_003, torch.float32, dev)
+    C.all_reduce(pg, t, algorithm="two_shot", wire_dtype=torch.bfloat16)
+    want = expected(W, 100_003, torch.float32, "sum", dev)
+    assert (t.double() - want).abs().max().item() < 0.05
+    # broadcast from every root
+    for src in range(W):
+        t = seeded(r, 4097, torch.float32, dev)
+        C.broadcast(pg, t, src=src)
+        assert torch.equal(t, seeded(src, 4097, torch.float32, dev))
+    # all_gather in rank order
+    t = seeded(r, 6 * 13, torch.bfloat16, dev).view(6, 13)
+    got = C.all_gather(pg, t)
+    for i, g in enumerate(got):
+        assert torch.equal(g, seeded(i, 6 * 13, torch.bfloat16, dev).view(6, 13))
+    # reduce_scatter: my chunk of the sum, input untouched
+    n = 1000 * W
+    t = seeded(r, n, torch.float32, dev)
+    before = t.clone()
+    mine = C.reduce_scatter(pg, t)
+    want = expected(W, n, torch.float32, "sum", dev).view(W, -1)[r]
+    assert (mine.double() - want).abs().max().item() < 1e-4
+    assert torch.equal(t, before)
+    # all_to_all
+    n = 9 * W
+    out = C.all_to_all(pg, seeded(r, n, torch.float32, dev))
+    for src in range(W):
+        assert torch.equal(out.view(W, -1)[src], seeded(src, n, torch.float32, dev).view(W, -1)[r])
+    # large message through a grown staging buffer
+    big = seeded(r, 40 << 20, torch.bfloat16, dev)  # 80 MB > initial staging
+    C.all_reduce(pg, big)
+    C.barrier(pg)
+    dc.synchronize()
+
+
+@needs2
+def test_device_collective_battery():
+    run(_battery, 2, devices="cuda", timeout=600.0, op_timeout=60.0)
+
+
+def _ddp_parity(pg) -> None:
+    import copy
+
+    import torch.nn.functional as F
+    from torch import nn
+
+    from mini_nccl_b200.ddp import DistributedDataParallel
+
+    dev = torch.device("cuda", torch.cuda.current_device())
+    W, per = pg.world_size, 8
+    torch.manual_seed(0)
+    model = nn.Sequential(nn.Linear(16, 64), nn.Tanh(), nn.Linear(64, 1)).to(dev)
+    ref = copy.deepcopy(model)
+    ddp = DistributedDataParallel(model, pg, bucket_cap_mb=0.001)
+    assert len(ddp._buckets) > 1
+    opt = torch.optim.SGD(model.parameters(), lr=0.1, momentum=0.9)
+    ropt = torch.optim.SGD(ref.parameters(), lr=0.1, momentum=0.9)
+    gen = torch.Generator().manual_seed(42)
+    for _ in range(5):
+        x = torch.randn(W * per, 16, generator=gen).to(dev)
+        y = torch.randn(W * per, 1, generator=gen).to(dev)
+        mine = slice(pg.rank * per, (pg.rank + 1) * per)
+        ddp.zero_grad()
+        F.mse_loss(ddp(x[mine]), y[mine]).backward()
+        ddp.sync()
+        opt.step()
+        ropt.zero_grad()
+        F.mse_loss(ref(x), y).backward()
+        ropt.step()
+    for p, q in zip(model.parameters(), ref.parameters()):
+        torch.testing.assert_close(p, q, rtol=1e-4, atol=1e-5)
+
+
+@needs2
+def test_ddp_on_gpus_matches_single_process():
+    run(_ddp_parity, 2, devices="cuda", timeout=600.0, op_timeout=60.0)
+
+
+def _timeout(pg) -> str:
+    """Rank 1 never launches its half: rank 0's kernel must time out cleanly."""
+    from mini_nccl_b200.errors import CollectiveTimeoutError
+
+    dev = torch.device("cuda", torch.cuda.current_device())
+    dc = pg.device_comm()
+    dc.set_timeout(1.0)
+    C.barrier(pg)  # host barrier: both communicators exist
+    if pg.rank == 1:
+        C.barrier(pg)  # wait (on the host) until rank 0 has seen its error
+        return "withheld"
+    t = torch.ones(1024, device=dev)
+    dc.all_reduce(t, algorithm="one_shot")
+    try:
+        dc.synchronize()
+    except CollectiveTimeoutError as exc:
+        assert "timed out waiting for rank 1" in str(exc)
+        outcome = "timeout"
+    else:
+        outcome = "no error"
+    # the context must still work afterwards
+    x = torch.arange(10.0, device=dev)
+    assert float(x.sum()) == 45.0
+    C.barrier(pg)
+    return outcome
+
+
+@needs2
+def test_device_wait_times_out_without_hanging(monkeypatch):
+    monkeypatch.setenv("NCCL_NVLS_ENABLE", "0")
+    results = run(_timeout, 2, devices="cuda", timeout=300.0, op_timeout=60.0)
+    assert results[0] == "timeout", results
