@@ -1,0 +1,352 @@
+// Causal flash-attention forward on the 5th-generation tensor cores (tcgen05).
+//
+// One CTA computes 128 query rows of one (batch, head).  Roles:
+//   warp 0      TMA producer: Q once, then K_j / V_j tiles (128 keys x D,
+//               128-byte swizzle) into a KV_STAGES-deep ring.
+//   warp 1      TMEM owner; one lane issues the MMAs:
+//                 S_j  = Q K_j^T        (M=128, N=128 keys, K=D)   -> TMEM cols [0, 128)
+//                 O_j  = P_j V_j        (M=128, N=D,   K=128 keys) -> TMEM cols [128, 128+D)
+//               P_j comes from shared memory (bf16, K-major); V_j is read
+//               MN-major straight from its TMA tile.
+//   warps 2..5  softmax: thread = one query row.  tcgen05.ld S_j, online
+//               softmax in base 2, write P_j to shared memory, then fold
+//               O_{j-1} from TMEM into a register accumulator with the
+//               running rescale; finally normalise and store O and the LSE.
+// S_{j+1} = Q K_{j+1}^T is issued as soon as the softmax has read S_j, so the
+// tensor core overlaps the softmax of the previous tile.  256 TMEM columns
+// per CTA lets two CTAs share an SM.  All waits are bounded (status word).
+//
+// Same algorithm as the mma.sync kernel in attention.cu (FlashAttention-2
+// online softmax, causal tile skipping); inputs/outputs identical.
+#include <ATen/cuda/CUDAContext.h>
+#include <c10/cuda/CUDAGuard.h>
+#include <torch/extension.h>
+
+#include "common.cuh"
+
+namespace mnb {
+
+CUtensorMap make_tma_2d_bf16(const void* base, uint64_t inner, uint64_t outer, uint64_t row_stride_elems,
+                             uint32_t box_inner, uint32_t box_outer);
+
+namespace fatc {
+
+constexpr int kQ = 128;        // queries per CTA
+constexpr int kKV = 128;       // keys per tile
+constexpr int kSoftWarps = 8;  // two per TMEM lane quadrant, each owning half the keys
+constexpr int kSoftThreads = 32 * kSoftWarps;
+constexpr int kThreads = 64 + kSoftThreads;  // producer, MMA, softmax warps
+constexpr float kLog2e = 1.4426950408889634f;
+
+MNB_DEVICE void fence_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+MNB_DEVICE float fast_exp2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+MNB_DEVICE void softmax_barrier() { asm volatile("bar.sync 1, %0;" ::"n"(kSoftThreads) : "memory"); }
+
+template <int D, int KV_STAGES>
+struct Smem {
+  static constexpr uint32_t q_bytes = kQ * D * 2;
+  static constexpr uint32_t kv_bytes = kKV * D * 2;
+  static constexpr uint32_t p_bytes = kQ * kKV * 2;
+  static constexpr uint32_t q_off = 0;
+  static constexpr uint32_t k_off = q_bytes;
+  static constexpr uint32_t v_off = k_off + KV_STAGES * kv_bytes;
+  static constexpr uint32_t p_off = v_off + KV_STAGES * kv_bytes;
+  // float [3][2][kQ]: row-max exchange for even / odd tiles, then the row sums
+  static constexpr uint32_t red_off = p_off + p_bytes;
+  static constexpr uint32_t bar_off = red_off + 3 * 2 * kQ * 4;
+  static constexpr int n_bars = 7 + 4 * KV_STAGES;
+  static constexpr uint32_t total = bar_off + n_bars * 8 + 16 + 1024;
+};
+
+template <int D, int KV_STAGES>
+__global__ void __launch_bounds__(kThreads, D == 64 ? 2 : 1)
+    fa_fwd_tc_kernel(const __grid_constant__ CUtensorMap map_qkv, __nv_bfloat16* __restrict__ o,
+                     float* __restrict__ lse, int H, int T, float scale, int* status) {
+  using S = Smem<D, KV_STAGES>;
+  constexpr uint32_t kTmemCols = 256;
+  constexpr uint32_t kIdescS = idesc_bf16(kQ, kKV, false, false);
+  constexpr uint32_t kIdescO = idesc_bf16(kQ, D, false, true);
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const uint32_t sbase = smem_u32(sm);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sm + S::bar_off);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + S::n_bars);
+  const uint32_t b0 = smem_u32(bars);
+  const uint32_t q_full = b0, s_full = b0 + 8, s_free = b0 + 16, p_full = b0 + 24, p_free = b0 + 32,
+                 o_full = b0 + 40, o_free = b0 + 48;
+  // K_j is released as soon as S_j has been computed, V_j once P_j V_j has:
+  // separate barriers so a single-stage ring cannot deadlock on V.
+  const uint32_t k_full0 = b0 + 56, v_full0 = k_full0 + 8 * KV_STAGES, k_empty0 = v_full0 + 8 * KV_STAGES,
+                 v_empty0 = k_empty0 + 8 * KV_STAGES;
+
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  const int qt = gridDim.x - 1 - blockIdx.x;  // longest causal rows first
+  const int bh = blockIdx.y;
+  const int b = bh / H, h = bh % H;
+  const int q0 = qt * kQ;
+  const int C = H * D;
+  const int n_kv = min(qt + 1, (T + kKV - 1) / kKV);
+
+  if (threadIdx.x == 0) {
+    mbar_init(q_full, 1);
+    mbar_init(s_full, 1);
+    mbar_init(s_free, kSoftThreads);
+    mbar_init(p_full, kSoftThreads);
+    mbar_init(p_free, 1);
+    mbar_init(o_full, 1);
+    mbar_init(o_free, kSoftThreads);
+    for (int s = 0; s < KV_STAGES; ++s) {
+      mbar_init(k_full0 + 8 * s, 1);
+      mbar_init(v_full0 + 8 * s, 1);
+      mbar_init(k_empty0 + 8 * s, 1);
+      mbar_init(v_empty0 + 8 * s, 1);
+    }
+    fence_mbar_init();
+    tma_prefetch_desc(&map_qkv);
+  }
+  if (warp == 1) {
+    tmem_alloc(smem_u32(tmem_slot), kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  const uint32_t tS = tmem, tO = tmem + kKV;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      const int row0 = b * T;
+      mbar_arrive_expect_tx(q_full, S::q_bytes);
+#pragma unroll
+      for (int c = 0; c < D / 64; ++c)
+        tma_load_2d(sbase + S::q_off + c * (kQ * 128), &map_qkv, h * D + c * 64, row0 + q0, q_full);
+      for (int j = 0; j < n_kv; ++j) {
+        const int st = j % KV_STAGES;
+        const uint32_t ph = (j / KV_STAGES) & 1;
+        if (!mbar_wait(k_empty0 + 8 * st, ph ^ 1, status)) break;
+        mbar_arrive_expect_tx(k_full0 + 8 * st, S::kv_bytes);
+#pragma unroll
+        for (int c = 0; c < D / 64; ++c)
+          tma_load_2d(sbase + S::k_off + st * S::kv_bytes + c * (kKV * 128), &map_qkv, C + h * D + c * 64,
+                      row0 + j * kKV, k_full0 + 8 * st);
+        if (!mbar_wait(v_empty0 + 8 * st, ph ^ 1, status)) break;
+        mbar_arrive_expect_tx(v_full0 + 8 * st, S::kv_bytes);
+#pragma unroll
+        for (int c = 0; c < D / 64; ++c)
+          tma_load_2d(sbase + S::v_off + st * S::kv_bytes + c * (kKV * 128), &map_qkv, 2 * C + h * D + c * 64,
+                      row0 + j * kKV, v_full0 + 8 * st);
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      bool ok = mbar_wait(q_full, 0, status);
+      auto pv = [&](int i) -> bool {
+        const int st = i % KV_STAGES;
+        if (!mbar_wait(v_full0 + 8 * st, (i / KV_STAGES) & 1, status)) return false;
+        if (!mbar_wait(p_full, i & 1, status)) return false;
+        if (!mbar_wait(o_free, (i & 1) ^ 1, status)) return false;
+        tc_fence_after();
+        const uint32_t pa = sbase + S::p_off;
+        const uint32_t vb = sbase + S::v_off + st * S::kv_bytes;
+#pragma unroll
+        for (int kk = 0; kk < kKV / 16; ++kk) {
+          const uint64_t ad = smem_desc_sw128(pa + (kk / 4) * (kQ * 128) + (kk % 4) * 32, 16, 1024);
+          const uint64_t bd = smem_desc_sw128(vb + kk * 2048, kKV * 128, 1024);
+          tc_mma(tO, ad, bd, kIdescO, kk > 0 ? 1u : 0u);
+        }
+        tc_commit(o_full);
+        tc_commit(p_free);
+        tc_commit(v_empty0 + 8 * st);
+        return true;
+      };
+      for (int j = 0; j < n_kv && ok; ++j) {
+        const int st = j % KV_STAGES;
+        ok = mbar_wait(k_full0 + 8 * st, (j / KV_STAGES) & 1, status) && mbar_wait(s_free, (j & 1) ^ 1, status);
+        if (!ok) break;
+        tc_fence_after();
+        const uint32_t qa = sbase + S::q_off;
+        const uint32_t kb = sbase + S::k_off + st * S::kv_bytes;
+#pragma unroll
+        for (int kk = 0; kk < D / 16; ++kk) {
+          const uint64_t ad = smem_desc_sw128(qa + (kk / 4) * (kQ * 128) + (kk % 4) * 32, 16, 1024);
+          const uint64_t bd = smem_desc_sw128(kb + (kk / 4) * (kKV * 128) + (kk % 4) * 32, 16, 1024);
+          tc_mma(tS, ad, bd, kIdescS, kk > 0 ? 1u : 0u);
+        }
+        tc_commit(s_full);
+        tc_commit(k_empty0 + 8 * st);
+        if (j >= 1) ok = pv(j - 1);
+      }
+      if (ok && n_kv > 0) pv(n_kv - 1);
+    }
+  } else {
+    // softmax: warp w owns TMEM lanes 32*(w%4) (query rows); warps w and w+4
+    // split each row's 128 keys (and the D output columns) in halves.
+    const int qd = warp & 3;
+    const int half = (warp - 2) / 4;
+    const int r = qd * 32 + lane;  // row within the tile
+    const int qrow = q0 + r;
+    const uint32_t lane_base = static_cast<uint32_t>(qd * 32) << 16;
+    const uint32_t s_cols = tS + lane_base + half * (kKV / 2);
+    const uint32_t o_cols = tO + lane_base + half * (D / 2);
+    float* red = reinterpret_cast<float*>(sm + S::red_off);  // [tile parity][half][row]
+    const float sl2 = scale * kLog2e;
+    float oacc[D / 2];
+#pragma unroll
+    for (int i = 0; i < D / 2; ++i) oacc[i] = 0.f;
+    float m_run = -INFINITY, l_run = 0.f, alpha_prev = 0.f;  // m_run in scaled log2 units
+    bool ok = true;
+    uint8_t* pbase = sm + S::p_off + half * (kQ * 128);      // this half's 64-key atom
+    for (int j = 0; j < n_kv; ++j) {
+      ok = __all_sync(0xffffffffu, mbar_wait(s_full, j & 1, status));
+      if (!ok) break;
+      tc_fence_after();
+      const int k0 = j * kKV + half * (kKV / 2);
+      const bool masked = (j * kKV + kKV - 1 > q0) || (j * kKV + kKV > T);
+      // pass 1: this half-row's max of the raw scores
+      float mraw = -INFINITY;
+#pragma unroll 1
+      for (int c = 0; c < kKV / 64; ++c) {
+        float sv[32];
+        tmem_ld_32(s_cols + c * 32, sv);
+        if (masked) {
+#pragma unroll
+          for (int i = 0; i < 32; ++i) {
+            const int key = k0 + c * 32 + i;
+            if (key <= qrow && key < T) mraw = fmaxf(mraw, sv[i]);
+          }
+        } else {
+#pragma unroll
+          for (int i = 0; i < 32; ++i) mraw = fmaxf(mraw, sv[i]);
+        }
+      }
+      red[(j & 1) * 2 * kQ + half * kQ + r] = mraw;
+      softmax_barrier();
+      mraw = fmaxf(mraw, red[(j & 1) * 2 * kQ + (half ^ 1) * kQ + r]);
+      const float mx = fmaxf(m_run, mraw * sl2);
+      const float alpha = (m_run == -INFINITY) ? 0.f : fast_exp2(m_run - mx);
+      m_run = mx;
+      if (j >= 1) {
+        ok = __all_sync(0xffffffffu, mbar_wait(p_free, (j - 1) & 1, status));
+        if (!ok) break;
+      }
+      // pass 2: p = 2^(s*scale*log2e - m), row sum, bf16 P into this half's atom
+      float rs = 0.f;
+#pragma unroll 1
+      for (int c = 0; c < kKV / 64; ++c) {
+        float sv[32];
+        tmem_ld_32(s_cols + c * 32, sv);
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+          float pv = fast_exp2(fmaf(sv[i], sl2, -mx));
+          if (masked) {
+            const int key = k0 + c * 32 + i;
+            pv = (key <= qrow && key < T) ? pv : 0.f;
+          }
+          sv[i] = pv;
+          rs += pv;
+        }
+#pragma unroll
+        for (int q8 = 0; q8 < 4; ++q8) {
+          const int chunk = c * 4 + q8;  // 16-byte chunk within the 64-key atom
+          const uint32_t off = (r / 8) * 1024 + (r % 8) * 128 + ((chunk ^ (r % 8)) * 16);
+          const float* f = sv + 8 * q8;
+          *reinterpret_cast<uint4*>(pbase + off) =
+              make_uint4(pack_bf16x2(f[0], f[1]), pack_bf16x2(f[2], f[3]), pack_bf16x2(f[4], f[5]),
+                         pack_bf16x2(f[6], f[7]));
+        }
+      }
+      tc_fence_before();
+      mbar_arrive(s_free);
+      l_run = l_run * alpha + rs;
+      fence_async_smem();
+      mbar_arrive(p_full);
+      if (j >= 1) {
+        ok = __all_sync(0xffffffffu, mbar_wait(o_full, (j - 1) & 1, status));
+        if (!ok) break;
+        tc_fence_after();
+#pragma unroll
+        for (int c = 0; c < D / 64; ++c) {
+          float ov[32];
+          tmem_ld_32(o_cols + c * 32, ov);
+#pragma unroll
+          for (int i = 0; i < 32; ++i) oacc[c * 32 + i] = fmaf(oacc[c * 32 + i], alpha_prev, ov[i]);
+        }
+        tc_fence_before();
+        mbar_arrive(o_free);
+      }
+      alpha_prev = alpha;
+    }
+    if (ok && n_kv > 0) {
+      ok = __all_sync(0xffffffffu, mbar_wait(o_full, (n_kv - 1) & 1, status));
+      if (ok) {
+        tc_fence_after();
+#pragma unroll
+        for (int c = 0; c < D / 64; ++c) {
+          float ov[32];
+          tmem_ld_32(o_cols + c * 32, ov);
+#pragma unroll
+          for (int i = 0; i < 32; ++i) oacc[c * 32 + i] = fmaf(oacc[c * 32 + i], alpha_prev, ov[i]);
+        }
+        tc_fence_before();
+      }
+    }
+    // the two halves' row sums share m_run, so the full sum is their total
+    red[4 * kQ + half * kQ + r] = l_run;
+    softmax_barrier();
+    const float l_tot = l_run + red[4 * kQ + (half ^ 1) * kQ + r];
+    if (ok && qrow < T) {
+      const float inv = l_tot > 0.f ? 1.f / l_tot : 0.f;
+      __nv_bfloat16* orow = o + (static_cast<long long>(b) * T + qrow) * C + h * D + half * (D / 2);
+#pragma unroll
+      for (int c = 0; c < D / 16; ++c) {
+        uint4 v = make_uint4(pack_bf16x2(oacc[8 * c] * inv, oacc[8 * c + 1] * inv),
+                             pack_bf16x2(oacc[8 * c + 2] * inv, oacc[8 * c + 3] * inv),
+                             pack_bf16x2(oacc[8 * c + 4] * inv, oacc[8 * c + 5] * inv),
+                             pack_bf16x2(oacc[8 * c + 6] * inv, oacc[8 * c + 7] * inv));
+        *reinterpret_cast<uint4*>(orow + 8 * c) = v;
+      }
+      if (half == 0) lse[(static_cast<long long>(b) * H + h) * T + qrow] = (m_run + log2f(l_tot)) / kLog2e;
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, kTmemCols);
+  }
+}
+
+}  // namespace fatc
+
+// qkv: [B, T, 3*H*D] bf16 (row stride 3C, q|k|v thirds); o: [B, T, H*D]; lse: [B, H, T].
+void flash_attn_fwd_tc(torch::Tensor qkv, torch::Tensor o, torch::Tensor lse, int64_t n_head, double scale,
+                       torch::Tensor status) {
+  TORCH_CHECK(qkv.is_cuda() && qkv.scalar_type() == at::kBFloat16 && qkv.dim() == 3 && qkv.is_contiguous(),
+              "qkv must be a contiguous CUDA bf16 [B, T, 3C] tensor");
+  const int B = static_cast<int>(qkv.size(0)), T = static_cast<int>(qkv.size(1));
+  const int C3 = static_cast<int>(qkv.size(2));
+  const int H = static_cast<int>(n_head);
+  const int D = C3 / 3 / H;
+  TORCH_CHECK(D == 64 || D == 128, "tcgen05 attention supports head dim 64 or 128");
+  c10::cuda::CUDAGuard g(qkv.device());
+  CUtensorMap map = make_tma_2d_bf16(qkv.data_ptr(), C3, static_cast<uint64_t>(B) * T, C3, 64, 128);
+  dim3 grid((T + fatc::kQ - 1) / fatc::kQ, B * H);
+  auto stream = at::cuda::getCurrentCUDAStream();
+  auto run = [&](auto kern, uint32_t smem) {
+    C10_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+    kern<<<grid, fatc::kThreads, smem, stream>>>(map, reinterpret_cast<__nv_bfloat16*>(o.data_ptr()),
+                                                 lse.data_ptr<float>(), H, T, static_cast<float>(scale),
+                                                 status.data_ptr<int>());
+  };
+  if (D == 64) run(fatc::fa_fwd_tc_kernel<64, 2>, fatc::Smem<64, 2>::total);
+  else run(fatc::fa_fwd_tc_kernel<128, 2>, fatc::Smem<128, 2>::total);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+}  // namespace mnb

@@ -28,6 +28,9 @@ void flash_attn_fwd(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Te
 void flash_attn_bwd(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tensor o, torch::Tensor dout,
                     torch::Tensor lse, torch::Tensor dq, torch::Tensor dk, torch::Tensor dv, torch::Tensor dq_acc,
                     torch::Tensor delta, int64_t n_head, double scale);
+// attention_tc.cu
+void flash_attn_fwd_tc(torch::Tensor qkv, torch::Tensor o, torch::Tensor lse, int64_t n_head, double scale,
+                       torch::Tensor status);
 // comm.cu
 void register_comm(pybind11::module_& m);
 }  // namespace mnb
@@ -48,5 +51,6 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("adamw_step", &mnb::adamw_step);
   m.def("flash_attn_fwd", &mnb::flash_attn_fwd);
   m.def("flash_attn_bwd", &mnb::flash_attn_bwd);
+  m.def("flash_attn_fwd_tc", &mnb::flash_attn_fwd_tc, "tcgen05 flash attention forward");
   mnb::register_comm(m);
 }

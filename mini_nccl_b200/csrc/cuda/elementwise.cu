@@ -185,18 +185,31 @@ __global__ void layernorm_bwd_kernel(const __nv_bfloat16* __restrict__ dy, const
 }
 
 // out[c] (+)= sum over `nparts` rows of part[:, c]; bf16 or fp32 destination.
-__global__ void fold_partials_kernel(const float* __restrict__ part, int nparts, long long stride, int C,
-                                     void* out, int out_f32, int accumulate) {
-  const int c = blockIdx.x * blockDim.x + threadIdx.x;
-  if (c >= C) return;
+// Block = 32 columns x 8 warps; warp w sums parts w, w+8, ... and the 8 warp
+// sums are combined in shared memory, so long part lists stay parallel.
+__global__ void __launch_bounds__(256) fold_partials_kernel(const float* __restrict__ part, int nparts,
+                                                            long long stride, int C, void* out, int out_f32,
+                                                            int accumulate) {
+  __shared__ float red[8][33];
+  const int lane = threadIdx.x % 32, warp = threadIdx.x / 32;
+  const int c = blockIdx.x * 32 + lane;
   float s = 0.f;
-  for (int p = 0; p < nparts; ++p) s += part[p * stride + c];
+  if (c < C) {
+#pragma unroll 4
+    for (int p = warp; p < nparts; p += 8) s += part[p * stride + c];
+  }
+  red[warp][lane] = s;
+  __syncthreads();
+  if (warp != 0 || c >= C) return;
+  float t = 0.f;
+#pragma unroll
+  for (int w = 0; w < 8; ++w) t += red[w][lane];
   if (out_f32) {
     float* o = reinterpret_cast<float*>(out);
-    o[c] = accumulate ? o[c] + s : s;
+    o[c] = accumulate ? o[c] + t : t;
   } else {
     __nv_bfloat16* o = reinterpret_cast<__nv_bfloat16*>(out);
-    o[c] = f32_to_bf16(accumulate ? bf16_to_f32(o[c]) + s : s);
+    o[c] = f32_to_bf16(accumulate ? bf16_to_f32(o[c]) + t : t);
   }
 }
 
@@ -415,12 +428,27 @@ __global__ void __launch_bounds__(kXentThreads) xent_smem_kernel(__nv_bfloat16* 
   extern __shared__ __align__(16) uint8_t xs_raw[];
   __nv_bfloat16* row_s = reinterpret_cast<__nv_bfloat16*>(xs_raw);
   __shared__ float sm[32], ss[32];
+  __shared__ __align__(8) uint64_t bar;
   const int row = blockIdx.x;
   __nv_bfloat16* z = logits + static_cast<long long>(row) * ld;
+  // One bulk (TMA) copy brings the whole row in: far more bytes in flight per
+  // SM than per-thread loads, which is what a streaming kernel needs.
+  const uint32_t bar_a = smem_u32(&bar);
+  if (threadIdx.x == 0) {
+    mbar_init(bar_a, 1);
+    fence_mbar_init();
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    const uint32_t bytes = static_cast<uint32_t>(V) * 2;
+    mbar_arrive_expect_tx(bar_a, bytes);
+    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
+                 ::"r"(smem_u32(row_s)), "l"(z), "r"(bytes), "r"(bar_a) : "memory");
+  }
+  mbar_wait(bar_a, 0, nullptr);
   float m = -INFINITY, s = 0.f;
   for (int c = threadIdx.x * 8; c < V; c += kXentThreads * 8) {
-    uint4 raw = ld_v4(z + c);
-    st_v4(row_s + c, raw);
+    uint4 raw = ld_v4(row_s + c);
     float f[8];
     const uint32_t ws[4] = {raw.x, raw.y, raw.z, raw.w};
 #pragma unroll
@@ -594,10 +622,10 @@ void layernorm_bwd(torch::Tensor dy, torch::Tensor x, torch::Tensor w, torch::Te
   else launch(layernorm_bwd_kernel<0>);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
   const bool f32 = dw.scalar_type() == at::kFloat;
-  fold_partials_kernel<<<(C + 255) / 256, 256, 0, stream>>>(partials.data_ptr<float>(), blocks, 2LL * C, C,
-                                                             dw.data_ptr(), f32, accumulate);
-  fold_partials_kernel<<<(C + 255) / 256, 256, 0, stream>>>(partials.data_ptr<float>() + C, blocks, 2LL * C, C,
-                                                             db.data_ptr(), f32, accumulate);
+  fold_partials_kernel<<<(C + 31) / 32, 256, 0, stream>>>(partials.data_ptr<float>(), blocks, 2LL * C, C,
+                                                           dw.data_ptr(), f32, accumulate);
+  fold_partials_kernel<<<(C + 31) / 32, 256, 0, stream>>>(partials.data_ptr<float>() + C, blocks, 2LL * C, C,
+                                                           db.data_ptr(), f32, accumulate);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
@@ -614,8 +642,8 @@ void bias_grad(torch::Tensor g, torch::Tensor out, torch::Tensor partials, bool 
   auto stream = at::cuda::getCurrentCUDAStream();
   colsum_partial_kernel<<<dim3((C + 255) / 256, yb), 256, 0, stream>>>(
       reinterpret_cast<const __nv_bfloat16*>(g.data_ptr()), partials.data_ptr<float>(), rows, C);
-  fold_partials_kernel<<<(C + 255) / 256, 256, 0, stream>>>(partials.data_ptr<float>(), yb, C, C, out.data_ptr(),
-                                                             out.scalar_type() == at::kFloat, accumulate);
+  fold_partials_kernel<<<(C + 31) / 32, 256, 0, stream>>>(partials.data_ptr<float>(), yb, C, C, out.data_ptr(),
+                                                           out.scalar_type() == at::kFloat, accumulate);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
@@ -685,7 +713,8 @@ void xent_fwd_bwd(torch::Tensor logits, torch::Tensor targets, torch::Tensor los
   TORCH_CHECK(logits.stride(0) % 8 == 0, "logits row stride must be a multiple of 8");
   c10::cuda::CUDAGuard g(logits.device());
   const size_t row_bytes = static_cast<size_t>(V) * 2;
-  if (V % 8 == 0 && row_bytes <= 200 * 1024) {
+  if (V % 8 == 0 && row_bytes <= 200 * 1024 && (logits.stride(0) * 2) % 16 == 0 &&
+      reinterpret_cast<uintptr_t>(logits.data_ptr()) % 16 == 0) {
     static size_t configured = 0;
     if (row_bytes > configured) {
       C10_CUDA_CHECK(cudaFuncSetAttribute(xent_smem_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,

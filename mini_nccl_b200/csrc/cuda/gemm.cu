@@ -62,7 +62,8 @@ struct GemmArgs {
 
 constexpr int kBM = 128;
 constexpr int kBK = 64;
-constexpr int kGemmThreads = 192;
+constexpr int kEpiWarps = 8;  // two warps per TMEM lane quadrant, each owning half the columns
+constexpr int kGemmThreads = 64 + 32 * kEpiWarps;
 
 template <int BN, int STAGES>
 struct GemmSmem {
@@ -212,7 +213,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     }
     for (int s = 0; s < 2; ++s) {
       mbar_init(tfull0 + 8 * s, 1);
-      mbar_init(tempty0 + 8 * s, 128);
+      mbar_init(tempty0 + 8 * s, 32 * kEpiWarps);
     }
     fence_mbar_init();
     tma_prefetch_desc(&map_a);
@@ -305,8 +306,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       }
     }
   } else {
-    // Epilogue warps 2..5: warp w may only touch TMEM lanes 32*(w%4) .. +31.
+    // Epilogue warps 2..9: warp w may only touch TMEM lanes 32*(w%4) .. +31;
+    // warps w and w+4 share a quadrant and split its columns in halves.
     const int q = warp & 3;
+    const int half = (warp - 2) / 4;
     const int row_in_tile = q * 32 + lane;
     int acc = 0;
     uint32_t acc_phase = 0;
@@ -323,7 +326,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       const int row = mb * kBM + row_in_tile;
       const uint32_t lane_addr = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + acc * BN;
 #pragma unroll 1
-      for (int c = 0; c < BN / 32; ++c) {
+      for (int c = half * (BN / 64); c < (half + 1) * (BN / 64); ++c) {
         float v[32];
         tmem_ld_32(lane_addr + c * 32, v);
         const int col0 = nb * BN + c * 32;

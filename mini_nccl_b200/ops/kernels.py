@@ -21,6 +21,9 @@ import torch
 
 EPI_BIAS, EPI_GELU, EPI_RESID, EPI_GELU_GRAD, EPI_ACCUM = 1, 2, 4, 8, 16
 
+#: Head dims whose attention forward runs on tcgen05 (others use mma.sync).
+TC_ATTENTION_HEAD_DIMS = (64, 128)
+
 _EXT = None
 _STATUS: dict[int, torch.Tensor] = {}
 NUM_SMS = 148
@@ -272,7 +275,10 @@ class FlashAttention(torch.autograd.Function):
         q, k, v = qkv[..., :C], qkv[..., C : 2 * C], qkv[..., 2 * C :]
         o = torch.empty((B, T, C), dtype=qkv.dtype, device=qkv.device)
         lse = torch.empty((B, n_head, T), dtype=torch.float32, device=qkv.device)
-        ext().flash_attn_fwd(q, k, v, o, lse, n_head, scale)
+        if D in TC_ATTENTION_HEAD_DIMS and qkv.is_contiguous():
+            ext().flash_attn_fwd_tc(qkv, o, lse, n_head, scale, status_word(qkv.device))
+        else:
+            ext().flash_attn_fwd(q, k, v, o, lse, n_head, scale)
         ctx.save_for_backward(qkv, o, lse)
         ctx.n_head, ctx.scale = n_head, scale
         return o.view(B, T, n_head, D)
@@ -345,10 +351,13 @@ class HeadCrossEntropy(torch.autograd.Function):
     @staticmethod
     def backward(ctx, g):
         dx, dw = ctx.saved_tensors
-        gs = g.to(torch.float32)
-        dx = (dx * gs.to(dx.dtype)).view(ctx.x_shape)
-        dw = (dw * gs).to(ctx.w_dtype)
-        return dx, dw, None, None
+        # In place: the gradients were computed for a unit upstream gradient.
+        dx.mul_(g.to(dx.dtype))
+        if dw.dtype != ctx.w_dtype:
+            dw = dw.mul_(g.to(dw.dtype)).to(ctx.w_dtype)
+        else:
+            dw.mul_(g.to(dw.dtype))
+        return dx.view(ctx.x_shape), dw, None, None
 
 
 class Embedding(torch.autograd.Function):

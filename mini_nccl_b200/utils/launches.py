@@ -26,6 +26,7 @@ KERNELS_PER_CALL = {
     "xent_fwd_bwd": 1,
     "adamw_step": 1,
     "flash_attn_fwd": 1,
+    "flash_attn_fwd_tc": 1,
     "flash_attn_bwd": 3,
     "all_reduce": 1,
     "reduce_scatter": 1,
