@@ -57,6 +57,7 @@ struct GemmArgs {
   const __nv_bfloat16* resid;
   long long ldr;
   int epi;
+  int tma_out;  // bf16 output (and GELU aux) written through shared memory + TMA store
   int* status;
 };
 
@@ -70,8 +71,12 @@ struct GemmSmem {
   static constexpr uint32_t a_bytes = kBM * kBK * 2;
   static constexpr uint32_t b_bytes = BN * kBK * 2;
   static constexpr uint32_t ring = STAGES * (a_bytes + b_bytes);
+  // 32-row x 128-byte staging boxes per epilogue warp: two (output + GELU aux)
+  // in the 3-stage configuration, one in the 4-stage configuration
+  static constexpr uint32_t boxes = STAGES <= 3 ? 2 : 1;
+  static constexpr uint32_t staging = 8 * boxes * 4096;
   static constexpr uint32_t bars = (2 * STAGES + 4) * 8;
-  static constexpr uint32_t total = ring + bars + 16 + 1024;  // + tmem slot + alignment slack
+  static constexpr uint32_t total = ring + staging + bars + 16 + 1024;  // + tmem slot + alignment slack
 };
 
 MNB_DEVICE void epilogue_store(const GemmArgs& a, int row, int col0, float* v) {
@@ -184,10 +189,96 @@ MNB_DEVICE void epilogue_store(const GemmArgs& a, int row, int col0, float* v) {
   }
 }
 
+MNB_DEVICE void tma_store_2d(const CUtensorMap* map, uint32_t src, int32_t x, int32_t y) {
+  asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%1, %2}], [%3];" ::"l"(
+                   reinterpret_cast<uint64_t>(map)),
+               "r"(x), "r"(y), "r"(src)
+               : "memory");
+}
+MNB_DEVICE void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+template <int N>
+MNB_DEVICE void bulk_wait_read() {
+  asm volatile("cp.async.bulk.wait_group.read %0;" ::"n"(N) : "memory");
+}
+MNB_DEVICE void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+
+// Write 32 bf16 values (one row segment) as 16-byte chunks sub*4.. of a
+// 32-row x 128-byte box laid out in the 128-byte swizzle (conflict-free).
+MNB_DEVICE void stage_row32(uint8_t* box, int row, int sub, const float* v) {
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    const int chunk = sub * 4 + k;
+    *reinterpret_cast<uint4*>(box + row * 128 + ((chunk ^ (row & 7)) * 16)) =
+        make_uint4(pack_bf16x2(v[8 * k], v[8 * k + 1]), pack_bf16x2(v[8 * k + 2], v[8 * k + 3]),
+                   pack_bf16x2(v[8 * k + 4], v[8 * k + 5]), pack_bf16x2(v[8 * k + 6], v[8 * k + 7]));
+  }
+}
+
+// Bias / GELU' / residual on 32 consecutive columns of one row (no stores).
+MNB_DEVICE void epilogue_inputs(const GemmArgs& a, int row, int col0, float* v) {
+  const int N = a.N;
+  const bool in_rows = row < a.M;
+  const bool full = col0 + 32 <= N;
+  if (a.epi & kEpiBias) {
+    if (full) {
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const uint4 w = ld_v4(a.bias + col0 + 8 * i);
+        const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const float2 f = unpack_bf16x2(ws[j]);
+          v[8 * i + 2 * j] += f.x;
+          v[8 * i + 2 * j + 1] += f.y;
+        }
+      }
+    } else {
+      for (int i = 0; i < 32 && col0 + i < N; ++i) v[i] += bf16_to_f32(a.bias[col0 + i]);
+    }
+  }
+  if ((a.epi & kEpiGeluGrad) && in_rows) {
+    const __nv_bfloat16* ap = a.aux + static_cast<long long>(row) * a.ldaux + col0;
+    if (full) {
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        uint4 w = ld_v4(ap + 8 * i);
+        const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const float2 f = unpack_bf16x2(ws[j]);
+          v[8 * i + 2 * j] *= gelu_grad(f.x);
+          v[8 * i + 2 * j + 1] *= gelu_grad(f.y);
+        }
+      }
+    } else {
+      for (int i = 0; i < 32 && col0 + i < N; ++i) v[i] *= gelu_grad(bf16_to_f32(ap[i]));
+    }
+  }
+  if ((a.epi & kEpiResid) && in_rows) {
+    const __nv_bfloat16* rp = a.resid + static_cast<long long>(row) * a.ldr + col0;
+    if (full) {
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        uint4 w = ld_v4(rp + 8 * i);
+        const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const float2 f = unpack_bf16x2(ws[j]);
+          v[8 * i + 2 * j] += f.x;
+          v[8 * i + 2 * j + 1] += f.y;
+        }
+      }
+    } else {
+      for (int i = 0; i < 32 && col0 + i < N; ++i) v[i] += bf16_to_f32(rp[i]);
+    }
+  }
+}
+
 template <int BN, bool A_MN, bool B_MN, int STAGES>
 __global__ void __launch_bounds__(kGemmThreads, 1)
-    gemm_tcgen05_kernel(const __grid_constant__ CUtensorMap map_a,
-                        const __grid_constant__ CUtensorMap map_b, const GemmArgs args) {
+    gemm_tcgen05_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
+                        const __grid_constant__ CUtensorMap map_out, const __grid_constant__ CUtensorMap map_aux,
+                        const GemmArgs args) {
   using S = GemmSmem<BN, STAGES>;
   constexpr uint32_t kIdesc = idesc_bf16(kBM, BN, A_MN, B_MN);
   constexpr uint32_t kTmemCols = 2 * BN;
@@ -196,7 +287,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
   uint8_t* ring_a = smem;
   uint8_t* ring_b = smem + STAGES * S::a_bytes;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + S::ring);
+  uint8_t* staging = smem + S::ring;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + S::ring + S::staging);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * STAGES + 4);
   const uint32_t full0 = smem_u32(bars);
   const uint32_t empty0 = smem_u32(bars + STAGES);
@@ -325,12 +417,52 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         a.out = reinterpret_cast<float*>(args.out) + static_cast<long long>(split) * args.split_stride;
       const int row = mb * kBM + row_in_tile;
       const uint32_t lane_addr = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + acc * BN;
+      if (a.tma_out) {
+        // 64-column groups: TMEM -> registers -> epilogue math -> swizzled
+        // staging box -> one TMA store per 32 x 64 block (rows/cols past the
+        // matrix are clipped by the TMA unit).
+        uint8_t* box_out = staging + (warp - 2) * (S::boxes * 4096);
+        uint8_t* box_aux = box_out + (S::boxes - 1) * 4096;  // == box_out with one box
+        const bool gelu = (a.epi & kEpiGelu) != 0;
 #pragma unroll 1
-      for (int c = half * (BN / 64); c < (half + 1) * (BN / 64); ++c) {
-        float v[32];
-        tmem_ld_32(lane_addr + c * 32, v);
-        const int col0 = nb * BN + c * 32;
-        if (col0 < a.N) epilogue_store(a, row, col0, v);
+        for (int g = half * (BN / 128); g < (half + 1) * (BN / 128); ++g) {
+          const int colg = nb * BN + g * 64;
+          if (colg >= a.N) break;
+          // with two boxes and a single output, alternate them (double buffer)
+          uint8_t* bo = (!gelu && S::boxes == 2 && (g & 1)) ? box_aux : box_out;
+          if (lane == 0) {
+            if (gelu || S::boxes == 1) bulk_wait_read<0>();
+            else bulk_wait_read<1>();
+          }
+          __syncwarp();
+#pragma unroll
+          for (int sub = 0; sub < 2; ++sub) {
+            float v[32];
+            tmem_ld_32(lane_addr + g * 64 + sub * 32, v);
+            epilogue_inputs(a, row, colg + sub * 32, v);
+            if (gelu) {
+              stage_row32(box_aux, lane, sub, v);  // pre-activation
+#pragma unroll
+              for (int i = 0; i < 32; ++i) v[i] = gelu_exact(v[i]);
+            }
+            stage_row32(bo, lane, sub, v);
+          }
+          asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+          __syncwarp();
+          if (lane == 0) {
+            tma_store_2d(&map_out, smem_u32(bo), colg, mb * kBM + q * 32);
+            if (gelu) tma_store_2d(&map_aux, smem_u32(box_aux), colg, mb * kBM + q * 32);
+            bulk_commit();
+          }
+        }
+      } else {
+#pragma unroll 1
+        for (int c = half * (BN / 64); c < (half + 1) * (BN / 64); ++c) {
+          float v[32];
+          tmem_ld_32(lane_addr + c * 32, v);
+          const int col0 = nb * BN + c * 32;
+          if (col0 < a.N) epilogue_store(a, row, col0, v);
+        }
       }
       tc_fence_before();
       mbar_arrive(tempty0 + 8 * acc);
@@ -339,6 +471,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     }
   }
 
+  if (warp >= 2 && lane == 0) bulk_wait_all();  // staging boxes fully drained before exit
   tc_fence_before();
   __syncthreads();
   if (warp == 1) {
@@ -425,8 +558,8 @@ int num_sms() {
 }
 
 template <int BN, bool A_MN, bool B_MN, int STAGES>
-void launch_gemm(const CUtensorMap& ma, const CUtensorMap& mb, const GemmArgs& args, int units,
-                 cudaStream_t stream) {
+void launch_gemm(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& mo, const CUtensorMap& mx,
+                 const GemmArgs& args, int units, cudaStream_t stream) {
   using S = GemmSmem<BN, STAGES>;
   auto kern = gemm_tcgen05_kernel<BN, A_MN, B_MN, STAGES>;
   static bool configured = false;
@@ -435,7 +568,7 @@ void launch_gemm(const CUtensorMap& ma, const CUtensorMap& mb, const GemmArgs& a
     configured = true;
   }
   const int grid = std::min(units, num_sms());
-  kern<<<grid, kGemmThreads, S::total, stream>>>(ma, mb, args);
+  kern<<<grid, kGemmThreads, S::total, stream>>>(ma, mb, mo, mx, args);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
@@ -514,19 +647,32 @@ void gemm(torch::Tensor a, torch::Tensor b, torch::Tensor out, bool a_mn, bool b
                         : make_tma_2d_bf16(a.data_ptr(), K, M, lda, 64, kBM);
   CUtensorMap mb = b_mn ? make_tma_2d_bf16(b.data_ptr(), N, K, ldb, 64, 64)
                         : make_tma_2d_bf16(b.data_ptr(), K, N, ldb, 64, BN);
+  // bf16 outputs without read-modify-write go through the TMA-store epilogue
+  args.tma_out = (splits == 1 && !out_f32 && !(args.epi & kEpiAccum)) ? 1 : 0;
+  CUtensorMap mo = ma, mx = ma;  // placeholders when unused (never dereferenced)
+  if (args.tma_out) {
+    mo = make_tma_2d_bf16(out.data_ptr(), N, M, out.stride(0), 64, 32);
+    if (args.epi & kEpiGelu) mx = make_tma_2d_bf16(aux->data_ptr(), N, M, args.ldaux, 64, 32);
+  }
   cudaStream_t stream = at::cuda::getCurrentCUDAStream();
 #define MNB_GEMM_CASE(BNV, AM, BMJ, ST)                                   \
   if (BN == BNV && a_mn == AM && b_mn == BMJ) {                            \
-    launch_gemm<BNV, AM, BMJ, ST>(ma, mb, args, units, stream);            \
+    launch_gemm<BNV, AM, BMJ, ST>(ma, mb, mo, mx, args, units, stream);    \
+  } else
+  const bool gelu_out = (args.epi & kEpiGelu) != 0;
+  if (gelu_out) {
+    TORCH_CHECK(!a_mn && !b_mn, "the GELU epilogue is for the forward (K-major) layout");
+    if (BN == 256) launch_gemm<256, false, false, 3>(ma, mb, mo, mx, args, units, stream);
+    else launch_gemm<128, false, false, 3>(ma, mb, mo, mx, args, units, stream);
   } else
   MNB_GEMM_CASE(256, false, false, 4)
   MNB_GEMM_CASE(256, false, true, 4)
   MNB_GEMM_CASE(256, true, false, 4)
   MNB_GEMM_CASE(256, true, true, 4)
-  MNB_GEMM_CASE(128, false, false, 6)
-  MNB_GEMM_CASE(128, false, true, 6)
-  MNB_GEMM_CASE(128, true, false, 6)
-  MNB_GEMM_CASE(128, true, true, 6) { TORCH_CHECK(false, "unsupported GEMM configuration"); }
+  MNB_GEMM_CASE(128, false, false, 4)
+  MNB_GEMM_CASE(128, false, true, 4)
+  MNB_GEMM_CASE(128, true, false, 4)
+  MNB_GEMM_CASE(128, true, true, 4) { TORCH_CHECK(false, "unsupported GEMM configuration"); }
 #undef MNB_GEMM_CASE
   if (splits > 1) {
     const long long total4 = static_cast<long long>(M) * N / 4;
