@@ -9,7 +9,9 @@ attention splits by head, the MLP by hidden unit, two all-reduces per block
 the tied head stay replicated and stay *bitwise* identical because every rank
 receives the identical activation gradient.  ``--sequence-parallel`` keeps
 the activations between TP layers split along the sequence (all-gather before
-each column GEMM, reduce-scatter after each row GEMM).
+each column GEMM, reduce-scatter after each row GEMM; on GPUs each pair is one
+fused kernel); LayerNorm and row-bias gradients, which then cover only local
+tokens, are summed over the group after backward.
 """
 
 from __future__ import annotations
@@ -25,7 +27,14 @@ from _common import batch, encode, load_corpus, to_device
 
 import mini_nccl_b200 as mn
 from mini_nccl_b200 import collectives
-from mini_nccl_b200.tensor_parallel import ParallelMLP, ParallelSelfAttention
+from mini_nccl_b200.tensor_parallel import (
+    ParallelMLP,
+    ParallelSelfAttention,
+    allreduce_sequence_parallel_grads,
+    gather_from_sequence_parallel,
+    mark_sequence_parallel,
+    scatter_to_sequence_parallel,
+)
 
 
 class ParallelBlock(nn.Module):
@@ -35,10 +44,12 @@ class ParallelBlock(nn.Module):
         self.attn = ParallelSelfAttention(width, n_head, pg, sequence_parallel=sp)
         self.ln2 = nn.LayerNorm(width)
         self.mlp = ParallelMLP(width, pg, sequence_parallel=sp)
+        if sp:
+            mark_sequence_parallel(self.ln1, self.ln2)
 
     def forward(self, x):
-        x = x + self.attn(self.ln1(x))
-        return x + self.mlp(self.ln2(x))
+        x = self.attn(self.ln1(x), residual=x)
+        return self.mlp(self.ln2(x), residual=x)
 
 
 class TPGPT(nn.Module):
@@ -57,19 +68,11 @@ class TPGPT(nn.Module):
         T = idx.shape[1]
         x = self.tok_emb(idx) + self.pos_emb[:, :T]
         if self.sp:  # sequence-major, this rank's run of positions
-            W, r = self.pg.world_size, self.pg.rank
-            per = T // W
-            x = x.transpose(0, 1)[r * per : (r + 1) * per].contiguous()
+            x = scatter_to_sequence_parallel(self.pg, x.transpose(0, 1))
         for blk in self.blocks:
             x = blk(x)
-        if self.sp:
-            parts = collectives.all_gather(self.pg, x.detach())
-            full = torch.cat(parts, 0)
-            # keep the autograd path through this rank's slice only; gradients of
-            # the replicated head are identical on every rank either way
-            r, per = self.pg.rank, x.shape[0]
-            full = torch.cat([full[: r * per], x, full[(r + 1) * per :]], 0).transpose(0, 1)
-            x = full
+        if self.sp:  # every rank runs the replicated head on all tokens
+            x = gather_from_sequence_parallel(self.pg, x).transpose(0, 1)
         logits = F.linear(self.ln_f(x), self.tok_emb.weight)
         return F.cross_entropy(logits.reshape(-1, logits.shape[-1]).float(), targets.reshape(-1))
 
@@ -88,6 +91,8 @@ def worker(pg, data, vocab_size: int, cfg: dict) -> float:
         loss = model(x.to(dev), y.to(dev))
         opt.zero_grad(set_to_none=True)
         loss.backward()
+        if cfg["sequence_parallel"]:
+            allreduce_sequence_parallel_grads(model, pg)
         opt.step()
         final = float(loss.detach())
         if pg.rank == 0 and (step % 20 == 0 or step == cfg["steps"] - 1):

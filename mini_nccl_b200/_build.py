@@ -85,8 +85,10 @@ def _stale(target: Path, sources: list[Path], extra: str = "") -> bool:
     return stamp.read_text().strip() != _digest(sources, extra)
 
 
-def _stamp(target: Path, sources: list[Path], extra: str = "") -> None:
-    target.with_name(target.name + ".sha256").write_text(_digest(sources, extra))
+def _stamp(target: Path, digest: str) -> None:
+    """Record the digest the build started from (an edit made during the
+    build then leaves the library stale, as it is)."""
+    target.with_name(target.name + ".sha256").write_text(digest)
 
 
 def _cxx() -> str:
@@ -110,6 +112,7 @@ def build_host(force: bool = False, verbose: bool = False) -> Path:
     with _lock("host"):
         if not force and not _stale(out, HOST_SRC):
             return out
+        digest = _digest(HOST_SRC)
         out.parent.mkdir(parents=True, exist_ok=True)
         cmd = [
             _cxx(),
@@ -130,7 +133,7 @@ def build_host(force: bool = False, verbose: bool = False) -> Path:
             print(" ".join(cmd), flush=True)
         subprocess.run(cmd, check=True)
         os.replace(str(out) + ".tmp", out)
-        _stamp(out, HOST_SRC)
+        _stamp(out, digest)
     return out
 
 
@@ -151,6 +154,7 @@ def build_cuda(force: bool = False, verbose: bool = False) -> Path:
         deps = cuda_sources() + cuda_headers()
         if not force and not _stale(out, deps, " ".join(NVCC_FLAGS)):
             return out
+        digest = _digest(deps, " ".join(NVCC_FLAGS))
         os.environ.setdefault("TORCH_CUDA_ARCH_LIST", "10.0a")
         os.environ["CXX"] = _cxx()
         os.environ.setdefault("MAX_JOBS", str(max(1, os.cpu_count() or 1)))
@@ -171,7 +175,7 @@ def build_cuda(force: bool = False, verbose: bool = False) -> Path:
             with_cuda=True,
             is_python_module=True,
         )
-        _stamp(out, deps, " ".join(NVCC_FLAGS))
+        _stamp(out, digest)
     return out
 
 

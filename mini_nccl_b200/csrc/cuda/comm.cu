@@ -44,15 +44,13 @@
 #include <vector>
 
 #include "common.cuh"
+#include "peer.cuh"
 
 namespace cg = cooperative_groups;
 
 namespace mnb {
 
-constexpr int kMaxRanks = 16;
-constexpr int kMaxBlocks = 64;
 constexpr int kCommThreads = 512;
-constexpr int kSigSlots = kMaxBlocks * kMaxRanks;
 constexpr int kRingCap = 4096;
 
 enum OpCode : int { kSum = 0, kProd = 1, kMax = 2, kMin = 3 };
@@ -68,7 +66,8 @@ struct DevEvent {
 };
 
 struct CommArgs {
-  void* data[kMaxRanks];     // per-rank peer-visible buffer for this call
+  void* data[kMaxRanks];     // per-rank peer-visible staging region for this call
+  void* dst[kMaxRanks];      // per-rank symmetric output (in-place all-reduce), or null
   uint32_t* sig[kMaxRanks];  // per-rank signal pads
   const void* in;
   void* out;
@@ -225,35 +224,91 @@ MNB_DEVICE void copy_in_units(const CommArgs& a, long long lo, long long hi) {
   }
 }
 
+// L2-only 16-byte load (bypasses L1: staging is rewritten by peers every call).
+MNB_DEVICE uint4 ld_v4_cg(const void* p) {
+  uint4 v;
+  asm volatile("ld.global.cg.v4.u32 {%0,%1,%2,%3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "l"(p));
+  return v;
+}
+template <typename TW, typename TA>
+MNB_DEVICE void unpack_vec(uint4 raw, TA* v) {
+  const TW* e = reinterpret_cast<const TW*>(&raw);
+#pragma unroll
+  for (int i = 0; i < Vec<TW>::n; ++i) v[i] = widen<TA, TW>(e[i]);
+}
+template <typename TW, typename TA>
+MNB_DEVICE uint4 pack_vec(const TA* v) {
+  uint4 raw;
+  TW* e = reinterpret_cast<TW*>(&raw);
+#pragma unroll
+  for (int i = 0; i < Vec<TW>::n; ++i) e[i] = narrow<TW, TA>(v[i]);
+  return raw;
+}
+// One VEC of the (possibly wider) input, converted to the accumulation type.
+template <typename TI, typename TA, int V>
+MNB_DEVICE void load_in(const TI* p, TA* v) {
+  if constexpr (sizeof(TI) * V == 16) {
+    uint4 raw = ld_v4(p);
+    const TI* e = reinterpret_cast<const TI*>(&raw);
+#pragma unroll
+    for (int i = 0; i < V; ++i) v[i] = widen<TA, TI>(e[i]);
+  } else {
+#pragma unroll
+    for (int i = 0; i < V; ++i) v[i] = widen<TA, TI>(p[i]);
+  }
+}
+template <typename T>
+MNB_DEVICE T* at(void* base, long long elems) {
+  return reinterpret_cast<T*>(base) + elems;
+}
+
 // ---------------------------------------------------------------------------
-// one-shot all-reduce
+// all-reduce, one shot, push (latency path, small messages)
+//   staging (wire type): [parity 2][W slots][n_pad].  Every rank stores its
+//   whole input into slot `rank` of every peer (posted NVLink writes), one
+//   barrier, then every rank reduces its W local slots in rank order, so all
+//   ranks produce identical bits.  Calls alternate the parity half so a fast
+//   peer's next call never overwrites slots still being reduced here.
 // ---------------------------------------------------------------------------
 template <typename TI, typename TW, int OP>
-__global__ void __launch_bounds__(kCommThreads) ar_one_shot_kernel(CommArgs a) {
+__global__ void __launch_bounds__(kCommThreads) ar_push_one_shot_kernel(CommArgs a, long long n_pad) {
   using TA = typename Acc<TW>::type;
   constexpr int V = Vec<TW>::n;
   ring_begin(a);
-  const long long nu = a.n / V;
-  const long long tail = a.n - nu * V;
+  const int W = a.world, r = a.rank;
+  const long long nu = a.n / V, tail = a.n - nu * V;
+  const long long par = 0;  // the host already selected this call's staging half
   long long lo, hi;
   block_range(nu, &lo, &hi);
-  if (a.copy_in) {
-    copy_in_units<TI, TW>(a, lo, hi);
-    if (blockIdx.x == 0 && threadIdx.x < tail) {
-      reinterpret_cast<TW*>(a.data[a.rank])[nu * V + threadIdx.x] =
-          narrow<TW, TA>(widen<TA, TI>(reinterpret_cast<const TI*>(a.in)[nu * V + threadIdx.x]));
+  const TI* in = reinterpret_cast<const TI*>(a.in);
+  for (long long u = lo + threadIdx.x; u < hi; u += blockDim.x) {
+    TA v[V];
+    load_in<TI, TA, V>(in + u * V, v);
+    const uint4 w = pack_vec<TW, TA>(v);
+    for (int k = 1; k < W; ++k) {
+      const int p = (r + k) % W;
+      st_v4(at<TW>(a.data[p], par + r * n_pad + u * V), w);
     }
+  }
+  if (blockIdx.x == 0 && threadIdx.x < tail) {
+    const TW w = narrow<TW, TA>(widen<TA, TI>(in[nu * V + threadIdx.x]));
+    for (int p = 0; p < W; ++p) *at<TW>(a.data[p], par + r * n_pad + nu * V + threadIdx.x) = w;
   }
   bool ok = peer_barrier(a, a.epoch + 1);
   if (ok) {
     TI* out = reinterpret_cast<TI*>(a.out);
     for (long long u = lo + threadIdx.x; u < hi; u += blockDim.x) {
       TA acc[V], v[V];
-      load_vec<TW, TA>(reinterpret_cast<const TW*>(a.data[0]) + u * V, acc);
-      for (int p = 1; p < a.world; ++p) {
-        load_vec<TW, TA>(reinterpret_cast<const TW*>(a.data[p]) + u * V, v);
+      for (int p = 0; p < W; ++p) {  // rank order on every rank: identical bits everywhere
+        if (p == r) {
+          load_in<TI, TA, V>(in + u * V, v);
 #pragma unroll
-        for (int i = 0; i < V; ++i) acc[i] = combine<OP>(acc[i], v[i]);
+          for (int i = 0; i < V; ++i) v[i] = widen<TA, TW>(narrow<TW, TA>(v[i]));
+        } else {
+          unpack_vec<TW, TA>(ld_v4_cg(at<TW>(a.data[r], par + p * n_pad + u * V)), v);
+        }
+#pragma unroll
+        for (int i = 0; i < V; ++i) acc[i] = p == 0 ? v[i] : combine<OP>(acc[i], v[i]);
       }
 #pragma unroll
       for (int i = 0; i < V; ++i) acc[i] = widen<TA, TW>(narrow<TW, TA>(finish<OP>(acc[i], a.scale)));
@@ -261,95 +316,180 @@ __global__ void __launch_bounds__(kCommThreads) ar_one_shot_kernel(CommArgs a) {
     }
     if (blockIdx.x == 0 && threadIdx.x < tail) {
       const long long e = nu * V + threadIdx.x;
-      TA acc = widen<TA, TW>(reinterpret_cast<const TW*>(a.data[0])[e]);
-      for (int p = 1; p < a.world; ++p) acc = combine<OP>(acc, widen<TA, TW>(reinterpret_cast<const TW*>(a.data[p])[e]));
+      TA acc = widen<TA, TW>(*reinterpret_cast<volatile TW*>(at<TW>(a.data[r], par + e)));
+      for (int p = 1; p < W; ++p)
+        acc = combine<OP>(acc, widen<TA, TW>(*reinterpret_cast<volatile TW*>(at<TW>(a.data[r], par + p * n_pad + e))));
       out[e] = narrow<TI, TA>(widen<TA, TW>(narrow<TW, TA>(finish<OP>(acc, a.scale))));
     }
-    ok = peer_barrier(a, a.epoch + 2);
   }
   ring_end(a, ok);
 }
 
 // ---------------------------------------------------------------------------
-// two-shot all-reduce (reduce-scatter + all-gather), in place on symmetric data
+// all-reduce, two shot, push (bandwidth path)
+//   staging (wire type): [W slots][chunk] | [W][chunk] results | [W][V] tail
+//   phase 1  rank r stores chunk c of its input into slot r of rank c
+//   phase 2  rank r reduces its W slots (local reads, rank order), scales,
+//            and stores the result into chunk r of every rank: straight into
+//            their tensors when those are symmetric (DDP buckets, in place),
+//            else into their result region
+//   phase 3  (non-symmetric) copy the other ranks' chunks out of the result
+//            region.
+//   Every element is reduced once, by its owner, so all ranks hold
+//   identical bits.  Two barriers; no trailing one is needed because a
+//   peer's next phase-1 writes wait for this rank's phase-2 signal.
 // ---------------------------------------------------------------------------
 template <typename TI, typename TW, int OP>
-__global__ void __launch_bounds__(kCommThreads) ar_two_shot_kernel(CommArgs a) {
+__global__ void __launch_bounds__(kCommThreads) ar_push_two_shot_kernel(CommArgs a, long long chunk_u) {
   using TA = typename Acc<TW>::type;
   constexpr int V = Vec<TW>::n;
   ring_begin(a);
   const int W = a.world, r = a.rank;
-  const long long nu = a.n / V;
-  const long long tail = a.n - nu * V;
-  const long long cu = (nu + W - 1) / W;  // units per rank chunk
-  const long long sub = (cu + gridDim.x - 1) / gridDim.x;
+  const long long nu = a.n / V, tail = a.n - nu * V;
+  const long long cw = chunk_u * V;                   // chunk length in elements
+  const long long res_off = W * cw, tail_off = 2 * W * cw;
+  const long long sub = (chunk_u + gridDim.x - 1) / gridDim.x;
   auto sub_range = [&](int c, long long* lo, long long* hi) {
-    const long long c0 = min(nu, c * cu), c1 = min(nu, c0 + cu);
+    const long long c0 = min(nu, c * chunk_u), c1 = min(nu, c0 + chunk_u);
     *lo = min(c1, c0 + sub * blockIdx.x);
     *hi = min(c1, *lo + sub);
   };
-  if (a.copy_in) {
-    for (int c = 0; c < W; ++c) {
-      long long lo, hi;
-      sub_range(c, &lo, &hi);
-      copy_in_units<TI, TW>(a, lo, hi);
+  const bool sym = a.dst[r] != nullptr;
+  const TI* in = reinterpret_cast<const TI*>(a.in);
+  // phase 1: scatter my chunks into their owners' slot r (my own chunk stays
+  // in my input; phase 2 reads it from there)
+  for (int k = 1; k < W; ++k) {
+    const int c = (r + k) % W;
+    long long lo, hi;
+    sub_range(c, &lo, &hi);
+    constexpr int U = 4;  // independent 16-byte loads in flight per thread before the stores
+    for (long long u0 = lo + threadIdx.x; u0 < hi; u0 += U * blockDim.x) {
+      uint4 w[U];
+#pragma unroll
+      for (int j = 0; j < U; ++j) {
+        const long long u = u0 + j * blockDim.x;
+        if (u < hi) {
+          TA v[V];
+          load_in<TI, TA, V>(in + u * V, v);
+          w[j] = pack_vec<TW, TA>(v);
+        }
+      }
+#pragma unroll
+      for (int j = 0; j < U; ++j) {
+        const long long u = u0 + j * blockDim.x;
+        if (u < hi) st_v4(at<TW>(a.data[c], r * cw + (u - c * chunk_u) * V), w[j]);
+      }
     }
-    if (blockIdx.x == 0 && threadIdx.x < tail) {
-      reinterpret_cast<TW*>(a.data[r])[nu * V + threadIdx.x] =
-          narrow<TW, TA>(widen<TA, TI>(reinterpret_cast<const TI*>(a.in)[nu * V + threadIdx.x]));
-    }
+  }
+  if (blockIdx.x == 0 && threadIdx.x < tail) {
+    const TW w = narrow<TW, TA>(widen<TA, TI>(in[nu * V + threadIdx.x]));
+    for (int p = 0; p < W; ++p) *at<TW>(a.data[p], tail_off + r * V + threadIdx.x) = w;
   }
   bool ok = peer_barrier(a, a.epoch + 1);
   TI* out = reinterpret_cast<TI*>(a.out);
-  TW* mine = reinterpret_cast<TW*>(a.data[r]);
-  TA tail_val = 0;
   if (ok) {
     long long lo, hi;
     sub_range(r, &lo, &hi);
-    for (long long u = lo + threadIdx.x; u < hi; u += blockDim.x) {
-      TA acc[V], v[V];
-      load_vec<TW, TA>(reinterpret_cast<const TW*>(a.data[0]) + u * V, acc);
-      for (int p = 1; p < W; ++p) {
-        load_vec<TW, TA>(reinterpret_cast<const TW*>(a.data[p]) + u * V, v);
+    constexpr int U2 = 4;  // units per thread per pass: U2 independent loads per source rank
+    for (long long u0 = lo + threadIdx.x; u0 < hi; u0 += U2 * blockDim.x) {
+      TA accs[U2][V];
+      // rank order 0..W-1 on every owner: a fixed summation order
+      for (int p = 0; p < W; ++p) {
+        uint4 raw[U2];
 #pragma unroll
-        for (int i = 0; i < V; ++i) acc[i] = combine<OP>(acc[i], v[i]);
+        for (int j = 0; j < U2; ++j) {
+          const long long u = u0 + j * blockDim.x;
+          if (u < hi && p != r) raw[j] = ld_v4_cg(at<TW>(a.data[r], p * cw + (u - r * chunk_u) * V));
+        }
+#pragma unroll
+        for (int j = 0; j < U2; ++j) {
+          const long long u = u0 + j * blockDim.x;
+          if (u >= hi) continue;
+          TA v[V];
+          if (p == r) {
+            load_in<TI, TA, V>(in + u * V, v);
+#pragma unroll
+            for (int i = 0; i < V; ++i) v[i] = widen<TA, TW>(narrow<TW, TA>(v[i]));  // same wire rounding as peers'
+          } else {
+            unpack_vec<TW, TA>(raw[j], v);
+          }
+#pragma unroll
+          for (int i = 0; i < V; ++i) accs[j][i] = p == 0 ? v[i] : combine<OP>(accs[j][i], v[i]);
+        }
       }
 #pragma unroll
-      for (int i = 0; i < V; ++i) acc[i] = finish<OP>(acc[i], a.scale);
-      store_vec<TW, TA>(mine + u * V, acc);  // publish the reduced chunk (wire type)
-      TA back[V];
+      for (int j = 0; j < U2; ++j) {
+      const long long u = u0 + j * blockDim.x;
+      if (u >= hi) continue;
+      TA* acc = accs[j];
 #pragma unroll
-      for (int i = 0; i < V; ++i) back[i] = widen<TA, TW>(narrow<TW, TA>(acc[i]));
-      if (static_cast<const void*>(out) != static_cast<const void*>(mine)) store_out<TI, TA, V>(out + u * V, back);
+      for (int i = 0; i < V; ++i) acc[i] = widen<TA, TW>(narrow<TW, TA>(finish<OP>(acc[i], a.scale)));
+      if (sym) {
+        // everyone's tensor, chunk r, in the tensor's own type
+        TI res[V];
+#pragma unroll
+        for (int i = 0; i < V; ++i) res[i] = narrow<TI, TA>(acc[i]);
+        for (int k = 0; k < W; ++k) {
+          const int p = (r + k) % W;
+          TI* d = at<TI>(a.dst[p], u * V);
+          if constexpr (sizeof(TI) * V == 16) {
+            st_v4(d, *reinterpret_cast<const uint4*>(res));
+          } else {
+#pragma unroll
+            for (int i = 0; i < V; ++i) d[i] = res[i];
+          }
+        }
+      } else {
+        const uint4 w = pack_vec<TW, TA>(acc);
+        for (int k = 1; k < W; ++k) {
+          const int p = (r + k) % W;
+          st_v4(at<TW>(a.data[p], res_off + u * V), w);
+        }
+        store_out<TI, TA, V>(out + u * V, acc);
+      }
+      }
     }
-    if (blockIdx.x == 0 && threadIdx.x < tail) {
-      const long long e = nu * V + threadIdx.x;
-      TA acc = widen<TA, TW>(reinterpret_cast<const TW*>(a.data[0])[e]);
-      for (int p = 1; p < W; ++p) acc = combine<OP>(acc, widen<TA, TW>(reinterpret_cast<const TW*>(a.data[p])[e]));
-      tail_val = widen<TA, TW>(narrow<TW, TA>(finish<OP>(acc, a.scale)));
+    if (blockIdx.x == 0 && threadIdx.x < tail) {  // every rank reduces the tail itself, in rank order
+      const long long e = threadIdx.x;
+      TA acc = widen<TA, TW>(*reinterpret_cast<volatile TW*>(at<TW>(a.data[r], tail_off + e)));
+      for (int p = 1; p < W; ++p)
+        acc = combine<OP>(acc, widen<TA, TW>(*reinterpret_cast<volatile TW*>(at<TW>(a.data[r], tail_off + p * V + e))));
+      out[nu * V + e] = narrow<TI, TA>(widen<TA, TW>(narrow<TW, TA>(finish<OP>(acc, a.scale))));
     }
     ok = peer_barrier(a, a.epoch + 2);
   }
-  if (ok) {
-    for (int c = 0; c < W; ++c) {
-      if (c == r) continue;
+  if (ok && !sym) {
+    for (int k = 1; k < W; ++k) {
+      const int c = (r + k) % W;
       long long lo, hi;
       sub_range(c, &lo, &hi);
-      for (long long u = lo + threadIdx.x; u < hi; u += blockDim.x) {
-        TA v[V];
-        load_vec<TW, TA>(reinterpret_cast<const TW*>(a.data[c]) + u * V, v);
-        store_out<TI, TA, V>(out + u * V, v);
+      constexpr int U = 4;
+      for (long long u0 = lo + threadIdx.x; u0 < hi; u0 += U * blockDim.x) {
+        uint4 w[U];
+#pragma unroll
+        for (int j = 0; j < U; ++j) {
+          const long long u = u0 + j * blockDim.x;
+          if (u < hi) w[j] = ld_v4_cg(at<TW>(a.data[r], res_off + u * V));
+        }
+#pragma unroll
+        for (int j = 0; j < U; ++j) {
+          const long long u = u0 + j * blockDim.x;
+          if (u < hi) {
+            TA v[V];
+            unpack_vec<TW, TA>(w[j], v);
+            store_out<TI, TA, V>(out + u * V, v);
+          }
+        }
       }
     }
-    ok = peer_barrier(a, a.epoch + 3);
-    // the tail is written last: it may live inside `mine`, which peers read until the barrier above
-    if (ok && blockIdx.x == 0 && threadIdx.x < tail) out[nu * V + threadIdx.x] = narrow<TI, TA>(tail_val);
   }
   ring_end(a, ok);
 }
 
 // ---------------------------------------------------------------------------
-// reduce-scatter: out[chunk] = scale * reduce_p in_p[rank*chunk : (rank+1)*chunk]
+// reduce-scatter, push: staging [parity 2][W slots][chunk] (wire type)
+//   rank r stores chunk c of its input into slot r of rank c, one barrier,
+//   then reduces its W local slots into its output chunk.
 // ---------------------------------------------------------------------------
 template <typename TI, typename TW, int OP>
 __global__ void __launch_bounds__(kCommThreads) reduce_scatter_kernel(CommArgs a) {
@@ -358,158 +498,174 @@ __global__ void __launch_bounds__(kCommThreads) reduce_scatter_kernel(CommArgs a
   ring_begin(a);
   const int W = a.world, r = a.rank;
   const long long chunk = a.n;
+  const long long par = 0;
   const bool vec = chunk % V == 0;
-  if (a.copy_in) {
-    const long long total = chunk * W;
-    long long lo, hi;
-    block_range(total, &lo, &hi);
-    const TI* in = reinterpret_cast<const TI*>(a.in);
-    TW* w = reinterpret_cast<TW*>(a.data[r]);
-    for (long long e = lo + threadIdx.x; e < hi; e += blockDim.x) w[e] = narrow<TW, TA>(widen<TA, TI>(in[e]));
-  }
-  // The copy-in partition (whole message) differs from the reduce partition
-  // (my chunk), so every block must finish staging before any peer reads:
-  // barrier across all blocks of all ranks via block 0's slots is not enough,
-  // hence a grid-uniform partition -- every block staged a slice of the whole
-  // message and waits for *every* block index of every peer below.
-  bool ok = peer_barrier(a, a.epoch + 1);
-  if (ok && a.copy_in) {
-    // wait until all peers' other blocks have staged too: poll their slots for all block ids
-    const int t = threadIdx.x;
-    if (t < a.world * gridDim.x) {
-      const int p = t % a.world, blk = t / a.world;
-      if (p != r) {
-        const uint32_t* slot = a.sig[r] + blk * kMaxRanks + p;
-        const uint64_t t0 = globaltimer_ns();
-        uint32_t spins = 0;
-        while (static_cast<int32_t>(ld_acquire_sys(slot) - (a.epoch + 1)) < 0) {
-          if ((++spins & 255u) == 0) {
-            if (a.status[0] != 0 || globaltimer_ns() - t0 > a.timeout_ns) {
-              if (a.status[0] == 0) {
-                a.status[1] = p; a.status[2] = blk; a.status[3] = static_cast<int>(a.seq);
-                __threadfence_system();
-                a.status[0] = kErrPeerTimeout;
-              }
-              break;
-            }
-            __nanosleep(64);
+  const TI* in = reinterpret_cast<const TI*>(a.in);
+  long long lo, hi;
+  block_range(vec ? chunk / V : chunk, &lo, &hi);
+  for (int k = 1; k < W; ++k) {  // my own chunk is read from the input in the reduce
+    const int c = (r + k) % W;
+    if (vec) {
+      constexpr int U = 4;
+      for (long long u0 = lo + threadIdx.x; u0 < hi; u0 += U * blockDim.x) {
+        uint4 w[U];
+#pragma unroll
+        for (int j = 0; j < U; ++j) {
+          const long long u = u0 + j * blockDim.x;
+          if (u < hi) {
+            TA v[V];
+            load_in<TI, TA, V>(in + c * chunk + u * V, v);
+            w[j] = pack_vec<TW, TA>(v);
           }
         }
-      }
-    }
-    ok = __syncthreads_and(a.status[0] == 0) != 0;
-  }
-  if (ok) {
-    TI* out = reinterpret_cast<TI*>(a.out);
-    if (vec) {
-      long long lo, hi;
-      block_range(chunk / V, &lo, &hi);
-      for (long long u = lo + threadIdx.x; u < hi; u += blockDim.x) {
-        TA acc[V], v[V];
-        const long long off = r * chunk + u * V;
-        load_vec<TW, TA>(reinterpret_cast<const TW*>(a.data[0]) + off, acc);
-        for (int p = 1; p < W; ++p) {
-          load_vec<TW, TA>(reinterpret_cast<const TW*>(a.data[p]) + off, v);
 #pragma unroll
-          for (int i = 0; i < V; ++i) acc[i] = combine<OP>(acc[i], v[i]);
+        for (int j = 0; j < U; ++j) {
+          const long long u = u0 + j * blockDim.x;
+          if (u < hi) st_v4(at<TW>(a.data[c], par + r * chunk + u * V), w[j]);
         }
-#pragma unroll
-        for (int i = 0; i < V; ++i) acc[i] = widen<TA, TW>(narrow<TW, TA>(finish<OP>(acc[i], a.scale)));
-        store_out<TI, TA, V>(out + u * V, acc);
       }
     } else {
-      long long lo, hi;
-      block_range(chunk, &lo, &hi);
+      for (long long e = lo + threadIdx.x; e < hi; e += blockDim.x)
+        *at<TW>(a.data[c], par + r * chunk + e) = narrow<TW, TA>(widen<TA, TI>(in[c * chunk + e]));
+    }
+  }
+  bool ok = peer_barrier(a, a.epoch + 1);
+  if (ok) {
+    TI* out = reinterpret_cast<TI*>(a.out);
+    const TI* own = in + r * chunk;
+    if (vec) {
+      constexpr int U2 = 4;
+      for (long long u0 = lo + threadIdx.x; u0 < hi; u0 += U2 * blockDim.x) {
+        TA accs[U2][V];
+        for (int p = 0; p < W; ++p) {  // rank order
+          uint4 raw[U2];
+#pragma unroll
+          for (int j = 0; j < U2; ++j) {
+            const long long u = u0 + j * blockDim.x;
+            if (u < hi && p != r) raw[j] = ld_v4_cg(at<TW>(a.data[r], par + p * chunk + u * V));
+          }
+#pragma unroll
+          for (int j = 0; j < U2; ++j) {
+            const long long u = u0 + j * blockDim.x;
+            if (u >= hi) continue;
+            TA v[V];
+            if (p == r) {
+              load_in<TI, TA, V>(own + u * V, v);
+#pragma unroll
+              for (int i = 0; i < V; ++i) v[i] = widen<TA, TW>(narrow<TW, TA>(v[i]));
+            } else {
+              unpack_vec<TW, TA>(raw[j], v);
+            }
+#pragma unroll
+            for (int i = 0; i < V; ++i) accs[j][i] = p == 0 ? v[i] : combine<OP>(accs[j][i], v[i]);
+          }
+        }
+#pragma unroll
+        for (int j = 0; j < U2; ++j) {
+          const long long u = u0 + j * blockDim.x;
+          if (u >= hi) continue;
+#pragma unroll
+          for (int i = 0; i < V; ++i) accs[j][i] = widen<TA, TW>(narrow<TW, TA>(finish<OP>(accs[j][i], a.scale)));
+          store_out<TI, TA, V>(out + u * V, accs[j]);
+        }
+      }
+    } else {
       for (long long e = lo + threadIdx.x; e < hi; e += blockDim.x) {
-        const long long off = r * chunk + e;
-        TA acc = widen<TA, TW>(reinterpret_cast<const TW*>(a.data[0])[off]);
-        for (int p = 1; p < W; ++p) acc = combine<OP>(acc, widen<TA, TW>(reinterpret_cast<const TW*>(a.data[p])[off]));
+        TA acc = 0;
+        for (int p = 0; p < W; ++p) {
+          const TA v = p == r ? widen<TA, TW>(narrow<TW, TA>(widen<TA, TI>(own[e])))
+                              : widen<TA, TW>(*reinterpret_cast<volatile TW*>(at<TW>(a.data[r], par + p * chunk + e)));
+          acc = p == 0 ? v : combine<OP>(acc, v);
+        }
         out[e] = narrow<TI, TA>(widen<TA, TW>(narrow<TW, TA>(finish<OP>(acc, a.scale))));
       }
     }
-    ok = peer_barrier(a, a.epoch + 2);
   }
   ring_end(a, ok);
 }
 
 // ---------------------------------------------------------------------------
-// data movement without reduction (byte-level): all-gather, broadcast, all-to-all
-//   kind 0 all_gather: out[p*chunk + e] = data[p][e]
-//   kind 1 broadcast : out[e] = data[root][e]
-//   kind 2 all_to_all: out[p*chunk + e] = data[p][rank*chunk + e]
-// sizes in bytes (n = per-rank chunk bytes for 0/2, message bytes for 1)
+// data movement without reduction, push, byte level (parity-buffered slots):
+//   kind 0 all_gather : rank r stores its shard into slot r of every rank
+//   kind 1 broadcast  : the root stores the tensor into slot 0 of every rank
+//   kind 2 all_to_all : rank r stores its chunk c into slot r of rank c
+//   after one barrier every rank copies its slots into its output.
+//   n = per-slot bytes (shard / message / chunk)
 // ---------------------------------------------------------------------------
-__global__ void __launch_bounds__(kCommThreads) move_kernel(CommArgs a, int kind, long long in_bytes) {
+__global__ void __launch_bounds__(kCommThreads) move_kernel(CommArgs a, int kind) {
   ring_begin(a);
   const int W = a.world, r = a.rank;
   const long long nb = a.n;
-  if (a.copy_in) {
-    const bool stage = kind != 1 || r == a.root;
-    if (stage) {
-      long long lo, hi;
-      const bool v16 = in_bytes % 16 == 0;
-      const long long units = v16 ? in_bytes / 16 : in_bytes;
-      block_range(units, &lo, &hi);
-      for (long long u = lo + threadIdx.x; u < hi; u += blockDim.x) {
-        if (v16) st_v4(reinterpret_cast<uint8_t*>(a.data[r]) + 16 * u, ld_v4(reinterpret_cast<const uint8_t*>(a.in) + 16 * u));
-        else reinterpret_cast<uint8_t*>(a.data[r])[u] = reinterpret_cast<const uint8_t*>(a.in)[u];
-      }
+  const int slots = kind == 1 ? 1 : W;
+  const long long par = 0;
+  const bool v16 = nb % 16 == 0;
+  const long long units = v16 ? nb / 16 : nb;
+  long long lo, hi;
+  block_range(units, &lo, &hi);
+  const uint8_t* in = reinterpret_cast<const uint8_t*>(a.in);
+  auto push = [&](const uint8_t* src, int peer, int slot) {
+    uint8_t* d = reinterpret_cast<uint8_t*>(a.data[peer]) + par + slot * nb;
+    if (!v16) {
+      for (long long u = lo + threadIdx.x; u < hi; u += blockDim.x) d[u] = src[u];
+      return;
+    }
+    constexpr int U = 4;
+    for (long long u0 = lo + threadIdx.x; u0 < hi; u0 += U * blockDim.x) {
+      uint4 w[U];
+#pragma unroll
+      for (int j = 0; j < U; ++j)
+        if (u0 + j * blockDim.x < hi) w[j] = ld_v4(src + 16 * (u0 + j * blockDim.x));
+#pragma unroll
+      for (int j = 0; j < U; ++j)
+        if (u0 + j * blockDim.x < hi) st_v4(d + 16 * (u0 + j * blockDim.x), w[j]);
+    }
+  };
+  if (kind == 0) {
+    for (int k = 0; k < W; ++k) push(in, (r + k) % W, r);
+  } else if (kind == 1) {
+    if (r == a.root)
+      for (int k = 1; k < W; ++k) push(in, (r + k) % W, 0);
+  } else {
+    for (int k = 0; k < W; ++k) {
+      const int c = (r + k) % W;
+      push(in + c * nb, c, r);
     }
   }
   bool ok = peer_barrier(a, a.epoch + 1);
-  // staging partition (bytes of the input) can differ from the read partition; wait for all block ids
-  if (ok && a.copy_in) {
-    const int t = threadIdx.x;
-    if (t < W * gridDim.x) {
-      const int p = t % W, blk = t / W;
-      if (p != r) {
-        const uint32_t* slot = a.sig[r] + blk * kMaxRanks + p;
-        const uint64_t t0 = globaltimer_ns();
-        uint32_t spins = 0;
-        while (static_cast<int32_t>(ld_acquire_sys(slot) - (a.epoch + 1)) < 0) {
-          if ((++spins & 255u) == 0) {
-            if (a.status[0] != 0 || globaltimer_ns() - t0 > a.timeout_ns) {
-              if (a.status[0] == 0) {
-                a.status[1] = p; a.status[2] = blk; a.status[3] = static_cast<int>(a.seq);
-                __threadfence_system();
-                a.status[0] = kErrPeerTimeout;
-              }
-              break;
-            }
-            __nanosleep(64);
-          }
-        }
-      }
-    }
-    ok = __syncthreads_and(a.status[0] == 0) != 0;
-  }
   if (ok) {
-    const bool v16 = nb % 16 == 0 && (kind != 2 || (static_cast<long long>(r) * nb) % 16 == 0);
-    const long long units = v16 ? nb / 16 : nb;
-    long long lo, hi;
-    block_range(units, &lo, &hi);
     uint8_t* out = reinterpret_cast<uint8_t*>(a.out);
-    for (int p = 0; p < W; ++p) {
+    const uint8_t* mine = reinterpret_cast<const uint8_t*>(a.data[r]) + par;
+    for (int s = 0; s < slots; ++s) {
       const uint8_t* src;
       uint8_t* dst;
-      if (kind == 0) {
-        src = reinterpret_cast<const uint8_t*>(a.data[p]);
-        dst = out + p * nb;
-      } else if (kind == 1) {
-        if (p != 0) break;
-        if (r == a.root && a.out == a.in) break;
-        src = reinterpret_cast<const uint8_t*>(a.data[a.root]);
+      if (kind == 1) {
+        if (r == a.root) {
+          if (a.out == a.in) break;
+          src = in;
+        } else {
+          src = mine;
+        }
         dst = out;
       } else {
-        src = reinterpret_cast<const uint8_t*>(a.data[p]) + r * nb;
-        dst = out + p * nb;
+        src = mine + s * nb;
+        dst = out + s * nb;
       }
-      for (long long u = lo + threadIdx.x; u < hi; u += blockDim.x) {
-        if (v16) st_v4(dst + 16 * u, ld_v4_volatile(src + 16 * u));
-        else dst[u] = src[u];
+      if (!v16) {
+        for (long long u = lo + threadIdx.x; u < hi; u += blockDim.x)
+          dst[u] = *reinterpret_cast<const volatile uint8_t*>(src + u);
+        continue;
+      }
+      constexpr int U = 4;
+      for (long long u0 = lo + threadIdx.x; u0 < hi; u0 += U * blockDim.x) {
+        uint4 w[U];
+#pragma unroll
+        for (int j = 0; j < U; ++j)
+          if (u0 + j * blockDim.x < hi) w[j] = ld_v4_cg(src + 16 * (u0 + j * blockDim.x));
+#pragma unroll
+        for (int j = 0; j < U; ++j)
+          if (u0 + j * blockDim.x < hi) st_v4(dst + 16 * (u0 + j * blockDim.x), w[j]);
       }
     }
-    ok = peer_barrier(a, a.epoch + 2);
   }
   ring_end(a, ok);
 }
@@ -569,6 +725,7 @@ __global__ void __launch_bounds__(kCommThreads) stepped_kernel(CommArgs a, const
     TI* out = reinterpret_cast<TI*>(a.out);
     for (long long e = gt; e < n; e += gs) out[e] = narrow<TI, TA>(finish<OP>(widen<TA, TK>(work[e]), a.scale));
   }
+  if (ok) ok = grid_peer_barrier(a, a.epoch + 2 + n_steps, grid);  // peers done reading my work buffer
   grid.sync();
   ring_end(a, ok);
 }
@@ -598,6 +755,12 @@ void* ipc_open(const std::string& bytes) {
 }
 
 }  // namespace
+
+// tcgen05 GEMM fused with a reduce-scatter (fuse 1) or an all-gather (fuse 2); gemm.cu.
+void gemm_fused(int fuse, torch::Tensor a, torch::Tensor b, torch::Tensor out, bool b_mn,
+                c10::optional<torch::Tensor> bias, c10::optional<torch::Tensor> aux,
+                c10::optional<torch::Tensor> resid, int64_t epi, torch::Tensor status, const PeerCtx& ctx,
+                c10::optional<torch::Tensor> ag_buf, c10::optional<torch::Tensor> ag_ready);
 
 struct Segment {
   void* local = nullptr;
@@ -738,8 +901,14 @@ class DeviceCommImpl {
     const Segment& s = segs_.at(seg);
     TORCH_CHECK(s.opened, "symmetric segment not mapped on every rank yet");
     TORCH_CHECK(sig_opened_ || world_ == 1, "signal pads not mapped");
+    // Calls alternate between the two halves of the staging buffer, so a peer
+    // that has already moved on to the next call never writes into memory
+    // this rank is still reading (call k+2 cannot start before every rank
+    // has entered call k+1).
+    const int64_t half = seg == staging_ ? (s.bytes / 2) / 256 * 256 : 0;
+    const int64_t par_off = seg == staging_ ? static_cast<int64_t>(seq_ & 1) * half : 0;
     for (int r = 0; r < world_; ++r) {
-      a.data[r] = static_cast<uint8_t*>(s.peers[r]) + offset;
+      a.data[r] = static_cast<uint8_t*>(s.peers[r]) + offset + par_off;
       a.sig[r] = sig_peers_[r];
     }
     a.in = in;
@@ -760,8 +929,73 @@ class DeviceCommImpl {
   }
 
   int blocks_for(int64_t bytes, int max_blocks) const {
-    int64_t b = (bytes + (256 << 10) - 1) / (256 << 10);  // ~256 KiB per CTA
-    return static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(b, std::min(max_blocks, kMaxBlocks))));
+    int64_t b = (bytes + (64 << 10) - 1) / (64 << 10);  // ~64 KiB per CTA per call
+    return static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(b, std::min(max_blocks, kMaxBlocks - 1))));
+  }
+
+  // Staging bytes a call needs (wire elements of `wsz` bytes); mirrors the
+  // layouts documented on each kernel.  kind: 0 one-shot AR, 1 two-shot AR,
+  // 2 reduce-scatter (n = input elements), 3 all_gather / all_to_all
+  // (n = bytes per rank), 4 broadcast (n = bytes).
+  int64_t staging_need(int kind, int64_t n, int64_t wsz) const {
+    const int64_t W = world_;
+    const int64_t V = 16 / std::max<int64_t>(1, wsz);
+    // Each call uses one half of the staging buffer: the need is doubled.
+    switch (kind) {
+      case 0: return 2 * W * ((n + V - 1) / V * V) * wsz;
+      case 1: {
+        const int64_t chunk_u = ((n / V) + W - 1) / W;
+        return 2 * (2 * W * chunk_u * V + W * V) * wsz;
+      }
+      case 2: return 2 * n * wsz;
+      case 3: return 2 * W * n;
+      case 5: return 2 * n * wsz;  // stepped schedules: one working copy
+      default: return 2 * n;
+    }
+  }
+
+  static PeerCtx peer_ctx(const CommArgs& a) {
+    PeerCtx c{};
+    for (int r = 0; r < a.world; ++r) {
+      c.data[r] = a.data[r];
+      c.sig[r] = a.sig[r];
+    }
+    c.rank = a.rank;
+    c.world = a.world;
+    c.epoch = a.epoch;
+    c.seq = a.seq;
+    c.status = a.status;
+    c.timeout_ns = a.timeout_ns;
+    return c;
+  }
+
+  // out[M/W, N] = (sum over ranks of x_r @ w_r^T)[this rank's rows] + bias + resid,
+  // as one kernel: tiles are pushed to their owners as they finish.
+  void gemm_rs(torch::Tensor x, torch::Tensor w, torch::Tensor out, bool w_mn, c10::optional<torch::Tensor> bias,
+               c10::optional<torch::Tensor> resid, torch::Tensor status) {
+    c10::cuda::CUDAGuard g(device_);
+    const int64_t M = x.size(0);
+    const int64_t N = w_mn ? w.size(1) : w.size(0);
+    const int64_t need = 2 * M * N * 2;  // two parity halves of W slots of [M/W, N] bf16
+    TORCH_CHECK(need <= segs_[staging_].bytes, "staging buffer too small for the fused reduce-scatter");
+    CommArgs a = base_args(staging_, 0, x.data_ptr(), out.data_ptr(), M * N, 7, M * N * 2, 1);
+    gemm_fused(1, x, w, out, w_mn, bias, c10::nullopt, resid, 0, status, peer_ctx(a), c10::nullopt, c10::nullopt);
+  }
+
+  // out[M, N] = epi(all_gather(x_shard) @ w^T); `gathered` [M, K] receives the
+  // gathered input, `ready` is int32 [W] scratch.
+  void ag_gemm(torch::Tensor x_shard, torch::Tensor w, torch::Tensor out, torch::Tensor gathered,
+               torch::Tensor ready, bool w_mn, c10::optional<torch::Tensor> bias, c10::optional<torch::Tensor> aux,
+               c10::optional<torch::Tensor> resid, int64_t epi, torch::Tensor status) {
+    c10::cuda::CUDAGuard g(device_);
+    TORCH_CHECK(x_shard.is_contiguous() && x_shard.scalar_type() == at::kBFloat16, "x shard: contiguous bf16");
+    const int64_t bytes = x_shard.numel() * 2;
+    TORCH_CHECK(2 * bytes <= segs_[staging_].bytes, "staging buffer too small for the fused all-gather");
+    CommArgs a = base_args(staging_, 0, x_shard.data_ptr(), out.data_ptr(), x_shard.numel(), 8, bytes, 1);
+    auto stream = at::cuda::getCurrentCUDAStream();
+    // peers read my shard from my staging (their kernels wait for my ready signal)
+    ck(cudaMemcpyAsync(a.data[rank_], x_shard.data_ptr(), bytes, cudaMemcpyDeviceToDevice, stream), "shard copy");
+    gemm_fused(2, x_shard, w, out, w_mn, bias, aux, resid, epi, status, peer_ctx(a), gathered, ready);
   }
 
   // algorithm: 0 one_shot, 1 two_shot
@@ -772,33 +1006,35 @@ class DeviceCommImpl {
     const auto dt = in.scalar_type();
     const int64_t n = in.numel();
     const int64_t wsz = wire_bf16 ? 2 : in.element_size();
-    auto loc = locate(in.data_ptr(), n * in.element_size());
-    const bool zero_copy = algorithm == 1 && !wire_bf16 && loc.first >= 0 && in.data_ptr() == out.data_ptr();
-    int seg = staging_;
-    int64_t off = 0;
-    if (zero_copy) {
-      seg = loc.first;
-      off = loc.second;
-    } else {
-      TORCH_CHECK(n * wsz <= segs_[staging_].bytes, "message larger than the staging buffer");
-    }
-    CommArgs a = base_args(seg, off, in.data_ptr(), out.data_ptr(), n, 0, n * wsz, 3);
+    TORCH_CHECK(staging_need(algorithm, n, wsz) <= segs_[staging_].bytes, "staging buffer too small");
+    CommArgs a = base_args(staging_, 0, in.data_ptr(), out.data_ptr(), n, 0, n * wsz, 2);
     a.scale = static_cast<float>(scale);
-    a.copy_in = zero_copy ? 0 : 1;
-    const int blocks = blocks_for(n * wsz / std::max(1, algorithm == 1 ? 1 : 1), max_blocks);
+    if (algorithm == 1 && in.data_ptr() == out.data_ptr()) {
+      // in place on a symmetric tensor: results go straight into every rank's copy
+      auto loc = locate(in.data_ptr(), n * in.element_size());
+      if (loc.first >= 0) {
+        const Segment& sg = segs_[loc.first];
+        for (int r = 0; r < world_; ++r) a.dst[r] = static_cast<uint8_t*>(sg.peers[r]) + loc.second;
+      }
+    }
+    const int64_t V = 16 / wsz;
+    const long long chunk_u = ((n / V) + world_ - 1) / world_;
+    const int64_t n_pad = (n + V - 1) / V * V;
+    const int blocks = blocks_for(algorithm == 1 ? n * wsz / world_ : n * wsz, max_blocks);
     auto stream = at::cuda::getCurrentCUDAStream();
-#define MNB_AR(TI, TW)                                                                              \
-  do {                                                                                             \
-    switch (op) {                                                                                  \
-      case kSum: (algorithm ? ar_two_shot_kernel<TI, TW, kSum> : ar_one_shot_kernel<TI, TW, kSum>)  \
-          <<<blocks, kCommThreads, 0, stream>>>(a); break;                                          \
-      case kProd: (algorithm ? ar_two_shot_kernel<TI, TW, kProd> : ar_one_shot_kernel<TI, TW, kProd>) \
-          <<<blocks, kCommThreads, 0, stream>>>(a); break;                                          \
-      case kMax: (algorithm ? ar_two_shot_kernel<TI, TW, kMax> : ar_one_shot_kernel<TI, TW, kMax>)  \
-          <<<blocks, kCommThreads, 0, stream>>>(a); break;                                          \
-      default: (algorithm ? ar_two_shot_kernel<TI, TW, kMin> : ar_one_shot_kernel<TI, TW, kMin>)    \
-          <<<blocks, kCommThreads, 0, stream>>>(a); break;                                          \
-    }                                                                                              \
+#define MNB_AR1(TI, TW, OPV)                                                                         \
+  do {                                                                                              \
+    if (algorithm) ar_push_two_shot_kernel<TI, TW, OPV><<<blocks, kCommThreads, 0, stream>>>(a, chunk_u); \
+    else ar_push_one_shot_kernel<TI, TW, OPV><<<blocks, kCommThreads, 0, stream>>>(a, n_pad);       \
+  } while (0)
+#define MNB_AR(TI, TW)                          \
+  do {                                         \
+    switch (op) {                              \
+      case kSum: MNB_AR1(TI, TW, kSum); break;  \
+      case kProd: MNB_AR1(TI, TW, kProd); break; \
+      case kMax: MNB_AR1(TI, TW, kMax); break;  \
+      default: MNB_AR1(TI, TW, kMin); break;    \
+    }                                          \
   } while (0)
     if (dt == at::kFloat && wire_bf16) MNB_AR(float, __nv_bfloat16);
     else if (dt == at::kFloat) MNB_AR(float, float);
@@ -808,6 +1044,7 @@ class DeviceCommImpl {
     else if (dt == at::kInt) MNB_AR(int32_t, int32_t);
     else TORCH_CHECK(false, "unsupported dtype for device all_reduce");
 #undef MNB_AR
+#undef MNB_AR1
     C10_CUDA_KERNEL_LAUNCH_CHECK();
   }
 
@@ -818,19 +1055,10 @@ class DeviceCommImpl {
     TORCH_CHECK(in.numel() == chunk * world_, "input must hold world_size chunks");
     const auto dt = in.scalar_type();
     const int64_t bytes = in.numel() * in.element_size();
-    auto loc = locate(in.data_ptr(), bytes);
-    int seg = staging_;
-    int64_t off = 0;
-    if (loc.first >= 0) {
-      seg = loc.first;
-      off = loc.second;
-    } else {
-      TORCH_CHECK(bytes <= segs_[staging_].bytes, "message larger than the staging buffer");
-    }
-    CommArgs a = base_args(seg, off, in.data_ptr(), out.data_ptr(), chunk, 1, bytes, 2);
+    TORCH_CHECK(staging_need(2, in.numel(), in.element_size()) <= segs_[staging_].bytes, "staging buffer too small");
+    CommArgs a = base_args(staging_, 0, in.data_ptr(), out.data_ptr(), chunk, 1, bytes, 1);
     a.scale = static_cast<float>(scale);
-    a.copy_in = loc.first >= 0 ? 0 : 1;
-    const int blocks = blocks_for(chunk * in.element_size() * world_, max_blocks);
+    const int blocks = blocks_for(chunk * in.element_size(), max_blocks);
     auto stream = at::cuda::getCurrentCUDAStream();
 #define MNB_RS(T)                                                                                   \
   do {                                                                                             \
@@ -856,21 +1084,12 @@ class DeviceCommImpl {
     c10::cuda::CUDAGuard g(device_);
     TORCH_CHECK(in.is_contiguous() && out.is_contiguous(), "contiguous tensors required");
     const int64_t in_bytes = in.numel() * in.element_size();
-    const int64_t nb = kind == 0 ? in_bytes : (kind == 1 ? in_bytes : in_bytes / world_);
-    auto loc = locate(in.data_ptr(), in_bytes);
-    int seg = staging_;
-    int64_t off = 0;
-    if (loc.first >= 0) {
-      seg = loc.first;
-      off = loc.second;
-    } else {
-      TORCH_CHECK(in_bytes <= segs_[staging_].bytes, "message larger than the staging buffer");
-    }
-    CommArgs a = base_args(seg, off, in.data_ptr(), out.data_ptr(), nb, 2 + kind, in_bytes, 2);
+    const int64_t nb = kind == 2 ? in_bytes / world_ : in_bytes;
+    TORCH_CHECK(staging_need(kind == 1 ? 4 : 3, nb, 1) <= segs_[staging_].bytes, "staging buffer too small");
+    CommArgs a = base_args(staging_, 0, in.data_ptr(), out.data_ptr(), nb, 2 + kind, in_bytes, 1);
     a.root = root;
-    a.copy_in = loc.first >= 0 ? 0 : 1;
-    const int blocks = blocks_for(kind == 1 ? in_bytes : in_bytes * world_, max_blocks);
-    move_kernel<<<blocks, kCommThreads, 0, at::cuda::getCurrentCUDAStream()>>>(a, kind, in_bytes);
+    const int blocks = blocks_for(nb, max_blocks);
+    move_kernel<<<blocks, kCommThreads, 0, at::cuda::getCurrentCUDAStream()>>>(a, kind);
     C10_CUDA_KERNEL_LAUNCH_CHECK();
   }
 
@@ -890,9 +1109,9 @@ class DeviceCommImpl {
     const int n_steps = static_cast<int>(steps.size(0));
     const bool narrow_in = dt == at::kBFloat16 || dt == at::kHalf;
     const int64_t work_elem = (narrow_in && round_bf16) ? 4 : in.element_size();
-    TORCH_CHECK(n * work_elem <= segs_[staging_].bytes, "message larger than the staging buffer");
+    TORCH_CHECK(staging_need(5, n, work_elem) <= segs_[staging_].bytes, "message larger than the staging buffer");
     CommArgs a = base_args(staging_, 0, in.data_ptr(), out.data_ptr(), n, 6, n * (round_bf16 ? 2 : in.element_size()),
-                           n_steps + 2);
+                           n_steps + 3);
     a.scale = static_cast<float>(scale);
     const long long* sp = reinterpret_cast<const long long*>(steps.data_ptr<int64_t>());
     int round = round_bf16;
@@ -969,6 +1188,9 @@ void register_comm(py::module_& m) {
       .def("move", &DeviceCommImpl::move)
       .def("barrier", &DeviceCommImpl::barrier)
       .def("stepped_all_reduce", &DeviceCommImpl::stepped_all_reduce)
+      .def("staging_need", &DeviceCommImpl::staging_need)
+      .def("gemm_rs", &DeviceCommImpl::gemm_rs)
+      .def("ag_gemm", &DeviceCommImpl::ag_gemm)
       .def("close", &DeviceCommImpl::close)
       .def_property_readonly("rank", &DeviceCommImpl::rank)
       .def_property_readonly("world", &DeviceCommImpl::world);

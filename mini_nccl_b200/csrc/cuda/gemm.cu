@@ -23,6 +23,25 @@
 //               i^1 for the next tile.
 // TMA loads are per-CTA (no cluster multicast).  Every wait is bounded and
 // reports through args.status instead of hanging.
+//
+// Fused with a collective (tensor parallelism with a sequence-parallel
+// layout; the ranks of one device communicator run the same launch):
+//   kFuseRS  GEMM -> reduce-scatter.  Every rank computes partial sums for all
+//            M rows; the epilogue stores each finished tile straight into the
+//            staging slot of the rank that owns those rows (NVLink stores from
+//            registers), so the transfer of tile i overlaps the MMAs of tile
+//            i+1.  Tiles are visited starting with the next rank's rows and
+//            ending with this rank's own.  When a CTA has no tiles left it
+//            signals every owner; once all CTAs of all ranks have signalled,
+//            the CTAs sum the W slots of this rank's rows in rank order and
+//            add bias and residual (bf16 out).
+//   kFuseAG  all-gather -> GEMM.  A is gathered into a local [M, K] buffer by
+//            two extra gather warps per CTA (16-byte peer loads, local
+//            stores), own shard first; per-shard counters tell the TMA
+//            producer when a shard's rows may be loaded.  Tiles of this
+//            rank's own rows come first, so the gather runs under them.
+//            Remote rows cross NVLink once; the TMA unit only ever reads
+//            local memory.
 #include <ATen/cuda/CUDAContext.h>
 #include <c10/cuda/CUDAGuard.h>
 #include <cudaTypedefs.h>
@@ -31,6 +50,7 @@
 #include <mutex>
 
 #include "common.cuh"
+#include "peer.cuh"
 
 namespace mnb {
 
@@ -59,12 +79,65 @@ struct GemmArgs {
   int epi;
   int tma_out;  // bf16 output (and GELU aux) written through shared memory + TMA store
   int* status;
+  // fused collectives
+  int rows_per_rank;                // M / world (RS: rows each rank owns; AG: rows of each shard)
+  const __nv_bfloat16* ag_local;    // AG: this rank's shard of A, [rows_per_rank, K]
+  __nv_bfloat16* ag_buf;            // AG: gathered A, [M, K], row stride K
+  int* ag_ready;                    // AG: per-shard count of CTAs done copying (zeroed per call)
 };
+
+enum : int { kFuseNone = 0, kFuseRS = 1, kFuseAG = 2 };
 
 constexpr int kBM = 128;
 constexpr int kBK = 64;
 constexpr int kEpiWarps = 8;  // two warps per TMEM lane quadrant, each owning half the columns
 constexpr int kGemmThreads = 64 + 32 * kEpiWarps;
+constexpr int kGatherThreads = 64;  // kFuseAG: two gather warps after the epilogue warps
+template <int FUSE>
+constexpr int gemm_threads() { return kGemmThreads + (FUSE == kFuseAG ? kGatherThreads : 0); }
+
+MNB_DEVICE uint32_t ld_acquire_gpu(const int* p) {
+  uint32_t v;
+  asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+MNB_DEVICE void red_release_gpu_add(int* p, int v) {
+  asm volatile("red.release.gpu.global.add.s32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+MNB_DEVICE void fence_proxy_async_global() { asm volatile("fence.proxy.async.global;" ::: "memory"); }
+
+// Output tile visiting order.  RS: start with the next rank's rows and end
+// with our own (their transfer is local); AG: our own rows first (no wait).
+template <int FUSE>
+MNB_DEVICE int remap_mblock(int mb, int m_tiles, const GemmArgs& a, const PeerCtx& ctx) {
+  if constexpr (FUSE == kFuseNone) {
+    return mb;
+  } else {
+    if (a.rows_per_rank % kBM != 0) return mb;
+    const int per = a.rows_per_rank / kBM;
+    const int first = FUSE == kFuseRS ? (ctx.rank + 1) % ctx.world : ctx.rank;
+    return (mb + first * per) % m_tiles;
+  }
+}
+
+// RS epilogue: 32 consecutive columns of one row of partial sums go to the
+// owner's slot for this rank, as bf16.
+MNB_DEVICE void rs_store(const GemmArgs& a, const PeerCtx& ctx, int row, int col0, const float* v) {
+  if (row >= a.M) return;
+  const int o = row / a.rows_per_rank;
+  const long long lr = row - static_cast<long long>(o) * a.rows_per_rank;
+  __nv_bfloat16* d = reinterpret_cast<__nv_bfloat16*>(ctx.data[o]) +
+                     (static_cast<long long>(ctx.rank) * a.rows_per_rank + lr) * a.N + col0;
+  if (col0 + 32 <= a.N) {
+    uint32_t pk[16];
+#pragma unroll
+    for (int i = 0; i < 16; ++i) pk[i] = pack_bf16x2(v[2 * i], v[2 * i + 1]);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) st_v4(d + 8 * i, make_uint4(pk[4 * i], pk[4 * i + 1], pk[4 * i + 2], pk[4 * i + 3]));
+  } else {
+    for (int i = 0; i < 32 && col0 + i < a.N; ++i) d[i] = f32_to_bf16(v[i]);
+  }
+}
 
 template <int BN, int STAGES>
 struct GemmSmem {
@@ -274,11 +347,127 @@ MNB_DEVICE void epilogue_inputs(const GemmArgs& a, int row, int col0, float* v) 
   }
 }
 
-template <int BN, bool A_MN, bool B_MN, int STAGES>
-__global__ void __launch_bounds__(kGemmThreads, 1)
+// kFuseAG gather warps (64 threads): copy this CTA's slice of every shard
+// into the gathered buffer, own shard first, then bump the shard's counter.
+MNB_DEVICE void gather_shards(const GemmArgs& a, const PeerCtx& ctx, int gt) {
+  const int W = ctx.world, r = ctx.rank;
+  const uint32_t want = ctx.epoch + 1;
+  if (blockIdx.x == 0 && gt == 0) {  // my shard (in my staging) is ready for the peers
+    __threadfence_system();
+    for (int p = 0; p < W; ++p)
+      if (p != r) st_release_sys(ctx.sig[p] + kReadyRow * kMaxRanks + r, want);
+  }
+  const long long row_units = a.K / 8;  // 16-byte units per row
+  const long long per = (a.rows_per_rank + gridDim.x - 1) / gridDim.x;
+  const long long rpr = a.rows_per_rank;
+  const long long lo = min(rpr, per * static_cast<long long>(blockIdx.x));
+  const long long hi = min(rpr, lo + per);
+  const long long units = (hi - lo) * row_units;
+  const uint64_t t0 = globaltimer_ns();
+  __shared__ int gather_ok;
+  for (int k = 0; k < W; ++k) {
+    const int sh = (r + k) % W;
+    if (gt == 0) {
+      bool ok = ctx.status[0] == 0 && *reinterpret_cast<volatile int*>(a.status) == 0;
+      if (ok && sh != r)
+        ok = wait_signal(ctx.sig[r] + kReadyRow * kMaxRanks + sh, want, ctx.status, sh, blockIdx.x, ctx.seq,
+                         ctx.timeout_ns, t0);
+      if (!ok) atomicCAS(a.status, 0, kErrPeerTimeout);
+      gather_ok = ok;
+    }
+    asm volatile("bar.sync 2, %0;" ::"n"(kGatherThreads) : "memory");
+    if (!gather_ok) return;
+    const __nv_bfloat16* src = sh == r ? a.ag_local : reinterpret_cast<const __nv_bfloat16*>(ctx.data[sh]);
+    const __nv_bfloat16* s0 = src + lo * a.K;
+    __nv_bfloat16* d0 = a.ag_buf + (static_cast<long long>(sh) * a.rows_per_rank + lo) * a.K;
+    constexpr int U = 8;
+    for (long long u0 = gt; u0 < units; u0 += U * kGatherThreads) {
+      uint4 v[U];
+#pragma unroll
+      for (int j = 0; j < U; ++j)
+        if (u0 + j * kGatherThreads < units) v[j] = ld_v4_volatile(s0 + 8 * (u0 + j * kGatherThreads));
+#pragma unroll
+      for (int j = 0; j < U; ++j)
+        if (u0 + j * kGatherThreads < units) st_v4(d0 + 8 * (u0 + j * kGatherThreads), v[j]);
+    }
+    fence_proxy_async_global();
+    asm volatile("bar.sync 2, %0;" ::"n"(kGatherThreads) : "memory");
+    if (gt == 0) {
+      __threadfence();
+      red_release_gpu_add(a.ag_ready + sh, 1);
+    }
+  }
+}
+
+// kFuseRS tail (all threads): announce that this CTA's tiles have landed,
+// wait for every CTA of every rank, then reduce this rank's rows.
+MNB_DEVICE void rs_finish(const GemmArgs& a, const PeerCtx& ctx) {
+  const int W = ctx.world, r = ctx.rank;
+  const uint32_t want = ctx.epoch + 1;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    __threadfence_system();
+    for (int p = 0; p < W; ++p) st_release_sys(ctx.sig[p] + blockIdx.x * kMaxRanks + r, want);
+  }
+  bool ok = *reinterpret_cast<volatile int*>(a.status) == 0;
+  const uint64_t t0 = globaltimer_ns();
+  for (int i = threadIdx.x; ok && i < static_cast<int>(gridDim.x) * W; i += blockDim.x) {
+    const int b = i / W, src = i % W;
+    ok = wait_signal(ctx.sig[r] + b * kMaxRanks + src, want, ctx.status, src, b, ctx.seq, ctx.timeout_ns, t0);
+  }
+  if (!__syncthreads_and(ok)) return;
+  // out[row, col] = bias[col] + resid[row, col] + sum_p slot_p[row, col]   (rows of this rank)
+  const long long cu = a.N / 8;
+  const long long total = static_cast<long long>(a.rows_per_rank) * cu;
+  const long long slot = static_cast<long long>(a.rows_per_rank) * a.N;
+  const __nv_bfloat16* base = reinterpret_cast<const __nv_bfloat16*>(ctx.data[r]);
+  __nv_bfloat16* out = reinterpret_cast<__nv_bfloat16*>(a.out);
+  for (long long u = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; u < total;
+       u += static_cast<long long>(gridDim.x) * blockDim.x) {
+    const long long row = u / cu, col = (u - row * cu) * 8;
+    float acc[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) acc[i] = 0.f;
+    for (int p = 0; p < W; ++p) {
+      const uint4 w = ld_v4_volatile(base + p * slot + row * a.N + col);
+      const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const float2 f = unpack_bf16x2(ws[j]);
+        acc[2 * j] += f.x;
+        acc[2 * j + 1] += f.y;
+      }
+    }
+    if (a.bias != nullptr) {
+      const uint4 w = ld_v4(a.bias + col);
+      const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const float2 f = unpack_bf16x2(ws[j]);
+        acc[2 * j] += f.x;
+        acc[2 * j + 1] += f.y;
+      }
+    }
+    if (a.resid != nullptr) {
+      const uint4 w = ld_v4(a.resid + row * a.ldr + col);
+      const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const float2 f = unpack_bf16x2(ws[j]);
+        acc[2 * j] += f.x;
+        acc[2 * j + 1] += f.y;
+      }
+    }
+    st_v4(out + row * a.ldo + col, make_uint4(pack_bf16x2(acc[0], acc[1]), pack_bf16x2(acc[2], acc[3]),
+                                             pack_bf16x2(acc[4], acc[5]), pack_bf16x2(acc[6], acc[7])));
+  }
+}
+
+template <int BN, bool A_MN, bool B_MN, int STAGES, int FUSE>
+__global__ void __launch_bounds__(gemm_threads<FUSE>(), 1)
     gemm_tcgen05_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
                         const __grid_constant__ CUtensorMap map_out, const __grid_constant__ CUtensorMap map_aux,
-                        const GemmArgs args) {
+                        const GemmArgs args, const PeerCtx ctx) {
   using S = GemmSmem<BN, STAGES>;
   constexpr uint32_t kIdesc = idesc_bf16(kBM, BN, A_MN, B_MN);
   constexpr uint32_t kTmemCols = 2 * BN;
@@ -330,14 +519,41 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     if (lane == 0) {
       int stage = 0;
       uint32_t phase = 0;
+      uint32_t ready_mask = 0;  // kFuseAG: shards known to be gathered
+      (void)ready_mask;
       for (int u = blockIdx.x; u < units; u += gridDim.x) {
         const int split = u / (m_tiles * n_tiles);
         const int t = u % (m_tiles * n_tiles);
-        const int mb = t % m_tiles, nb = t / m_tiles;
+        const int mb = remap_mblock<FUSE>(t % m_tiles, m_tiles, args, ctx), nb = t / m_tiles;
         const int kb0 = split * args.k_blocks_per_split;
         const int kb1 = min(k_blocks, kb0 + args.k_blocks_per_split);
         bool ok = true;
-        for (int kb = kb0; kb < kb1; ++kb) {
+        if constexpr (FUSE == kFuseAG) {
+          // rows of this tile come from shards s0..s1: wait until every CTA
+          // has copied its part of them into the gathered buffer
+          const int s0 = (mb * kBM) / args.rows_per_rank;
+          const int s1 = min(args.M - 1, mb * kBM + kBM - 1) / args.rows_per_rank;
+          for (int sh = s0; sh <= s1 && ok; ++sh) {
+            if (ready_mask & (1u << sh)) continue;
+            const uint64_t t0 = globaltimer_ns();
+            uint32_t spins = 0;
+            while (static_cast<int>(ld_acquire_gpu(args.ag_ready + sh)) < static_cast<int>(gridDim.x)) {
+              if ((++spins & 255u) == 0) {
+                if (*reinterpret_cast<volatile int*>(status) != 0 || ctx.status[0] != 0) { ok = false; break; }
+                if (globaltimer_ns() - t0 > ctx.timeout_ns) {
+                  report_timeout(ctx.status, sh, blockIdx.x, ctx.seq);
+                  atomicCAS(status, 0, kErrPeerTimeout);
+                  ok = false;
+                  break;
+                }
+                __nanosleep(32);
+              }
+            }
+            ready_mask |= 1u << sh;
+          }
+          fence_proxy_async_global();  // generic-proxy writes of the gather -> TMA reads
+        }
+        for (int kb = kb0; kb < kb1 && ok; ++kb) {
           if (!mbar_wait(empty0 + 8 * stage, phase ^ 1, status)) { ok = false; break; }
           const uint32_t full = full0 + 8 * stage;
           mbar_arrive_expect_tx(full, S::a_bytes + S::b_bytes);
@@ -397,7 +613,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         if (acc == 0) acc_phase ^= 1;
       }
     }
-  } else {
+  } else if (warp < 2 + kEpiWarps) {
     // Epilogue warps 2..9: warp w may only touch TMEM lanes 32*(w%4) .. +31;
     // warps w and w+4 share a quadrant and split its columns in halves.
     const int q = warp & 3;
@@ -408,7 +624,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     for (int u = blockIdx.x; u < units; u += gridDim.x) {
       const int split = u / (m_tiles * n_tiles);
       const int t = u % (m_tiles * n_tiles);
-      const int mb = t % m_tiles, nb = t / m_tiles;
+      const int mb = remap_mblock<FUSE>(t % m_tiles, m_tiles, args, ctx), nb = t / m_tiles;
       bool ok = mbar_wait(tfull0 + 8 * acc, acc_phase, status);
       if (!__all_sync(0xffffffffu, ok)) break;
       tc_fence_after();
@@ -417,7 +633,15 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         a.out = reinterpret_cast<float*>(args.out) + static_cast<long long>(split) * args.split_stride;
       const int row = mb * kBM + row_in_tile;
       const uint32_t lane_addr = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + acc * BN;
-      if (a.tma_out) {
+      if (FUSE == kFuseRS) {
+#pragma unroll 1
+        for (int c = half * (BN / 64); c < (half + 1) * (BN / 64); ++c) {
+          float v[32];
+          tmem_ld_32(lane_addr + c * 32, v);
+          const int col0 = nb * BN + c * 32;
+          if (col0 < a.N) rs_store(a, ctx, row, col0, v);
+        }
+      } else if (a.tma_out) {
         // 64-column groups: TMEM -> registers -> epilogue math -> swizzled
         // staging box -> one TMA store per 32 x 64 block (rows/cols past the
         // matrix are clipped by the TMA unit).
@@ -469,15 +693,18 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       acc ^= 1;
       if (acc == 0) acc_phase ^= 1;
     }
+  } else if constexpr (FUSE == kFuseAG) {
+    gather_shards(args, ctx, threadIdx.x - kGemmThreads);
   }
 
-  if (warp >= 2 && lane == 0) bulk_wait_all();  // staging boxes fully drained before exit
+  if (warp >= 2 && warp < 2 + kEpiWarps && lane == 0) bulk_wait_all();  // staging boxes drained before exit
   tc_fence_before();
   __syncthreads();
   if (warp == 1) {
     tc_fence_after();
     tmem_dealloc(tmem_base, kTmemCols);
   }
+  if constexpr (FUSE == kFuseRS) rs_finish(args, ctx);
 }
 
 // Sum split-K fp32 partials into the final output (bf16 or fp32), optionally
@@ -557,18 +784,20 @@ int num_sms() {
   return n;
 }
 
-template <int BN, bool A_MN, bool B_MN, int STAGES>
+template <int BN, bool A_MN, bool B_MN, int STAGES, int FUSE = kFuseNone>
 void launch_gemm(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& mo, const CUtensorMap& mx,
-                 const GemmArgs& args, int units, cudaStream_t stream) {
+                 const GemmArgs& args, int units, cudaStream_t stream, const PeerCtx& ctx = PeerCtx{}) {
   using S = GemmSmem<BN, STAGES>;
-  auto kern = gemm_tcgen05_kernel<BN, A_MN, B_MN, STAGES>;
+  auto kern = gemm_tcgen05_kernel<BN, A_MN, B_MN, STAGES, FUSE>;
   static bool configured = false;
   if (!configured) {
     C10_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, S::total));
     configured = true;
   }
+  // Fused launches wait on one another across CTAs (and ranks): one CTA per
+  // SM at most, so every CTA of the grid is resident at once.
   const int grid = std::min(units, num_sms());
-  kern<<<grid, kGemmThreads, S::total, stream>>>(ma, mb, mo, mx, args);
+  kern<<<grid, gemm_threads<FUSE>(), S::total, stream>>>(ma, mb, mo, mx, args, ctx);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
@@ -684,6 +913,130 @@ void gemm(torch::Tensor a, torch::Tensor b, torch::Tensor out, bool a_mn, bool b
         (epi & kEpiAccum) ? 1 : 0);
     C10_CUDA_KERNEL_LAUNCH_CHECK();
   }
+}
+
+// Fused GEMM + collective (see the top of this file).  Called by the device
+// communicator, which fills `ctx` for this call.
+//   kFuseRS: a = X [M, K] (this rank's partial-sum input, all rows), b = W,
+//            out = [M / world, N] (this rank's rows), bias [N] and resid
+//            [M / world, N] are added once, after the reduction.
+//   kFuseAG: a = X shard [M / world, K], ag_buf = [M, K] gathered A (local
+//            scratch, also the caller's copy of the full input afterwards),
+//            ag_ready = int32 [world] zeroed here; epilogue as in gemm().
+void gemm_fused(int fuse, torch::Tensor a, torch::Tensor b, torch::Tensor out, bool b_mn,
+                c10::optional<torch::Tensor> bias, c10::optional<torch::Tensor> aux,
+                c10::optional<torch::Tensor> resid, int64_t epi, torch::Tensor status, const PeerCtx& ctx,
+                c10::optional<torch::Tensor> ag_buf, c10::optional<torch::Tensor> ag_ready) {
+  c10::cuda::CUDAGuard guard(a.device());
+  const int W = ctx.world;
+  TORCH_CHECK(fuse == kFuseRS || fuse == kFuseAG, "unknown fused mode");
+  const int64_t lda = row_stride(a, "A");
+  const int64_t ldb = row_stride(b, "B");
+  const int K = static_cast<int>(a.size(1));
+  const int N = static_cast<int>(b_mn ? b.size(1) : b.size(0));
+  TORCH_CHECK((b_mn ? b.size(0) : b.size(1)) == K, "A and B disagree on K");
+  TORCH_CHECK(N % 8 == 0 && K % 8 == 0, "N and K must be multiples of 8");
+  TORCH_CHECK(out.scalar_type() == at::kBFloat16 && out.stride(1) == 1 && (out.stride(0) % 8) == 0,
+              "fused output must be bf16 with 16-byte rows");
+  GemmArgs args{};
+  args.N = N;
+  args.K = K;
+  args.status = status.data_ptr<int>();
+  args.k_blocks_per_split = (K + kBK - 1) / kBK;
+  args.splits = 1;
+  args.out = out.data_ptr();
+  args.ldo = out.stride(0);
+  CUtensorMap ma, mo, mx;
+  const bool wide = N >= 256;
+  const int BN = wide ? 256 : 128;
+  if (fuse == kFuseRS) {
+    const int M = static_cast<int>(a.size(0));
+    TORCH_CHECK(M % W == 0, "rows must divide evenly across ranks");
+    TORCH_CHECK(out.size(0) == M / W && out.size(1) == N, "RS output must be [M / world, N]");
+    TORCH_CHECK(lda == K, "A must be contiguous");
+    args.M = M;
+    args.rows_per_rank = M / W;
+    if (bias) {
+      TORCH_CHECK(bias->scalar_type() == at::kBFloat16 && bias->numel() == N, "bias must be bf16 [N]");
+      args.bias = reinterpret_cast<const __nv_bfloat16*>(bias->data_ptr());
+    }
+    if (resid) {
+      TORCH_CHECK(resid->scalar_type() == at::kBFloat16 && resid->size(0) == M / W && resid->size(1) == N &&
+                      resid->stride(1) == 1 && resid->stride(0) % 8 == 0,
+                  "resid must be bf16 [M / world, N] with 16-byte rows");
+      args.resid = reinterpret_cast<const __nv_bfloat16*>(resid->data_ptr());
+      args.ldr = resid->stride(0);
+    }
+    args.epi = 0;
+    args.tma_out = 0;
+    ma = make_tma_2d_bf16(a.data_ptr(), K, M, lda, 64, kBM);
+    mo = mx = ma;
+  } else {
+    const int rows = static_cast<int>(a.size(0));
+    const int M = rows * W;
+    TORCH_CHECK(lda == K, "A shard must be contiguous");
+    TORCH_CHECK(ag_buf && ag_buf->scalar_type() == at::kBFloat16 && ag_buf->is_contiguous() &&
+                    ag_buf->size(0) == M && ag_buf->size(1) == K,
+                "ag_buf must be a contiguous bf16 [M, K]");
+    TORCH_CHECK(ag_ready && ag_ready->scalar_type() == at::kInt && ag_ready->numel() >= W, "ag_ready: int32 [W]");
+    TORCH_CHECK(out.size(0) == M && out.size(1) == N, "AG output must be [M, N]");
+    args.M = M;
+    args.rows_per_rank = rows;
+    args.ag_local = reinterpret_cast<const __nv_bfloat16*>(a.data_ptr());
+    args.ag_buf = reinterpret_cast<__nv_bfloat16*>(ag_buf->data_ptr());
+    args.ag_ready = ag_ready->data_ptr<int>();
+    args.epi = static_cast<int>(epi);
+    if (bias) {
+      TORCH_CHECK(bias->scalar_type() == at::kBFloat16 && bias->numel() == N, "bias must be bf16 [N]");
+      args.bias = reinterpret_cast<const __nv_bfloat16*>(bias->data_ptr());
+      args.epi |= kEpiBias;
+    }
+    if (aux) {
+      TORCH_CHECK(aux->scalar_type() == at::kBFloat16 && aux->stride(1) == 1, "aux must be bf16 row-major");
+      args.aux = reinterpret_cast<__nv_bfloat16*>(aux->data_ptr());
+      args.ldaux = aux->stride(0);
+    }
+    if (resid) {
+      TORCH_CHECK(resid->scalar_type() == at::kBFloat16 && resid->stride(1) == 1, "resid must be bf16 row-major");
+      args.resid = reinterpret_cast<const __nv_bfloat16*>(resid->data_ptr());
+      args.ldr = resid->stride(0);
+      args.epi |= kEpiResid;
+    }
+    TORCH_CHECK(!(args.epi & kEpiAccum), "AG-GEMM epilogues: bias, GELU, GELU', residual");
+    TORCH_CHECK(!(args.epi & (kEpiGelu | kEpiGeluGrad)) || aux.has_value(), "GELU epilogues need aux");
+    args.tma_out = 1;
+    C10_CUDA_CHECK(cudaMemsetAsync(args.ag_ready, 0, W * sizeof(int), at::cuda::getCurrentCUDAStream()));
+    ma = make_tma_2d_bf16(args.ag_buf, K, M, K, 64, kBM);
+    mo = make_tma_2d_bf16(out.data_ptr(), N, M, out.stride(0), 64, 32);
+    mx = (args.epi & kEpiGelu) ? make_tma_2d_bf16(aux->data_ptr(), N, M, args.ldaux, 64, 32) : mo;
+  }
+  CUtensorMap mb = b_mn ? make_tma_2d_bf16(b.data_ptr(), N, K, ldb, 64, 64)
+                        : make_tma_2d_bf16(b.data_ptr(), K, N, ldb, 64, BN);
+  const int units = ((args.M + kBM - 1) / kBM) * ((N + BN - 1) / BN);
+  cudaStream_t stream = at::cuda::getCurrentCUDAStream();
+  const bool gelu = (args.epi & kEpiGelu) != 0;
+#define MNB_FUSED(BNV, BMJ, ST, F)                                                   \
+  if (BN == BNV && b_mn == BMJ) {                                                   \
+    launch_gemm<BNV, false, BMJ, ST, F>(ma, mb, mo, mx, args, units, stream, ctx);   \
+    return;                                                                         \
+  }
+  if (fuse == kFuseRS) {
+    MNB_FUSED(256, false, 4, kFuseRS)
+    MNB_FUSED(256, true, 4, kFuseRS)
+    MNB_FUSED(128, false, 4, kFuseRS)
+    MNB_FUSED(128, true, 4, kFuseRS)
+  } else if (gelu) {
+    TORCH_CHECK(!b_mn, "the GELU epilogue is for the forward (K-major) layout");
+    MNB_FUSED(256, false, 3, kFuseAG)
+    MNB_FUSED(128, false, 3, kFuseAG)
+  } else {
+    MNB_FUSED(256, false, 4, kFuseAG)
+    MNB_FUSED(256, true, 4, kFuseAG)
+    MNB_FUSED(128, false, 4, kFuseAG)
+    MNB_FUSED(128, true, 4, kFuseAG)
+  }
+#undef MNB_FUSED
+  TORCH_CHECK(false, "unsupported fused GEMM configuration");
 }
 
 }  // namespace mnb

@@ -40,11 +40,14 @@ from .errors import CollectiveTimeoutError, DeviceCommError
 ONE_SHOT_MAX_BYTES = int(os.environ.get("MINI_NCCL_ONE_SHOT_MAX_BYTES", 512 << 10))
 #: Initial staging buffer per rank (grows on demand, collectively).
 STAGING_BYTES = int(os.environ.get("MINI_NCCL_STAGING_BYTES", 64 << 20))
-#: CTAs a collective may use (the device meaning of "channels").
-MAX_BLOCKS = int(os.environ.get("MINI_NCCL_DEVICE_BLOCKS", 32))
+#: CTAs a collective may use (the device meaning of "channels").  Bandwidth
+#: grows with CTAs up to about one per SM; fewer leave SMs to overlapped compute.
+MAX_BLOCKS = int(os.environ.get("MINI_NCCL_DEVICE_BLOCKS", 255))
 
 _OPS = {"sum": 0, "prod": 1, "max": 2, "min": 3}
-OPNAMES = ["all_reduce", "reduce_scatter", "all_gather", "broadcast", "all_to_all", "barrier", "all_reduce_stepped"]
+kMaxRanks = 16
+OPNAMES = ["all_reduce", "reduce_scatter", "all_gather", "broadcast", "all_to_all", "barrier", "all_reduce_stepped",
+           "gemm_reduce_scatter", "all_gather_gemm"]
 
 
 def _ext():
@@ -116,6 +119,7 @@ class DeviceComm:
         return torch.zeros(numel, dtype=dtype, device=self.device)
 
     def _ensure_staging(self, nbytes: int) -> None:
+        """Grow the staging buffer (collectively: every rank makes the same call)."""
         if nbytes <= self.staging_bytes:
             return
         torch.cuda.current_stream(self.device).synchronize()
@@ -177,6 +181,7 @@ class DeviceComm:
         algorithm: str = "auto",
         wire_dtype: torch.dtype | None = None,
         scale: float = 1.0,
+        blocks: int | None = None,
     ) -> torch.Tensor:
         if op not in _OPS:
             raise ValueError(f"unknown op {op!r}; expected one of {sorted(_OPS)}")
@@ -203,14 +208,13 @@ class DeviceComm:
         try:
             if algorithm in ("one_shot", "two_shot"):
                 wire_bf16 = wire_bf16 if tensor.dtype == torch.float32 else 0
-                step_bytes = tensor.numel() * (2 if wire_bf16 else tensor.element_size())
-                zero_copy = algorithm == "two_shot" and not wire_bf16 and self.impl.is_symmetric(tensor)
-                if not zero_copy:
-                    self._ensure_staging(step_bytes)
-                self.impl.all_reduce(tensor, tensor, _OPS[op], 1 if algorithm == "two_shot" else 0,
-                                     wire_bf16, float(scale), MAX_BLOCKS)
+                wsz = 2 if wire_bf16 else tensor.element_size()
+                kind = 1 if algorithm == "two_shot" else 0
+                self._ensure_staging(self.impl.staging_need(kind, tensor.numel(), wsz))
+                self.impl.all_reduce(tensor, tensor, _OPS[op], kind, wire_bf16, float(scale), blocks or MAX_BLOCKS)
             elif algorithm in ("ring", "tree", "halving", "naive"):
-                self._ensure_staging(tensor.numel() * max(4, tensor.element_size()))
+                narrow = tensor.dtype in (torch.bfloat16, torch.float16) and wire_bf16
+                self._ensure_staging(self.impl.staging_need(5, tensor.numel(), 4 if narrow else tensor.element_size()))
                 steps = self._schedule(algorithm, tensor.numel())
                 self.impl.stepped_all_reduce(tensor, tensor, steps, _OPS[op], wire_bf16, float(scale))
             else:
@@ -219,7 +223,8 @@ class DeviceComm:
             self._finish(ev)
         return tensor
 
-    def reduce_scatter(self, flat: torch.Tensor, op: str = "sum", scale: float = 1.0) -> torch.Tensor:
+    def reduce_scatter(self, flat: torch.Tensor, op: str = "sum", scale: float = 1.0,
+                       blocks: int | None = None) -> torch.Tensor:
         W = self.world_size
         if flat.numel() % W:
             raise ValueError(f"numel {flat.numel()} not divisible by world_size {W}")
@@ -228,16 +233,16 @@ class DeviceComm:
             out.copy_(flat)
             return out.mul_(scale) if scale != 1.0 else out
         nbytes = flat.numel() * flat.element_size()
-        if not self.impl.is_symmetric(flat):
-            self._ensure_staging(nbytes)
+        self._ensure_staging(self.impl.staging_need(2, flat.numel(), flat.element_size()))
         ev = self._record("reduce_scatter", "direct", nbytes, op=op)
         try:
-            self.impl.reduce_scatter(flat, out, _OPS[op], float(scale), min(MAX_BLOCKS, 512 // W))
+            self.impl.reduce_scatter(flat, out, _OPS[op], float(scale), blocks or MAX_BLOCKS)
         finally:
             self._finish(ev)
         return out
 
-    def all_gather(self, shard: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
+    def all_gather(self, shard: torch.Tensor, out: torch.Tensor | None = None,
+                   blocks: int | None = None) -> torch.Tensor:
         W = self.world_size
         if out is None:
             out = torch.empty((W, shard.numel()), dtype=shard.dtype, device=shard.device)
@@ -245,11 +250,10 @@ class DeviceComm:
             out.view(-1).copy_(shard.reshape(-1))
             return out
         nbytes = shard.numel() * shard.element_size()
-        if not self.impl.is_symmetric(shard):
-            self._ensure_staging(nbytes)
+        self._ensure_staging(self.impl.staging_need(3, nbytes, 1))
         ev = self._record("all_gather", "direct", nbytes)
         try:
-            self.impl.move(shard.contiguous(), out, 0, 0, min(MAX_BLOCKS, 512 // W))
+            self.impl.move(shard.contiguous(), out, 0, 0, blocks or MAX_BLOCKS)
         finally:
             self._finish(ev)
         return out
@@ -258,11 +262,10 @@ class DeviceComm:
         if self.world_size == 1:
             return tensor
         nbytes = tensor.numel() * tensor.element_size()
-        if not self.impl.is_symmetric(tensor):
-            self._ensure_staging(nbytes)
+        self._ensure_staging(self.impl.staging_need(4, nbytes, 1))
         ev = self._record("broadcast", "direct", nbytes, root=src)
         try:
-            self.impl.move(tensor, tensor, 1, int(src), min(MAX_BLOCKS, 512 // self.world_size))
+            self.impl.move(tensor, tensor, 1, int(src), MAX_BLOCKS)
         finally:
             self._finish(ev)
         return tensor
@@ -273,11 +276,10 @@ class DeviceComm:
         if W == 1:
             return out.copy_(flat)
         nbytes = flat.numel() * flat.element_size()
-        if not self.impl.is_symmetric(flat):
-            self._ensure_staging(nbytes)
+        self._ensure_staging(self.impl.staging_need(3, nbytes // W, 1))
         ev = self._record("all_to_all", "direct", nbytes)
         try:
-            self.impl.move(flat, out, 2, 0, min(MAX_BLOCKS, 512 // W))
+            self.impl.move(flat, out, 2, 0, MAX_BLOCKS)
         finally:
             self._finish(ev)
         return out
@@ -302,6 +304,85 @@ class DeviceComm:
             t.copy_(flat[at : at + n].view_as(t))
             at += n
         return flat.numel() * flat.element_size()
+
+    # ---- GEMMs fused with a collective (tensor parallelism, sequence-parallel layout) ---
+
+    def gemm_reduce_scatter(self, x: torch.Tensor, w: torch.Tensor, *, w_mn: bool = False,
+                            bias: torch.Tensor | None = None, resid: torch.Tensor | None = None) -> torch.Tensor:
+        """``reduce_scatter_rows(x @ w^T) + bias + resid`` as one kernel.
+
+        ``x`` [M, K] holds this rank's partial-sum input for all M rows (the
+        row-parallel layer's local K slice); ``w`` is [N, K] (or [K, N] with
+        ``w_mn``).  Returns this rank's [M / W, N] rows of the sum over ranks,
+        with ``bias`` [N] and ``resid`` [M / W, N] added once.  The GEMM's
+        epilogue stores each finished tile into its owner's memory, so the
+        transfer overlaps the remaining MMAs (replaces the reference's
+        forward all-reduce in ``tensor_parallel.py:74-91`` with the
+        sequence-parallel reduce-scatter).
+        """
+        from .ops import kernels as K
+
+        W = self.world_size
+        M = x.shape[0]
+        N = w.shape[1] if w_mn else w.shape[0]
+        if M % W:
+            raise ValueError(f"rows {M} not divisible by world_size {W}")
+        if W == 1:
+            return K.gemm(x, w, b_mn=w_mn, bias=bias, resid=resid)
+        self._ensure_staging(2 * M * N * 2)
+        out = torch.empty(M // W, N, dtype=torch.bfloat16, device=x.device)
+        ev = self._record("gemm_reduce_scatter", "fused", M * N * 2)
+        try:
+            self.impl.gemm_rs(x.contiguous(), w, out, w_mn, bias, resid, K.status_word(x.device))
+        finally:
+            self._finish(ev)
+        return out
+
+    def all_gather_gemm(self, x_shard: torch.Tensor, w: torch.Tensor, *, w_mn: bool = False,
+                        bias: torch.Tensor | None = None, gelu_out_aux: torch.Tensor | None = None,
+                        gelu_grad_aux: torch.Tensor | None = None, resid: torch.Tensor | None = None,
+                        gathered: torch.Tensor | None = None) -> tuple[torch.Tensor, torch.Tensor]:
+        """``epi(all_gather_rows(x_shard) @ w^T)`` as one kernel; returns (out, gathered).
+
+        ``x_shard`` [M / W, K] is this rank's rows.  Gather warps inside the
+        GEMM copy every shard into ``gathered`` [M, K] (local memory; each
+        remote row crosses NVLink once) while the tiles of the local shard
+        compute; ``gathered`` is returned for reuse (the weight gradient needs
+        the full input).  With ``gelu_out_aux`` the epilogue is
+        ``out = gelu(acc + bias)``, ``aux = acc + bias``; with
+        ``gelu_grad_aux`` it is ``out = acc * gelu'(aux)`` (an MLP backward).
+        """
+        from .ops import kernels as K
+
+        W = self.world_size
+        rows, Kd = x_shard.shape
+        N = w.shape[1] if w_mn else w.shape[0]
+        if W == 1:
+            out = K.gemm(x_shard, w, b_mn=w_mn, bias=bias, gelu_out_aux=gelu_out_aux, gelu_grad_aux=gelu_grad_aux,
+                         resid=resid)
+            return out, x_shard
+        if gathered is None:
+            gathered = torch.empty(rows * W, Kd, dtype=torch.bfloat16, device=x_shard.device)
+        ready = self._ag_ready()
+        self._ensure_staging(2 * rows * Kd * 2)
+        out = torch.empty(rows * W, N, dtype=torch.bfloat16, device=x_shard.device)
+        if gelu_out_aux is not None and gelu_grad_aux is not None:
+            raise ValueError("gelu_out_aux and gelu_grad_aux are exclusive")
+        epi, aux = (2, gelu_out_aux) if gelu_out_aux is not None else ((8, gelu_grad_aux) if gelu_grad_aux is not None
+                                                                      else (0, None))
+        ev = self._record("all_gather_gemm", "fused", rows * Kd * 2)
+        try:
+            self.impl.ag_gemm(x_shard.contiguous(), w, out, gathered, ready, w_mn, bias, aux, resid, epi,
+                              K.status_word(x_shard.device))
+        finally:
+            self._finish(ev)
+        return out, gathered
+
+    def _ag_ready(self) -> torch.Tensor:
+        buf = getattr(self, "_ready_buf", None)
+        if buf is None:
+            buf = self._ready_buf = torch.zeros(kMaxRanks, dtype=torch.int32, device=self.device)
+        return buf
 
     # ---- parity schedules -------------------------------------------------------------
 
@@ -408,3 +489,239 @@ def _owned_after_halving(W: int, rank: int, n: int, stop_mask: int) -> tuple[int
     # Doubling below stop_mask has already widened the range back up to the
     # block covered at level stop_mask, which is exactly (lo, hi) above.
     return lo, hi
+
+
+# ====================================================================================
+# Host-staged path: GPU tensors between ranks that share no peer memory
+# ====================================================================================
+#
+# The entry points the reference offers for device tensors (mini_nccl/device.py:
+# 57-320: is_accelerated, Staging, all_reduce_staged, all_reduce_pipelined,
+# device_report).  On one NVSwitch box the peer-memory kernels above replace
+# them; across hosts (MINI_NCCL_HOSTS naming several machines) a GPU tensor
+# still has to cross a socket, and these functions move it through pinned host
+# memory with the copies overlapped against the wire.
+
+#: Bytes per staged chunk.
+DEFAULT_CHUNK_BYTES = 4 << 20
+
+
+def is_accelerated(tensor: torch.Tensor) -> bool:
+    """True for tensors on a CUDA device."""
+    return tensor.device.type == "cuda"
+
+
+class _Window:
+    """One pinned host window: an outbound and an inbound buffer and their events."""
+
+    __slots__ = ("out", "inp", "down", "up", "uploading")
+
+    def __init__(self, numel: int, dtype: torch.dtype, pinned: bool) -> None:
+        self.out = torch.empty(numel, dtype=dtype, pin_memory=pinned)
+        self.inp = torch.empty(numel, dtype=dtype, pin_memory=pinned)
+        self.down = torch.cuda.Event() if pinned else None
+        self.up = torch.cuda.Event() if pinned else None
+        self.uploading = False
+
+
+class Staging:
+    """Pinned host windows plus a copy stream, reused by every step of a collective.
+
+    A payload of ``numel`` elements is cut into ``n_chunks`` chunks of at most
+    ``chunk_bytes``; ``n_slots`` windows let the download of chunk k+1 run on
+    the copy engine while chunk k is on the wire.  On CPU tensors the windows
+    are ordinary memory and every copy is synchronous, so the same chunking
+    logic runs (and is tested) without a GPU.
+    """
+
+    def __init__(self, numel: int, dtype: torch.dtype, device: torch.device,
+                 chunk_bytes: int = DEFAULT_CHUNK_BYTES, n_slots: int = 2) -> None:
+        self.device = torch.device(device)
+        self.accelerated = self.device.type == "cuda"
+        itemsize = torch.empty(0, dtype=dtype).element_size()
+        self.chunk_numel = max(1, min(max(1, numel), chunk_bytes // itemsize))
+        self.n_chunks = max(1, -(-numel // self.chunk_numel))
+        self.stream = torch.cuda.Stream(self.device) if self.accelerated else None
+        self.slots = [_Window(self.chunk_numel, dtype, self.accelerated)
+                      for _ in range(max(1, min(n_slots, self.n_chunks)))]
+        #: How many times the copy stream was ordered behind the compute stream
+        #: (one per exchange; tests read it to check the dependency is expressed).
+        self.orderings = 0
+
+    def ranges(self, numel: int) -> list[tuple[int, int]]:
+        return [(lo, min(numel, lo + self.chunk_numel)) for lo in range(0, numel, self.chunk_numel)]
+
+    def order_after_compute(self) -> None:
+        """Copy stream waits for everything already queued on the compute stream.
+
+        Each exchange reads a block that the compute stream produced (the
+        caller's data or the previous ring step's reduction); without this
+        wait the download can read it before the reduction lands.
+        """
+        self.orderings += 1
+        if self.accelerated:
+            self.stream.wait_stream(torch.cuda.current_stream(self.device))
+
+    def download(self, w: _Window, src: torch.Tensor) -> None:
+        dst = w.out[: src.numel()]
+        if not self.accelerated:
+            dst.copy_(src)
+            return
+        with torch.cuda.stream(self.stream):
+            dst.copy_(src, non_blocking=True)
+        w.down.record(self.stream)
+
+    def wait_download(self, w: _Window) -> None:
+        if self.accelerated:
+            w.down.synchronize()
+
+    def upload(self, w: _Window, dst: torch.Tensor) -> None:
+        src = w.inp[: dst.numel()]
+        if not self.accelerated:
+            dst.copy_(src)
+            return
+        with torch.cuda.stream(self.stream):
+            dst.copy_(src, non_blocking=True)
+        w.up.record(self.stream)
+        w.uploading = True
+
+    def wait_upload(self, w: _Window) -> None:
+        if self.accelerated and w.uploading:
+            w.up.synchronize()
+            w.uploading = False
+
+    def order_compute_after_uploads(self) -> None:
+        """Compute stream waits for the uploads in flight (the CPU does not block)."""
+        if self.accelerated:
+            cur = torch.cuda.current_stream(self.device)
+            for w in self.slots:
+                if w.uploading:
+                    cur.wait_event(w.up)
+
+
+def staged_exchange(pg, send: torch.Tensor, recv: torch.Tensor, dst: int, src: int, staging: Staging) -> None:
+    """Send ``send`` to ``dst`` while receiving ``recv`` from ``src``, chunk by chunk.
+
+    Downloads run ``len(staging.slots) - 1`` chunks ahead of the wire, so the
+    copy engine and the socket work at the same time.  Chunk k uses window
+    ``k % n_slots``; a window's inbound half is reused only after its upload
+    finished.
+    """
+    spans = staging.ranges(send.numel())
+    wins = staging.slots
+    depth = len(wins)
+    staging.order_after_compute()
+    for k in range(min(depth, len(spans))):
+        lo, hi = spans[k]
+        staging.download(wins[k], send[lo:hi])
+    for k, (lo, hi) in enumerate(spans):
+        w = wins[k % depth]
+        staging.wait_download(w)
+        staging.wait_upload(w)
+        n = hi - lo
+        # send_recv returns once w.out is on the wire and w.inp is full, so
+        # w.out can take the next download right after it.
+        pg.send_recv(w.out[:n], dst, w.inp[:n], src)
+        staging.upload(w, recv[lo:hi])
+        nxt = k + depth
+        if nxt < len(spans):
+            nlo, nhi = spans[nxt]
+            staging.download(w, send[nlo:nhi])
+    staging.order_compute_after_uploads()
+
+
+_PINNED: dict[tuple, torch.Tensor] = {}
+
+
+def _pinned(numel: int, dtype: torch.dtype) -> torch.Tensor:
+    """A cached pinned host buffer (page-locking is slow; reuse it across calls)."""
+    key = (numel, dtype)
+    buf = _PINNED.get(key)
+    if buf is None:
+        if len(_PINNED) > 8:
+            _PINNED.clear()
+        buf = _PINNED[key] = torch.empty(numel, dtype=dtype, pin_memory=True)
+    return buf
+
+
+def all_reduce_staged(pg, tensor: torch.Tensor, op: str = "sum", algorithm: str = "auto",
+                      wire_dtype: torch.dtype | None = None) -> torch.Tensor:
+    """All-reduce a GPU tensor through pinned host memory and the host collectives.
+
+    The whole tensor goes down, the CPU algorithm (``algorithm``, channels,
+    narrow wire) runs on the host copy, and the result goes back up.  CPU
+    tensors go straight to the host collectives.
+    """
+    if not is_accelerated(tensor):
+        return _hostc.all_reduce(pg, tensor, op=op, algorithm=algorithm, wire_dtype=wire_dtype)
+    if not tensor.is_contiguous():
+        raise ValueError("all_reduce_staged requires a contiguous tensor")
+    flat = tensor.view(-1)
+    host = _pinned(flat.numel(), flat.dtype)
+    host.copy_(flat, non_blocking=True)
+    torch.cuda.current_stream(tensor.device).synchronize()
+    _hostc.all_reduce(pg, host, op=op, algorithm=algorithm, wire_dtype=wire_dtype)
+    flat.copy_(host, non_blocking=True)
+    torch.cuda.current_stream(tensor.device).synchronize()  # the host buffer is reused by the next call
+    return tensor
+
+
+def all_reduce_pipelined(pg, tensor: torch.Tensor, op: str = "sum",
+                         chunk_bytes: int = DEFAULT_CHUNK_BYTES) -> torch.Tensor:
+    """Ring all-reduce whose arithmetic stays on the device; only transfers are staged.
+
+    2(W-1) ring steps; each moves one block through :func:`staged_exchange`
+    and (in the reduce-scatter half) folds the received block into ours on
+    the tensor's own device.
+    """
+    _hostc._check_op(op)
+    if not tensor.is_contiguous():
+        raise ValueError("all_reduce_pipelined requires a contiguous tensor")
+    W, r = pg.world_size, pg.rank
+    if W == 1:
+        return tensor
+    flat = tensor.view(-1)
+    padded, blocks = _hostc._padded_blocks(flat, W)
+    chunk = blocks.shape[1]
+    staging = Staging(chunk, flat.dtype, flat.device, chunk_bytes=chunk_bytes)
+    inbox = torch.empty(chunk, dtype=flat.dtype, device=flat.device)
+    fold = _hostc._OPS[op]
+    right, left = (r + 1) % W, (r - 1) % W
+    rec = getattr(pg, "recorder", None)
+    ev = rec.start("all_reduce_pipelined", "ring", channel=-1, nbytes=flat.numel() * flat.element_size(),
+                   op=op, chunks=staging.n_chunks) if rec is not None else None
+    try:
+        for s in range(W - 1):  # reduce-scatter: block (r-s-1) accumulates
+            staged_exchange(pg, blocks[(r - s) % W], inbox, right, left, staging)
+            fold(blocks[(r - s - 1) % W], inbox)
+        for s in range(W - 1):  # all-gather: finished blocks travel around
+            staged_exchange(pg, blocks[(r + 1 - s) % W], blocks[(r - s) % W], right, left, staging)
+        if padded.data_ptr() != flat.data_ptr():
+            flat.copy_(padded[: flat.numel()])
+        if staging.accelerated:
+            torch.cuda.current_stream(flat.device).synchronize()
+    finally:
+        if rec is not None:
+            rec.finish(ev)
+    return tensor
+
+
+def device_report() -> dict[str, object]:
+    """What this machine can run: torch/CUDA versions, devices, peer access, our extension."""
+    rep: dict[str, object] = {"torch": torch.__version__, "cuda_built": torch.version.cuda,
+                              "cuda_available": torch.cuda.is_available()}
+    try:
+        from ._build import cuda_lib_path
+
+        rep["extension_built"] = cuda_lib_path().exists()
+    except Exception:  # noqa: BLE001 - a report never raises
+        rep["extension_built"] = False
+    if not torch.cuda.is_available():
+        return rep
+    n = torch.cuda.device_count()
+    props = torch.cuda.get_device_properties(0)
+    rep.update(device_name=props.name, device_count=n, compute_capability=f"{props.major}.{props.minor}",
+               sm_count=props.multi_processor_count, total_memory_gib=round(props.total_memory / 2**30, 2),
+               sm100a=(props.major, props.minor) == (10, 0))
+    rep["peer_access"] = [[i == j or torch.cuda.can_device_access_peer(i, j) for j in range(n)] for i in range(n)]
+    return rep

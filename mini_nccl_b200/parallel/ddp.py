@@ -25,6 +25,7 @@ Two engines:
 
 from __future__ import annotations
 
+import os
 import threading
 import time
 from concurrent.futures import Future, ThreadPoolExecutor
@@ -35,6 +36,10 @@ from torch import nn
 
 from .. import collectives
 from ..communicator import Communicator
+
+#: CTAs a bucket all-reduce may use while backward runs beside it (0: the
+#: device communicator's default).
+DDP_COMM_BLOCKS = int(os.environ.get("MINI_NCCL_DDP_BLOCKS", "0"))
 
 
 def average_gradients(pg: Communicator, params, algorithm: str = "ring") -> int:
@@ -218,7 +223,8 @@ class DistributedDataParallel(nn.Module):
             with torch.cuda.stream(self._comm_stream):
                 self._comm_stream.wait_event(produced)
                 self._dc.all_reduce(
-                    bucket.buffer, op="sum", algorithm="auto", scale=1.0 / self.pg.world_size
+                    bucket.buffer, op="sum", algorithm="auto", scale=1.0 / self.pg.world_size,
+                    blocks=DDP_COMM_BLOCKS or None,
                 )
                 done = torch.cuda.Event()
                 done.record(self._comm_stream)

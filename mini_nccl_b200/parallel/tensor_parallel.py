@@ -19,7 +19,13 @@ an all-gather of the token shards before the column GEMM and ``g`` becomes a
 reduce-scatter after the row GEMM (Megatron-SP).  Same FLOPs, half the
 activation traffic of the all-reduce pair, and LayerNorm/residual work is done
 once per token instead of once per rank.  On CUDA these boundaries run as
-the fused peer-memory kernels in :mod:`mini_nccl_b200.ops.fused_tp`.
+the fused peer-memory kernels in :mod:`mini_nccl_b200.ops.fused_tp` (one
+kernel per GEMM + collective pair).  Parameters that see only this rank's
+tokens under sequence parallelism (the row-parallel bias, LayerNorms inside
+the region) get partial gradients: :func:`allreduce_sequence_parallel_grads`
+sums them over the group after backward.  :func:`scatter_to_sequence_parallel`
+and :func:`gather_from_sequence_parallel` enter and leave the region from
+replicated compute (embeddings, the head).
 """
 
 from __future__ import annotations
@@ -31,6 +37,7 @@ from torch import nn
 from .. import collectives
 from ..communicator import Communicator
 from ..ops import functional as OF
+from ..ops import fused_tp as FT
 
 
 class _CopyToGroup(torch.autograd.Function):
@@ -133,6 +140,104 @@ class _ScatterTokens(torch.autograd.Function):
         return None, out
 
 
+class _SplitTokens(torch.autograd.Function):
+    """Enter the sequence-parallel region from replicated compute.
+
+    Forward keeps this rank's run of tokens (dim 0); backward all-gathers the
+    gradient, so replicated producers (embeddings) see every token's gradient.
+    """
+
+    @staticmethod
+    def forward(ctx, pg: Communicator, x: torch.Tensor):
+        ctx.pg = pg
+        W, r = pg.world_size, pg.rank
+        if W == 1:
+            return x
+        if x.shape[0] % W:
+            raise ValueError("sequence parallelism needs tokens divisible by the group size")
+        per = x.shape[0] // W
+        return x[r * per : (r + 1) * per].contiguous()
+
+    @staticmethod
+    def backward(ctx, grad: torch.Tensor):
+        pg = ctx.pg
+        if pg.world_size == 1:
+            return None, grad
+        g = grad.contiguous()
+        out = torch.empty((pg.world_size * g.shape[0], *g.shape[1:]), dtype=g.dtype, device=g.device)
+        collectives.all_gather_into(pg, out.view(-1), g)
+        return None, out
+
+
+class _JoinTokens(torch.autograd.Function):
+    """Leave the sequence-parallel region into replicated compute.
+
+    Forward all-gathers the token shards; the consumer runs identically on
+    every rank, so backward just keeps this rank's slice of the gradient.
+    """
+
+    @staticmethod
+    def forward(ctx, pg: Communicator, x: torch.Tensor):
+        ctx.pg = pg
+        if pg.world_size == 1:
+            return x
+        x = x.contiguous()
+        out = torch.empty((pg.world_size * x.shape[0], *x.shape[1:]), dtype=x.dtype, device=x.device)
+        collectives.all_gather_into(pg, out.view(-1), x)
+        ctx.per = x.shape[0]
+        return out
+
+    @staticmethod
+    def backward(ctx, grad: torch.Tensor):
+        pg = ctx.pg
+        if pg.world_size == 1:
+            return None, grad
+        r, per = pg.rank, ctx.per
+        return None, grad[r * per : (r + 1) * per].contiguous()
+
+
+def scatter_to_sequence_parallel(pg: Communicator, x: torch.Tensor) -> torch.Tensor:
+    """This rank's tokens (dim 0, sequence-major) of a replicated activation."""
+    return _SplitTokens.apply(pg, x)
+
+
+def gather_from_sequence_parallel(pg: Communicator, x: torch.Tensor) -> torch.Tensor:
+    """Every rank's tokens (dim 0) for replicated compute after the region."""
+    return _JoinTokens.apply(pg, x)
+
+
+def mark_sequence_parallel(*modules: nn.Module) -> None:
+    """Tag the parameters of replicated modules that run inside the region."""
+    for m in modules:
+        for p in m.parameters():
+            p.sequence_parallel = True
+
+
+def allreduce_sequence_parallel_grads(module: nn.Module, pg: Communicator) -> int:
+    """Sum, over the group, the gradients of parameters tagged ``sequence_parallel``.
+
+    Under sequence parallelism each rank's gradient of a replicated parameter
+    inside the region covers only its own tokens; the full gradient is the
+    sum.  One all-reduce over the concatenated gradients; returns its bytes.
+    """
+    grads = [p.grad for p in module.parameters() if getattr(p, "sequence_parallel", False) and p.grad is not None]
+    if pg.world_size == 1 or not grads:
+        return 0
+    by_dtype: dict[torch.dtype, list[torch.Tensor]] = {}
+    for g in grads:
+        by_dtype.setdefault(g.dtype, []).append(g)
+    total = 0
+    for group in by_dtype.values():
+        flat = torch.cat([g.reshape(-1) for g in group])
+        collectives.all_reduce(pg, flat)
+        at = 0
+        for g in group:
+            g.copy_(flat[at : at + g.numel()].view_as(g))
+            at += g.numel()
+        total += flat.numel() * flat.element_size()
+    return total
+
+
 def _shard_size(total: int, world_size: int, rank: int) -> tuple[int, int]:
     """(start, size) of an even split with the remainder on the leading ranks."""
     q, extra = divmod(total, world_size)
@@ -172,6 +277,11 @@ class ColumnParallelLinear(nn.Module):
         nn.init.normal_(self.weight, std=0.02)
 
     def forward(self, x: torch.Tensor) -> torch.Tensor:
+        if self.sequence_parallel and not self.gather_output:
+            dc = FT.usable(self.pg, x, self.weight)
+            if dc is not None:  # one kernel: gather the token shards inside the GEMM
+                y2 = FT.AllGatherLinear.apply(dc, x.reshape(-1, x.shape[-1]), self.weight, self.bias)
+                return y2.view(self.pg.world_size * x.shape[0], *x.shape[1:-1], self.shard_size)
         if self.sequence_parallel:
             x = _GatherTokens.apply(self.pg, x)
         else:
@@ -222,11 +332,22 @@ class RowParallelLinear(nn.Module):
         kw = {"device": device, "dtype": dtype}
         self.weight = nn.Parameter(torch.empty(out_features, self.shard_size, **kw))
         self.bias = nn.Parameter(torch.zeros(out_features, **kw)) if bias else None
+        if self.bias is not None and sequence_parallel:
+            self.bias.sequence_parallel = True  # added to this rank's tokens only
         nn.init.normal_(self.weight, std=0.02)
 
-    def forward(self, x: torch.Tensor) -> torch.Tensor:
+    def forward(self, x: torch.Tensor, residual: torch.Tensor | None = None) -> torch.Tensor:
+        """``x W^T + b`` reduced over the group (+ ``residual``, same shape as the output)."""
         if not self.input_is_sharded:
             x = x[..., self.shard_start : self.shard_start + self.shard_size]
+        if self.sequence_parallel:
+            dc = FT.usable(self.pg, x, self.weight)
+            if dc is not None and (residual is None or residual.dtype == torch.bfloat16):
+                # one kernel: tiles go to the ranks owning their tokens, bias and residual added once
+                lead = x.shape[:-1]
+                r2 = residual.reshape(-1, self.out_features) if residual is not None else None
+                y2 = FT.LinearReduceScatter.apply(dc, x.reshape(-1, x.shape[-1]), self.weight, self.bias, r2)
+                return y2.view(lead[0] // self.pg.world_size, *lead[1:], self.out_features)
         partial = OF.linear(x, self.weight, None)
         if self.sequence_parallel:
             y = _ScatterTokens.apply(self.pg, partial)
@@ -234,7 +355,7 @@ class RowParallelLinear(nn.Module):
             y = _ReduceFromGroup.apply(self.pg, partial)
         if self.bias is not None:
             y = y + self.bias
-        return y
+        return y if residual is None else residual + y
 
     @torch.no_grad()
     def load_full_weight(self, weight: torch.Tensor, bias: torch.Tensor | None = None) -> None:
@@ -255,8 +376,16 @@ class ParallelMLP(nn.Module):
         self.up = ColumnParallelLinear(width, expansion * width, pg, sequence_parallel=sequence_parallel, **kw)
         self.down = RowParallelLinear(expansion * width, width, pg, sequence_parallel=sequence_parallel, **kw)
 
-    def forward(self, x: torch.Tensor) -> torch.Tensor:
-        return self.down(OF.gelu(self.up(x)))
+    def forward(self, x: torch.Tensor, residual: torch.Tensor | None = None) -> torch.Tensor:
+        if self.up.sequence_parallel and self.down.sequence_parallel:
+            dc = FT.usable(self.up.pg, x, self.up.weight, self.down.weight)
+            if dc is not None and (residual is None or residual.dtype == torch.bfloat16):
+                # AG->GEMM+GELU and GEMM->RS(+bias+residual): two kernels forward, two backward
+                r2 = residual.reshape(-1, x.shape[-1]) if residual is not None else None
+                y2 = FT.ParallelMLPFused.apply(dc, x.reshape(-1, x.shape[-1]), self.up.weight, self.up.bias,
+                                               self.down.weight, self.down.bias, r2)
+                return y2.view(x.shape)
+        return self.down(OF.gelu(self.up(x)), residual=residual)
 
 
 def _qkv_shard_rows(width: int, n_head: int, head_dim: int, pg: Communicator) -> torch.Tensor:
@@ -292,15 +421,15 @@ class ParallelSelfAttention(nn.Module):
         )
         self.proj = RowParallelLinear(width, width, pg, sequence_parallel=sequence_parallel, **kw)
 
-    def forward(self, x: torch.Tensor) -> torch.Tensor:
+    def forward(self, x: torch.Tensor, residual: torch.Tensor | None = None) -> torch.Tensor:
         qkv = self.qkv(x)
         if self.sequence_parallel:
             # Sequence-parallel activations are sequence-major, [T, B, C]: the
             # token gather concatenates along T, attention wants [B, T, C].
-            y = self._attend(qkv.transpose(0, 1)).transpose(0, 1).contiguous()
+            y = self._attend(qkv.transpose(0, 1).contiguous()).transpose(0, 1).contiguous()
         else:
             y = self._attend(qkv)
-        return self.proj(y)
+        return self.proj(y, residual=residual)
 
     def _attend(self, qkv: torch.Tensor) -> torch.Tensor:
         B, T, _ = qkv.shape
@@ -315,4 +444,8 @@ __all__ = [
     "RowParallelLinear",
     "_qkv_shard_rows",
     "_shard_size",
+    "allreduce_sequence_parallel_grads",
+    "gather_from_sequence_parallel",
+    "mark_sequence_parallel",
+    "scatter_to_sequence_parallel",
 ]

@@ -33,6 +33,8 @@ KERNELS_PER_CALL = {
     "move": 1,
     "barrier": 1,
     "stepped_all_reduce": 1,
+    "gemm_rs": 1,
+    "ag_gemm": 1,
 }
 
 

@@ -180,3 +180,96 @@ def test_device_wait_times_out_without_hanging(monkeypatch):
     monkeypatch.setenv("NCCL_NVLS_ENABLE", "0")
     results = run(_timeout, 2, devices="cuda", timeout=300.0, op_timeout=60.0)
     assert results[0] == "timeout", results
+
+
+def _host_staged(pg) -> None:
+    from mini_nccl_b200 import device as D
+
+    dev = torch.device("cuda", torch.cuda.current_device())
+    W, r = pg.world_size, pg.rank
+    for fn in (lambda t: D.all_reduce_staged(pg, t), lambda t: D.all_reduce_pipelined(pg, t, chunk_bytes=1 << 16)):
+        calls = []
+        orig = torch.cuda.Stream.wait_stream
+
+        def spy(self, other):
+            calls.append(1)
+            return orig(self, other)
+
+        torch.cuda.Stream.wait_stream = spy
+        try:
+            t = torch.full((300_001,), float(r + 1), device=dev)
+            fn(t)
+        finally:
+            torch.cuda.Stream.wait_stream = orig
+        torch.cuda.synchronize()
+        assert torch.equal(t, torch.full_like(t, W * (W + 1) / 2))
+    # the pipelined ring ordered its copy stream behind compute on every exchange
+    assert len(calls) >= 2 * (W - 1)
+
+
+@needs2
+def test_host_staged_paths_on_gpus():
+    run(_host_staged, 2, timeout=300.0, devices="cuda")
+
+
+def _fused_tp(pg) -> None:
+    """GEMM->reduce-scatter and all-gather->GEMM kernels against fp32 torch."""
+    from mini_nccl_b200.ops import kernels as K
+
+    dev = torch.device("cuda", torch.cuda.current_device())
+    W, r = pg.world_size, pg.rank
+    dc = pg.device_comm()
+
+    def rnd(seed, *shape, scale=1.0):
+        g = torch.Generator().manual_seed(seed)
+        return (torch.randn(*shape, generator=g) * scale).to(torch.bfloat16).to(dev)
+
+    for M, Kd, N in ((2 * 200, 384, 640), (4096, 1024, 1536)):
+        # row-parallel: partial sums on every rank, this rank keeps its rows
+        for w_mn in (False, True):
+            xs = [rnd(100 + q, M, Kd, scale=0.5) for q in range(W)]
+            ws = [rnd(200 + q, N, Kd, scale=0.05) for q in range(W)]
+            bias = rnd(300, N)
+            rows = M // W
+            resid = rnd(400 + r, rows, N)
+            w_arg = ws[r].t().contiguous() if w_mn else ws[r]
+            out = dc.gemm_reduce_scatter(xs[r], w_arg, w_mn=w_mn, bias=bias, resid=resid)
+            dc.synchronize()
+            K.check_status(dev)
+            full = sum(xs[q].float() @ ws[q].float().t() for q in range(W))
+            want = full[r * rows:(r + 1) * rows] + bias.float() + resid.float()
+            err = (out.float() - want).abs().max().item()
+            assert err <= 0.02 * want.abs().max().item() + 0.05, ("rs", M, Kd, N, w_mn, err)
+        # column-parallel: gather the rows, multiply by this rank's weight slice
+        for w_mn, gelu in ((False, False), (False, True), (True, False)):
+            shards = [rnd(500 + q, M // W, Kd, scale=0.5) for q in range(W)]
+            w = rnd(600 + r, N, Kd, scale=0.05)
+            bias = rnd(700 + r, N)
+            aux = torch.empty(M, N, dtype=torch.bfloat16, device=dev) if gelu else None
+            out, gathered = dc.all_gather_gemm(shards[r], w.t().contiguous() if w_mn else w, w_mn=w_mn,
+                                               bias=bias, gelu_out_aux=aux)
+            dc.synchronize()
+            K.check_status(dev)
+            xfull = torch.cat(shards)
+            assert torch.equal(gathered, xfull)
+            pre = xfull.float() @ w.float().t() + bias.float()
+            want = torch.nn.functional.gelu(pre) if gelu else pre
+            err = (out.float() - want).abs().max().item()
+            assert err <= 0.02 * want.abs().max().item() + 0.05, ("ag", M, Kd, N, w_mn, gelu, err)
+            if gelu:
+                assert (aux.float() - pre).abs().max().item() <= 0.02 * pre.abs().max().item() + 0.05
+    # many calls in a row (parity halves, epochs) stay correct
+    x = rnd(900 + r, 1024, 512, scale=0.5)
+    w = rnd(901 + r, 768, 512, scale=0.05)
+    ref = None
+    for _ in range(6):
+        out = dc.gemm_reduce_scatter(x, w)
+        if ref is None:
+            ref = out.clone()
+        assert torch.equal(out, ref)
+    dc.synchronize()
+
+
+@needs2
+def test_fused_gemm_collectives_on_gpus():
+    run(_fused_tp, 2, timeout=600.0, devices="cuda", op_timeout=60.0)

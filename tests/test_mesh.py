@@ -107,7 +107,7 @@ def _two_d(pg) -> None:
     m = ParallelMesh(pg, dp=2, tp=2)
     tp, dp = m.group("tp"), m.group("dp")
     torch.manual_seed(3)
-    ref = nn.Sequential(nn.Linear(WIDTH, 4 * WIDTH), nn.GELU(approximate="tanh"), nn.Linear(4 * WIDTH, WIDTH))
+    ref = nn.Sequential(nn.Linear(WIDTH, 4 * WIDTH), nn.GELU(), nn.Linear(4 * WIDTH, WIDTH))
     par = ParallelMLP(WIDTH, tp)
     par.up.load_full_weight(ref[0].weight.detach(), ref[0].bias.detach())
     par.down.load_full_weight(ref[2].weight.detach(), ref[2].bias.detach())
@@ -133,7 +133,7 @@ def _three_d(pg) -> dict:
     m = ParallelMesh(pg, dp=2, pp=2, tp=2)
     tp, pp, dp = m.group("tp"), m.group("pp"), m.group("dp")
     torch.manual_seed(5)
-    full = [nn.Sequential(nn.Linear(WIDTH, 4 * WIDTH), nn.GELU(approximate="tanh"), nn.Linear(4 * WIDTH, WIDTH))
+    full = [nn.Sequential(nn.Linear(WIDTH, 4 * WIDTH), nn.GELU(), nn.Linear(4 * WIDTH, WIDTH))
             for _ in range(2)]
     ref = nn.Sequential(*copy.deepcopy(full))
     s = m.coordinate("pp")

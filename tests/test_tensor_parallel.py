@@ -21,7 +21,7 @@ WIDTH, BATCH = 16, 4
 
 def _mlp(pg) -> None:
     torch.manual_seed(3)
-    ref = nn.Sequential(nn.Linear(WIDTH, 4 * WIDTH), nn.GELU(approximate="tanh"), nn.Linear(4 * WIDTH, WIDTH))
+    ref = nn.Sequential(nn.Linear(WIDTH, 4 * WIDTH), nn.GELU(), nn.Linear(4 * WIDTH, WIDTH))
     up, down = ref[0], ref[2]
     par = ParallelMLP(WIDTH, pg)
     par.up.load_full_weight(up.weight.detach(), up.bias.detach())
@@ -149,6 +149,76 @@ def _drift(pg, steps: int = 8) -> None:
 
 def test_replicated_layers_stay_bitwise_identical() -> None:
     run(_drift, 4)
+
+
+def _sp_drift(pg, steps: int = 6) -> None:
+    """Sequence parallel: LayerNorm and row bias see only local tokens; after
+    ``allreduce_sequence_parallel_grads`` they match the unsharded gradients and
+    stay bitwise identical across ranks."""
+    from mini_nccl_b200.tensor_parallel import (
+        allreduce_sequence_parallel_grads, gather_from_sequence_parallel, mark_sequence_parallel,
+        scatter_to_sequence_parallel)
+
+    torch.manual_seed(41)
+    norm = nn.LayerNorm(WIDTH)
+    mlp = ParallelMLP(WIDTH, pg, sequence_parallel=True)
+    mark_sequence_parallel(norm)
+    params = list(norm.parameters()) + list(mlp.parameters())
+    opt = torch.optim.SGD(params, lr=0.1)
+    g = torch.Generator().manual_seed(43)
+    T = 4 * pg.world_size
+    for _ in range(steps):
+        x = torch.randn(T, 2, WIDTH, generator=g)  # sequence-major, replicated
+        opt.zero_grad()
+        xs = scatter_to_sequence_parallel(pg, x)
+        y = gather_from_sequence_parallel(pg, mlp(norm(xs), residual=xs))
+        y.square().mean().backward()
+        allreduce_sequence_parallel_grads(norm, pg)
+        allreduce_sequence_parallel_grads(mlp, pg)
+        opt.step()
+    for name, p_ in list(norm.named_parameters()) + [("mlp.down.bias", mlp.down.bias)]:
+        got = collectives.all_gather(pg, p_.detach())
+        for r, other in enumerate(got):
+            assert torch.equal(other, got[0]), f"replicated {name} diverged on rank {r}"
+
+
+def test_sequence_parallel_replicated_params_stay_identical() -> None:
+    run(_sp_drift, 2)
+
+
+def _sp_grads_match(pg) -> None:
+    """SP MLP block gradients (incl. the replicated bias and LN) equal a single process."""
+    from mini_nccl_b200.tensor_parallel import (
+        allreduce_sequence_parallel_grads, gather_from_sequence_parallel, mark_sequence_parallel,
+        scatter_to_sequence_parallel)
+
+    torch.manual_seed(51)
+    ref_norm, ref_up, ref_down = nn.LayerNorm(WIDTH), nn.Linear(WIDTH, 4 * WIDTH), nn.Linear(4 * WIDTH, WIDTH)
+    norm = nn.LayerNorm(WIDTH)
+    norm.load_state_dict(ref_norm.state_dict())
+    mlp = ParallelMLP(WIDTH, pg, sequence_parallel=True)
+    mlp.up.load_full_weight(ref_up.weight.detach(), ref_up.bias.detach())
+    mlp.down.load_full_weight(ref_down.weight.detach(), ref_down.bias.detach())
+    mark_sequence_parallel(norm)
+    T = 3 * pg.world_size
+    x = torch.randn(T, 2, WIDTH, generator=torch.Generator().manual_seed(53))
+    xr = x.clone().requires_grad_(True)
+    h = ref_norm(xr)
+    (xr + ref_down(F.gelu(ref_up(h)))).square().mean().backward()
+    xp = x.clone().requires_grad_(True)
+    xs = scatter_to_sequence_parallel(pg, xp)
+    gather_from_sequence_parallel(pg, mlp(norm(xs), residual=xs)).square().mean().backward()
+    allreduce_sequence_parallel_grads(norm, pg)
+    allreduce_sequence_parallel_grads(mlp, pg)
+    torch.testing.assert_close(xp.grad, xr.grad, rtol=1e-4, atol=1e-6)
+    torch.testing.assert_close(norm.weight.grad, ref_norm.weight.grad, rtol=1e-4, atol=1e-6)
+    torch.testing.assert_close(mlp.down.bias.grad, ref_down.bias.grad, rtol=1e-4, atol=1e-6)
+    s0, n = mlp.up.shard_start, mlp.up.shard_size
+    torch.testing.assert_close(mlp.up.weight.grad, ref_up.weight.grad[s0 : s0 + n], rtol=1e-4, atol=1e-6)
+
+
+def test_sequence_parallel_grads_match_single_process() -> None:
+    run(_sp_grads_match, 2)
 
 
 def _unsharded_input(pg) -> None:
