@@ -470,7 +470,8 @@ def all_gather_into(pg: Communicator, out: torch.Tensor, tensor: torch.Tensor) -
     if tensor.is_cuda and W > 1:
         dc = _device_comm(pg)
         if dc is not None:
-            return dc.all_gather(tensor.contiguous(), out=out.view(W, -1))
+            dc.all_gather(tensor.contiguous(), out=out.view(W, -1))
+            return out
     parts = all_gather(pg, tensor)
     out.view(W, -1).copy_(torch.stack([p.reshape(-1) for p in parts]))
     return out

@@ -585,6 +585,94 @@ __global__ void __launch_bounds__(kCommThreads) reduce_scatter_kernel(CommArgs a
 }
 
 // ---------------------------------------------------------------------------
+// reduce-scatter fused with AdamW on the owned shard (FSDP gradients)
+//   Phase 1 is the push reduce-scatter above (grad chunk c -> rank c, slot r).
+//   Phase 2: each owned element's gradient is summed over the W slots in rank
+//   order, scaled (1/W), and used at once for the AdamW update of the fp32
+//   master weight and moments; the rounded parameter is written into the
+//   shard.  The reduced gradient never goes to memory.
+// ---------------------------------------------------------------------------
+struct AdamArgs {
+  float* master;  // fp32 master shard, or null (parameters are fp32 themselves)
+  float* m;
+  float* v;
+  void* param;    // shard, bf16 or fp32
+  float lr, b1, b2, eps, wd, c1, c2;  // c1 = 1 / (1 - b1^t), c2 = 1 / (1 - b2^t)
+};
+
+template <bool P_BF16>
+MNB_DEVICE void adam_update(const AdamArgs& o, long long e, float g) {
+  float w = o.master ? o.master[e]
+                     : (P_BF16 ? bf16_to_f32(reinterpret_cast<const __nv_bfloat16*>(o.param)[e])
+                               : reinterpret_cast<const float*>(o.param)[e]);
+  const float m = o.b1 * o.m[e] + (1.f - o.b1) * g;
+  const float v = o.b2 * o.v[e] + (1.f - o.b2) * g * g;
+  o.m[e] = m;
+  o.v[e] = v;
+  w -= o.lr * o.wd * w;
+  w -= o.lr * (m * o.c1) / (sqrtf(v * o.c2) + o.eps);
+  if (o.master) o.master[e] = w;
+  if (P_BF16) reinterpret_cast<__nv_bfloat16*>(o.param)[e] = f32_to_bf16(w);
+  else reinterpret_cast<float*>(o.param)[e] = w;
+}
+
+template <typename TG, bool P_BF16>
+__global__ void __launch_bounds__(kCommThreads) rs_adamw_kernel(CommArgs a, AdamArgs o) {
+  constexpr int V = Vec<TG>::n;
+  ring_begin(a);
+  const int W = a.world, r = a.rank;
+  const long long chunk = a.n;
+  const bool vec = chunk % V == 0;
+  const TG* in = reinterpret_cast<const TG*>(a.in);
+  long long lo, hi;
+  block_range(vec ? chunk / V : chunk, &lo, &hi);
+  for (int k = 1; k < W; ++k) {
+    const int c = (r + k) % W;
+    if (vec) {
+      constexpr int U = 4;
+      for (long long u0 = lo + threadIdx.x; u0 < hi; u0 += U * blockDim.x) {
+        uint4 w[U];
+#pragma unroll
+        for (int j = 0; j < U; ++j)
+          if (u0 + j * blockDim.x < hi) w[j] = ld_v4(in + c * chunk + (u0 + j * blockDim.x) * V);
+#pragma unroll
+        for (int j = 0; j < U; ++j)
+          if (u0 + j * blockDim.x < hi) st_v4(at<TG>(a.data[c], r * chunk + (u0 + j * blockDim.x) * V), w[j]);
+      }
+    } else {
+      for (long long e = lo + threadIdx.x; e < hi; e += blockDim.x) *at<TG>(a.data[c], r * chunk + e) = in[c * chunk + e];
+    }
+  }
+  const bool ok = peer_barrier(a, a.epoch + 1);
+  if (ok) {
+    const TG* own = in + r * chunk;
+    if (vec) {
+      for (long long u = lo + threadIdx.x; u < hi; u += blockDim.x) {
+        float g[V];
+        for (int p = 0; p < W; ++p) {  // rank order
+          float x[V];
+          unpack_vec<TG, float>(p == r ? ld_v4(own + u * V) : ld_v4_cg(at<TG>(a.data[r], p * chunk + u * V)), x);
+#pragma unroll
+          for (int i = 0; i < V; ++i) g[i] = p == 0 ? x[i] : g[i] + x[i];
+        }
+#pragma unroll
+        for (int i = 0; i < V; ++i) adam_update<P_BF16>(o, u * V + i, g[i] * a.scale);
+      }
+    } else {
+      for (long long e = lo + threadIdx.x; e < hi; e += blockDim.x) {
+        float g = 0.f;
+        for (int p = 0; p < W; ++p) {
+          const float x = to_f<TG>(p == r ? own[e] : *reinterpret_cast<volatile TG*>(at<TG>(a.data[r], p * chunk + e)));
+          g = p == 0 ? x : g + x;
+        }
+        adam_update<P_BF16>(o, e, g * a.scale);
+      }
+    }
+  }
+  ring_end(a, ok);
+}
+
+// ---------------------------------------------------------------------------
 // data movement without reduction, push, byte level (parity-buffered slots):
 //   kind 0 all_gather : rank r stores its shard into slot r of every rank
 //   kind 1 broadcast  : the root stores the tensor into slot 0 of every rank
@@ -760,7 +848,7 @@ void* ipc_open(const std::string& bytes) {
 void gemm_fused(int fuse, torch::Tensor a, torch::Tensor b, torch::Tensor out, bool b_mn,
                 c10::optional<torch::Tensor> bias, c10::optional<torch::Tensor> aux,
                 c10::optional<torch::Tensor> resid, int64_t epi, torch::Tensor status, const PeerCtx& ctx,
-                c10::optional<torch::Tensor> ag_buf, c10::optional<torch::Tensor> ag_ready);
+                uint32_t* ag_base, c10::optional<torch::Tensor> stamps);
 
 struct Segment {
   void* local = nullptr;
@@ -930,7 +1018,7 @@ class DeviceCommImpl {
 
   int blocks_for(int64_t bytes, int max_blocks) const {
     int64_t b = (bytes + (64 << 10) - 1) / (64 << 10);  // ~64 KiB per CTA per call
-    return static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(b, std::min(max_blocks, kMaxBlocks - 1))));
+    return static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(b, std::min(max_blocks, kMaxCommBlocks))));
   }
 
   // Staging bytes a call needs (wire elements of `wsz` bytes); mirrors the
@@ -972,30 +1060,83 @@ class DeviceCommImpl {
   // out[M/W, N] = (sum over ranks of x_r @ w_r^T)[this rank's rows] + bias + resid,
   // as one kernel: tiles are pushed to their owners as they finish.
   void gemm_rs(torch::Tensor x, torch::Tensor w, torch::Tensor out, bool w_mn, c10::optional<torch::Tensor> bias,
-               c10::optional<torch::Tensor> resid, torch::Tensor status) {
+               c10::optional<torch::Tensor> resid, torch::Tensor status, c10::optional<torch::Tensor> stamps) {
     c10::cuda::CUDAGuard g(device_);
     const int64_t M = x.size(0);
     const int64_t N = w_mn ? w.size(1) : w.size(0);
     const int64_t need = 2 * M * N * 2;  // two parity halves of W slots of [M/W, N] bf16
     TORCH_CHECK(need <= segs_[staging_].bytes, "staging buffer too small for the fused reduce-scatter");
     CommArgs a = base_args(staging_, 0, x.data_ptr(), out.data_ptr(), M * N, 7, M * N * 2, 1);
-    gemm_fused(1, x, w, out, w_mn, bias, c10::nullopt, resid, 0, status, peer_ctx(a), c10::nullopt, c10::nullopt);
+    gemm_fused(1, x, w, out, w_mn, bias, c10::nullopt, resid, 0, status, peer_ctx(a), &rs_base_, stamps);
   }
 
-  // out[M, N] = epi(all_gather(x_shard) @ w^T); `gathered` [M, K] receives the
-  // gathered input, `ready` is int32 [W] scratch.
-  void ag_gemm(torch::Tensor x_shard, torch::Tensor w, torch::Tensor out, torch::Tensor gathered,
-               torch::Tensor ready, bool w_mn, c10::optional<torch::Tensor> bias, c10::optional<torch::Tensor> aux,
+  // out[M, N] = epi(all_gather(x_shard) @ w^T); when given, `gathered` [M, K]
+  // receives a copy of the gathered input (copy engine, after the kernel).
+  void ag_gemm(torch::Tensor x_shard, torch::Tensor w, torch::Tensor out, c10::optional<torch::Tensor> gathered,
+               bool w_mn, c10::optional<torch::Tensor> bias, c10::optional<torch::Tensor> aux,
                c10::optional<torch::Tensor> resid, int64_t epi, torch::Tensor status) {
     c10::cuda::CUDAGuard g(device_);
     TORCH_CHECK(x_shard.is_contiguous() && x_shard.scalar_type() == at::kBFloat16, "x shard: contiguous bf16");
     const int64_t bytes = x_shard.numel() * 2;
-    TORCH_CHECK(2 * bytes <= segs_[staging_].bytes, "staging buffer too small for the fused all-gather");
+    const int64_t full = bytes * world_;
+    TORCH_CHECK(2 * full <= segs_[staging_].bytes, "staging buffer too small for the fused all-gather");
     CommArgs a = base_args(staging_, 0, x_shard.data_ptr(), out.data_ptr(), x_shard.numel(), 8, bytes, 1);
     auto stream = at::cuda::getCurrentCUDAStream();
-    // peers read my shard from my staging (their kernels wait for my ready signal)
-    ck(cudaMemcpyAsync(a.data[rank_], x_shard.data_ptr(), bytes, cudaMemcpyDeviceToDevice, stream), "shard copy");
-    gemm_fused(2, x_shard, w, out, w_mn, bias, aux, resid, epi, status, peer_ctx(a), gathered, ready);
+    // my own row block of the gathered operand; peers' blocks arrive by push
+    ck(cudaMemcpyAsync(static_cast<uint8_t*>(a.data[rank_]) + rank_ * bytes, x_shard.data_ptr(), bytes,
+                       cudaMemcpyDeviceToDevice, stream),
+       "shard copy");
+    gemm_fused(2, x_shard, w, out, w_mn, bias, aux, resid, epi, status, peer_ctx(a), &ag_base_, c10::nullopt);
+    if (gathered) {
+      TORCH_CHECK(gathered->is_contiguous() && gathered->numel() * gathered->element_size() == full,
+                  "gathered must be a contiguous [M, K] bf16 tensor");
+      ck(cudaMemcpyAsync(gathered->data_ptr(), a.data[rank_], full, cudaMemcpyDeviceToDevice, stream), "gathered copy");
+    }
+  }
+
+  // shard of sum_r(grad_r) * scale fed straight into AdamW on this rank's shard
+  void reduce_scatter_adamw(torch::Tensor grad, torch::Tensor param, c10::optional<torch::Tensor> master,
+                            torch::Tensor m, torch::Tensor v, double lr, double b1, double b2, double eps, double wd,
+                            double bc1, double bc2, double scale, int max_blocks) {
+    c10::cuda::CUDAGuard g(device_);
+    TORCH_CHECK(grad.is_contiguous() && param.is_contiguous(), "contiguous grad and param shard");
+    const int64_t n = grad.numel();
+    TORCH_CHECK(n % world_ == 0, "gradient length must divide by world size");
+    const int64_t chunk = n / world_;
+    TORCH_CHECK(param.numel() == chunk && m.numel() == chunk && v.numel() == chunk, "shard sizes disagree");
+    TORCH_CHECK(m.scalar_type() == at::kFloat && v.scalar_type() == at::kFloat, "moments must be fp32");
+    const auto gt = grad.scalar_type();
+    TORCH_CHECK(gt == at::kBFloat16 || gt == at::kFloat, "gradient must be bf16 or fp32");
+    const auto pt = param.scalar_type();
+    TORCH_CHECK(pt == at::kBFloat16 || pt == at::kFloat, "parameters must be bf16 or fp32");
+    TORCH_CHECK(staging_need(2, n, grad.element_size()) <= segs_[staging_].bytes, "staging buffer too small");
+    CommArgs a = base_args(staging_, 0, grad.data_ptr(), param.data_ptr(), chunk, 9, n * grad.element_size(), 1);
+    a.scale = static_cast<float>(scale);
+    AdamArgs o{};
+    if (master) {
+      TORCH_CHECK(master->scalar_type() == at::kFloat && master->numel() == chunk, "master must be fp32 [shard]");
+      o.master = master->data_ptr<float>();
+    }
+    o.m = m.data_ptr<float>();
+    o.v = v.data_ptr<float>();
+    o.param = param.data_ptr();
+    o.lr = static_cast<float>(lr);
+    o.b1 = static_cast<float>(b1);
+    o.b2 = static_cast<float>(b2);
+    o.eps = static_cast<float>(eps);
+    o.wd = static_cast<float>(wd);
+    o.c1 = static_cast<float>(1.0 / bc1);
+    o.c2 = static_cast<float>(1.0 / bc2);
+    const int blocks = blocks_for(chunk * grad.element_size(), max_blocks);
+    auto stream = at::cuda::getCurrentCUDAStream();
+    if (gt == at::kBFloat16) {
+      if (pt == at::kBFloat16) rs_adamw_kernel<__nv_bfloat16, true><<<blocks, kCommThreads, 0, stream>>>(a, o);
+      else rs_adamw_kernel<__nv_bfloat16, false><<<blocks, kCommThreads, 0, stream>>>(a, o);
+    } else {
+      if (pt == at::kBFloat16) rs_adamw_kernel<float, true><<<blocks, kCommThreads, 0, stream>>>(a, o);
+      else rs_adamw_kernel<float, false><<<blocks, kCommThreads, 0, stream>>>(a, o);
+    }
+    C10_CUDA_KERNEL_LAUNCH_CHECK();
   }
 
   // algorithm: 0 one_shot, 1 two_shot
@@ -1159,6 +1300,8 @@ class DeviceCommImpl {
   DevEvent* ring_h_ = nullptr;
   DevEvent* ring_d_ = nullptr;
   uint32_t epoch_ = 1;
+  uint32_t ag_base_ = 0;  // total arrival-counter increments of fused all-gathers so far
+  uint32_t rs_base_ = 0;  // ... and of fused reduce-scatters
   uint32_t seq_ = 0;
   unsigned long long timeout_ns_ = 300ull * 1000000000ull;
   bool closed_ = false;
@@ -1190,6 +1333,7 @@ void register_comm(py::module_& m) {
       .def("stepped_all_reduce", &DeviceCommImpl::stepped_all_reduce)
       .def("staging_need", &DeviceCommImpl::staging_need)
       .def("gemm_rs", &DeviceCommImpl::gemm_rs)
+      .def("reduce_scatter_adamw", &DeviceCommImpl::reduce_scatter_adamw)
       .def("ag_gemm", &DeviceCommImpl::ag_gemm)
       .def("close", &DeviceCommImpl::close)
       .def_property_readonly("rank", &DeviceCommImpl::rank)

@@ -35,13 +35,16 @@
 //            signals every owner; once all CTAs of all ranks have signalled,
 //            the CTAs sum the W slots of this rank's rows in rank order and
 //            add bias and residual (bf16 out).
-//   kFuseAG  all-gather -> GEMM.  A is gathered into a local [M, K] buffer by
-//            two extra gather warps per CTA (16-byte peer loads, local
-//            stores), own shard first; per-shard counters tell the TMA
-//            producer when a shard's rows may be loaded.  Tiles of this
-//            rank's own rows come first, so the gather runs under them.
-//            Remote rows cross NVLink once; the TMA unit only ever reads
-//            local memory.
+//   kFuseAG  all-gather -> GEMM.  The gathered A is this call's staging
+//            region ([M, K], row block s = rank s's shard, own block copied in
+//            by the copy engine before the launch).  Two extra warps per CTA
+//            push this CTA's slice of the own shard into every peer's staging
+//            (16-byte coalesced NVLink stores) and then bump the peer's
+//            arrival counter for this source with a release atomic; the TMA
+//            producer waits for a shard's counter before loading its rows.
+//            Tiles of the own rows come first, so the exchange runs under
+//            them; every remote row crosses NVLink once and the TMA unit only
+//            reads local memory.
 #include <ATen/cuda/CUDAContext.h>
 #include <c10/cuda/CUDAGuard.h>
 #include <cudaTypedefs.h>
@@ -82,8 +85,9 @@ struct GemmArgs {
   // fused collectives
   int rows_per_rank;                // M / world (RS: rows each rank owns; AG: rows of each shard)
   const __nv_bfloat16* ag_local;    // AG: this rank's shard of A, [rows_per_rank, K]
-  __nv_bfloat16* ag_buf;            // AG: gathered A, [M, K], row stride K
-  int* ag_ready;                    // AG: per-shard count of CTAs done copying (zeroed per call)
+  uint32_t ag_target;               // AG: counter value meaning "every CTA of that rank has pushed"
+  uint32_t rs_target;               // RS: counter value meaning "every CTA of that rank has stored its tiles"
+  unsigned long long* stamps;       // optional %globaltimer phase stamps (CTA 0 / slowest CTA), or null
 };
 
 enum : int { kFuseNone = 0, kFuseRS = 1, kFuseAG = 2 };
@@ -120,22 +124,25 @@ MNB_DEVICE int remap_mblock(int mb, int m_tiles, const GemmArgs& a, const PeerCt
   }
 }
 
-// RS epilogue: 32 consecutive columns of one row of partial sums go to the
-// owner's slot for this rank, as bf16.
-MNB_DEVICE void rs_store(const GemmArgs& a, const PeerCtx& ctx, int row, int col0, const float* v) {
-  if (row >= a.M) return;
-  const int o = row / a.rows_per_rank;
-  const long long lr = row - static_cast<long long>(o) * a.rows_per_rank;
-  __nv_bfloat16* d = reinterpret_cast<__nv_bfloat16*>(ctx.data[o]) +
-                     (static_cast<long long>(ctx.rank) * a.rows_per_rank + lr) * a.N + col0;
-  if (col0 + 32 <= a.N) {
-    uint32_t pk[16];
+// RS epilogue: a staged 32-row x 64-column bf16 box (128-byte swizzle) goes
+// to the owners' slots for this rank; lane l moves 16-byte chunk l%8 of rows
+// l/8, l/8+4, ...
+MNB_DEVICE void rs_push_box(const GemmArgs& a, const PeerCtx& ctx, const uint8_t* box, int row0, int col0,
+                            int lane) {
+  const int chunk = lane & 7;
+  const int col = col0 + chunk * 8;
+  if (col >= a.N) return;  // N is a multiple of 8: a chunk is all in or all out
 #pragma unroll
-    for (int i = 0; i < 16; ++i) pk[i] = pack_bf16x2(v[2 * i], v[2 * i + 1]);
-#pragma unroll
-    for (int i = 0; i < 4; ++i) st_v4(d + 8 * i, make_uint4(pk[4 * i], pk[4 * i + 1], pk[4 * i + 2], pk[4 * i + 3]));
-  } else {
-    for (int i = 0; i < 32 && col0 + i < a.N; ++i) d[i] = f32_to_bf16(v[i]);
+  for (int it = 0; it < 8; ++it) {
+    const int rr = it * 4 + (lane >> 3);
+    const int row = row0 + rr;
+    if (row >= a.M) break;
+    const uint4 val = *reinterpret_cast<const uint4*>(box + rr * 128 + ((chunk ^ (rr & 7)) * 16));
+    const int o = row / a.rows_per_rank;
+    const long long lr = row - static_cast<long long>(o) * a.rows_per_rank;
+    __nv_bfloat16* d = reinterpret_cast<__nv_bfloat16*>(ctx.data[o]) +
+                       (static_cast<long long>(ctx.rank) * a.rows_per_rank + lr) * a.N + col;
+    st_v4(d, val);
   }
 }
 
@@ -347,55 +354,35 @@ MNB_DEVICE void epilogue_inputs(const GemmArgs& a, int row, int col0, float* v) 
   }
 }
 
-// kFuseAG gather warps (64 threads): copy this CTA's slice of every shard
-// into the gathered buffer, own shard first, then bump the shard's counter.
-MNB_DEVICE void gather_shards(const GemmArgs& a, const PeerCtx& ctx, int gt) {
+// kFuseAG exchange warps (64 threads): push this CTA's slice of the own
+// shard into every peer's staging, then count the arrival there.
+MNB_DEVICE void push_shard(const GemmArgs& a, const PeerCtx& ctx, int gt) {
   const int W = ctx.world, r = ctx.rank;
-  const uint32_t want = ctx.epoch + 1;
-  if (blockIdx.x == 0 && gt == 0) {  // my shard (in my staging) is ready for the peers
-    __threadfence_system();
-    for (int p = 0; p < W; ++p)
-      if (p != r) st_release_sys(ctx.sig[p] + kReadyRow * kMaxRanks + r, want);
-  }
   const long long row_units = a.K / 8;  // 16-byte units per row
-  const long long per = (a.rows_per_rank + gridDim.x - 1) / gridDim.x;
   const long long rpr = a.rows_per_rank;
+  const long long per = (rpr + gridDim.x - 1) / gridDim.x;
   const long long lo = min(rpr, per * static_cast<long long>(blockIdx.x));
   const long long hi = min(rpr, lo + per);
   const long long units = (hi - lo) * row_units;
-  const uint64_t t0 = globaltimer_ns();
-  __shared__ int gather_ok;
-  for (int k = 0; k < W; ++k) {
-    const int sh = (r + k) % W;
-    if (gt == 0) {
-      bool ok = ctx.status[0] == 0 && *reinterpret_cast<volatile int*>(a.status) == 0;
-      if (ok && sh != r)
-        ok = wait_signal(ctx.sig[r] + kReadyRow * kMaxRanks + sh, want, ctx.status, sh, blockIdx.x, ctx.seq,
-                         ctx.timeout_ns, t0);
-      if (!ok) atomicCAS(a.status, 0, kErrPeerTimeout);
-      gather_ok = ok;
-    }
-    asm volatile("bar.sync 2, %0;" ::"n"(kGatherThreads) : "memory");
-    if (!gather_ok) return;
-    const __nv_bfloat16* src = sh == r ? a.ag_local : reinterpret_cast<const __nv_bfloat16*>(ctx.data[sh]);
-    const __nv_bfloat16* s0 = src + lo * a.K;
-    __nv_bfloat16* d0 = a.ag_buf + (static_cast<long long>(sh) * a.rows_per_rank + lo) * a.K;
-    constexpr int U = 8;
-    for (long long u0 = gt; u0 < units; u0 += U * kGatherThreads) {
-      uint4 v[U];
+  const __nv_bfloat16* s0 = a.ag_local + lo * a.K;
+  const long long dst_off = (static_cast<long long>(r) * rpr + lo) * a.K;  // own block in everyone's staging
+  constexpr int U = 8;
+  for (long long u0 = gt; u0 < units; u0 += U * kGatherThreads) {
+    uint4 v[U];
 #pragma unroll
-      for (int j = 0; j < U; ++j)
-        if (u0 + j * kGatherThreads < units) v[j] = ld_v4_volatile(s0 + 8 * (u0 + j * kGatherThreads));
+    for (int j = 0; j < U; ++j)
+      if (u0 + j * kGatherThreads < units) v[j] = ld_v4(s0 + 8 * (u0 + j * kGatherThreads));
+    for (int k = 1; k < W; ++k) {
+      __nv_bfloat16* d0 = reinterpret_cast<__nv_bfloat16*>(ctx.data[(r + k) % W]) + dst_off;
 #pragma unroll
       for (int j = 0; j < U; ++j)
         if (u0 + j * kGatherThreads < units) st_v4(d0 + 8 * (u0 + j * kGatherThreads), v[j]);
     }
-    fence_proxy_async_global();
-    asm volatile("bar.sync 2, %0;" ::"n"(kGatherThreads) : "memory");
-    if (gt == 0) {
-      __threadfence();
-      red_release_gpu_add(a.ag_ready + sh, 1);
-    }
+  }
+  asm volatile("bar.sync 2, %0;" ::"n"(kGatherThreads) : "memory");
+  if (gt == 0) {
+    __threadfence_system();
+    for (int k = 1; k < W; ++k) red_release_sys_add(ctx.sig[(r + k) % W] + kCountRow * kMaxRanks + r, 1u);
   }
 }
 
@@ -403,63 +390,67 @@ MNB_DEVICE void gather_shards(const GemmArgs& a, const PeerCtx& ctx, int gt) {
 // wait for every CTA of every rank, then reduce this rank's rows.
 MNB_DEVICE void rs_finish(const GemmArgs& a, const PeerCtx& ctx) {
   const int W = ctx.world, r = ctx.rank;
-  const uint32_t want = ctx.epoch + 1;
   __syncthreads();
-  if (threadIdx.x == 0) {
-    __threadfence_system();
-    for (int p = 0; p < W; ++p) st_release_sys(ctx.sig[p] + blockIdx.x * kMaxRanks + r, want);
-  }
+  // stamps: [1] latest "my tiles are done", [2] latest "all flags seen", [3] latest "reduced"
+  if (a.stamps != nullptr && threadIdx.x == 0) atomicMax(a.stamps + 1, globaltimer_ns());
   bool ok = *reinterpret_cast<volatile int*>(a.status) == 0;
-  const uint64_t t0 = globaltimer_ns();
-  for (int i = threadIdx.x; ok && i < static_cast<int>(gridDim.x) * W; i += blockDim.x) {
-    const int b = i / W, src = i % W;
-    ok = wait_signal(ctx.sig[r] + b * kMaxRanks + src, want, ctx.status, src, b, ctx.seq, ctx.timeout_ns, t0);
+  if (threadIdx.x == 0) {
+    __threadfence_system();  // this CTA's tile stores are visible before its arrival is
+    for (int p = 0; p < W; ++p) red_release_sys_add(ctx.sig[p] + kRsCountRow * kMaxRanks + r, 1u);
+    const uint64_t t0 = globaltimer_ns();
+    for (int src = 0; ok && src < W; ++src)
+      ok = wait_signal(ctx.sig[r] + kRsCountRow * kMaxRanks + src, a.rs_target, ctx.status, src, blockIdx.x,
+                       ctx.seq, ctx.timeout_ns, t0);
   }
   if (!__syncthreads_and(ok)) return;
+  if (a.stamps != nullptr && threadIdx.x == 0) atomicMax(a.stamps + 2, globaltimer_ns());
   // out[row, col] = bias[col] + resid[row, col] + sum_p slot_p[row, col]   (rows of this rank)
   const long long cu = a.N / 8;
   const long long total = static_cast<long long>(a.rows_per_rank) * cu;
   const long long slot = static_cast<long long>(a.rows_per_rank) * a.N;
   const __nv_bfloat16* base = reinterpret_cast<const __nv_bfloat16*>(ctx.data[r]);
   __nv_bfloat16* out = reinterpret_cast<__nv_bfloat16*>(a.out);
-  for (long long u = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; u < total;
-       u += static_cast<long long>(gridDim.x) * blockDim.x) {
-    const long long row = u / cu, col = (u - row * cu) * 8;
-    float acc[8];
+  const long long nthr = static_cast<long long>(gridDim.x) * blockDim.x;
+  constexpr int U = 4;  // independent 16-byte units per thread per pass
+  auto add8 = [](float* acc, uint4 w) {
+    const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
 #pragma unroll
-    for (int i = 0; i < 8; ++i) acc[i] = 0.f;
-    for (int p = 0; p < W; ++p) {
-      const uint4 w = ld_v4_volatile(base + p * slot + row * a.N + col);
-      const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
-#pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        const float2 f = unpack_bf16x2(ws[j]);
-        acc[2 * j] += f.x;
-        acc[2 * j + 1] += f.y;
-      }
+    for (int j = 0; j < 4; ++j) {
+      const float2 f = unpack_bf16x2(ws[j]);
+      acc[2 * j] += f.x;
+      acc[2 * j + 1] += f.y;
     }
-    if (a.bias != nullptr) {
-      const uint4 w = ld_v4(a.bias + col);
-      const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
+  };
+  for (long long u0 = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; u0 < total; u0 += U * nthr) {
+    float acc[U][8];
 #pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        const float2 f = unpack_bf16x2(ws[j]);
-        acc[2 * j] += f.x;
-        acc[2 * j + 1] += f.y;
-      }
-    }
-    if (a.resid != nullptr) {
-      const uint4 w = ld_v4(a.resid + row * a.ldr + col);
-      const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
+    for (int k = 0; k < U; ++k)
 #pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        const float2 f = unpack_bf16x2(ws[j]);
-        acc[2 * j] += f.x;
-        acc[2 * j + 1] += f.y;
-      }
+      for (int i = 0; i < 8; ++i) acc[k][i] = 0.f;
+    for (int p = 0; p < W; ++p) {  // rank order
+      uint4 w[U];
+#pragma unroll
+      for (int k = 0; k < U; ++k)
+        if (u0 + k * nthr < total) w[k] = ld_v4_volatile(base + p * slot + (u0 + k * nthr) * 8);
+#pragma unroll
+      for (int k = 0; k < U; ++k)
+        if (u0 + k * nthr < total) add8(acc[k], w[k]);
     }
-    st_v4(out + row * a.ldo + col, make_uint4(pack_bf16x2(acc[0], acc[1]), pack_bf16x2(acc[2], acc[3]),
-                                             pack_bf16x2(acc[4], acc[5]), pack_bf16x2(acc[6], acc[7])));
+#pragma unroll
+    for (int k = 0; k < U; ++k) {
+      const long long u = u0 + k * nthr;
+      if (u >= total) continue;
+      const long long row = u / cu, col = (u - row * cu) * 8;
+      if (a.bias != nullptr) add8(acc[k], ld_v4(a.bias + col));
+      if (a.resid != nullptr) add8(acc[k], ld_v4(a.resid + row * a.ldr + col));
+      st_v4(out + row * a.ldo + col,
+            make_uint4(pack_bf16x2(acc[k][0], acc[k][1]), pack_bf16x2(acc[k][2], acc[k][3]),
+                       pack_bf16x2(acc[k][4], acc[k][5]), pack_bf16x2(acc[k][6], acc[k][7])));
+    }
+  }
+  if (a.stamps != nullptr) {
+    __syncthreads();
+    if (threadIdx.x == 0) atomicMax(a.stamps + 3, globaltimer_ns());
   }
 }
 
@@ -508,6 +499,7 @@ __global__ void __launch_bounds__(gemm_threads<FUSE>(), 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  if (args.stamps != nullptr && blockIdx.x == 0 && threadIdx.x == 0) args.stamps[0] = globaltimer_ns();
 
   const int m_tiles = (args.M + kBM - 1) / kBM;
   const int n_tiles = (args.N + BN - 1) / BN;
@@ -530,28 +522,17 @@ __global__ void __launch_bounds__(gemm_threads<FUSE>(), 1)
         bool ok = true;
         if constexpr (FUSE == kFuseAG) {
           // rows of this tile come from shards s0..s1: wait until every CTA
-          // has copied its part of them into the gathered buffer
+          // of those ranks has pushed its part into this rank's staging
           const int s0 = (mb * kBM) / args.rows_per_rank;
           const int s1 = min(args.M - 1, mb * kBM + kBM - 1) / args.rows_per_rank;
           for (int sh = s0; sh <= s1 && ok; ++sh) {
-            if (ready_mask & (1u << sh)) continue;
-            const uint64_t t0 = globaltimer_ns();
-            uint32_t spins = 0;
-            while (static_cast<int>(ld_acquire_gpu(args.ag_ready + sh)) < static_cast<int>(gridDim.x)) {
-              if ((++spins & 255u) == 0) {
-                if (*reinterpret_cast<volatile int*>(status) != 0 || ctx.status[0] != 0) { ok = false; break; }
-                if (globaltimer_ns() - t0 > ctx.timeout_ns) {
-                  report_timeout(ctx.status, sh, blockIdx.x, ctx.seq);
-                  atomicCAS(status, 0, kErrPeerTimeout);
-                  ok = false;
-                  break;
-                }
-                __nanosleep(32);
-              }
-            }
+            if (sh == ctx.rank || (ready_mask & (1u << sh))) continue;
+            ok = wait_signal(ctx.sig[ctx.rank] + kCountRow * kMaxRanks + sh, args.ag_target, ctx.status, sh,
+                             blockIdx.x, ctx.seq, ctx.timeout_ns, globaltimer_ns());
+            if (!ok) atomicCAS(status, 0, kErrPeerTimeout);
             ready_mask |= 1u << sh;
           }
-          fence_proxy_async_global();  // generic-proxy writes of the gather -> TMA reads
+          fence_proxy_async_global();  // generic-proxy (peer) writes -> TMA reads
         }
         for (int kb = kb0; kb < kb1 && ok; ++kb) {
           if (!mbar_wait(empty0 + 8 * stage, phase ^ 1, status)) { ok = false; break; }
@@ -634,12 +615,23 @@ __global__ void __launch_bounds__(gemm_threads<FUSE>(), 1)
       const int row = mb * kBM + row_in_tile;
       const uint32_t lane_addr = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + acc * BN;
       if (FUSE == kFuseRS) {
+        // 32 rows x 64 columns at a time: registers -> swizzled smem box ->
+        // 128-byte row segments stored into the owner's slot (a warp store
+        // covers four whole segments, the efficient shape for NVLink writes)
+        uint8_t* box = staging + (warp - 2) * (S::boxes * 4096);
 #pragma unroll 1
-        for (int c = half * (BN / 64); c < (half + 1) * (BN / 64); ++c) {
-          float v[32];
-          tmem_ld_32(lane_addr + c * 32, v);
-          const int col0 = nb * BN + c * 32;
-          if (col0 < a.N) rs_store(a, ctx, row, col0, v);
+        for (int g = half * (BN / 128); g < (half + 1) * (BN / 128); ++g) {
+          const int colg = nb * BN + g * 64;
+          if (colg >= a.N) break;
+#pragma unroll
+          for (int sub = 0; sub < 2; ++sub) {
+            float v[32];
+            tmem_ld_32(lane_addr + g * 64 + sub * 32, v);
+            stage_row32(box, lane, sub, v);
+          }
+          __syncwarp();
+          rs_push_box(a, ctx, box, mb * kBM + q * 32, colg, lane);
+          __syncwarp();
         }
       } else if (a.tma_out) {
         // 64-column groups: TMEM -> registers -> epilogue math -> swizzled
@@ -694,7 +686,7 @@ __global__ void __launch_bounds__(gemm_threads<FUSE>(), 1)
       if (acc == 0) acc_phase ^= 1;
     }
   } else if constexpr (FUSE == kFuseAG) {
-    gather_shards(args, ctx, threadIdx.x - kGemmThreads);
+    push_shard(args, ctx, threadIdx.x - kGemmThreads);
   }
 
   if (warp >= 2 && warp < 2 + kEpiWarps && lane == 0) bulk_wait_all();  // staging boxes drained before exit
@@ -920,16 +912,19 @@ void gemm(torch::Tensor a, torch::Tensor b, torch::Tensor out, bool a_mn, bool b
 //   kFuseRS: a = X [M, K] (this rank's partial-sum input, all rows), b = W,
 //            out = [M / world, N] (this rank's rows), bias [N] and resid
 //            [M / world, N] are added once, after the reduction.
-//   kFuseAG: a = X shard [M / world, K], ag_buf = [M, K] gathered A (local
-//            scratch, also the caller's copy of the full input afterwards),
-//            ag_ready = int32 [world] zeroed here; epilogue as in gemm().
+//   kFuseAG: a = X shard [M / world, K]; the gathered [M, K] is built in
+//            this call's staging region (ctx.data[rank]), whose own row block
+//            the caller has already filled.
+//   *ag_base is the running total of increments of this mode's arrival
+//   counters (advanced here by this launch's grid: one per CTA per rank).
 void gemm_fused(int fuse, torch::Tensor a, torch::Tensor b, torch::Tensor out, bool b_mn,
                 c10::optional<torch::Tensor> bias, c10::optional<torch::Tensor> aux,
                 c10::optional<torch::Tensor> resid, int64_t epi, torch::Tensor status, const PeerCtx& ctx,
-                c10::optional<torch::Tensor> ag_buf, c10::optional<torch::Tensor> ag_ready) {
+                uint32_t* ag_base, c10::optional<torch::Tensor> stamps) {
   c10::cuda::CUDAGuard guard(a.device());
   const int W = ctx.world;
   TORCH_CHECK(fuse == kFuseRS || fuse == kFuseAG, "unknown fused mode");
+  TORCH_CHECK(ag_base != nullptr, "fused GEMMs need their arrival-counter base");
   const int64_t lda = row_stride(a, "A");
   const int64_t ldb = row_stride(b, "B");
   const int K = static_cast<int>(a.size(1));
@@ -946,6 +941,10 @@ void gemm_fused(int fuse, torch::Tensor a, torch::Tensor b, torch::Tensor out, b
   args.splits = 1;
   args.out = out.data_ptr();
   args.ldo = out.stride(0);
+  if (stamps) {
+    TORCH_CHECK(stamps->scalar_type() == at::kLong && stamps->numel() >= 4 && stamps->is_cuda(), "stamps: int64 [4]");
+    args.stamps = reinterpret_cast<unsigned long long*>(stamps->data_ptr());
+  }
   CUtensorMap ma, mo, mx;
   const bool wide = N >= 256;
   const int BN = wide ? 256 : 128;
@@ -975,16 +974,10 @@ void gemm_fused(int fuse, torch::Tensor a, torch::Tensor b, torch::Tensor out, b
     const int rows = static_cast<int>(a.size(0));
     const int M = rows * W;
     TORCH_CHECK(lda == K, "A shard must be contiguous");
-    TORCH_CHECK(ag_buf && ag_buf->scalar_type() == at::kBFloat16 && ag_buf->is_contiguous() &&
-                    ag_buf->size(0) == M && ag_buf->size(1) == K,
-                "ag_buf must be a contiguous bf16 [M, K]");
-    TORCH_CHECK(ag_ready && ag_ready->scalar_type() == at::kInt && ag_ready->numel() >= W, "ag_ready: int32 [W]");
     TORCH_CHECK(out.size(0) == M && out.size(1) == N, "AG output must be [M, N]");
     args.M = M;
     args.rows_per_rank = rows;
     args.ag_local = reinterpret_cast<const __nv_bfloat16*>(a.data_ptr());
-    args.ag_buf = reinterpret_cast<__nv_bfloat16*>(ag_buf->data_ptr());
-    args.ag_ready = ag_ready->data_ptr<int>();
     args.epi = static_cast<int>(epi);
     if (bias) {
       TORCH_CHECK(bias->scalar_type() == at::kBFloat16 && bias->numel() == N, "bias must be bf16 [N]");
@@ -1005,14 +998,16 @@ void gemm_fused(int fuse, torch::Tensor a, torch::Tensor b, torch::Tensor out, b
     TORCH_CHECK(!(args.epi & kEpiAccum), "AG-GEMM epilogues: bias, GELU, GELU', residual");
     TORCH_CHECK(!(args.epi & (kEpiGelu | kEpiGeluGrad)) || aux.has_value(), "GELU epilogues need aux");
     args.tma_out = 1;
-    C10_CUDA_CHECK(cudaMemsetAsync(args.ag_ready, 0, W * sizeof(int), at::cuda::getCurrentCUDAStream()));
-    ma = make_tma_2d_bf16(args.ag_buf, K, M, K, 64, kBM);
+    ma = make_tma_2d_bf16(ctx.data[ctx.rank], K, M, K, 64, kBM);
     mo = make_tma_2d_bf16(out.data_ptr(), N, M, out.stride(0), 64, 32);
     mx = (args.epi & kEpiGelu) ? make_tma_2d_bf16(aux->data_ptr(), N, M, args.ldaux, 64, 32) : mo;
   }
   CUtensorMap mb = b_mn ? make_tma_2d_bf16(b.data_ptr(), N, K, ldb, 64, 64)
                         : make_tma_2d_bf16(b.data_ptr(), K, N, ldb, 64, BN);
   const int units = ((args.M + kBM - 1) / kBM) * ((N + BN - 1) / BN);
+  // one arrival per CTA of each rank on the matching counter row
+  *ag_base += static_cast<uint32_t>(std::min(units, num_sms()));
+  (fuse == kFuseAG ? args.ag_target : args.rs_target) = *ag_base;
   cudaStream_t stream = at::cuda::getCurrentCUDAStream();
   const bool gelu = (args.epi & kEpiGelu) != 0;
 #define MNB_FUSED(BNV, BMJ, ST, F)                                                   \

@@ -17,9 +17,15 @@ namespace mnb {
 constexpr int kMaxRanks = 16;
 constexpr int kMaxBlocks = 256;
 constexpr int kSigSlots = kMaxBlocks * kMaxRanks;
-// Slot row reserved for one-off "my input is ready" signals of fused kernels
-// (block rows 0..kMaxBlocks-2 are per-CTA slots).
-constexpr int kReadyRow = kMaxBlocks - 1;
+// Signal-pad rows 0..kMaxCommBlocks-1 are per-CTA barrier slots of the
+// collectives; the last two rows hold per-source-rank arrival counters that
+// the fused GEMMs bump with one remote atomic per CTA (monotonic: the host
+// passes the value that means "every CTA of that rank has arrived").  A
+// counter lets one thread per CTA wait on W words instead of every thread
+// polling a slot per CTA, which floods L2 and starves incoming NVLink writes.
+constexpr int kCountRow = kMaxBlocks - 1;    // all-gather -> GEMM pushes
+constexpr int kRsCountRow = kMaxBlocks - 2;  // GEMM -> reduce-scatter tiles
+constexpr int kMaxCommBlocks = kMaxBlocks - 2;
 
 struct PeerCtx {
   void* data[kMaxRanks];     // staging region of every rank (this call's half)
@@ -30,6 +36,10 @@ struct PeerCtx {
   volatile int* status;  // host-mapped {code, peer, block, seq}
   unsigned long long timeout_ns;
 };
+
+MNB_DEVICE void red_release_sys_add(uint32_t* p, uint32_t v) {
+  asm volatile("red.release.sys.global.add.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
 
 // Record a timeout in the status block (first writer wins).
 MNB_DEVICE void report_timeout(volatile int* status, int peer, int block, uint32_t seq) {
@@ -54,7 +64,7 @@ MNB_DEVICE bool wait_signal(const uint32_t* slot, uint32_t value, volatile int* 
         report_timeout(status, peer, block, seq);
         return false;
       }
-      __nanosleep(64);
+      __nanosleep(spins < 4096 ? 64 : 256);
     }
   }
   return true;

@@ -45,9 +45,8 @@ STAGING_BYTES = int(os.environ.get("MINI_NCCL_STAGING_BYTES", 64 << 20))
 MAX_BLOCKS = int(os.environ.get("MINI_NCCL_DEVICE_BLOCKS", 255))
 
 _OPS = {"sum": 0, "prod": 1, "max": 2, "min": 3}
-kMaxRanks = 16
 OPNAMES = ["all_reduce", "reduce_scatter", "all_gather", "broadcast", "all_to_all", "barrier", "all_reduce_stepped",
-           "gemm_reduce_scatter", "all_gather_gemm"]
+           "gemm_reduce_scatter", "all_gather_gemm", "reduce_scatter_adamw"]
 
 
 def _ext():
@@ -241,6 +240,30 @@ class DeviceComm:
             self._finish(ev)
         return out
 
+    def reduce_scatter_adamw(self, flat_grad: torch.Tensor, param_shard: torch.Tensor, state: dict,
+                             *, lr: float, betas: tuple[float, float], eps: float, weight_decay: float,
+                             step: int, scale: float = 1.0, blocks: int | None = None) -> None:
+        """Reduce-scatter ``flat_grad`` and apply AdamW to this rank's shard, in one kernel.
+
+        ``state`` holds fp32 ``m``, ``v`` and (for bf16 parameters) ``master``
+        tensors of the shard's length; ``step`` is the 1-based step count of
+        this shard's moments.  Same update as :class:`ops.kernels.FusedAdamW`
+        (decoupled weight decay, bias-corrected moments), applied to
+        ``sum over ranks of flat_grad`` times ``scale`` (1/W for an average).
+        """
+        W = self.world_size
+        if flat_grad.numel() % W:
+            raise ValueError(f"gradient length {flat_grad.numel()} not divisible by world_size {W}")
+        b1, b2 = betas
+        self._ensure_staging(self.impl.staging_need(2, flat_grad.numel(), flat_grad.element_size()))
+        ev = self._record("reduce_scatter_adamw", "fused", flat_grad.numel() * flat_grad.element_size())
+        try:
+            self.impl.reduce_scatter_adamw(flat_grad, param_shard, state.get("master"), state["m"], state["v"],
+                                           float(lr), float(b1), float(b2), float(eps), float(weight_decay),
+                                           1.0 - b1 ** step, 1.0 - b2 ** step, float(scale), blocks or MAX_BLOCKS)
+        finally:
+            self._finish(ev)
+
     def all_gather(self, shard: torch.Tensor, out: torch.Tensor | None = None,
                    blocks: int | None = None) -> torch.Tensor:
         W = self.world_size
@@ -308,7 +331,8 @@ class DeviceComm:
     # ---- GEMMs fused with a collective (tensor parallelism, sequence-parallel layout) ---
 
     def gemm_reduce_scatter(self, x: torch.Tensor, w: torch.Tensor, *, w_mn: bool = False,
-                            bias: torch.Tensor | None = None, resid: torch.Tensor | None = None) -> torch.Tensor:
+                            bias: torch.Tensor | None = None, resid: torch.Tensor | None = None,
+                            force_kernel: bool = False, stamps: torch.Tensor | None = None) -> torch.Tensor:
         """``reduce_scatter_rows(x @ w^T) + bias + resid`` as one kernel.
 
         ``x`` [M, K] holds this rank's partial-sum input for all M rows (the
@@ -318,7 +342,11 @@ class DeviceComm:
         epilogue stores each finished tile into its owner's memory, so the
         transfer overlaps the remaining MMAs (replaces the reference's
         forward all-reduce in ``tensor_parallel.py:74-91`` with the
-        sequence-parallel reduce-scatter).
+        sequence-parallel reduce-scatter).  On one rank the plain GEMM runs
+        unless ``force_kernel`` (profiling the fused kernel on one GPU).
+        ``stamps`` (int64 [4], zeroed) receives ``%globaltimer`` phase times:
+        kernel start, last CTA's tiles done, last CTA saw every rank's tiles,
+        last CTA finished its reduction.
         """
         from .ops import kernels as K
 
@@ -327,13 +355,13 @@ class DeviceComm:
         N = w.shape[1] if w_mn else w.shape[0]
         if M % W:
             raise ValueError(f"rows {M} not divisible by world_size {W}")
-        if W == 1:
+        if W == 1 and not force_kernel:
             return K.gemm(x, w, b_mn=w_mn, bias=bias, resid=resid)
         self._ensure_staging(2 * M * N * 2)
         out = torch.empty(M // W, N, dtype=torch.bfloat16, device=x.device)
         ev = self._record("gemm_reduce_scatter", "fused", M * N * 2)
         try:
-            self.impl.gemm_rs(x.contiguous(), w, out, w_mn, bias, resid, K.status_word(x.device))
+            self.impl.gemm_rs(x.contiguous(), w, out, w_mn, bias, resid, K.status_word(x.device), stamps)
         finally:
             self._finish(ev)
         return out
@@ -341,14 +369,16 @@ class DeviceComm:
     def all_gather_gemm(self, x_shard: torch.Tensor, w: torch.Tensor, *, w_mn: bool = False,
                         bias: torch.Tensor | None = None, gelu_out_aux: torch.Tensor | None = None,
                         gelu_grad_aux: torch.Tensor | None = None, resid: torch.Tensor | None = None,
-                        gathered: torch.Tensor | None = None) -> tuple[torch.Tensor, torch.Tensor]:
+                        gathered: torch.Tensor | None = None,
+                        force_kernel: bool = False) -> tuple[torch.Tensor, torch.Tensor]:
         """``epi(all_gather_rows(x_shard) @ w^T)`` as one kernel; returns (out, gathered).
 
-        ``x_shard`` [M / W, K] is this rank's rows.  Gather warps inside the
-        GEMM copy every shard into ``gathered`` [M, K] (local memory; each
-        remote row crosses NVLink once) while the tiles of the local shard
-        compute; ``gathered`` is returned for reuse (the weight gradient needs
-        the full input).  With ``gelu_out_aux`` the epilogue is
+        ``x_shard`` [M / W, K] is this rank's rows.  Two warps inside every
+        CTA of the GEMM push this rank's shard into every peer's staging
+        (each row crosses NVLink once) while the tiles of the local shard
+        compute; a peer's tiles start as soon as that peer's pushes have all
+        arrived.  The gathered [M, K] input is copied into ``gathered`` for
+        reuse (the weight gradient needs it).  With ``gelu_out_aux`` the epilogue is
         ``out = gelu(acc + bias)``, ``aux = acc + bias``; with
         ``gelu_grad_aux`` it is ``out = acc * gelu'(aux)`` (an MLP backward).
         """
@@ -357,14 +387,13 @@ class DeviceComm:
         W = self.world_size
         rows, Kd = x_shard.shape
         N = w.shape[1] if w_mn else w.shape[0]
-        if W == 1:
+        if W == 1 and not force_kernel:
             out = K.gemm(x_shard, w, b_mn=w_mn, bias=bias, gelu_out_aux=gelu_out_aux, gelu_grad_aux=gelu_grad_aux,
                          resid=resid)
             return out, x_shard
         if gathered is None:
             gathered = torch.empty(rows * W, Kd, dtype=torch.bfloat16, device=x_shard.device)
-        ready = self._ag_ready()
-        self._ensure_staging(2 * rows * Kd * 2)
+        self._ensure_staging(2 * W * rows * Kd * 2)
         out = torch.empty(rows * W, N, dtype=torch.bfloat16, device=x_shard.device)
         if gelu_out_aux is not None and gelu_grad_aux is not None:
             raise ValueError("gelu_out_aux and gelu_grad_aux are exclusive")
@@ -372,17 +401,11 @@ class DeviceComm:
                                                                       else (0, None))
         ev = self._record("all_gather_gemm", "fused", rows * Kd * 2)
         try:
-            self.impl.ag_gemm(x_shard.contiguous(), w, out, gathered, ready, w_mn, bias, aux, resid, epi,
+            self.impl.ag_gemm(x_shard.contiguous(), w, out, gathered, w_mn, bias, aux, resid, epi,
                               K.status_word(x_shard.device))
         finally:
             self._finish(ev)
         return out, gathered
-
-    def _ag_ready(self) -> torch.Tensor:
-        buf = getattr(self, "_ready_buf", None)
-        if buf is None:
-            buf = self._ready_buf = torch.zeros(kMaxRanks, dtype=torch.int32, device=self.device)
-        return buf
 
     # ---- parity schedules -------------------------------------------------------------
 

@@ -18,6 +18,15 @@ destination buffer (no staging copy), and the gradient reduce-scatter reads
 peers' gradient buffers directly and applies the ``1/W`` scale in its
 epilogue.  ``prefetch=True`` issues the next unit's gather on a side stream
 while the current unit computes.
+
+``optimizer_in_backward=dict(lr=..., betas=..., eps=..., weight_decay=...)``
+fuses the shard's AdamW step into the gradient reduce-scatter: on CUDA one
+kernel pushes every gradient chunk to its owner, sums the W slots in rank
+order and updates the fp32 master shard and moments in the same pass (the
+reduced gradient never touches memory); shards then carry no ``.grad`` and
+the user's optimizer only steps the replicated parameters.  The update is the
+same decoupled-weight-decay AdamW as ``ops.kernels.FusedAdamW``; ``lr`` may be
+changed between steps through :attr:`FullyShardedDataParallel.shard_optimizer`.
 """
 
 from __future__ import annotations
@@ -60,7 +69,9 @@ class _Unit:
         self.device = self.params[0].device if self.params else torch.device("cpu")
         W = pg.world_size
         self.total_numel = sum(e[3] for e in self.entries)
-        self.padded_numel = -(-self.total_numel // W) * W
+        # CUDA shards are a multiple of 8 elements (16-byte vector access in the kernels)
+        quantum = W * (8 if self.device.type == "cuda" else 1)
+        self.padded_numel = -(-self.total_numel // quantum) * quantum
         self.shard_numel = self.padded_numel // W
 
         flat = torch.zeros(self.padded_numel, dtype=self.dtype, device=self.device)
@@ -124,6 +135,10 @@ class _Unit:
             if g is not None:
                 flat[at : at + n].copy_(g.reshape(-1))
             at += n
+        opt = self.owner.shard_optimizer if self.owner is not None else None
+        if opt is not None:
+            opt.step_unit(self, flat)
+            return None
         if W == 1:
             return flat
         if flat.is_cuda:
@@ -132,6 +147,56 @@ class _Unit:
 
     def gather_full_flat(self) -> torch.Tensor:
         return self._gather(self.shard)
+
+
+class ShardAdamW:
+    """AdamW applied to each unit's shard as part of its gradient reduce-scatter.
+
+    Hyper-parameters live in :attr:`hp` (``lr``, ``betas``, ``eps``,
+    ``weight_decay``) and are read at every step, so schedules can change
+    them.  State per unit: fp32 ``m``, ``v`` and, for low-precision
+    parameters, an fp32 ``master`` copy of the shard; ``step`` counts the
+    unit's updates (bias correction).
+    """
+
+    def __init__(self, lr: float = 3e-4, betas: tuple[float, float] = (0.9, 0.95), eps: float = 1e-8,
+                 weight_decay: float = 0.1) -> None:
+        self.hp = {"lr": lr, "betas": tuple(betas), "eps": eps, "weight_decay": weight_decay}
+        self.state: dict[int, dict] = {}
+
+    def _state(self, unit: _Unit) -> dict:
+        st = self.state.get(id(unit))
+        if st is None:
+            shard = unit.shard.detach()
+            st = {"step": 0, "m": torch.zeros(shard.numel(), dtype=torch.float32, device=shard.device),
+                  "v": torch.zeros(shard.numel(), dtype=torch.float32, device=shard.device)}
+            if shard.dtype != torch.float32:
+                st["master"] = shard.float().clone()
+            self.state[id(unit)] = st
+        return st
+
+    @torch.no_grad()
+    def step_unit(self, unit: _Unit, flat_grad: torch.Tensor) -> None:
+        st = self._state(unit)
+        st["step"] += 1
+        W = unit.pg.world_size
+        hp = self.hp
+        if flat_grad.is_cuda:
+            unit.pg.device_comm().reduce_scatter_adamw(
+                flat_grad, unit.shard.data, st, lr=hp["lr"], betas=hp["betas"], eps=hp["eps"],
+                weight_decay=hp["weight_decay"], step=st["step"], scale=1.0 / W)
+            return
+        g = flat_grad if W == 1 else collectives.reduce_scatter(unit.pg, flat_grad, op="sum")
+        g = g.float() / W
+        b1, b2 = hp["betas"]
+        w = st["master"] if "master" in st else unit.shard.data
+        st["m"].mul_(b1).add_(g, alpha=1 - b1)
+        st["v"].mul_(b2).addcmul_(g, g, value=1 - b2)
+        w.mul_(1 - hp["lr"] * hp["weight_decay"])
+        denom = (st["v"] / (1 - b2 ** st["step"])).sqrt_().add_(hp["eps"])
+        w.addcdiv_(st["m"] / (1 - b1 ** st["step"]), denom, value=-hp["lr"])
+        if "master" in st:
+            unit.shard.data.copy_(w)
 
 
 class _ShardedForward(torch.autograd.Function):
@@ -207,11 +272,13 @@ class FullyShardedDataParallel(nn.Module):
         unit_cls: type | tuple[type, ...] | None = None,
         units: list[nn.Module] | None = None,
         prefetch: bool = False,
+        optimizer_in_backward: dict | None = None,
     ) -> None:
         super().__init__()
         if unit_cls is None and units is None:
             raise ValueError("pass unit_cls or units to say what should be sharded")
         self.pg = pg
+        self.shard_optimizer = ShardAdamW(**optimizer_in_backward) if optimizer_in_backward is not None else None
         self.units: list[_Unit] = []
         self._live_bytes = 0
         self.peak_materialized_bytes = 0

@@ -34,6 +34,7 @@ KERNELS_PER_CALL = {
     "barrier": 1,
     "stepped_all_reduce": 1,
     "gemm_rs": 1,
+    "reduce_scatter_adamw": 1,
     "ag_gemm": 1,
 }
 

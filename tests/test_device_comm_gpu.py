@@ -273,3 +273,50 @@ def _fused_tp(pg) -> None:
 @needs2
 def test_fused_gemm_collectives_on_gpus():
     run(_fused_tp, 2, timeout=600.0, devices="cuda", op_timeout=60.0)
+
+
+def _fsdp_opt_in_backward(pg) -> None:
+    """FSDP with AdamW fused into the reduce-scatter kernel == FSDP + FusedAdamW."""
+    import copy
+
+    import torch.nn.functional as F
+    from torch import nn
+
+    from mini_nccl_b200.fsdp import FullyShardedDataParallel
+    from mini_nccl_b200.ops.kernels import FusedAdamW
+
+    dev = torch.device("cuda", torch.cuda.current_device())
+
+    class Block(nn.Module):
+        def __init__(self):
+            super().__init__()
+            self.fc1 = nn.Linear(64, 256)
+            self.fc2 = nn.Linear(256, 64)
+
+        def forward(self, x):
+            return x + self.fc2(torch.relu(self.fc1(x)))
+
+    torch.manual_seed(0)
+    base = nn.Sequential(Block(), Block()).to(dev, torch.bfloat16)
+    hp = dict(lr=1e-3, betas=(0.9, 0.95), eps=1e-8, weight_decay=0.1)
+    fused = FullyShardedDataParallel(copy.deepcopy(base), pg, unit_cls=Block, optimizer_in_backward=hp)
+    plain = FullyShardedDataParallel(copy.deepcopy(base), pg, unit_cls=Block)
+    opt = FusedAdamW(plain.parameters(), **hp)
+    g = torch.Generator().manual_seed(5 + pg.rank)
+    for _ in range(4):
+        x = torch.randn(32, 64, generator=g).to(dev, torch.bfloat16)
+        for model in (fused, plain):
+            model.zero_grad()
+            F.mse_loss(model(x).float(), torch.zeros(32, 64, device=dev)).backward()
+            model.sync()
+        opt.step()
+    pg.device_comm().synchronize()
+    a, b = fused.full_state_dict(), plain.full_state_dict()
+    for name in a:
+        err = (a[name].float() - b[name].float()).abs().max().item()
+        assert err <= 2e-2 * (b[name].float().abs().max().item() + 1e-3), (name, err)
+
+
+@needs2
+def test_fsdp_optimizer_in_backward_on_gpus():
+    run(_fsdp_opt_in_backward, 2, timeout=600.0, devices="cuda", op_timeout=60.0)

@@ -175,3 +175,35 @@ def _sharded_ckpt(pg, path) -> None:
 
 def test_sharded_checkpoint_round_trip(tmp_path) -> None:
     run(_sharded_ckpt, 2, str(tmp_path))
+
+
+def _opt_in_backward(pg, steps: int = 4) -> None:
+    """AdamW fused into the gradient reduce-scatter == single-process AdamW."""
+    W, per = pg.world_size, 6
+    torch.manual_seed(0)
+    model = Model()
+    ref = copy.deepcopy(model)
+    hp = dict(lr=1e-2, betas=(0.9, 0.95), eps=1e-8, weight_decay=0.1)
+    fsdp = FullyShardedDataParallel(model, pg, unit_cls=Block, optimizer_in_backward=hp)
+    rest = torch.optim.AdamW([p for p in fsdp.parameters() if all(p is not u.shard for u in fsdp.units)], **hp)
+    ref_opt = torch.optim.AdamW(ref.parameters(), **hp)
+    gen = torch.Generator().manual_seed(11)
+    for _ in range(steps):
+        x = torch.randn(W * per, 8, generator=gen)
+        y = torch.randn(W * per, 1, generator=gen)
+        mine = slice(pg.rank * per, (pg.rank + 1) * per)
+        fsdp.zero_grad()
+        F.mse_loss(fsdp(x[mine]), y[mine]).backward()
+        assert all(u.shard.grad is None for u in fsdp.units)  # consumed inside the reduce-scatter
+        fsdp.sync()
+        rest.step()
+        ref_opt.zero_grad()
+        F.mse_loss(ref(x), y).backward()
+        ref_opt.step()
+    state = fsdp.full_state_dict()
+    for name, p in ref.named_parameters():
+        torch.testing.assert_close(state[name], p.detach(), rtol=1e-4, atol=1e-5, msg=lambda m, n=name: f"{n}: {m}")
+
+
+def test_optimizer_in_backward_matches_single_process() -> None:
+    run(_opt_in_backward, 2)
