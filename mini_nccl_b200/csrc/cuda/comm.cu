@@ -1082,15 +1082,30 @@ class DeviceCommImpl {
     TORCH_CHECK(2 * full <= segs_[staging_].bytes, "staging buffer too small for the fused all-gather");
     CommArgs a = base_args(staging_, 0, x_shard.data_ptr(), out.data_ptr(), x_shard.numel(), 8, bytes, 1);
     auto stream = at::cuda::getCurrentCUDAStream();
-    // my own row block of the gathered operand; peers' blocks arrive by push
-    ck(cudaMemcpyAsync(static_cast<uint8_t*>(a.data[rank_]) + rank_ * bytes, x_shard.data_ptr(), bytes,
-                       cudaMemcpyDeviceToDevice, stream),
-       "shard copy");
+    // Peers' row blocks arrive by push.  My own rows are read in place when
+    // they tile evenly (128-row tiles); otherwise they are copied into my block.
+    const bool own_in_place = x_shard.size(0) % 128 == 0;
+    uint8_t* mine = static_cast<uint8_t*>(a.data[rank_]);
+    if (!own_in_place)
+      ck(cudaMemcpyAsync(mine + rank_ * bytes, x_shard.data_ptr(), bytes, cudaMemcpyDeviceToDevice, stream),
+         "shard copy");
     gemm_fused(2, x_shard, w, out, w_mn, bias, aux, resid, epi, status, peer_ctx(a), &ag_base_, c10::nullopt);
     if (gathered) {
       TORCH_CHECK(gathered->is_contiguous() && gathered->numel() * gathered->element_size() == full,
                   "gathered must be a contiguous [M, K] bf16 tensor");
-      ck(cudaMemcpyAsync(gathered->data_ptr(), a.data[rank_], full, cudaMemcpyDeviceToDevice, stream), "gathered copy");
+      uint8_t* g8 = static_cast<uint8_t*>(gathered->data_ptr());
+      if (own_in_place) {  // blocks before mine, mine from the input, blocks after mine
+        if (rank_ > 0) ck(cudaMemcpyAsync(g8, mine, rank_ * bytes, cudaMemcpyDeviceToDevice, stream), "gathered copy");
+        ck(cudaMemcpyAsync(g8 + rank_ * bytes, x_shard.data_ptr(), bytes, cudaMemcpyDeviceToDevice, stream),
+           "gathered copy");
+        const int64_t after = full - (rank_ + 1) * bytes;
+        if (after > 0)
+          ck(cudaMemcpyAsync(g8 + (rank_ + 1) * bytes, mine + (rank_ + 1) * bytes, after, cudaMemcpyDeviceToDevice,
+                             stream),
+             "gathered copy");
+      } else {
+        ck(cudaMemcpyAsync(g8, mine, full, cudaMemcpyDeviceToDevice, stream), "gathered copy");
+      }
     }
   }
 

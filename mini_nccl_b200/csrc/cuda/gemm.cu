@@ -87,6 +87,7 @@ struct GemmArgs {
   const __nv_bfloat16* ag_local;    // AG: this rank's shard of A, [rows_per_rank, K]
   uint32_t ag_target;               // AG: counter value meaning "every CTA of that rank has pushed"
   uint32_t rs_target;               // RS: counter value meaning "every CTA of that rank has stored its tiles"
+  int ag_own_map;                   // AG: own rows are read through map_own from the input (rows % 128 == 0)
   unsigned long long* stamps;       // optional %globaltimer phase stamps (CTA 0 / slowest CTA), or null
 };
 
@@ -458,7 +459,7 @@ template <int BN, bool A_MN, bool B_MN, int STAGES, int FUSE>
 __global__ void __launch_bounds__(gemm_threads<FUSE>(), 1)
     gemm_tcgen05_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
                         const __grid_constant__ CUtensorMap map_out, const __grid_constant__ CUtensorMap map_aux,
-                        const GemmArgs args, const PeerCtx ctx) {
+                        const __grid_constant__ CUtensorMap map_own, const GemmArgs args, const PeerCtx ctx) {
   using S = GemmSmem<BN, STAGES>;
   constexpr uint32_t kIdesc = idesc_bf16(kBM, BN, A_MN, B_MN);
   constexpr uint32_t kTmemCols = 2 * BN;
@@ -542,7 +543,10 @@ __global__ void __launch_bounds__(gemm_threads<FUSE>(), 1)
           const uint32_t sb = smem_u32(ring_b + stage * S::b_bytes);
           const int k0 = kb * kBK;
           if (!A_MN) {
-            tma_load_2d(sa, &map_a, k0, mb * kBM, full);
+            if (FUSE == kFuseAG && args.ag_own_map && mb * kBM / args.rows_per_rank == ctx.rank)
+              tma_load_2d(sa, &map_own, k0, mb * kBM - ctx.rank * args.rows_per_rank, full);  // own rows, in place
+            else
+              tma_load_2d(sa, &map_a, k0, mb * kBM, full);
           } else {
 #pragma unroll
             for (int j = 0; j < kBM / 64; ++j) tma_load_2d(sa + j * 8192, &map_a, mb * kBM + 64 * j, k0, full);
@@ -778,7 +782,8 @@ int num_sms() {
 
 template <int BN, bool A_MN, bool B_MN, int STAGES, int FUSE = kFuseNone>
 void launch_gemm(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& mo, const CUtensorMap& mx,
-                 const GemmArgs& args, int units, cudaStream_t stream, const PeerCtx& ctx = PeerCtx{}) {
+                 const GemmArgs& args, int units, cudaStream_t stream, const PeerCtx& ctx = PeerCtx{},
+                 const CUtensorMap* mown = nullptr) {
   using S = GemmSmem<BN, STAGES>;
   auto kern = gemm_tcgen05_kernel<BN, A_MN, B_MN, STAGES, FUSE>;
   static bool configured = false;
@@ -789,7 +794,7 @@ void launch_gemm(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap
   // Fused launches wait on one another across CTAs (and ranks): one CTA per
   // SM at most, so every CTA of the grid is resident at once.
   const int grid = std::min(units, num_sms());
-  kern<<<grid, gemm_threads<FUSE>(), S::total, stream>>>(ma, mb, mo, mx, args, ctx);
+  kern<<<grid, gemm_threads<FUSE>(), S::total, stream>>>(ma, mb, mo, mx, mown ? *mown : ma, args, ctx);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
@@ -913,8 +918,9 @@ void gemm(torch::Tensor a, torch::Tensor b, torch::Tensor out, bool a_mn, bool b
 //            out = [M / world, N] (this rank's rows), bias [N] and resid
 //            [M / world, N] are added once, after the reduction.
 //   kFuseAG: a = X shard [M / world, K]; the gathered [M, K] is built in
-//            this call's staging region (ctx.data[rank]), whose own row block
-//            the caller has already filled.
+//            this call's staging region (ctx.data[rank]); with rows % 128 == 0
+//            the own rows are read in place from `a`, else the caller has
+//            copied them into their block of the staging region.
 //   *ag_base is the running total of increments of this mode's arrival
 //   counters (advanced here by this launch's grid: one per CTA per rank).
 void gemm_fused(int fuse, torch::Tensor a, torch::Tensor b, torch::Tensor out, bool b_mn,
@@ -945,7 +951,7 @@ void gemm_fused(int fuse, torch::Tensor a, torch::Tensor b, torch::Tensor out, b
     TORCH_CHECK(stamps->scalar_type() == at::kLong && stamps->numel() >= 4 && stamps->is_cuda(), "stamps: int64 [4]");
     args.stamps = reinterpret_cast<unsigned long long*>(stamps->data_ptr());
   }
-  CUtensorMap ma, mo, mx;
+  CUtensorMap ma, mo, mx, mown;
   const bool wide = N >= 256;
   const int BN = wide ? 256 : 128;
   if (fuse == kFuseRS) {
@@ -969,7 +975,7 @@ void gemm_fused(int fuse, torch::Tensor a, torch::Tensor b, torch::Tensor out, b
     args.epi = 0;
     args.tma_out = 0;
     ma = make_tma_2d_bf16(a.data_ptr(), K, M, lda, 64, kBM);
-    mo = mx = ma;
+    mo = mx = mown = ma;
   } else {
     const int rows = static_cast<int>(a.size(0));
     const int M = rows * W;
@@ -998,7 +1004,9 @@ void gemm_fused(int fuse, torch::Tensor a, torch::Tensor b, torch::Tensor out, b
     TORCH_CHECK(!(args.epi & kEpiAccum), "AG-GEMM epilogues: bias, GELU, GELU', residual");
     TORCH_CHECK(!(args.epi & (kEpiGelu | kEpiGeluGrad)) || aux.has_value(), "GELU epilogues need aux");
     args.tma_out = 1;
+    args.ag_own_map = rows % kBM == 0 ? 1 : 0;
     ma = make_tma_2d_bf16(ctx.data[ctx.rank], K, M, K, 64, kBM);
+    mown = make_tma_2d_bf16(a.data_ptr(), K, rows, K, 64, kBM);
     mo = make_tma_2d_bf16(out.data_ptr(), N, M, out.stride(0), 64, 32);
     mx = (args.epi & kEpiGelu) ? make_tma_2d_bf16(aux->data_ptr(), N, M, args.ldaux, 64, 32) : mo;
   }
@@ -1012,7 +1020,7 @@ void gemm_fused(int fuse, torch::Tensor a, torch::Tensor b, torch::Tensor out, b
   const bool gelu = (args.epi & kEpiGelu) != 0;
 #define MNB_FUSED(BNV, BMJ, ST, F)                                                   \
   if (BN == BNV && b_mn == BMJ) {                                                   \
-    launch_gemm<BNV, false, BMJ, ST, F>(ma, mb, mo, mx, args, units, stream, ctx);   \
+    launch_gemm<BNV, false, BMJ, ST, F>(ma, mb, mo, mx, args, units, stream, ctx, &mown); \
     return;                                                                         \
   }
   if (fuse == kFuseRS) {
