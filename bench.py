@@ -23,6 +23,11 @@ by a barrier and torch.cuda.synchronize() on both sides, max over ranks:
    copies that step's inputs from pinned host memory and reads the loss back
    to the host.
 
+``--mode fsdp`` runs BASELINE config 4 instead: GPT 24 layers, d_model 2048,
+16 heads, sequence 2048, micro-batch 4 per GPU, one FSDP unit per block with
+parameters, gradients and AdamW state sharded N ways (fp32 master weights;
+ours fuses each block's AdamW step into its gradient reduce-scatter).
+
 Arms: ``ours`` (this library: sm_100a kernels, peer-memory DDP all-reduce),
 ``reference`` (the unmodified reference package from baseline/_ref with its
 own example GPT; gradients averaged with its GPU entry point
@@ -46,10 +51,22 @@ from pathlib import Path
 ROOT = Path(__file__).resolve().parent
 REF_ROOT = ROOT / "baseline" / "_ref"
 
-VOCAB, SEQ, LAYERS, HEADS, EMBD = 50304, 1024, 12, 12, 768
-MICRO_BATCH = 16
+VOCAB = 50304
 BUCKET_MB = 25.0
-METRIC = "GPT tok/s/box (DDP)"
+# (layers, d_model, heads, seq, micro-batch per GPU) of each BASELINE config
+MODES = {
+    "ddp": dict(layers=12, embd=768, heads=12, seq=1024, micro=16, metric="GPT tok/s/box (DDP)"),
+    "fsdp": dict(layers=24, embd=2048, heads=16, seq=2048, micro=4, metric="GPT tok/s/box (FSDP)"),
+}
+LAYERS, EMBD, HEADS, SEQ, MICRO_BATCH = 12, 768, 12, 1024, 16  # the default (DDP) config
+METRIC = MODES["ddp"]["metric"]
+
+
+def set_mode(mode: str) -> None:
+    """Point the module-level config at one BASELINE config."""
+    global LAYERS, EMBD, HEADS, SEQ, MICRO_BATCH, METRIC
+    m = MODES[mode]
+    LAYERS, EMBD, HEADS, SEQ, MICRO_BATCH, METRIC = m["layers"], m["embd"], m["heads"], m["seq"], m["micro"], m["metric"]
 
 
 def parse_args():
@@ -58,7 +75,9 @@ def parse_args():
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference", "torch"], default="ours")
-    ap.add_argument("--micro-batch", type=int, default=MICRO_BATCH)
+    ap.add_argument("--mode", choices=sorted(MODES), default="ddp",
+                    help="ddp: config 3 (default); fsdp: config 4")
+    ap.add_argument("--micro-batch", type=int, default=None)
     ap.add_argument("--no-e2e", action="store_true", help="skip the end-to-end phase")
     return ap.parse_args()
 
@@ -188,14 +207,14 @@ def emit(args, world, impl, ms, e2e_ms, clocks, launches, extra=None):
         "dtype": "bf16",
         "data": "synthetic uniform token ids, random-init weights",
         "config": {
-            "model": f"GPT {LAYERS}L/{EMBD}/{HEADS}H V{VOCAB} T{SEQ} (124M, tied head)",
+            "model": f"GPT {LAYERS}L/{EMBD}/{HEADS}H V{VOCAB} T{SEQ} (tied head)",
             "global_batch": world * args.micro_batch,
             "micro_batch_per_gpu": args.micro_batch,
             "seq_len": SEQ,
-            "parallelism": f"dp{world}",
-            "bucket_mb": BUCKET_MB,
+            "parallelism": f"{args.mode if args.mode != 'ddp' else 'dp'}{world}",
+            "bucket_mb": BUCKET_MB if args.mode == "ddp" else None,
             "optimizer": "AdamW(0.9,0.95,wd0.1), fp32 master",
-            "l2": "no flush: per-step working set (activations, 124M params, grads, Adam state) >> 126 MB L2",
+            "l2": "no flush: per-step working set (activations, params, grads, Adam state) >> 126 MB L2",
         },
         "clocks": clocks.summary(),
         "impl": impl,
@@ -235,8 +254,18 @@ def run_ours(args):
         pg = mn.ProcessGroup(0, 1, device=dev)
     torch.manual_seed(0)
     model = GPT(VOCAB, SEQ, LAYERS, HEADS, EMBD).to(dev, torch.bfloat16)
-    ddp = mn.DistributedDataParallel(model, pg, bucket_cap_mb=BUCKET_MB, overlap=True, algorithm="auto")
-    opt = FusedAdamW(model.parameters(), lr=3e-4, betas=(0.9, 0.95), weight_decay=0.1)
+    hp = dict(lr=3e-4, betas=(0.9, 0.95), weight_decay=0.1)
+    if args.mode == "fsdp":
+        from mini_nccl_b200.models.gpt import Block
+
+        # one unit per block; each block's AdamW runs inside its gradient reduce-scatter
+        ddp = mn.FullyShardedDataParallel(model, pg, unit_cls=Block, prefetch=True,
+                                          optimizer_in_backward=dict(hp, eps=1e-8))
+        shard_ids = {id(u.shard) for u in ddp.units}
+        opt = FusedAdamW([p for p in ddp.parameters() if id(p) not in shard_ids], **hp)
+    else:
+        ddp = mn.DistributedDataParallel(model, pg, bucket_cap_mb=BUCKET_MB, overlap=True, algorithm="auto")
+        opt = FusedAdamW(model.parameters(), **hp)
     B = args.micro_batch
     xs, ys = batches_on_device(torch, 4, B, dev, seed=1000 + rank)
 
@@ -308,6 +337,12 @@ def _store_addrs(torch, rank, world):
 
 def run_reference(args):
     rank, world, local = env_rank()
+    if args.mode != "ddp":
+        if rank == 0:
+            print(json.dumps({"impl": "reference", "unavailable":
+                              f"the reference's {args.mode} path moves tensors over TCP from host memory only "
+                              "(mini_nccl/transport.py byte_view); it has no GPU path for this config"}))
+        return
     if not (REF_ROOT / "mini_nccl" / "__init__.py").exists() or not (REF_ROOT / "examples" / "model.py").exists():
         if rank == 0:
             print(json.dumps({"impl": "reference", "unavailable":
@@ -405,31 +440,47 @@ def run_torch(args):
     xs, ys = batches_on_device(torch, 4, B, dev, seed=1000 + rank)
     import torch.nn.functional as F
 
-    class StockGPT(torch.nn.Module):
-        """The same parameters run through stock torch ops only (cuBLAS, SDPA)."""
+    class StockBlock(torch.nn.Module):
+        """One block of the same parameters through stock torch ops (cuBLAS, SDPA)."""
 
+        def __init__(self, blk):
+            super().__init__()
+            self.ln1, self.qkv, self.proj, self.ln2, self.mlp = blk.ln1, blk.qkv, blk.proj, blk.ln2, blk.mlp
+            self.n_head = blk.n_head
+
+        def forward(self, h):
+            Bq, T, C = h.shape
+            q, k, v = self.qkv(self.ln1(h)).split(C, dim=-1)
+            q, k, v = (t.view(Bq, T, self.n_head, C // self.n_head).transpose(1, 2) for t in (q, k, v))
+            a = F.scaled_dot_product_attention(q, k, v, is_causal=True)
+            h = h + self.proj(a.transpose(1, 2).reshape(Bq, T, C))
+            return h + self.mlp(self.ln2(h))
+
+    class StockGPT(torch.nn.Module):
         def __init__(self, m):
             super().__init__()
-            self.m = m
+            self.tok_emb, self.pos_emb, self.ln_f, self.head = m.tok_emb, m.pos_emb, m.ln_f, m.head
+            self.blocks = torch.nn.ModuleList(StockBlock(b) for b in m.blocks)
 
         def forward(self, x, y):
-            m = self.m
             T = x.shape[1]
-            h = m.tok_emb(x) + m.pos_emb[:, :T]
-            for blk in m.blocks:
-                C = h.shape[-1]
-                q, k, v = blk.qkv(blk.ln1(h)).split(C, dim=-1)
-                q, k, v = (t.view(x.shape[0], T, blk.n_head, C // blk.n_head).transpose(1, 2) for t in (q, k, v))
-                a = F.scaled_dot_product_attention(q, k, v, is_causal=True)
-                h = h + blk.proj(a.transpose(1, 2).reshape(x.shape[0], T, C))
-                h = h + blk.mlp(blk.ln2(h))
-            logits = m.head(m.ln_f(h))
+            h = self.tok_emb(x) + self.pos_emb[:, :T]
+            for blk in self.blocks:
+                h = blk(h)
+            logits = self.head(self.ln_f(h))
             return F.cross_entropy(logits.view(-1, logits.shape[-1]).float(), y.view(-1))
 
     net = StockGPT(model)
-    if world > 1:
+    if world > 1 and args.mode == "fsdp":
+        from torch.distributed.fsdp import MixedPrecisionPolicy, fully_shard
+
+        mp = MixedPrecisionPolicy(param_dtype=torch.bfloat16, reduce_dtype=torch.float32)
+        for blk in net.blocks:
+            fully_shard(blk, mp_policy=mp)
+        fully_shard(net, mp_policy=mp)
+    elif world > 1:
         net = torch.nn.parallel.DistributedDataParallel(net, bucket_cap_mb=BUCKET_MB)
-    opt = torch.optim.AdamW(model.parameters(), lr=3e-4, betas=(0.9, 0.95), weight_decay=0.1, fused=True)
+    opt = torch.optim.AdamW(net.parameters(), lr=3e-4, betas=(0.9, 0.95), weight_decay=0.1, fused=True)
 
     def train(x, y):
         opt.zero_grad(set_to_none=True)
@@ -472,6 +523,9 @@ def run_torch(args):
 
 def main():
     args = parse_args()
+    set_mode(args.mode)
+    if args.micro_batch is None:
+        args.micro_batch = MICRO_BATCH
     _, world, _ = env_rank()
     if args.gpus != world:
         raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={world}: launch N>1 with torch.distributed.run")

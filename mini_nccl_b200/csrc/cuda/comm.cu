@@ -616,6 +616,53 @@ MNB_DEVICE void adam_update(const AdamArgs& o, long long e, float g) {
   else reinterpret_cast<float*>(o.param)[e] = w;
 }
 
+// Eight consecutive elements e0..e0+7 (16-byte aligned groups): vector loads
+// and stores of the fp32 state and the parameter.
+template <bool P_BF16>
+MNB_DEVICE void adam_update8(const AdamArgs& o, long long e0, const float* g) {
+  float w[8], m[8], v[8];
+  auto ld8 = [](const float* p, float* d) {
+    const float4 a = *reinterpret_cast<const float4*>(p), b = *reinterpret_cast<const float4*>(p + 4);
+    d[0] = a.x; d[1] = a.y; d[2] = a.z; d[3] = a.w; d[4] = b.x; d[5] = b.y; d[6] = b.z; d[7] = b.w;
+  };
+  auto st8 = [](float* p, const float* d) {
+    *reinterpret_cast<float4*>(p) = make_float4(d[0], d[1], d[2], d[3]);
+    *reinterpret_cast<float4*>(p + 4) = make_float4(d[4], d[5], d[6], d[7]);
+  };
+  ld8(o.m + e0, m);
+  ld8(o.v + e0, v);
+  if (o.master) {
+    ld8(o.master + e0, w);
+  } else if (P_BF16) {
+    const uint4 raw = *reinterpret_cast<const uint4*>(reinterpret_cast<const __nv_bfloat16*>(o.param) + e0);
+    const uint32_t rs[4] = {raw.x, raw.y, raw.z, raw.w};
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const float2 f = unpack_bf16x2(rs[j]);
+      w[2 * j] = f.x;
+      w[2 * j + 1] = f.y;
+    }
+  } else {
+    ld8(reinterpret_cast<const float*>(o.param) + e0, w);
+  }
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    m[i] = o.b1 * m[i] + (1.f - o.b1) * g[i];
+    v[i] = o.b2 * v[i] + (1.f - o.b2) * g[i] * g[i];
+    w[i] -= o.lr * o.wd * w[i];
+    w[i] -= o.lr * (m[i] * o.c1) / (sqrtf(v[i] * o.c2) + o.eps);
+  }
+  st8(o.m + e0, m);
+  st8(o.v + e0, v);
+  if (o.master) st8(o.master + e0, w);
+  if (P_BF16) {
+    *reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(o.param) + e0) =
+        make_uint4(pack_bf16x2(w[0], w[1]), pack_bf16x2(w[2], w[3]), pack_bf16x2(w[4], w[5]), pack_bf16x2(w[6], w[7]));
+  } else {
+    st8(reinterpret_cast<float*>(o.param) + e0, w);
+  }
+}
+
 template <typename TG, bool P_BF16>
 __global__ void __launch_bounds__(kCommThreads) rs_adamw_kernel(CommArgs a, AdamArgs o) {
   constexpr int V = Vec<TG>::n;
@@ -656,7 +703,13 @@ __global__ void __launch_bounds__(kCommThreads) rs_adamw_kernel(CommArgs a, Adam
           for (int i = 0; i < V; ++i) g[i] = p == 0 ? x[i] : g[i] + x[i];
         }
 #pragma unroll
-        for (int i = 0; i < V; ++i) adam_update<P_BF16>(o, u * V + i, g[i] * a.scale);
+        for (int i = 0; i < V; ++i) g[i] *= a.scale;
+        if constexpr (V == 8) {
+          adam_update8<P_BF16>(o, u * V, g);
+        } else {
+#pragma unroll
+          for (int i = 0; i < V; ++i) adam_update<P_BF16>(o, u * V + i, g[i]);
+        }
       }
     } else {
       for (long long e = lo + threadIdx.x; e < hi; e += blockDim.x) {

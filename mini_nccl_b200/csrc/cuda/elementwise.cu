@@ -184,6 +184,66 @@ __global__ void layernorm_bwd_kernel(const __nv_bfloat16* __restrict__ dy, const
   for (int i = threadIdx.x; i < 2 * C; i += blockDim.x) mine[i] = sacc[i];
 }
 
+// Wide rows (C = 8 * blockDim.x, e.g. 2048 / 4096): one block per row, each
+// thread owns 8 columns; the two row sums go through a block reduction, and
+// each thread keeps its columns' weight-gradient sums in registers across
+// the rows its block visits.  Per-block partials as above.
+__global__ void __launch_bounds__(512) layernorm_bwd_wide_kernel(
+    const __nv_bfloat16* __restrict__ dy, const __nv_bfloat16* __restrict__ x, const __nv_bfloat16* __restrict__ w,
+    const float* __restrict__ mean, const float* __restrict__ rstd, __nv_bfloat16* __restrict__ dx,
+    float* __restrict__ part, int rows, int C) {
+  __shared__ float red[2][16][2];
+  const int c0 = threadIdx.x * 8;
+  const int lane = threadIdx.x % 32, warp = threadIdx.x / 32, nw = blockDim.x / 32;
+  float ww[8], dg[8], dbb[8];
+  load8(w + c0, ww);
+#pragma unroll
+  for (int j = 0; j < 8; ++j) dg[j] = dbb[j] = 0.f;
+  int par = 0;
+  for (int row = blockIdx.x; row < rows; row += gridDim.x, par ^= 1) {
+    const long long off = static_cast<long long>(row) * C + c0;
+    float xh[8], g[8];
+    load8(x + off, xh);
+    load8(dy + off, g);
+    const float mu = mean[row], rs = rstd[row];
+    float a = 0.f, bsum = 0.f;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      xh[j] = (xh[j] - mu) * rs;
+      const float d = g[j] * ww[j];
+      a += d;
+      bsum += d * xh[j];
+      dg[j] += g[j] * xh[j];
+      dbb[j] += g[j];
+    }
+    a = warp_sum(a);
+    bsum = warp_sum(bsum);
+    if (lane == 0) {
+      red[par][warp][0] = a;
+      red[par][warp][1] = bsum;
+    }
+    __syncthreads();  // double-buffered by row parity: one barrier per row
+    a = 0.f;
+    bsum = 0.f;
+    for (int i = 0; i < nw; ++i) {
+      a += red[par][i][0];
+      bsum += red[par][i][1];
+    }
+    a /= C;
+    bsum /= C;
+    float o[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) o[j] = rs * (g[j] * ww[j] - a - xh[j] * bsum);
+    store8(dx + off, o);
+  }
+  float* mine = part + static_cast<long long>(blockIdx.x) * 2 * C;
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    mine[c0 + j] = dg[j];
+    mine[C + c0 + j] = dbb[j];
+  }
+}
+
 // out[c] (+)= sum over `nparts` rows of part[:, c]; bf16 or fp32 destination.
 // Block = 32 columns x 8 warps; warp w sums parts w, w+8, ... and the 8 warp
 // sums are combined in shared memory, so long part lists stay parallel.
@@ -619,6 +679,11 @@ void layernorm_bwd(torch::Tensor dy, torch::Tensor x, torch::Tensor w, torch::Te
   else if (C == 512) launch(layernorm_bwd_kernel<2>);
   else if (C == 768) launch(layernorm_bwd_kernel<3>);
   else if (C == 1024) launch(layernorm_bwd_kernel<4>);
+  else if (C % 256 == 0 && C >= 1536 && C <= 4096)
+    layernorm_bwd_wide_kernel<<<blocks, C / 8, 0, stream>>>(
+        reinterpret_cast<const __nv_bfloat16*>(dy.data_ptr()), reinterpret_cast<const __nv_bfloat16*>(x.data_ptr()),
+        reinterpret_cast<const __nv_bfloat16*>(w.data_ptr()), mean.data_ptr<float>(), rstd.data_ptr<float>(),
+        reinterpret_cast<__nv_bfloat16*>(dx.data_ptr()), partials.data_ptr<float>(), rows, C);
   else launch(layernorm_bwd_kernel<0>);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
   const bool f32 = dw.scalar_type() == at::kFloat;

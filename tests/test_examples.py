@@ -76,3 +76,18 @@ def test_multinode_allreduce_env_bootstrap() -> None:
     outs = [p.communicate(timeout=300)[0] for p in procs]
     assert all(p.returncode == 0 for p in procs), outs
     assert "world_size=2" in outs[0] and "1048576" in outs[0], outs[0]
+
+
+@pytest.mark.examples
+def test_launch_multinode_script_runs_local_ranks(tmp_path) -> None:
+    """The ssh launcher with every rank on this host (no ssh needed)."""
+    from mini_nccl_b200.launcher import _free_ports
+
+    port = _free_ports(1)[0]
+    hosts = tmp_path / "hosts.txt"
+    hosts.write_text(f"# two ranks on this machine\n127.0.0.1:{port}:2\n")
+    out = subprocess.run(["bash", "examples/launch_multinode.sh", str(hosts), "examples/multinode_allreduce.py",
+                          "--max-mib", "1", "--iters", "1"], cwd=ROOT, capture_output=True, text=True, timeout=300)
+    assert out.returncode == 0, out.stdout + out.stderr
+    assert f"hosts=127.0.0.1:{port},127.0.0.1:{port + 1}" in out.stdout
+    assert "world_size=2" in out.stdout and "1048576" in out.stdout

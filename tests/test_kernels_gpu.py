@@ -102,15 +102,16 @@ def test_gemm_split_k_accumulate():
     close(dw, want, 1e-2)
 
 
-def test_layernorm_forward_backward():
-    x = rnd(1000, 768, seed=15).requires_grad_(True)
-    w = (1 + 0.1 * rnd(768, seed=16).float()).to(torch.bfloat16).requires_grad_(True)
-    b = rnd(768, seed=17, scale=0.1).requires_grad_(True)
-    gy = rnd(1000, 768, seed=18)
+@pytest.mark.parametrize("rows,C", [(1000, 768), (777, 2048), (300, 4096), (64, 640)])
+def test_layernorm_forward_backward(rows, C):
+    x = rnd(rows, C, seed=15).requires_grad_(True)
+    w = (1 + 0.1 * rnd(C, seed=16).float()).to(torch.bfloat16).requires_grad_(True)
+    b = rnd(C, seed=17, scale=0.1).requires_grad_(True)
+    gy = rnd(rows, C, seed=18)
     y = K.LayerNorm.apply(x, w, b, 1e-5)
     y.backward(gy)
     xr, wr, br = (t.detach().float().requires_grad_(True) for t in (x, w, b))
-    yr = F.layer_norm(xr, (768,), wr, br, 1e-5)
+    yr = F.layer_norm(xr, (C,), wr, br, 1e-5)
     yr.backward(gy.float())
     close(y, yr, 2e-2)
     close(x.grad, xr.grad, 3e-2)
