@@ -23,6 +23,12 @@ by a barrier and torch.cuda.synchronize() on both sides, max over ranks:
    copies that step's inputs from pinned host memory and reads the loss back
    to the host.
 
+``--mode 3d`` runs BASELINE config 5: GPT 32 layers, d_model 4096, 32 heads,
+sequence 2048, on a tp x pp x dp mesh (N=8: 2 x 2 x 2; N=4: 2 x 2 x 1; N=2:
+2 x 1 x 1), 1F1B over 8 microbatches of 2 sequences per pipeline, sequence-
+parallel TP whose GEMM / collective pairs run as fused kernels, stage
+send/recv over NCCL p2p; total work per step is fixed (strong scaling).
+
 ``--mode fsdp`` runs BASELINE config 4 instead: GPT 24 layers, d_model 2048,
 16 heads, sequence 2048, micro-batch 4 per GPU, one FSDP unit per block with
 parameters, gradients and AdamW state sharded N ways (fp32 master weights;
@@ -57,7 +63,15 @@ BUCKET_MB = 25.0
 MODES = {
     "ddp": dict(layers=12, embd=768, heads=12, seq=1024, micro=16, metric="GPT tok/s/box (DDP)"),
     "fsdp": dict(layers=24, embd=2048, heads=16, seq=2048, micro=4, metric="GPT tok/s/box (FSDP)"),
+    # 3D: micro = sequences per microbatch; MICROBATCHES of them per pipeline per step
+    "3d": dict(layers=32, embd=4096, heads=32, seq=2048, micro=2, metric="GPT tok/s/box (3D TPxPPxDP)"),
 }
+MICROBATCHES = 8
+
+
+def mesh_dims(world: int) -> tuple[int, int, int]:
+    """(dp, pp, tp) for the 3D config on N GPUs: tp first, then pp, then dp."""
+    return {1: (1, 1, 1), 2: (1, 1, 2), 4: (1, 2, 2), 8: (2, 2, 2)}[world]
 LAYERS, EMBD, HEADS, SEQ, MICRO_BATCH = 12, 768, 12, 1024, 16  # the default (DDP) config
 METRIC = MODES["ddp"]["metric"]
 
@@ -76,7 +90,7 @@ def parse_args():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference", "torch"], default="ours")
     ap.add_argument("--mode", choices=sorted(MODES), default="ddp",
-                    help="ddp: config 3 (default); fsdp: config 4")
+                    help="ddp: config 3 (default); fsdp: config 4; 3d: config 5 (N in 1, 2, 4, 8)")
     ap.add_argument("--micro-batch", type=int, default=None)
     ap.add_argument("--no-e2e", action="store_true", help="skip the end-to-end phase")
     return ap.parse_args()
@@ -191,7 +205,12 @@ def run_phases(torch, args, step_fn, barrier, reduce_max, dev, clocks: ClockSamp
 
 
 def emit(args, world, impl, ms, e2e_ms, clocks, launches, extra=None):
-    tokens = world * args.micro_batch * SEQ * args.steps
+    if args.mode == "3d":
+        dp, pp, tp = mesh_dims(world)
+        seqs = dp * MICROBATCHES * args.micro_batch  # per step, whole job
+    else:
+        seqs = world * args.micro_batch
+    tokens = seqs * SEQ * args.steps
     value = tokens / (ms / 1e3)
     line = {
         "metric": METRIC,
@@ -202,16 +221,19 @@ def emit(args, world, impl, ms, e2e_ms, clocks, launches, extra=None):
         "warmup": args.warmup,
         "ms_per_step": round(ms / args.steps, 3),
         "higher_is_better": True,
-        "scaling": "weak",
+        "scaling": "strong" if args.mode == "3d" else "weak",
         "vs_baseline": None,
         "dtype": "bf16",
         "data": "synthetic uniform token ids, random-init weights",
         "config": {
-            "model": f"GPT {LAYERS}L/{EMBD}/{HEADS}H V{VOCAB} T{SEQ} (tied head)",
-            "global_batch": world * args.micro_batch,
+            "model": f"GPT {LAYERS}L/{EMBD}/{HEADS}H V{VOCAB} T{SEQ}"
+                     + (" (head untied: it lives on the last pipeline stage)" if args.mode == "3d" else " (tied head)"),
+            "global_batch": seqs,
             "micro_batch_per_gpu": args.micro_batch,
             "seq_len": SEQ,
-            "parallelism": f"{args.mode if args.mode != 'ddp' else 'dp'}{world}",
+            "parallelism": (("tp{2}xpp{1}xdp{0}, 1F1B x{3} microbatches, sequence parallel".format(
+                *mesh_dims(world), MICROBATCHES)) if args.mode == "3d"
+                else f"{args.mode if args.mode != 'ddp' else 'dp'}{world}"),
             "bucket_mb": BUCKET_MB if args.mode == "ddp" else None,
             "optimizer": "AdamW(0.9,0.95,wd0.1), fp32 master",
             "l2": "no flush: per-step working set (activations, params, grads, Adam state) >> 126 MB L2",
@@ -223,7 +245,7 @@ def emit(args, world, impl, ms, e2e_ms, clocks, launches, extra=None):
         line["e2e"] = {
             "value": round(tokens / (e2e_ms / 1e3), 1),
             "unit": "tokens/s",
-            "h2d_bytes_per_step": 2 * args.micro_batch * SEQ * 8,
+            "h2d_bytes_per_step": (2 * MICROBATCHES if args.mode == "3d" else 2) * args.micro_batch * SEQ * 8,
             "d2h_bytes_per_step": 4,
             "ms_per_step": round(e2e_ms / args.steps, 3),
         }
@@ -237,9 +259,92 @@ def emit(args, world, impl, ms, e2e_ms, clocks, launches, extra=None):
 # ---------------------------------------------------------------------------
 # ours
 # ---------------------------------------------------------------------------
+def run_ours_3d(args):
+    """Config 5: tensor x pipeline x data parallel GPT (fused TP kernels, 1F1B over NCCL p2p)."""
+    import torch
+
+    sys.path.insert(0, str(ROOT))
+    import mini_nccl_b200 as mn
+    from mini_nccl_b200.models.tp_gpt import GPTStage, sync_tensor_parallel_grads
+    from mini_nccl_b200.ops.kernels import FusedAdamW
+
+    rank, world, local = env_rank()
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    dp, pp, tp = mesh_dims(world)
+    if world > 1:
+        pg = mn.init_process_group(rank, world, device=dev, op_timeout=300.0, nccl_p2p=pp > 1)
+    else:
+        pg = mn.ProcessGroup(0, 1, device=dev)
+    mesh = mn.ParallelMesh(pg, dp=dp, pp=pp, tp=tp)
+    dpg, ppg, tpg = mesh.group("dp"), mesh.group("pp"), mesh.group("tp")
+    d, s = mesh.coordinate("dp"), mesh.coordinate("pp")
+    torch.manual_seed(1000 + s)  # replicated parameters identical across the tp group and the replicas
+    with torch.device(dev):  # billions of parameters: initialise on the GPU
+        stage = GPTStage(VOCAB, SEQ, LAYERS, HEADS, EMBD, tpg, s, pp, sequence_parallel=tp > 1)
+    stage = stage.to(torch.bfloat16)
+    B = args.micro_batch
+    act = (SEQ // tp, B, EMBD) if tp > 1 else (B, SEQ, EMBD)
+    pipe = mn.PipelineParallel(stage, ppg, activation_shape=act, loss_fn=stage.loss if s == pp - 1 else None,
+                               schedule="1f1b", dtype=torch.bfloat16, device=dev)
+    opt = FusedAdamW(stage.parameters(), lr=3e-4, betas=(0.9, 0.95), weight_decay=0.1)
+    first, last = s == 0, s == pp - 1
+    n_seq = MICROBATCHES * B
+    xs, ys = batches_on_device(torch, 2, n_seq, dev, seed=1000 + d)
+    params = list(stage.parameters())
+
+    def train(x, y):
+        opt.zero_grad(set_to_none=True)
+        loss = pipe.step(x if first else None, y if last else None, n_microbatches=MICROBATCHES)
+        sync_tensor_parallel_grads(stage, tpg)
+        if dp > 1:
+            mn.average_gradients(dpg, params)
+        opt.step()
+        return loss
+
+    def step(i):
+        train(xs[i % 2], ys[i % 2])
+
+    hx = torch.empty((n_seq, SEQ), dtype=torch.int64).pin_memory()
+    hy = torch.empty((n_seq, SEQ), dtype=torch.int64).pin_memory()
+    gen = torch.Generator().manual_seed(77 + d)
+    losses = []
+
+    def e2e_step(i):
+        torch.randint(0, VOCAB, (n_seq, SEQ), generator=gen, out=hx)
+        torch.randint(0, VOCAB, (n_seq, SEQ), generator=gen, out=hy)
+        x = hx.to(dev, non_blocking=True) if first else None
+        y = hy.to(dev, non_blocking=True) if last else None
+        losses.append(train(x, y))  # the pipeline returns the loss as a host float on the last stage
+
+    def barrier():
+        if world > 1:
+            mn.collectives.barrier(pg)
+
+    def reduce_max(v):
+        if world == 1:
+            return v
+        t = torch.tensor([v], dtype=torch.float64)
+        mn.collectives.all_reduce(pg, t, op="max")
+        return float(t.item())
+
+    clocks = ClockSampler(dev.index)
+    ms, e2e_ms, n_launch = run_phases(torch, args, step, barrier, reduce_max, dev, clocks, e2e_step)
+    if world > 1:
+        pg.device_comm().synchronize()
+    final = torch.tensor([losses[-1] if (losses and last) else 0.0], dtype=torch.float64)
+    if world > 1:
+        mn.collectives.all_reduce(pg, final, op="max")
+    if rank == 0:
+        emit(args, world, "ours", ms, e2e_ms, clocks, n_launch, {"final_loss": round(float(final.item()), 4)})
+    pg.close()
+
+
 def run_ours(args):
     import torch
 
+    if args.mode == "3d":
+        return run_ours_3d(args)
     sys.path.insert(0, str(ROOT))
     import mini_nccl_b200 as mn
     from mini_nccl_b200.models.gpt import GPT
@@ -425,6 +530,12 @@ def run_reference(args):
 def run_torch(args):
     import torch
     import torch.distributed as dist
+
+    if args.mode == "3d":
+        if env_rank()[0] == 0:
+            print(json.dumps({"impl": "torch", "unavailable": "no stock-torch tensor x pipeline parallel GPT is "
+                              "provided for config 5; compare against --impl ours with --mode ddp/fsdp arms"}))
+        return
 
     sys.path.insert(0, str(ROOT))
     from mini_nccl_b200.models.gpt import GPT

@@ -71,11 +71,11 @@ MUTATIONS: list[Mutation] = [
       "    for dst in range(1, W):\n        pg.send(flat.clone().zero_(), dst)\n",
       ["tests/test_collectives.py::test_collective_battery"],
       "rank 0 sends garbage instead of the result"),
-    M("split-remainder-to-the-end", "mini_nccl_b200/collectives.py",
-      "    sizes = [q + (i < extra) for i in range(parts)]\n",
-      "    sizes = [q + (i >= parts - extra) for i in range(parts)]\n",
+    M("split-drops-remainder", "mini_nccl_b200/collectives.py",
+      "    sizes = [q + (i < extra) for i in range(parts)]\n    return list(torch.split(flat, sizes))\n",
+      "    sizes = [q for i in range(parts)]\n    return list(torch.split(flat[: q * parts], sizes))\n",
       ["tests/test_collectives.py::test_multichannel_large_allreduce"],
-      "ranks still agree, but channel splits change shape -> the remainder rule is pinned"),
+      "the last n % channels elements of a multi-channel all-reduce are never reduced"),
     M("wire-not-rounded", "mini_nccl_b200/collectives.py",
       "        view = self.out[: x.numel()]\n        view.copy_(x)\n        return view\n",
       "        return x\n",
@@ -94,8 +94,8 @@ MUTATIONS: list[Mutation] = [
     M("ddp-bucket-order", "mini_nccl_b200/parallel/ddp.py",
       "        for p in reversed(list(self.module.parameters())):\n",
       "        for p in list(self.module.parameters()):\n",
-      ["tests/test_overlap.py::test_overlap_dispatches_the_reduction_during_backward"],
-      "buckets follow registration order, so the first bucket fills last and nothing overlaps"),
+      ["tests/test_ddp.py::test_gradients_live_in_the_buckets"],
+      "buckets follow registration order, so the first bucket to fill is reduced last"),
     M("fsdp-rng-not-replayed", "mini_nccl_b200/parallel/fsdp.py",
       "                torch.set_rng_state(ctx.cpu_rng)\n",
       "                pass\n",
@@ -138,8 +138,8 @@ MUTATIONS: list[Mutation] = [
       ["tests/test_faults.py::test_desync_times_out_with_diagnosis"],
       "every collective gets the same sequence number, so desyncs are invisible"),
     M("staging-no-stream-order", "mini_nccl_b200/device.py",
-      "        self.orderings += 1\n",
-      "        return\n",
+      "    staging.order_after_compute()\n",
+      "    pass\n",
       ["tests/test_device_staging.py::test_every_exchange_orders_the_copy_stream_behind_compute"],
       "the copy stream may read a block before the compute stream has reduced into it"),
     M("control-docstring", "mini_nccl_b200/collectives.py",

@@ -152,3 +152,65 @@ def _degenerate(pg):
 
 def test_degenerate_dimensions_reduce_to_data_parallel() -> None:
     run(_degenerate, 4, timeout=120.0)
+
+
+def _gpt_3d(pg):
+    """GPTStage (TP + SP blocks, 1F1B pipeline, DP replicas) == one process, same weights."""
+    import types
+
+    from mini_nccl_b200.models.tp_gpt import GPTStage, sync_tensor_parallel_grads
+
+    V, T, L, H, Cw = 37, 8, 2, 4, 16
+    mesh = ParallelMesh(pg, dp=2, pp=2, tp=2)
+    dp, pp, tp = mesh.group("dp"), mesh.group("pp"), mesh.group("tp")
+    d, s = mesh.coordinate("dp"), mesh.coordinate("pp")
+    torch.manual_seed(123)
+    solo = types.SimpleNamespace(world_size=1, rank=0)
+    ref = GPTStage(V, T, L, H, Cw, solo, 0, 1, sequence_parallel=False)
+    stage = GPTStage(V, T, L, H, Cw, tp, s, 2, sequence_parallel=True)
+    per = L // 2
+    with torch.no_grad():
+        if s == 0:
+            stage.tok_emb.weight.copy_(ref.tok_emb.weight)
+            stage.pos_emb.copy_(ref.pos_emb)
+        else:
+            stage.ln_f.load_state_dict(ref.ln_f.state_dict())
+            stage.head.weight.copy_(ref.head.weight)
+        for j, blk in enumerate(stage.blocks):
+            rb = ref.blocks[s * per + j]
+            blk.ln1.load_state_dict(rb.ln1.state_dict())
+            blk.ln2.load_state_dict(rb.ln2.state_dict())
+            blk.attn.qkv.load_full_weight(rb.attn.qkv.weight, rb.attn.qkv.bias)
+            blk.attn.proj.load_full_weight(rb.attn.proj.weight, rb.attn.proj.bias)
+            blk.mlp.up.load_full_weight(rb.mlp.up.weight, rb.mlp.up.bias)
+            blk.mlp.down.load_full_weight(rb.mlp.down.weight, rb.mlp.down.bias)
+    g = torch.Generator().manual_seed(7)
+    idx = torch.randint(0, V, (8, T), generator=g)  # 2 replicas x 2 microbatches x 2 sequences
+    tgt = torch.randint(0, V, (8, T), generator=g)
+    # reference: the whole batch at once
+    ref.loss(ref(idx), tgt).backward()
+    # 3D: this replica's half, two microbatches through the pipeline
+    pipe = PipelineParallel(stage, pp, activation_shape=(T // 2, 2, Cw), loss_fn=stage.loss if s == 1 else None)
+    mine = slice(4 * d, 4 * d + 4)
+    pipe.step(idx[mine] if s == 0 else None, tgt[mine] if s == 1 else None, n_microbatches=2)
+    sync_tensor_parallel_grads(stage, tp)
+    average_gradients(dp, list(stage.parameters()))
+    close = dict(rtol=2e-4, atol=2e-6)
+    if s == 0:
+        torch.testing.assert_close(stage.tok_emb.weight.grad, ref.tok_emb.weight.grad, **close)
+    else:
+        torch.testing.assert_close(stage.head.weight.grad, ref.head.weight.grad, **close)
+        torch.testing.assert_close(stage.ln_f.weight.grad, ref.ln_f.weight.grad, **close)
+    for j, blk in enumerate(stage.blocks):
+        rb = ref.blocks[s * per + j]
+        torch.testing.assert_close(blk.ln1.weight.grad, rb.ln1.weight.grad, **close)
+        torch.testing.assert_close(blk.attn.proj.bias.grad, rb.attn.proj.bias.grad, **close)
+        a, n = blk.mlp.up.shard_start, blk.mlp.up.shard_size
+        torch.testing.assert_close(blk.mlp.up.weight.grad, rb.mlp.up.weight.grad[a : a + n], **close)
+        rows = blk.attn.qkv.shard_rows
+        torch.testing.assert_close(blk.attn.qkv.weight.grad, rb.attn.qkv.weight.grad.index_select(0, rows), **close)
+    return True
+
+
+def test_gpt_stage_3d_matches_single_process() -> None:
+    run(_gpt_3d, 8, timeout=300.0)
