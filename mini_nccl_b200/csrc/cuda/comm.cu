@@ -811,6 +811,79 @@ __global__ void __launch_bounds__(kCommThreads) move_kernel(CommArgs a, int kind
   ring_end(a, ok);
 }
 
+// ---------------------------------------------------------------------------
+// broadcast as scatter + all-gather (W >= 4): the root's NVLink egress would
+// otherwise carry (W-1) copies of the message.
+//   phase A  the root stores chunk c of the message into rank c's staging
+//   phase B  rank c stores chunk c into every other non-root rank's staging
+//            (the root sends its own chunk from its input)
+//   phase C  non-root ranks copy the staging out.
+// Every rank's egress is about one message.  Each block moves the same
+// sub-range of every chunk in every phase, so the per-block barriers order
+// exactly the data that block depends on.
+// ---------------------------------------------------------------------------
+__global__ void __launch_bounds__(kCommThreads) bcast_scatter_gather_kernel(CommArgs a) {
+  ring_begin(a);
+  const int W = a.world, r = a.rank, root = a.root;
+  const long long nb = a.n;
+  const bool v16 = nb % 16 == 0;
+  const long long unit = v16 ? 16 : 1;
+  const long long units = nb / unit;
+  const long long cu = (units + W - 1) / W;  // units per chunk
+  const long long sub = (cu + gridDim.x - 1) / gridDim.x;
+  const uint8_t* in = reinterpret_cast<const uint8_t*>(a.in);
+  auto range = [&](int c, long long* lo, long long* hi) {  // this block's units of chunk c
+    const long long c0 = min(units, c * cu), c1 = min(units, c0 + cu);
+    *lo = min(c1, c0 + sub * blockIdx.x);
+    *hi = min(c1, *lo + sub);
+  };
+  auto copy = [&](const uint8_t* src, uint8_t* dst, long long lo, long long hi, bool volatile_src) {
+    if (!v16) {
+      for (long long u = lo + threadIdx.x; u < hi; u += blockDim.x)
+        dst[u] = volatile_src ? *reinterpret_cast<const volatile uint8_t*>(src + u) : src[u];
+      return;
+    }
+    constexpr int U = 4;
+    for (long long u0 = lo + threadIdx.x; u0 < hi; u0 += U * blockDim.x) {
+      uint4 w[U];
+#pragma unroll
+      for (int j = 0; j < U; ++j)
+        if (u0 + j * blockDim.x < hi)
+          w[j] = volatile_src ? ld_v4_cg(src + 16 * (u0 + j * blockDim.x)) : ld_v4(src + 16 * (u0 + j * blockDim.x));
+#pragma unroll
+      for (int j = 0; j < U; ++j)
+        if (u0 + j * blockDim.x < hi) st_v4(dst + 16 * (u0 + j * blockDim.x), w[j]);
+    }
+  };
+  long long lo, hi;
+  if (r == root) {
+    for (int k = 1; k < W; ++k) {
+      const int c = (r + k) % W;
+      range(c, &lo, &hi);
+      copy(in, reinterpret_cast<uint8_t*>(a.data[c]), lo, hi, false);
+    }
+  }
+  bool ok = peer_barrier(a, a.epoch + 1);
+  if (ok) {
+    range(r, &lo, &hi);
+    const uint8_t* src = r == root ? in : reinterpret_cast<const uint8_t*>(a.data[r]);
+    for (int k = 1; k < W; ++k) {
+      const int p = (r + k) % W;
+      if (p != root) copy(src, reinterpret_cast<uint8_t*>(a.data[p]), lo, hi, r != root);
+    }
+    ok = peer_barrier(a, a.epoch + 2);
+  }
+  if (ok) {
+    uint8_t* out = reinterpret_cast<uint8_t*>(a.out);
+    for (int c = 0; c < W; ++c) {
+      range(c, &lo, &hi);
+      if (r != root) copy(reinterpret_cast<const uint8_t*>(a.data[r]), out, lo, hi, true);
+      else if (a.out != a.in) copy(in, out, lo, hi, false);
+    }
+  }
+  ring_end(a, ok);
+}
+
 __global__ void barrier_kernel(CommArgs a) {
   ring_begin(a);
   const bool ok = peer_barrier(a, a.epoch + 1);
@@ -1295,10 +1368,16 @@ class DeviceCommImpl {
     const int64_t in_bytes = in.numel() * in.element_size();
     const int64_t nb = kind == 2 ? in_bytes / world_ : in_bytes;
     TORCH_CHECK(staging_need(kind == 1 ? 4 : 3, nb, 1) <= segs_[staging_].bytes, "staging buffer too small");
-    CommArgs a = base_args(staging_, 0, in.data_ptr(), out.data_ptr(), nb, 2 + kind, in_bytes, 1);
+    const bool scatter_gather = kind == 1 && world_ >= 4;
+    CommArgs a = base_args(staging_, 0, in.data_ptr(), out.data_ptr(), nb, 2 + kind, in_bytes, scatter_gather ? 2 : 1);
     a.root = root;
-    const int blocks = blocks_for(nb, max_blocks);
-    move_kernel<<<blocks, kCommThreads, 0, at::cuda::getCurrentCUDAStream()>>>(a, kind);
+    if (scatter_gather) {
+      const int blocks = blocks_for(nb / world_, max_blocks);
+      bcast_scatter_gather_kernel<<<blocks, kCommThreads, 0, at::cuda::getCurrentCUDAStream()>>>(a);
+    } else {
+      const int blocks = blocks_for(nb, max_blocks);
+      move_kernel<<<blocks, kCommThreads, 0, at::cuda::getCurrentCUDAStream()>>>(a, kind);
+    }
     C10_CUDA_KERNEL_LAUNCH_CHECK();
   }
 
