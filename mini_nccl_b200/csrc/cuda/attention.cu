@@ -541,4 +541,39 @@ void flash_attn_bwd(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Te
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
+void flash_attn_bwd_tc_launch(torch::Tensor qkv, torch::Tensor dout, torch::Tensor lse, torch::Tensor delta,
+                              torch::Tensor dq_acc, torch::Tensor dqkv, int64_t n_head, double scale,
+                              torch::Tensor status);
+
+// tcgen05 backward: qkv / dqkv [B, T, 3C] contiguous, o / dout [B, T, C]
+// contiguous, lse [B, H, T]; dq_acc [B, T, C] fp32 and delta [B, H, T] fp32
+// are scratch.  T % 128 == 0, head dim 64 or 128.
+void flash_attn_bwd_tc(torch::Tensor qkv, torch::Tensor o, torch::Tensor dout, torch::Tensor lse, torch::Tensor dqkv,
+                       torch::Tensor dq_acc, torch::Tensor delta, int64_t n_head, double scale, torch::Tensor status) {
+  TORCH_CHECK(o.is_contiguous() && dout.is_contiguous(), "o and dout must be contiguous");
+  const int B = static_cast<int>(qkv.size(0)), T = static_cast<int>(qkv.size(1));
+  const int H = static_cast<int>(n_head);
+  const int C = static_cast<int>(qkv.size(2)) / 3;
+  const int D = C / H;
+  c10::cuda::CUDAGuard g(qkv.device());
+  auto stream = at::cuda::getCurrentCUDAStream();
+  const long long rows = static_cast<long long>(B) * T * H;
+  C10_CUDA_CHECK(cudaMemsetAsync(dq_acc.data_ptr(), 0, dq_acc.numel() * sizeof(float), stream));
+  auto dot = [&](auto kern) {
+    kern<<<static_cast<unsigned>((rows + 7) / 8), 256, 0, stream>>>(
+        reinterpret_cast<const __nv_bfloat16*>(o.data_ptr()), reinterpret_cast<const __nv_bfloat16*>(dout.data_ptr()),
+        delta.data_ptr<float>(), H, T, rows);
+  };
+  if (D == 64) dot(fa::fa_bwd_dot_kernel<64>);
+  else if (D == 128) dot(fa::fa_bwd_dot_kernel<128>);
+  else TORCH_CHECK(false, "tcgen05 attention backward supports head dim 64 or 128");
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+  flash_attn_bwd_tc_launch(qkv, dout, lse, delta, dq_acc, dqkv, n_head, scale, status);
+  const long long n2 = rows * D / 2;
+  fa::fa_dq_convert_kernel<<<static_cast<unsigned>(std::min<long long>((n2 + 255) / 256, 148 * 16)), 256, 0,
+                             stream>>>(dq_acc.data_ptr<float>(), reinterpret_cast<__nv_bfloat16*>(dqkv.data_ptr()),
+                                       3LL * C, C, static_cast<long long>(B) * T);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
 }  // namespace mnb

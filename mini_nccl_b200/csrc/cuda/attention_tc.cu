@@ -322,6 +322,289 @@ __global__ void __launch_bounds__(kThreads, D == 64 ? 2 : 1)
   }
 }
 
+// ===========================================================================
+// Backward on tcgen05.  One CTA owns 128 keys (tile j) of one (batch, head)
+// and walks the query tiles i >= j (causal).  TMEM lanes are keys:
+//   S^T  = K_j Q_i^T          (M=128 keys, N=128 queries, K=D)  cols [0, 128)
+//   dP^T = V_j dO_i^T         (same shape)                      cols [128, 256)
+//   dV  += P^T dO_i           (M=keys, N=D, K=queries)          cols [256, 256+D)
+//   dK  += dS^T Q_i           (M=keys, N=D, K=queries)          cols [256+D, 256+2D)
+//   dQ_i = dS K_j             (M=queries, N=D, K=keys)          cols [128, 128+D) (reuses dP^T)
+// The compute warps turn S^T into P^T = exp(S^T*scale - lse) and dP^T into
+// dS^T = scale * P^T (dP^T - delta), both bf16 in 128-byte-swizzled shared
+// memory.  The same dS^T tile is the K-major A operand of dK and, read
+// MN-major (queries contiguous), the A operand of dQ.  dQ_i leaves TMEM as
+// fp32 vector atomics into a [B, T, C] accumulator; dK and dV are written
+// once at the end.  Warp roles as in the forward (producer, MMA, 8 compute).
+// ===========================================================================
+constexpr int kBwdThreads = 64 + 32 * 8;
+
+template <int D, int STAGES>
+struct BwdSmem {
+  static constexpr uint32_t tile = 128 * D * 2;  // one [128 rows x D] bf16 tile
+  static constexpr uint32_t k_off = 0;
+  static constexpr uint32_t v_off = tile;
+  static constexpr uint32_t stage_bytes = 2 * tile + 2 * 128 * 4;  // Q, dO, lse, delta
+  static constexpr uint32_t st_off = 2 * tile;
+  static constexpr uint32_t p_off = st_off + STAGES * stage_bytes;
+  static constexpr uint32_t ds_off = p_off + 128 * 128 * 2;
+  static constexpr uint32_t bar_off = ds_off + 128 * 128 * 2;
+  static constexpr int n_bars = 12 + 2 * STAGES;
+  static constexpr uint32_t total = bar_off + n_bars * 8 + 16 + 1024;
+  static_assert(st_off % 1024 == 0 && p_off % 1024 == 0 && ds_off % 1024 == 0, "1 KiB aligned tiles");
+};
+
+// 64 values -> bf16 row `r` of a [128 x 64] 128-byte-swizzled atom, chunk group c (32 values).
+MNB_DEVICE void store_swizzled32(uint8_t* atom, int r, int c, const float* v) {
+#pragma unroll
+  for (int q8 = 0; q8 < 4; ++q8) {
+    const int chunk = c * 4 + q8;
+    const uint32_t off = (r / 8) * 1024 + (r % 8) * 128 + ((chunk ^ (r % 8)) * 16);
+    const float* f = v + 8 * q8;
+    *reinterpret_cast<uint4*>(atom + off) = make_uint4(pack_bf16x2(f[0], f[1]), pack_bf16x2(f[2], f[3]),
+                                                       pack_bf16x2(f[4], f[5]), pack_bf16x2(f[6], f[7]));
+  }
+}
+
+template <int D, int STAGES>
+__global__ void __launch_bounds__(kBwdThreads, 1)
+    fa_bwd_tc_kernel(const __grid_constant__ CUtensorMap map_qkv, const __grid_constant__ CUtensorMap map_do,
+                     const float* __restrict__ lse, const float* __restrict__ delta, float* __restrict__ dq_acc,
+                     __nv_bfloat16* __restrict__ dqkv, int H, int T, float scale, int* status) {
+  using S = BwdSmem<D, STAGES>;
+  constexpr uint32_t kTmemCols = 512;
+  constexpr uint32_t kIdSq = idesc_bf16(128, 128, false, false);  // S^T, dP^T
+  constexpr uint32_t kIdKV = idesc_bf16(128, D, false, true);     // dV, dK
+  constexpr uint32_t kIdQ = idesc_bf16(128, D, true, true);       // dQ
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const uint32_t sbase = smem_u32(sm);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sm + S::bar_off);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + S::n_bars);
+  const uint32_t b0 = smem_u32(bars);
+  const uint32_t kv_full = b0, s_full = b0 + 8, s_free = b0 + 16, dp_full = b0 + 24, p_full = b0 + 32,
+                 p_free = b0 + 40, ds_full = b0 + 48, ds_free = b0 + 56, dq_full = b0 + 64, dq_free = b0 + 72,
+                 acc_full = b0 + 80;
+  const uint32_t q_full0 = b0 + 96, q_empty0 = q_full0 + 8 * STAGES;
+
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  const int j = blockIdx.x;  // key tile; j = 0 has the most query tiles, so it starts first
+  const int bh = blockIdx.y;
+  const int b = bh / H, h = bh % H;
+  const int C = H * D;
+  const int n_q = T / 128;
+  const int n_it = n_q - j;
+
+  if (threadIdx.x == 0) {
+    mbar_init(kv_full, 1);
+    mbar_init(s_full, 1);
+    mbar_init(s_free, 256);
+    mbar_init(dp_full, 1);
+    mbar_init(p_full, 256);
+    mbar_init(p_free, 1);
+    mbar_init(ds_full, 256);
+    mbar_init(ds_free, 1);
+    mbar_init(dq_full, 1);
+    mbar_init(dq_free, 256);
+    mbar_init(acc_full, 1);
+    for (int st = 0; st < STAGES; ++st) {
+      mbar_init(q_full0 + 8 * st, 1);
+      mbar_init(q_empty0 + 8 * st, 1);
+    }
+    fence_mbar_init();
+    tma_prefetch_desc(&map_qkv);
+    tma_prefetch_desc(&map_do);
+  }
+  if (warp == 1) {
+    tmem_alloc(smem_u32(tmem_slot), kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  const uint32_t tS = tmem, tP = tmem + 128, tV = tmem + 256, tK = tmem + 256 + D;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      const int row0 = b * T;
+      mbar_arrive_expect_tx(kv_full, 2 * S::tile);
+#pragma unroll
+      for (int c = 0; c < D / 64; ++c) {
+        tma_load_2d(sbase + S::k_off + c * 16384, &map_qkv, C + h * D + c * 64, row0 + j * 128, kv_full);
+        tma_load_2d(sbase + S::v_off + c * 16384, &map_qkv, 2 * C + h * D + c * 64, row0 + j * 128, kv_full);
+      }
+      for (int it = 0; it < n_it; ++it) {
+        const int i = j + it, st = it % STAGES;
+        if (!mbar_wait(q_empty0 + 8 * st, ((it / STAGES) & 1) ^ 1, status)) break;
+        const uint32_t qf = q_full0 + 8 * st;
+        const uint32_t so = sbase + S::st_off + st * S::stage_bytes;
+        mbar_arrive_expect_tx(qf, 2 * S::tile + 2 * 128 * 4);
+#pragma unroll
+        for (int c = 0; c < D / 64; ++c) {
+          tma_load_2d(so + c * 16384, &map_qkv, h * D + c * 64, row0 + i * 128, qf);
+          tma_load_2d(so + S::tile + c * 16384, &map_do, h * D + c * 64, row0 + i * 128, qf);
+        }
+        const float* lsrc = lse + (static_cast<long long>(b) * H + h) * T + i * 128;
+        const float* dsrc = delta + (static_cast<long long>(b) * H + h) * T + i * 128;
+        asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], 512, [%2];"
+                     ::"r"(so + 2 * S::tile), "l"(lsrc), "r"(qf) : "memory");
+        asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], 512, [%2];"
+                     ::"r"(so + 2 * S::tile + 512), "l"(dsrc), "r"(qf) : "memory");
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      bool ok = mbar_wait(kv_full, 0, status);
+      const uint32_t ka = sbase + S::k_off, va = sbase + S::v_off;
+      const uint32_t pa = sbase + S::p_off, dsa = sbase + S::ds_off;
+      for (int it = 0; it < n_it && ok; ++it) {
+        const int st = it % STAGES;
+        const uint32_t par = it & 1;
+        const uint32_t qa = sbase + S::st_off + st * S::stage_bytes, doa = qa + S::tile;
+        ok = mbar_wait(q_full0 + 8 * st, (it / STAGES) & 1, status) && mbar_wait(s_free, par ^ 1, status);
+        if (!ok) break;
+        tc_fence_after();
+#pragma unroll
+        for (int kk = 0; kk < D / 16; ++kk)  // S^T = K Q^T
+          tc_mma(tS, smem_desc_sw128(ka + (kk / 4) * 16384 + (kk % 4) * 32, 16, 1024),
+                 smem_desc_sw128(qa + (kk / 4) * 16384 + (kk % 4) * 32, 16, 1024), kIdSq, kk > 0 ? 1u : 0u);
+        tc_commit(s_full);
+        if (!(ok = mbar_wait(dq_free, par ^ 1, status))) break;
+        tc_fence_after();
+#pragma unroll
+        for (int kk = 0; kk < D / 16; ++kk)  // dP^T = V dO^T
+          tc_mma(tP, smem_desc_sw128(va + (kk / 4) * 16384 + (kk % 4) * 32, 16, 1024),
+                 smem_desc_sw128(doa + (kk / 4) * 16384 + (kk % 4) * 32, 16, 1024), kIdSq, kk > 0 ? 1u : 0u);
+        tc_commit(dp_full);
+        if (!(ok = mbar_wait(p_full, par, status))) break;
+        tc_fence_after();
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk)  // dV += P^T dO   (K = 128 queries)
+          tc_mma(tV, smem_desc_sw128(pa + (kk / 4) * 16384 + (kk % 4) * 32, 16, 1024),
+                 smem_desc_sw128(doa + kk * 2048, 16384, 1024), kIdKV, (it > 0 || kk > 0) ? 1u : 0u);
+        tc_commit(p_free);
+        if (!(ok = mbar_wait(ds_full, par, status))) break;
+        tc_fence_after();
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk)  // dK += dS^T Q
+          tc_mma(tK, smem_desc_sw128(dsa + (kk / 4) * 16384 + (kk % 4) * 32, 16, 1024),
+                 smem_desc_sw128(qa + kk * 2048, 16384, 1024), kIdKV, (it > 0 || kk > 0) ? 1u : 0u);
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk)  // dQ = dS K   (A = dS read MN-major, K = 128 keys)
+          tc_mma(tP, smem_desc_sw128(dsa + kk * 2048, 16384, 1024), smem_desc_sw128(ka + kk * 2048, 16384, 1024),
+                 kIdQ, kk > 0 ? 1u : 0u);
+        tc_commit(dq_full);
+        tc_commit(ds_free);
+        tc_commit(q_empty0 + 8 * st);
+      }
+      if (ok) tc_commit(acc_full);
+    }
+  } else {
+    const int qd = warp & 3;
+    const int half = (warp - 2) / 4;
+    const int r = qd * 32 + lane;  // key row (S^T, dP^T, dK, dV) or query row (dQ)
+    const uint32_t lane_base = static_cast<uint32_t>(qd * 32) << 16;
+    const float sl2 = scale * kLog2e;
+    uint8_t* p_atom = sm + S::p_off + half * 16384;
+    uint8_t* ds_atom = sm + S::ds_off + half * 16384;
+    bool ok = true;
+    for (int it = 0; it < n_it; ++it) {
+      const int i = j + it, st = it % STAGES;
+      const uint32_t par = it & 1;
+      const float* st_lse = reinterpret_cast<const float*>(sm + S::st_off + st * S::stage_bytes + 2 * S::tile);
+      const float* st_dl = st_lse + 128;
+      const bool diag = i == j;
+      float pr[64];
+      // P^T = exp2(S^T * scale * log2e - lse * log2e), causal mask on the diagonal tile
+      ok = __all_sync(0xffffffffu, mbar_wait(s_full, par, status));
+      if (ok && it > 0) ok = __all_sync(0xffffffffu, mbar_wait(p_free, par ^ 1, status));
+      if (!ok) break;
+      tc_fence_after();
+#pragma unroll
+      for (int c = 0; c < 2; ++c) {
+        float sv[32];
+        tmem_ld_32(tS + lane_base + half * 64 + c * 32, sv);
+#pragma unroll
+        for (int t = 0; t < 32; ++t) {
+          const int qq = half * 64 + c * 32 + t;
+          float pv = fast_exp2(fmaf(sv[t], sl2, -st_lse[qq] * kLog2e));
+          if (diag && qq < r) pv = 0.f;
+          pr[c * 32 + t] = pv;
+        }
+        store_swizzled32(p_atom, r, c, pr + c * 32);
+      }
+      tc_fence_before();
+      mbar_arrive(s_free);
+      fence_async_smem();
+      mbar_arrive(p_full);
+      // dS^T = scale * P^T (dP^T - delta)
+      ok = __all_sync(0xffffffffu, mbar_wait(dp_full, par, status));
+      if (ok && it > 0) ok = __all_sync(0xffffffffu, mbar_wait(ds_free, par ^ 1, status));
+      if (!ok) break;
+      tc_fence_after();
+#pragma unroll
+      for (int c = 0; c < 2; ++c) {
+        float dv[32];
+        tmem_ld_32(tP + lane_base + half * 64 + c * 32, dv);
+#pragma unroll
+        for (int t = 0; t < 32; ++t) {
+          const int qq = half * 64 + c * 32 + t;
+          dv[t] = scale * pr[c * 32 + t] * (dv[t] - st_dl[qq]);
+        }
+        store_swizzled32(ds_atom, r, c, dv);
+      }
+      tc_fence_before();
+      fence_async_smem();
+      mbar_arrive(ds_full);
+      // dQ_i rows (TMEM lane = query): fp32 vector atomics into the accumulator
+      ok = __all_sync(0xffffffffu, mbar_wait(dq_full, par, status));
+      if (!ok) break;
+      tc_fence_after();
+      float* dst = dq_acc + (static_cast<long long>(b) * T + i * 128 + r) * C + h * D + half * (D / 2);
+#pragma unroll
+      for (int c = 0; c < D / 64; ++c) {
+        float qv[32];
+        tmem_ld_32(tP + lane_base + half * (D / 2) + c * 32, qv);
+#pragma unroll
+        for (int t = 0; t < 32; t += 4)
+          atomicAdd(reinterpret_cast<float4*>(dst + c * 32 + t), make_float4(qv[t], qv[t + 1], qv[t + 2], qv[t + 3]));
+      }
+      tc_fence_before();
+      mbar_arrive(dq_free);
+    }
+    if (ok) ok = __all_sync(0xffffffffu, mbar_wait(acc_full, 0, status));
+    if (ok) {
+      tc_fence_after();
+      const long long row = static_cast<long long>(b) * T + j * 128 + r;
+      __nv_bfloat16* dk = dqkv + row * 3 * C + C + h * D + half * (D / 2);
+      __nv_bfloat16* dv = dk + C;
+#pragma unroll
+      for (int c = 0; c < D / 64; ++c) {
+        float kv[32], vv[32];
+        tmem_ld_32(tK + lane_base + half * (D / 2) + c * 32, kv);
+        tmem_ld_32(tV + lane_base + half * (D / 2) + c * 32, vv);
+#pragma unroll
+        for (int t = 0; t < 32; t += 8) {
+          *reinterpret_cast<uint4*>(dk + c * 32 + t) =
+              make_uint4(pack_bf16x2(kv[t], kv[t + 1]), pack_bf16x2(kv[t + 2], kv[t + 3]),
+                         pack_bf16x2(kv[t + 4], kv[t + 5]), pack_bf16x2(kv[t + 6], kv[t + 7]));
+          *reinterpret_cast<uint4*>(dv + c * 32 + t) =
+              make_uint4(pack_bf16x2(vv[t], vv[t + 1]), pack_bf16x2(vv[t + 2], vv[t + 3]),
+                         pack_bf16x2(vv[t + 4], vv[t + 5]), pack_bf16x2(vv[t + 6], vv[t + 7]));
+        }
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, kTmemCols);
+  }
+}
+
 }  // namespace fatc
 
 // qkv: [B, T, 3*H*D] bf16 (row stride 3C, q|k|v thirds); o: [B, T, H*D]; lse: [B, H, T].
@@ -346,6 +629,36 @@ void flash_attn_fwd_tc(torch::Tensor qkv, torch::Tensor o, torch::Tensor lse, in
   };
   if (D == 64) run(fatc::fa_fwd_tc_kernel<64, 2>, fatc::Smem<64, 2>::total);
   else run(fatc::fa_fwd_tc_kernel<128, 2>, fatc::Smem<128, 2>::total);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+// Backward launch (delta and the zeroed fp32 dq accumulator are prepared by the
+// caller, which also converts dq_acc afterwards): dqkv [B, T, 3C] receives dK
+// and dV; qkv [B, T, 3C], dout [B, T, C] contiguous; T % 128 == 0.
+void flash_attn_bwd_tc_launch(torch::Tensor qkv, torch::Tensor dout, torch::Tensor lse, torch::Tensor delta,
+                              torch::Tensor dq_acc, torch::Tensor dqkv, int64_t n_head, double scale,
+                              torch::Tensor status) {
+  const int B = static_cast<int>(qkv.size(0)), T = static_cast<int>(qkv.size(1));
+  const int C3 = static_cast<int>(qkv.size(2));
+  const int H = static_cast<int>(n_head);
+  const int C = C3 / 3;
+  const int D = C / H;
+  TORCH_CHECK(D == 64 || D == 128, "tcgen05 attention backward supports head dim 64 or 128");
+  TORCH_CHECK(T % 128 == 0, "tcgen05 attention backward needs T % 128 == 0");
+  TORCH_CHECK(qkv.is_contiguous() && dout.is_contiguous() && dqkv.is_contiguous(), "contiguous tensors");
+  c10::cuda::CUDAGuard g(qkv.device());
+  CUtensorMap mqkv = make_tma_2d_bf16(qkv.data_ptr(), C3, static_cast<uint64_t>(B) * T, C3, 64, 128);
+  CUtensorMap mdo = make_tma_2d_bf16(dout.data_ptr(), C, static_cast<uint64_t>(B) * T, C, 64, 128);
+  dim3 grid(T / 128, B * H);
+  auto stream = at::cuda::getCurrentCUDAStream();
+  auto run = [&](auto kern, uint32_t smem) {
+    C10_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+    kern<<<grid, fatc::kBwdThreads, smem, stream>>>(
+        mqkv, mdo, lse.data_ptr<float>(), delta.data_ptr<float>(), dq_acc.data_ptr<float>(),
+        reinterpret_cast<__nv_bfloat16*>(dqkv.data_ptr()), H, T, static_cast<float>(scale), status.data_ptr<int>());
+  };
+  if (D == 64) run(fatc::fa_bwd_tc_kernel<64, 2>, fatc::BwdSmem<64, 2>::total);
+  else run(fatc::fa_bwd_tc_kernel<128, 1>, fatc::BwdSmem<128, 1>::total);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 

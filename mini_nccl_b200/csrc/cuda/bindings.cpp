@@ -31,6 +31,8 @@ void flash_attn_bwd(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Te
 // attention_tc.cu
 void flash_attn_fwd_tc(torch::Tensor qkv, torch::Tensor o, torch::Tensor lse, int64_t n_head, double scale,
                        torch::Tensor status);
+void flash_attn_bwd_tc(torch::Tensor qkv, torch::Tensor o, torch::Tensor dout, torch::Tensor lse, torch::Tensor dqkv,
+                       torch::Tensor dq_acc, torch::Tensor delta, int64_t n_head, double scale, torch::Tensor status);
 // comm.cu
 void register_comm(pybind11::module_& m);
 }  // namespace mnb
@@ -52,5 +54,6 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("flash_attn_fwd", &mnb::flash_attn_fwd);
   m.def("flash_attn_bwd", &mnb::flash_attn_bwd);
   m.def("flash_attn_fwd_tc", &mnb::flash_attn_fwd_tc, "tcgen05 flash attention forward");
+  m.def("flash_attn_bwd_tc", &mnb::flash_attn_bwd_tc, "tcgen05 flash attention backward");
   mnb::register_comm(m);
 }

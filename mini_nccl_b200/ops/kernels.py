@@ -16,6 +16,7 @@ dW = dY^T X    dY [M, N] MN-major     X [M, K] MN-major
 from __future__ import annotations
 
 import math
+import os
 
 import torch
 
@@ -23,6 +24,8 @@ EPI_BIAS, EPI_GELU, EPI_RESID, EPI_GELU_GRAD, EPI_ACCUM = 1, 2, 4, 8, 16
 
 #: Head dims whose attention forward runs on tcgen05 (others use mma.sync).
 TC_ATTENTION_HEAD_DIMS = (64, 128)
+#: tcgen05 backward on/off (``MNB_ATTN_BWD=mma`` selects the mma.sync kernel, for comparisons)
+TC_ATTENTION_BWD = os.environ.get("MNB_ATTN_BWD", "tc") != "mma"
 
 _EXT = None
 _STATUS: dict[int, torch.Tensor] = {}
@@ -294,7 +297,12 @@ class FlashAttention(torch.autograd.Function):
         dq, dk, dv = dqkv[..., :C], dqkv[..., C : 2 * C], dqkv[..., 2 * C :]
         dq_acc = torch.empty((B, T, C), dtype=torch.float32, device=qkv.device)
         delta = torch.empty((B, ctx.n_head, T), dtype=torch.float32, device=qkv.device)
-        ext().flash_attn_bwd(q, k, v, o, go, lse, dq, dk, dv, dq_acc, delta, ctx.n_head, ctx.scale)
+        D = C // ctx.n_head
+        if D in TC_ATTENTION_HEAD_DIMS and T % 128 == 0 and qkv.is_contiguous() and TC_ATTENTION_BWD:
+            ext().flash_attn_bwd_tc(qkv, o, go, lse, dqkv, dq_acc, delta, ctx.n_head, ctx.scale,
+                                    status_word(qkv.device))
+        else:
+            ext().flash_attn_bwd(q, k, v, o, go, lse, dq, dk, dv, dq_acc, delta, ctx.n_head, ctx.scale)
         return dqkv, None
 
 

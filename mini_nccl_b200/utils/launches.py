@@ -28,6 +28,7 @@ KERNELS_PER_CALL = {
     "flash_attn_fwd": 1,
     "flash_attn_fwd_tc": 1,
     "flash_attn_bwd": 3,
+    "flash_attn_bwd_tc": 3,
     "all_reduce": 1,
     "reduce_scatter": 1,
     "move": 1,

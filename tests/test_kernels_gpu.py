@@ -130,7 +130,8 @@ def test_gelu_forward_backward():
     close(x.grad, xr.grad, 2e-2)
 
 
-@pytest.mark.parametrize("B,T,H,D", [(2, 64, 2, 64), (2, 200, 3, 64), (1, 256, 2, 128), (2, 130, 2, 32)])
+@pytest.mark.parametrize("B,T,H,D", [(2, 64, 2, 64), (2, 200, 3, 64), (1, 256, 2, 128), (2, 130, 2, 32),
+                                     (2, 512, 3, 64), (1, 1024, 2, 64), (2, 384, 2, 128)])
 def test_flash_attention(B, T, H, D):
     C = H * D
     qkv = rnd(B, T, 3 * C, seed=21).requires_grad_(True)
