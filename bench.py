@@ -32,7 +32,8 @@ send/recv over NCCL p2p; total work per step is fixed (strong scaling).
 ``--mode fsdp`` runs BASELINE config 4 instead: GPT 24 layers, d_model 2048,
 16 heads, sequence 2048, micro-batch 4 per GPU, one FSDP unit per block with
 parameters, gradients and AdamW state sharded N ways (fp32 master weights;
-ours fuses each block's AdamW step into its gradient reduce-scatter).
+ours fuses each block's AdamW step into its gradient reduce-scatter, and
+keeps activations rather than recomputing -- torch FSDP2's default).
 
 Arms: ``ours`` (this library: sm_100a kernels, peer-memory DDP all-reduce),
 ``reference`` (the unmodified reference package from baseline/_ref with its
@@ -364,7 +365,9 @@ def run_ours(args):
         from mini_nccl_b200.models.gpt import Block
 
         # one unit per block; each block's AdamW runs inside its gradient reduce-scatter
-        ddp = mn.FullyShardedDataParallel(model, pg, unit_cls=Block, prefetch=True,
+        # activations saved (as torch FSDP2 does by default); parameters still freed after each
+        # block's forward and gathered again for its backward
+        ddp = mn.FullyShardedDataParallel(model, pg, unit_cls=Block, prefetch=True, recompute=False,
                                           optimizer_in_backward=dict(hp, eps=1e-8))
         shard_ids = {id(u.shard) for u in ddp.units}
         opt = FusedAdamW([p for p in ddp.parameters() if id(p) not in shard_ids], **hp)

@@ -19,6 +19,14 @@ peers' gradient buffers directly and applies the ``1/W`` scale in its
 epilogue.  ``prefetch=True`` issues the next unit's gather on a side stream
 while the current unit computes.
 
+``recompute=False`` keeps the forward's activations instead (torch FSDP2's
+default): the gathered parameters are still freed after each unit's forward
+-- their storage shrinks to zero bytes -- and gathered back into the same
+storage by a hook just before the unit's backward, so saved tensors stay
+valid; each unit's gradients are reduce-scattered as soon as all of them
+have accumulated.  Peak memory then holds activations rather than extra
+compute.
+
 ``optimizer_in_backward=dict(lr=..., betas=..., eps=..., weight_decay=...)``
 fuses the shard's AdamW step into the gradient reduce-scatter: on CUDA one
 kernel pushes every gradient chunk to its owner, sums the W slots in rank
@@ -148,6 +156,74 @@ class _Unit:
     def gather_full_flat(self) -> torch.Tensor:
         return self._gather(self.shard)
 
+    # ---- no-recompute mode: activations saved, parameters resharded in between ----
+
+    def forward_saving_activations(self, x: torch.Tensor) -> torch.Tensor:
+        """Forward with the autograd graph kept; the gathered parameters are freed
+        right after it (their storage shrinks to 0 bytes) and gathered again into
+        the same storage just before this unit's backward runs."""
+        owner = self.owner
+        flat = owner._take_prefetched(self) if owner is not None else None
+        flat = self.materialize(self.shard, flat)
+        if owner is not None:
+            owner._prefetch_after(self)
+        self._arm_grad_hooks()
+        y = self.module(x)
+        if self.pg.world_size > 1 or flat.untyped_storage().data_ptr() != self.shard.untyped_storage().data_ptr():
+            nbytes = flat.untyped_storage().nbytes()
+            flat.untyped_storage().resize_(0)
+            self._saved_flat = (flat, nbytes)
+        else:
+            self._saved_flat = None  # one rank: the "gathered" buffer is the shard itself
+        if y.requires_grad:
+            y.register_hook(self._before_backward)
+        if owner is not None:
+            owner._note_released(self.full_bytes)
+        return y
+
+    def _before_backward(self, grad: torch.Tensor):
+        saved = self._saved_flat
+        if saved is not None:
+            flat, nbytes = saved
+            flat.untyped_storage().resize_(nbytes)
+            if self.pg.world_size > 1:
+                collectives.all_gather_into(self.pg, flat, self.shard.detach())
+            else:
+                flat.copy_(self.shard.detach().reshape(-1))
+            if self.owner is not None:
+                self.owner._note_materialized(self.full_bytes)
+        return grad
+
+    def _arm_grad_hooks(self) -> None:
+        if not getattr(self, "_hooks_installed", False):
+            for p in self.params:
+                p.register_post_accumulate_grad_hook(lambda _p, unit=self: unit._grad_arrived())
+            self._hooks_installed = True
+        self._pending = sum(1 for p in self.params if p.requires_grad)
+
+    def _grad_arrived(self) -> None:
+        self._pending -= 1
+        if self._pending == 0:
+            self.finish_backward()
+
+    def finish_backward(self) -> None:
+        """Reduce-scatter this unit's gradients into its shard and free everything full-size."""
+        grads = tuple(p.grad for p in self.params)
+        for p in self.params:
+            p.grad = None
+        shard_grad = self.reduce_scatter_grads(grads)
+        if shard_grad is not None:
+            if self.shard.grad is None:
+                self.shard.grad = shard_grad.view_as(self.shard)
+            else:
+                self.shard.grad.add_(shard_grad.view_as(self.shard))
+        saved = getattr(self, "_saved_flat", None)
+        if saved is not None:
+            saved[0].untyped_storage().resize_(0)
+            self._saved_flat = None
+        self.release()
+        self._pending = -1
+
 
 class ShardAdamW:
     """AdamW applied to each unit's shard as part of its gradient reduce-scatter.
@@ -259,6 +335,9 @@ class _UnitWrapper(nn.Module):
         self.shard = unit.shard
 
     def forward(self, x: torch.Tensor) -> torch.Tensor:
+        owner = self.unit.owner
+        if owner is not None and not owner.recompute and torch.is_grad_enabled():
+            return self.unit.forward_saving_activations(x)
         return _ShardedForward.apply(self.unit, self.shard, x)
 
 
@@ -273,12 +352,14 @@ class FullyShardedDataParallel(nn.Module):
         units: list[nn.Module] | None = None,
         prefetch: bool = False,
         optimizer_in_backward: dict | None = None,
+        recompute: bool = True,
     ) -> None:
         super().__init__()
         if unit_cls is None and units is None:
             raise ValueError("pass unit_cls or units to say what should be sharded")
         self.pg = pg
         self.shard_optimizer = ShardAdamW(**optimizer_in_backward) if optimizer_in_backward is not None else None
+        self.recompute = recompute
         self.units: list[_Unit] = []
         self._live_bytes = 0
         self.peak_materialized_bytes = 0
@@ -393,6 +474,9 @@ class FullyShardedDataParallel(nn.Module):
 
     def sync(self) -> None:
         """Average the replicated gradients (sharded ones were done in backward)."""
+        for u in self.units:  # units whose parameters did not all receive gradients
+            if getattr(u, "_pending", -1) > 0:
+                u.finish_backward()
         if self.pg.world_size == 1 or not self._replicated:
             return
         average_gradients(self.pg, self._replicated)

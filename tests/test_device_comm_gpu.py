@@ -75,11 +75,14 @@ def _battery(pg) -> None:
     C.all_reduce(pg, t, algorithm="two_shot", wire_dtype=torch.bfloat16)
     want = expected(W, 100_003, torch.float32, "sum", dev)
     assert (t.double() - want).abs().max().item() < 0.05
-    # broadcast from every root
+    # broadcast from every root (odd byte count and a 16-byte-multiple one)
     for src in range(W):
         t = seeded(r, 4097, torch.float32, dev)
         C.broadcast(pg, t, src=src)
         assert torch.equal(t, seeded(src, 4097, torch.float32, dev))
+        t = seeded(r, (1 << 20) + 24, torch.bfloat16, dev)
+        C.broadcast(pg, t, src=src)
+        assert torch.equal(t, seeded(src, (1 << 20) + 24, torch.bfloat16, dev))
     # all_gather in rank order
     t = seeded(r, 6 * 13, torch.bfloat16, dev).view(6, 13)
     got = C.all_gather(pg, t)
@@ -275,7 +278,7 @@ def test_fused_gemm_collectives_on_gpus():
     run(_fused_tp, 2, timeout=600.0, devices="cuda", op_timeout=60.0)
 
 
-def _fsdp_opt_in_backward(pg) -> None:
+def _fsdp_opt_in_backward(pg, recompute: bool = True) -> None:
     """FSDP with AdamW fused into the reduce-scatter kernel == FSDP + FusedAdamW."""
     import copy
 
@@ -299,7 +302,8 @@ def _fsdp_opt_in_backward(pg) -> None:
     torch.manual_seed(0)
     base = nn.Sequential(Block(), Block()).to(dev, torch.bfloat16)
     hp = dict(lr=1e-3, betas=(0.9, 0.95), eps=1e-8, weight_decay=0.1)
-    fused = FullyShardedDataParallel(copy.deepcopy(base), pg, unit_cls=Block, optimizer_in_backward=hp)
+    fused = FullyShardedDataParallel(copy.deepcopy(base), pg, unit_cls=Block, optimizer_in_backward=hp,
+                                     recompute=recompute)
     plain = FullyShardedDataParallel(copy.deepcopy(base), pg, unit_cls=Block)
     opt = FusedAdamW(plain.parameters(), **hp)
     g = torch.Generator().manual_seed(5 + pg.rank)
@@ -318,5 +322,15 @@ def _fsdp_opt_in_backward(pg) -> None:
 
 
 @needs2
-def test_fsdp_optimizer_in_backward_on_gpus():
-    run(_fsdp_opt_in_backward, 2, timeout=600.0, devices="cuda", op_timeout=60.0)
+@pytest.mark.parametrize("recompute", [True, False])
+def test_fsdp_optimizer_in_backward_on_gpus(recompute):
+    run(_fsdp_opt_in_backward, 2, recompute, timeout=600.0, devices="cuda", op_timeout=60.0)
+
+
+needs4 = pytest.mark.skipif(n_gpus() < 4, reason="needs at least 4 GPUs")
+
+
+@needs4
+def test_device_collective_battery_four_ranks():
+    """W=4 reaches the scatter + all-gather broadcast and 4-way push schedules."""
+    run(_battery, 4, devices="cuda", timeout=900.0, op_timeout=60.0)

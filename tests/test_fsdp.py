@@ -37,12 +37,12 @@ class Model(nn.Module):
         return self.head(h)
 
 
-def _parity(pg, steps: int = 5) -> dict:
+def _parity(pg, steps: int = 5, recompute: bool = True) -> dict:
     W, per = pg.world_size, 6
     torch.manual_seed(0)
     model = Model()
     ref = copy.deepcopy(model)
-    fsdp = FullyShardedDataParallel(model, pg, unit_cls=Block)
+    fsdp = FullyShardedDataParallel(model, pg, unit_cls=Block, recompute=recompute)
     assert len(fsdp.units) == 3
     assert all(u.shard.numel() < u.padded_numel or W == 1 for u in fsdp.units)
     opt = torch.optim.SGD(fsdp.parameters(), lr=0.05, momentum=0.9)
@@ -68,6 +68,13 @@ def _parity(pg, steps: int = 5) -> dict:
 def test_fsdp_matches_single_process() -> None:
     reports = run(_parity, 2)
     assert reports[0] == reports[1]
+
+
+def test_fsdp_without_recompute_matches_single_process() -> None:
+    """Activations saved, parameters freed after forward and gathered again for backward."""
+    reports = run(_parity, 2, 5, False)
+    assert reports[0] == reports[1]
+    run(_parity, 3, 3, False)
 
 
 def test_fsdp_matches_single_process_world4() -> None:
@@ -177,14 +184,14 @@ def test_sharded_checkpoint_round_trip(tmp_path) -> None:
     run(_sharded_ckpt, 2, str(tmp_path))
 
 
-def _opt_in_backward(pg, steps: int = 4) -> None:
+def _opt_in_backward(pg, steps: int = 4, recompute: bool = True) -> None:
     """AdamW fused into the gradient reduce-scatter == single-process AdamW."""
     W, per = pg.world_size, 6
     torch.manual_seed(0)
     model = Model()
     ref = copy.deepcopy(model)
     hp = dict(lr=1e-2, betas=(0.9, 0.95), eps=1e-8, weight_decay=0.1)
-    fsdp = FullyShardedDataParallel(model, pg, unit_cls=Block, optimizer_in_backward=hp)
+    fsdp = FullyShardedDataParallel(model, pg, unit_cls=Block, optimizer_in_backward=hp, recompute=recompute)
     rest = torch.optim.AdamW([p for p in fsdp.parameters() if all(p is not u.shard for u in fsdp.units)], **hp)
     ref_opt = torch.optim.AdamW(ref.parameters(), **hp)
     gen = torch.Generator().manual_seed(11)
@@ -207,3 +214,7 @@ def _opt_in_backward(pg, steps: int = 4) -> None:
 
 def test_optimizer_in_backward_matches_single_process() -> None:
     run(_opt_in_backward, 2)
+
+
+def test_optimizer_in_backward_without_recompute() -> None:
+    run(_opt_in_backward, 2, 4, False)
