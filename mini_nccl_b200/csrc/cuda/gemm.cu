@@ -181,7 +181,7 @@ MNB_DEVICE void epilogue_store(const GemmArgs& a, int row, int col0, float* v) {
       for (int i = 0; i < 4; ++i)
         st_v4(ap + 8 * i, make_uint4(pk[4 * i], pk[4 * i + 1], pk[4 * i + 2], pk[4 * i + 3]));
     } else {
-      for (int i = 0; i < 32 && col0 + i < N; ++i) ap[i] = f32_to_bf16(v[i]);
+      _Pragma("unroll") for (int i = 0; i < 32; ++i) if (col0 + i < N) ap[i] = f32_to_bf16(v[i]);
     }
 #pragma unroll
     for (int i = 0; i < 32; ++i) v[i] = gelu_exact(v[i]);
@@ -201,7 +201,7 @@ MNB_DEVICE void epilogue_store(const GemmArgs& a, int row, int col0, float* v) {
         }
       }
     } else {
-      for (int i = 0; i < 32 && col0 + i < N; ++i) v[i] *= gelu_grad(bf16_to_f32(ap[i]));
+      _Pragma("unroll") for (int i = 0; i < 32; ++i) if (col0 + i < N) v[i] *= gelu_grad(bf16_to_f32(ap[i]));
     }
   }
   if (a.epi & kEpiResid) {
@@ -219,7 +219,7 @@ MNB_DEVICE void epilogue_store(const GemmArgs& a, int row, int col0, float* v) {
         }
       }
     } else {
-      for (int i = 0; i < 32 && col0 + i < N; ++i) v[i] += bf16_to_f32(rp[i]);
+      _Pragma("unroll") for (int i = 0; i < 32; ++i) if (col0 + i < N) v[i] += bf16_to_f32(rp[i]);
     }
   }
   if (a.epi & kEpiOutF32) {
@@ -236,7 +236,7 @@ MNB_DEVICE void epilogue_store(const GemmArgs& a, int row, int col0, float* v) {
       for (int i = 0; i < 8; ++i)
         reinterpret_cast<float4*>(op)[i] = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
     } else {
-      for (int i = 0; i < 32 && col0 + i < N; ++i) op[i] = (a.epi & kEpiAccum) ? op[i] + v[i] : v[i];
+      _Pragma("unroll") for (int i = 0; i < 32; ++i) if (col0 + i < N) op[i] = (a.epi & kEpiAccum) ? op[i] + v[i] : v[i];
     }
     return;
   }
@@ -262,7 +262,7 @@ MNB_DEVICE void epilogue_store(const GemmArgs& a, int row, int col0, float* v) {
     for (int i = 0; i < 4; ++i)
       st_v4(op + 8 * i, make_uint4(pk[4 * i], pk[4 * i + 1], pk[4 * i + 2], pk[4 * i + 3]));
   } else {
-    for (int i = 0; i < 32 && col0 + i < N; ++i) {
+    _Pragma("unroll") for (int i = 0; i < 32; ++i) if (col0 + i < N) {
       float x = v[i];
       if (a.epi & kEpiAccum) x += bf16_to_f32(op[i]);
       op[i] = f32_to_bf16(x);
@@ -314,7 +314,7 @@ MNB_DEVICE void epilogue_inputs(const GemmArgs& a, int row, int col0, float* v) 
         }
       }
     } else {
-      for (int i = 0; i < 32 && col0 + i < N; ++i) v[i] += bf16_to_f32(a.bias[col0 + i]);
+      _Pragma("unroll") for (int i = 0; i < 32; ++i) if (col0 + i < N) v[i] += bf16_to_f32(a.bias[col0 + i]);
     }
   }
   if ((a.epi & kEpiGeluGrad) && in_rows) {
@@ -332,7 +332,7 @@ MNB_DEVICE void epilogue_inputs(const GemmArgs& a, int row, int col0, float* v) 
         }
       }
     } else {
-      for (int i = 0; i < 32 && col0 + i < N; ++i) v[i] *= gelu_grad(bf16_to_f32(ap[i]));
+      _Pragma("unroll") for (int i = 0; i < 32; ++i) if (col0 + i < N) v[i] *= gelu_grad(bf16_to_f32(ap[i]));
     }
   }
   if ((a.epi & kEpiResid) && in_rows) {
@@ -350,7 +350,76 @@ MNB_DEVICE void epilogue_inputs(const GemmArgs& a, int row, int col0, float* v) 
         }
       }
     } else {
-      for (int i = 0; i < 32 && col0 + i < N; ++i) v[i] += bf16_to_f32(rp[i]);
+      _Pragma("unroll") for (int i = 0; i < 32; ++i) if (col0 + i < N) v[i] += bf16_to_f32(rp[i]);
+    }
+  }
+}
+
+// Epilogue inputs without stalls on dependent global loads:
+//  * the bias of the warp's BN/2 columns is loaded once per tile, before the
+//    accumulator wait, BN/64 values per lane, and broadcast by shuffles;
+//  * the per-row input (residual or GELU pre-activation) of chunk k+1 is
+//    loaded while chunk k is being processed.
+struct EpiPrefetch {
+  uint2 bias;     // BN/64 bf16 values of this lane's slice of the warp's columns
+  uint4 row[4];   // 32 bf16 of the next chunk's row input
+};
+
+template <int BN>
+MNB_DEVICE void load_bias_slice(const GemmArgs& a, int colw, int lane, EpiPrefetch& f) {
+  constexpr int vpl = BN / 64;  // values per lane (4 or 2)
+  const int c = colw + vpl * lane;
+  f.bias = make_uint2(0u, 0u);
+  if (a.bias == nullptr) return;
+  if (vpl == 4) {
+    if (c + 4 <= a.N) f.bias = *reinterpret_cast<const uint2*>(a.bias + c);
+  } else {
+    if (c + 2 <= a.N) f.bias.x = *reinterpret_cast<const uint32_t*>(a.bias + c);
+  }
+}
+
+MNB_DEVICE const __nv_bfloat16* row_input(const GemmArgs& a, long long row, int col0) {
+  if (a.epi & kEpiResid) return a.resid + row * a.ldr + col0;
+  return a.aux + row * a.ldaux + col0;
+}
+
+MNB_DEVICE void load_row_chunk(const GemmArgs& a, int row, int col0, uint4* dst) {
+  if (row < a.M && col0 + 32 <= a.N) {
+    const __nv_bfloat16* p = row_input(a, row, col0);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) dst[i] = ld_v4(p + 8 * i);
+  }
+}
+
+// bias (shuffled) + row input (prefetched) on 32 values of warp-local chunk k
+template <int BN>
+MNB_DEVICE void apply_inputs_fast(const GemmArgs& a, const EpiPrefetch& f, int k, const uint4* rowv, float* v) {
+  constexpr int vpl = BN / 64;
+  if (a.epi & kEpiBias) {
+#pragma unroll
+    for (int jp = 0; jp < 16; ++jp) {
+      const int c = 32 * k + 2 * jp;
+      const uint32_t word = ((c % vpl) / 2 == 0) ? f.bias.x : f.bias.y;
+      const float2 b2 = unpack_bf16x2(__shfl_sync(0xffffffffu, word, c / vpl));
+      v[2 * jp] += b2.x;
+      v[2 * jp + 1] += b2.y;
+    }
+  }
+  if (a.epi & (kEpiResid | kEpiGeluGrad)) {
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const uint32_t ws[4] = {rowv[i].x, rowv[i].y, rowv[i].z, rowv[i].w};
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const float2 x = unpack_bf16x2(ws[j]);
+        if (a.epi & kEpiResid) {
+          v[8 * i + 2 * j] += x.x;
+          v[8 * i + 2 * j + 1] += x.y;
+        } else {
+          v[8 * i + 2 * j] *= gelu_grad(x.x);
+          v[8 * i + 2 * j + 1] *= gelu_grad(x.y);
+        }
+      }
     }
   }
 }
@@ -610,6 +679,16 @@ __global__ void __launch_bounds__(gemm_threads<FUSE>(), 1)
       const int split = u / (m_tiles * n_tiles);
       const int t = u % (m_tiles * n_tiles);
       const int mb = remap_mblock<FUSE>(t % m_tiles, m_tiles, args, ctx), nb = t / m_tiles;
+      // Fast input path: bf16 TMA-store epilogues with at most one per-row
+      // input; its loads are issued before the accumulator wait.
+      const bool fast = FUSE != kFuseRS && args.tma_out &&
+                        !((args.epi & kEpiResid) && (args.epi & kEpiGeluGrad));
+      const bool row_in = (args.epi & (kEpiResid | kEpiGeluGrad)) != 0;
+      EpiPrefetch pf;
+      if (fast) {
+        load_bias_slice<BN>(args, nb * BN + half * (BN / 2), lane, pf);
+        if (row_in) load_row_chunk(args, mb * kBM + row_in_tile, nb * BN + half * (BN / 2), pf.row);
+      }
       bool ok = mbar_wait(tfull0 + 8 * acc, acc_phase, status);
       if (!__all_sync(0xffffffffu, ok)) break;
       tc_fence_after();
@@ -659,7 +738,17 @@ __global__ void __launch_bounds__(gemm_threads<FUSE>(), 1)
           for (int sub = 0; sub < 2; ++sub) {
             float v[32];
             tmem_ld_32(lane_addr + g * 64 + sub * 32, v);
-            epilogue_inputs(a, row, colg + sub * 32, v);
+            const int k = (g - half * (BN / 128)) * 2 + sub;  // warp-local chunk
+            const int col0 = colg + sub * 32;
+            if (fast && col0 + 32 <= a.N) {
+              uint4 cur[4];
+#pragma unroll
+              for (int i = 0; i < 4; ++i) cur[i] = pf.row[i];
+              if (row_in && k + 1 < BN / 64) load_row_chunk(a, row, col0 + 32, pf.row);  // next chunk's input
+              apply_inputs_fast<BN>(a, pf, k, cur, v);
+            } else {
+              epilogue_inputs(a, row, col0, v);
+            }
             if (gelu) {
               stage_row32(box_aux, lane, sub, v);  // pre-activation
 #pragma unroll
