@@ -81,6 +81,45 @@ __global__ void layernorm_fwd_kernel(const __nv_bfloat16* __restrict__ x, const 
   }
 }
 
+// Grid-wide column sums without a second kernel.  `acc` is a persistent fp32
+// accumulator of n values followed by one u32 arrival counter, all zero
+// between calls: every block adds its partial sums atomically, and the last
+// block to arrive writes the results (bf16 or fp32, optionally accumulating)
+// and zeroes the accumulator and the counter again.  Calls that share `acc`
+// must be ordered (one stream).
+MNB_DEVICE void finish_fold(float* acc, int n, void* out0, void* out1, int split, int out_f32, int accumulate) {
+  __shared__ bool last;
+  __threadfence();
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    unsigned int* counter = reinterpret_cast<unsigned int*>(acc + n);
+    last = atomicAdd(counter, 1u) == gridDim.x * gridDim.y - 1;
+  }
+  __syncthreads();
+  if (!last) return;
+  __threadfence();
+  for (int i = threadIdx.x; i < n; i += blockDim.x) {
+    const float v = *reinterpret_cast<volatile float*>(acc + i);
+    acc[i] = 0.f;
+    void* out = i < split ? out0 : out1;
+    const int k = i < split ? i : i - split;
+    if (out_f32) {
+      float* o = reinterpret_cast<float*>(out) + k;
+      *o = accumulate ? *o + v : v;
+    } else {
+      __nv_bfloat16* o = reinterpret_cast<__nv_bfloat16*>(out) + k;
+      *o = f32_to_bf16(accumulate ? bf16_to_f32(*o) + v : v);
+    }
+  }
+  if (threadIdx.x == 0) *reinterpret_cast<unsigned int*>(acc + n) = 0u;
+}
+// Shared-memory partials of one block -> the accumulator, then finish.
+MNB_DEVICE void fold_into(float* acc, const float* sacc, int n, void* out0, void* out1, int split, int out_f32,
+                          int accumulate) {
+  for (int i = threadIdx.x; i < n; i += blockDim.x) atomicAdd(acc + i, sacc[i]);
+  finish_fold(acc, n, out0, out1, split, out_f32, accumulate);
+}
+
 // dx per row; per-block fp32 partials of dgamma/dbeta in `part` [gridDim.x, 2, C].
 // NCH > 0: the row (C = NCH*256 wide) stays in registers, one global read,
 // and each lane accumulates the weight gradients of its own columns in
@@ -89,7 +128,8 @@ template <int NCH>
 __global__ void layernorm_bwd_kernel(const __nv_bfloat16* __restrict__ dy, const __nv_bfloat16* __restrict__ x,
                                      const __nv_bfloat16* __restrict__ w, const float* __restrict__ mean,
                                      const float* __restrict__ rstd, __nv_bfloat16* __restrict__ dx,
-                                     float* __restrict__ part, int rows, int C) {
+                                     float* __restrict__ part, int rows, int C, void* out_dw, void* out_db,
+                                     int out_f32, int accumulate) {
   extern __shared__ float sacc[];  // [2][C]
   for (int i = threadIdx.x; i < 2 * C; i += blockDim.x) sacc[i] = 0.f;
   __syncthreads();
@@ -180,8 +220,7 @@ __global__ void layernorm_bwd_kernel(const __nv_bfloat16* __restrict__ dy, const
     }
   }
   __syncthreads();
-  float* mine = part + static_cast<long long>(blockIdx.x) * 2 * C;
-  for (int i = threadIdx.x; i < 2 * C; i += blockDim.x) mine[i] = sacc[i];
+  fold_into(part, sacc, 2 * C, out_dw, out_db, C, out_f32, accumulate);
 }
 
 // Wide rows (C = 8 * blockDim.x, e.g. 2048 / 4096): one block per row, each
@@ -191,7 +230,7 @@ __global__ void layernorm_bwd_kernel(const __nv_bfloat16* __restrict__ dy, const
 __global__ void __launch_bounds__(512) layernorm_bwd_wide_kernel(
     const __nv_bfloat16* __restrict__ dy, const __nv_bfloat16* __restrict__ x, const __nv_bfloat16* __restrict__ w,
     const float* __restrict__ mean, const float* __restrict__ rstd, __nv_bfloat16* __restrict__ dx,
-    float* __restrict__ part, int rows, int C) {
+    float* __restrict__ part, int rows, int C, void* out_dw, void* out_db, int out_f32, int accumulate) {
   __shared__ float red[2][16][2];
   const int c0 = threadIdx.x * 8;
   const int lane = threadIdx.x % 32, warp = threadIdx.x / 32, nw = blockDim.x / 32;
@@ -236,12 +275,13 @@ __global__ void __launch_bounds__(512) layernorm_bwd_wide_kernel(
     for (int j = 0; j < 8; ++j) o[j] = rs * (g[j] * ww[j] - a - xh[j] * bsum);
     store8(dx + off, o);
   }
-  float* mine = part + static_cast<long long>(blockIdx.x) * 2 * C;
+  // this block's column sums into the shared accumulator; the last block finishes
 #pragma unroll
   for (int j = 0; j < 8; ++j) {
-    mine[c0 + j] = dg[j];
-    mine[C + c0 + j] = dbb[j];
+    atomicAdd(part + c0 + j, dg[j]);
+    atomicAdd(part + C + c0 + j, dbb[j]);
   }
+  finish_fold(part, 2 * C, out_dw, out_db, C, out_f32, accumulate);
 }
 
 // out[c] (+)= sum over `nparts` rows of part[:, c]; bf16 or fp32 destination.
@@ -607,6 +647,54 @@ __global__ void __launch_bounds__(512) adamw_kernel(const AdamEntry* __restrict_
     const AdamChunk ch = chunks[ci];
     const AdamEntry e = table[ch.entry];
     const long long end = ch.start + ch.len;
+    // 4 elements per thread when every stream of this chunk is 16-byte (fp32) / 8-byte (bf16) aligned
+    const uintptr_t al = reinterpret_cast<uintptr_t>(e.m) | reinterpret_cast<uintptr_t>(e.v) |
+                         reinterpret_cast<uintptr_t>(e.master) |
+                         (reinterpret_cast<uintptr_t>(e.param) << (param_bf16 ? 1 : 0)) |
+                         (reinterpret_cast<uintptr_t>(e.grad) << (grad_bf16 ? 1 : 0));
+    if ((al & 15) == 0 && ch.start % 4 == 0 && ch.len % 4 == 0) {
+      for (long long k = ch.start + 4 * threadIdx.x; k < end; k += 4 * blockDim.x) {
+        float g[4], w[4];
+        if (grad_bf16) {
+          const uint2 raw = *reinterpret_cast<const uint2*>(reinterpret_cast<const __nv_bfloat16*>(e.grad) + k);
+          const float2 a = unpack_bf16x2(raw.x), b = unpack_bf16x2(raw.y);
+          g[0] = a.x; g[1] = a.y; g[2] = b.x; g[3] = b.y;
+        } else {
+          const float4 f = *reinterpret_cast<const float4*>(reinterpret_cast<const float*>(e.grad) + k);
+          g[0] = f.x; g[1] = f.y; g[2] = f.z; g[3] = f.w;
+        }
+        if (e.master) {
+          const float4 f = *reinterpret_cast<const float4*>(e.master + k);
+          w[0] = f.x; w[1] = f.y; w[2] = f.z; w[3] = f.w;
+        } else if (param_bf16) {
+          const uint2 raw = *reinterpret_cast<const uint2*>(reinterpret_cast<const __nv_bfloat16*>(e.param) + k);
+          const float2 a = unpack_bf16x2(raw.x), b = unpack_bf16x2(raw.y);
+          w[0] = a.x; w[1] = a.y; w[2] = b.x; w[3] = b.y;
+        } else {
+          const float4 f = *reinterpret_cast<const float4*>(reinterpret_cast<const float*>(e.param) + k);
+          w[0] = f.x; w[1] = f.y; w[2] = f.z; w[3] = f.w;
+        }
+        const float4 m4 = *reinterpret_cast<const float4*>(e.m + k), v4 = *reinterpret_cast<const float4*>(e.v + k);
+        float m[4] = {m4.x, m4.y, m4.z, m4.w}, v[4] = {v4.x, v4.y, v4.z, v4.w};
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          g[i] *= grad_scale;
+          m[i] = beta1 * m[i] + (1.f - beta1) * g[i];
+          v[i] = beta2 * v[i] + (1.f - beta2) * g[i] * g[i];
+          w[i] -= lr * wd * w[i];
+          w[i] -= lr * (m[i] * c1) / (sqrtf(v[i] * c2) + eps);
+        }
+        *reinterpret_cast<float4*>(e.m + k) = make_float4(m[0], m[1], m[2], m[3]);
+        *reinterpret_cast<float4*>(e.v + k) = make_float4(v[0], v[1], v[2], v[3]);
+        if (e.master) *reinterpret_cast<float4*>(e.master + k) = make_float4(w[0], w[1], w[2], w[3]);
+        if (param_bf16)
+          *reinterpret_cast<uint2*>(reinterpret_cast<__nv_bfloat16*>(e.param) + k) =
+              make_uint2(pack_bf16x2(w[0], w[1]), pack_bf16x2(w[2], w[3]));
+        else
+          *reinterpret_cast<float4*>(reinterpret_cast<float*>(e.param) + k) = make_float4(w[0], w[1], w[2], w[3]);
+      }
+      continue;
+    }
     for (long long k = ch.start + threadIdx.x; k < end; k += blockDim.x) {
       float g = grad_bf16 ? bf16_to_f32(reinterpret_cast<const __nv_bfloat16*>(e.grad)[k])
                           : reinterpret_cast<const float*>(e.grad)[k];
@@ -662,18 +750,20 @@ void layernorm_bwd(torch::Tensor dy, torch::Tensor x, torch::Tensor w, torch::Te
   const int C = static_cast<int>(x.size(-1));
   const int rows = static_cast<int>(x.numel() / C);
   const int blocks = ln_bwd_blocks(rows);
-  TORCH_CHECK(partials.numel() >= static_cast<int64_t>(blocks) * 2 * C && partials.scalar_type() == at::kFloat,
-              "partials workspace too small");
+  TORCH_CHECK(partials.numel() >= 2LL * C + 1 && partials.scalar_type() == at::kFloat,
+              "the fold accumulator must hold 2C + 1 floats (zeroed, persistent)");
   c10::cuda::CUDAGuard g(x.device());
   auto stream = at::cuda::getCurrentCUDAStream();
   const size_t smem = 2 * C * sizeof(float);
+  const bool f32 = dw.scalar_type() == at::kFloat;
   auto launch = [&](auto kern) {
     if (smem > 48 * 1024)
       C10_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
     kern<<<blocks, kRowWarps * 32, smem, stream>>>(
         reinterpret_cast<const __nv_bfloat16*>(dy.data_ptr()), reinterpret_cast<const __nv_bfloat16*>(x.data_ptr()),
         reinterpret_cast<const __nv_bfloat16*>(w.data_ptr()), mean.data_ptr<float>(), rstd.data_ptr<float>(),
-        reinterpret_cast<__nv_bfloat16*>(dx.data_ptr()), partials.data_ptr<float>(), rows, C);
+        reinterpret_cast<__nv_bfloat16*>(dx.data_ptr()), partials.data_ptr<float>(), rows, C, dw.data_ptr(),
+        db.data_ptr(), f32 ? 1 : 0, accumulate ? 1 : 0);
   };
   if (C == 256) launch(layernorm_bwd_kernel<1>);
   else if (C == 512) launch(layernorm_bwd_kernel<2>);
@@ -683,15 +773,40 @@ void layernorm_bwd(torch::Tensor dy, torch::Tensor x, torch::Tensor w, torch::Te
     layernorm_bwd_wide_kernel<<<blocks, C / 8, 0, stream>>>(
         reinterpret_cast<const __nv_bfloat16*>(dy.data_ptr()), reinterpret_cast<const __nv_bfloat16*>(x.data_ptr()),
         reinterpret_cast<const __nv_bfloat16*>(w.data_ptr()), mean.data_ptr<float>(), rstd.data_ptr<float>(),
-        reinterpret_cast<__nv_bfloat16*>(dx.data_ptr()), partials.data_ptr<float>(), rows, C);
+        reinterpret_cast<__nv_bfloat16*>(dx.data_ptr()), partials.data_ptr<float>(), rows, C, dw.data_ptr(),
+        db.data_ptr(), f32 ? 1 : 0, accumulate ? 1 : 0);
   else launch(layernorm_bwd_kernel<0>);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
-  const bool f32 = dw.scalar_type() == at::kFloat;
-  fold_partials_kernel<<<(C + 31) / 32, 256, 0, stream>>>(partials.data_ptr<float>(), blocks, 2LL * C, C,
-                                                           dw.data_ptr(), f32, accumulate);
-  fold_partials_kernel<<<(C + 31) / 32, 256, 0, stream>>>(partials.data_ptr<float>() + C, blocks, 2LL * C, C,
-                                                           db.data_ptr(), f32, accumulate);
-  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+// Bias gradient in one kernel: column sums of a 128-row band per block,
+// added into the persistent accumulator, finished by the last block.
+__global__ void __launch_bounds__(256) colsum_fold_kernel(const __nv_bfloat16* __restrict__ g, float* acc, int rows,
+                                                          int C, void* out, int out_f32, int accumulate) {
+  __shared__ float red[8][256];
+  const int lane = threadIdx.x % 32, warp = threadIdx.x / 32;
+  const int c0 = blockIdx.x * 256 + lane * 8;
+  const int r0 = blockIdx.y * kColRows;
+  const int r1 = min(rows, r0 + kColRows);
+  float s[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+  if (c0 < C) {
+#pragma unroll 4
+    for (int r = r0 + warp; r < r1; r += 8) {
+      float f[8];
+      load8(g + static_cast<long long>(r) * C + c0, f);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) s[j] += f[j];
+    }
+  }
+#pragma unroll
+  for (int j = 0; j < 8; ++j) red[warp][lane * 8 + j] = s[j];
+  __syncthreads();
+  float t = 0.f;
+#pragma unroll
+  for (int w = 0; w < 8; ++w) t += red[w][threadIdx.x];
+  const int c = blockIdx.x * 256 + threadIdx.x;
+  if (c < C) atomicAdd(acc + c, t);
+  finish_fold(acc, C, out, out, C, out_f32, accumulate);
 }
 
 int colsum_row_blocks(int rows) { return std::max(1, (rows + kColRows - 1) / kColRows); }
@@ -702,13 +817,13 @@ void bias_grad(torch::Tensor g, torch::Tensor out, torch::Tensor partials, bool 
   TORCH_CHECK(C % 8 == 0, "bias width must be a multiple of 8");
   const int rows = static_cast<int>(g.numel() / C);
   const int yb = colsum_row_blocks(rows);
-  TORCH_CHECK(partials.numel() >= static_cast<int64_t>(yb) * C, "partials workspace too small");
+  TORCH_CHECK(partials.numel() >= static_cast<int64_t>(C) + 1 && partials.scalar_type() == at::kFloat,
+              "the fold accumulator must hold C + 1 floats (zeroed, persistent)");
   c10::cuda::CUDAGuard guard(g.device());
   auto stream = at::cuda::getCurrentCUDAStream();
-  colsum_partial_kernel<<<dim3((C + 255) / 256, yb), 256, 0, stream>>>(
-      reinterpret_cast<const __nv_bfloat16*>(g.data_ptr()), partials.data_ptr<float>(), rows, C);
-  fold_partials_kernel<<<(C + 31) / 32, 256, 0, stream>>>(partials.data_ptr<float>(), yb, C, C, out.data_ptr(),
-                                                           out.scalar_type() == at::kFloat, accumulate);
+  colsum_fold_kernel<<<dim3((C + 255) / 256, yb), 256, 0, stream>>>(
+      reinterpret_cast<const __nv_bfloat16*>(g.data_ptr()), partials.data_ptr<float>(), rows, C, out.data_ptr(),
+      out.scalar_type() == at::kFloat ? 1 : 0, accumulate ? 1 : 0);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 

@@ -52,6 +52,20 @@ def status_word(device: torch.device) -> torch.Tensor:
     return st
 
 
+_FOLD: dict[int, torch.Tensor] = {}
+
+
+def fold_accumulator(device: torch.device, n: int) -> torch.Tensor:
+    """Persistent zeroed fp32 accumulator (n values + an arrival counter) for the
+    single-kernel column reductions; every call leaves it zeroed again, and the
+    calls are ordered on the device's stream."""
+    idx = device.index if device.index is not None else torch.cuda.current_device()
+    buf = _FOLD.get(idx)
+    if buf is None or buf.numel() < n + 1:
+        buf = _FOLD[idx] = torch.zeros(max(n + 1, 1 << 16), dtype=torch.float32, device=device)
+    return buf
+
+
 def check_status(device: torch.device | None = None) -> None:
     """Raise if a GEMM pipeline wait ran out of budget (device sync)."""
     for idx, st in _STATUS.items():
@@ -131,8 +145,7 @@ def _rows(x: torch.Tensor) -> torch.Tensor:
 def bias_grad(g2: torch.Tensor, dtype: torch.dtype) -> torch.Tensor:
     rows, C = g2.shape
     out = torch.empty(C, dtype=dtype, device=g2.device)
-    parts = torch.empty(ext().colsum_row_blocks(rows) * C, dtype=torch.float32, device=g2.device)
-    ext().bias_grad(g2, out, parts, False)
+    ext().bias_grad(g2, out, fold_accumulator(g2.device, C), False)
     return out
 
 
@@ -257,8 +270,7 @@ class LayerNorm(torch.autograd.Function):
         dx = torch.empty_like(x)
         dw = torch.empty_like(w)
         db = torch.empty_like(w)
-        parts = torch.empty(ext().ln_bwd_blocks(rows) * 2 * C, dtype=torch.float32, device=x.device)
-        ext().layernorm_bwd(gy.contiguous(), x, w, mean, rstd, dx, dw, db, parts, False)
+        ext().layernorm_bwd(gy.contiguous(), x, w, mean, rstd, dx, dw, db, fold_accumulator(x.device, 2 * C), False)
         return dx, dw, db, None
 
 

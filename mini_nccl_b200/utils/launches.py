@@ -17,8 +17,8 @@ _count = 0
 KERNELS_PER_CALL = {
     "gemm": 1,
     "layernorm_fwd": 1,
-    "layernorm_bwd": 3,
-    "bias_grad": 2,
+    "layernorm_bwd": 1,
+    "bias_grad": 1,
     "gelu_fwd": 1,
     "gelu_bwd": 1,
     "embed_fwd": 1,
