@@ -6,6 +6,7 @@
     python benchmarks/kernel_bench.py attn_fwd --b 16 --h 12 --t 1024 --d 64
     python benchmarks/kernel_bench.py attn_bwd --b 16 --h 12 --t 1024 --d 64
     python benchmarks/kernel_bench.py layernorm --m 16384 --n 768
+    python benchmarks/kernel_bench.py layernorm_bwd --m 16384 --n 768
     python benchmarks/kernel_bench.py xent --m 16384 --n 50304
     python benchmarks/kernel_bench.py adamw --numel 124000000
 
@@ -57,7 +58,7 @@ def timed(fn, iters: int, warmup: int, flush: torch.Tensor) -> float:
 
 def main() -> None:
     ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
-    ap.add_argument("kernel", choices=["gemm", "attn_fwd", "attn_bwd", "layernorm", "xent", "adamw"])
+    ap.add_argument("kernel", choices=["gemm", "attn_fwd", "attn_bwd", "layernorm", "layernorm_bwd", "xent", "adamw"])
     ap.add_argument("--m", type=int, default=16384)
     ap.add_argument("--n", type=int, default=2304)
     ap.add_argument("--k", type=int, default=768)
@@ -115,6 +116,13 @@ def main() -> None:
         x, w, bb = r(args.m, args.n), r(args.n), r(args.n)
         fn = lambda: K.LayerNorm.apply(x, w, bb, 1e-5)  # noqa: E731
         bytes_ = 2.0 * 2 * args.m * args.n
+    elif args.kernel == "layernorm_bwd":
+        x = r(args.m, args.n).requires_grad_(True)
+        w, bb = r(args.n).requires_grad_(True), r(args.n).requires_grad_(True)
+        y = K.LayerNorm.apply(x, w, bb, 1e-5)
+        gy = r(args.m, args.n)
+        fn = lambda: torch.autograd.grad(y, (x, w, bb), gy, retain_graph=True)  # noqa: E731
+        bytes_ = 3.0 * 2 * args.m * args.n
     elif args.kernel == "xent":
         z = r(args.m, args.n)
         t = torch.randint(0, args.n, (args.m,), device=dev)

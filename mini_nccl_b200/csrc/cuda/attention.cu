@@ -230,19 +230,28 @@ __global__ void __launch_bounds__(kThreads) fa_fwd_kernel(const __nv_bfloat16* _
 template <int D>
 __global__ void fa_bwd_dot_kernel(const __nv_bfloat16* __restrict__ o, const __nv_bfloat16* __restrict__ dout,
                                   float* __restrict__ delta, int H, int T, long long rows) {
-  const long long r = blockIdx.x * 8LL + threadIdx.x / 32;  // r indexes (b, t, h)
+  // delta[b, h, t] = sum_d O[b, t, h, d] * dO[b, t, h, d]; D / 8 lanes per row,
+  // 16-byte loads, 32 * 8 / D rows per warp at a time.
+  constexpr int LPR = D / 8;            // lanes per row
+  constexpr int RPW = 32 / LPR;         // rows per warp pass
   const int lane = threadIdx.x % 32;
-  if (r >= rows) return;
-  const __nv_bfloat16* op = o + r * D;
-  const __nv_bfloat16* gp = dout + r * D;
+  const long long warp = blockIdx.x * (blockDim.x / 32LL) + threadIdx.x / 32;
+  const long long r = warp * RPW + lane / LPR;  // r indexes (b, t, h)
+  const int c = (lane % LPR) * 8;
   float s = 0.f;
-  for (int c = lane * 2; c < D; c += 64) {
-    float2 a = unpack_bf16x2(*reinterpret_cast<const uint32_t*>(op + c));
-    float2 bb = unpack_bf16x2(*reinterpret_cast<const uint32_t*>(gp + c));
-    s += a.x * bb.x + a.y * bb.y;
+  if (r < rows) {
+    const uint4 a = *reinterpret_cast<const uint4*>(o + r * D + c);
+    const uint4 g = *reinterpret_cast<const uint4*>(dout + r * D + c);
+    const uint32_t av[4] = {a.x, a.y, a.z, a.w}, gv[4] = {g.x, g.y, g.z, g.w};
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      const float2 x = unpack_bf16x2(av[k]), y = unpack_bf16x2(gv[k]);
+      s += x.x * y.x + x.y * y.y;
+    }
   }
-  s = warp_sum(s);
-  if (lane == 0) {
+#pragma unroll
+  for (int off = LPR / 2; off > 0; off >>= 1) s += __shfl_xor_sync(0xffffffffu, s, off);
+  if (r < rows && lane % LPR == 0) {
     const long long bt = r / H;
     const int h = static_cast<int>(r % H);
     const long long b = bt / T;
@@ -440,14 +449,17 @@ __global__ void __launch_bounds__(kThreads) fa_bwd_kernel(
 
 __global__ void fa_dq_convert_kernel(const float* __restrict__ acc, __nv_bfloat16* __restrict__ dq, long long ld_dq,
                                      int HD, long long rows) {
-  const long long n = rows * HD / 2;
-  for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < n;
+  // 8 values per thread: two 16-byte loads, one 16-byte store (HD % 8 == 0)
+  const long long n8 = rows * HD / 8;
+  for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < n8;
        i += static_cast<long long>(gridDim.x) * blockDim.x) {
-    const long long e = 2 * i;
+    const long long e = 8 * i;
     const long long r = e / HD;
     const int c = static_cast<int>(e % HD);
-    float2 x = reinterpret_cast<const float2*>(acc)[i];
-    *reinterpret_cast<uint32_t*>(dq + r * ld_dq + c) = pack_bf16x2(x.x, x.y);
+    const float4 a = reinterpret_cast<const float4*>(acc)[2 * i];
+    const float4 b = reinterpret_cast<const float4*>(acc)[2 * i + 1];
+    *reinterpret_cast<uint4*>(dq + r * ld_dq + c) =
+        make_uint4(pack_bf16x2(a.x, a.y), pack_bf16x2(a.z, a.w), pack_bf16x2(b.x, b.y), pack_bf16x2(b.z, b.w));
   }
 }
 
@@ -506,7 +518,8 @@ void flash_attn_bwd(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Te
   const long long rows = static_cast<long long>(B) * T * H;
   dq_acc.zero_();
   auto dot = [&](auto kern) {
-    kern<<<static_cast<unsigned>((rows + 7) / 8), 256, 0, stream>>>(
+    const long long warps = (rows * D / 8 + 31) / 32;  // D/8 lanes per row
+    kern<<<static_cast<unsigned>((warps + 7) / 8), 256, 0, stream>>>(
         reinterpret_cast<const __nv_bfloat16*>(o.data_ptr()), reinterpret_cast<const __nv_bfloat16*>(dout.data_ptr()),
         delta.data_ptr<float>(), H, T, rows);
   };
@@ -534,7 +547,7 @@ void flash_attn_bwd(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Te
     TORCH_CHECK(false, "head dim must be 32, 64 or 128");
   }
   C10_CUDA_KERNEL_LAUNCH_CHECK();
-  const long long n2 = rows * D / 2;
+  const long long n2 = rows * D / 8;
   fa::fa_dq_convert_kernel<<<static_cast<unsigned>(std::min<long long>((n2 + 255) / 256, 148 * 16)), 256, 0,
                              stream>>>(dq_acc.data_ptr<float>(), reinterpret_cast<__nv_bfloat16*>(dq.data_ptr()),
                                        dq.stride(1), HD, static_cast<long long>(B) * T);
@@ -560,7 +573,8 @@ void flash_attn_bwd_tc(torch::Tensor qkv, torch::Tensor o, torch::Tensor dout, t
   const long long rows = static_cast<long long>(B) * T * H;
   C10_CUDA_CHECK(cudaMemsetAsync(dq_acc.data_ptr(), 0, dq_acc.numel() * sizeof(float), stream));
   auto dot = [&](auto kern) {
-    kern<<<static_cast<unsigned>((rows + 7) / 8), 256, 0, stream>>>(
+    const long long warps = (rows * D / 8 + 31) / 32;  // D/8 lanes per row
+    kern<<<static_cast<unsigned>((warps + 7) / 8), 256, 0, stream>>>(
         reinterpret_cast<const __nv_bfloat16*>(o.data_ptr()), reinterpret_cast<const __nv_bfloat16*>(dout.data_ptr()),
         delta.data_ptr<float>(), H, T, rows);
   };
@@ -569,7 +583,7 @@ void flash_attn_bwd_tc(torch::Tensor qkv, torch::Tensor o, torch::Tensor dout, t
   else TORCH_CHECK(false, "tcgen05 attention backward supports head dim 64 or 128");
   C10_CUDA_KERNEL_LAUNCH_CHECK();
   flash_attn_bwd_tc_launch(qkv, dout, lse, delta, dq_acc, dqkv, n_head, scale, status);
-  const long long n2 = rows * D / 2;
+  const long long n2 = rows * D / 8;
   fa::fa_dq_convert_kernel<<<static_cast<unsigned>(std::min<long long>((n2 + 255) / 256, 148 * 16)), 256, 0,
                              stream>>>(dq_acc.data_ptr<float>(), reinterpret_cast<__nv_bfloat16*>(dqkv.data_ptr()),
                                        3LL * C, C, static_cast<long long>(B) * T);

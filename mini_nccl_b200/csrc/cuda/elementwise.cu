@@ -81,6 +81,110 @@ __global__ void layernorm_fwd_kernel(const __nv_bfloat16* __restrict__ x, const 
   }
 }
 
+// LayerNorm forward with the row in registers (C = NCH * 256): one read of x,
+// mean and variance from registers (two-pass, exact), w and b loaded once per
+// warp for all the rows it visits (grid-stride).
+template <int NCH>
+__global__ void __launch_bounds__(256, 2) layernorm_fwd_reg_kernel(const __nv_bfloat16* __restrict__ x,
+                                                                const __nv_bfloat16* __restrict__ w,
+                                                                const __nv_bfloat16* __restrict__ b,
+                                                                __nv_bfloat16* __restrict__ y, float* __restrict__ mean_out,
+                                                                float* __restrict__ rstd_out, int rows, float eps) {
+  constexpr int C = NCH * 256;
+  const int lane = threadIdx.x % 32;
+  const int warps = gridDim.x * (blockDim.x / 32);
+  float ww[NCH][8], bb[NCH][8];
+#pragma unroll
+  for (int k = 0; k < NCH; ++k) {
+    load8(w + k * 256 + lane * 8, ww[k]);
+    load8(b + k * 256 + lane * 8, bb[k]);
+  }
+  for (int row = blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32; row < rows; row += warps) {
+    const __nv_bfloat16* xr = x + static_cast<long long>(row) * C;
+    float f[NCH][8];
+    float s = 0.f;
+#pragma unroll
+    for (int k = 0; k < NCH; ++k) {
+      load8(xr + k * 256 + lane * 8, f[k]);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) s += f[k][j];
+    }
+    const float mean = warp_sum(s) * (1.f / C);
+    float ss = 0.f;
+#pragma unroll
+    for (int k = 0; k < NCH; ++k)
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const float d = f[k][j] - mean;
+        ss += d * d;
+      }
+    const float rstd = rsqrtf(warp_sum(ss) * (1.f / C) + eps);
+    __nv_bfloat16* yr = y + static_cast<long long>(row) * C;
+#pragma unroll
+    for (int k = 0; k < NCH; ++k) {
+      float o[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) o[j] = (f[k][j] - mean) * rstd * ww[k][j] + bb[k][j];
+      store8(yr + k * 256 + lane * 8, o);
+    }
+    if (lane == 0) {
+      mean_out[row] = mean;
+      rstd_out[row] = rstd;
+    }
+  }
+}
+
+// Wide rows (C = 8 * blockDim.x, up to 4096): one block per row, 8 columns per thread.
+__global__ void __launch_bounds__(512) layernorm_fwd_wide_kernel(const __nv_bfloat16* __restrict__ x,
+                                                                 const __nv_bfloat16* __restrict__ w,
+                                                                 const __nv_bfloat16* __restrict__ b,
+                                                                 __nv_bfloat16* __restrict__ y,
+                                                                 float* __restrict__ mean_out,
+                                                                 float* __restrict__ rstd_out, int rows, int C,
+                                                                 float eps) {
+  __shared__ float red[2][16];
+  const int c0 = threadIdx.x * 8;
+  const int lane = threadIdx.x % 32, warp = threadIdx.x / 32, nw = blockDim.x / 32;
+  float ww[8], bb[8];
+  load8(w + c0, ww);
+  load8(b + c0, bb);
+  for (int row = blockIdx.x; row < rows; row += gridDim.x) {
+    const long long off = static_cast<long long>(row) * C + c0;
+    float f[8];
+    load8(x + off, f);
+    float s = 0.f;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) s += f[j];
+    s = warp_sum(s);
+    if (lane == 0) red[0][warp] = s;
+    __syncthreads();
+    float mean = 0.f;
+    for (int i = 0; i < nw; ++i) mean += red[0][i];
+    mean /= C;
+    float ss = 0.f;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const float d = f[j] - mean;
+      ss += d * d;
+    }
+    ss = warp_sum(ss);
+    if (lane == 0) red[1][warp] = ss;
+    __syncthreads();
+    float var = 0.f;
+    for (int i = 0; i < nw; ++i) var += red[1][i];
+    const float rstd = rsqrtf(var / C + eps);
+    float o[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) o[j] = (f[j] - mean) * rstd * ww[j] + bb[j];
+    store8(y + off, o);
+    if (threadIdx.x == 0) {
+      mean_out[row] = mean;
+      rstd_out[row] = rstd;
+    }
+    __syncthreads();  // red[] is rewritten by the next row
+  }
+}
+
 // Grid-wide column sums without a second kernel.  `acc` is a persistent fp32
 // accumulator of n values followed by one u32 arrival counter, all zero
 // between calls: every block adds its partial sums atomically, and the last
@@ -125,7 +229,7 @@ MNB_DEVICE void fold_into(float* acc, const float* sacc, int n, void* out0, void
 // and each lane accumulates the weight gradients of its own columns in
 // registers across all rows it visits.  NCH == 0: any C, shared-memory atomics.
 template <int NCH>
-__global__ void layernorm_bwd_kernel(const __nv_bfloat16* __restrict__ dy, const __nv_bfloat16* __restrict__ x,
+__global__ void __launch_bounds__(256, 1) layernorm_bwd_kernel(const __nv_bfloat16* __restrict__ dy, const __nv_bfloat16* __restrict__ x,
                                      const __nv_bfloat16* __restrict__ w, const float* __restrict__ mean,
                                      const float* __restrict__ rstd, __nv_bfloat16* __restrict__ dx,
                                      float* __restrict__ part, int rows, int C, void* out_dw, void* out_db,
@@ -143,35 +247,54 @@ __global__ void layernorm_bwd_kernel(const __nv_bfloat16* __restrict__ dy, const
 #pragma unroll
       for (int j = 0; j < 8; ++j) dg[k][j] = dbb[k][j] = 0.f;
     }
-    for (int row = blockIdx.x * kRowWarps + warp; row < rows; row += gridDim.x * kRowWarps) {
-      const __nv_bfloat16* xr = x + static_cast<long long>(row) * C;
-      const __nv_bfloat16* gr = dy + static_cast<long long>(row) * C;
-      const float mu = mean[row], rs = rstd[row];
-      float xh[NCH][8], g[NCH][8];
-      float a = 0.f, bsum = 0.f;
+    // PR rows per pass (2 while registers allow): their loads are all in
+    // flight before the first reduction
+    constexpr int PR = NCH <= 3 ? 2 : 1;
+    const int stride = gridDim.x * kRowWarps;
+    for (int row0 = blockIdx.x * kRowWarps + warp; row0 < rows; row0 += PR * stride) {
+      float xh[PR][NCH][8], g[PR][NCH][8];
+      float mu[PR], rs[PR];
 #pragma unroll
-      for (int k = 0; k < NCH; ++k) {
-        load8(xr + k * 256 + lane * 8, xh[k]);
-        load8(gr + k * 256 + lane * 8, g[k]);
+      for (int p = 0; p < PR; ++p) {
+        const int row = row0 + p * stride;
+        if (row < rows) {
+          const __nv_bfloat16* xr = x + static_cast<long long>(row) * C;
+          const __nv_bfloat16* gr = dy + static_cast<long long>(row) * C;
+          mu[p] = mean[row];
+          rs[p] = rstd[row];
 #pragma unroll
-        for (int j = 0; j < 8; ++j) {
-          xh[k][j] = (xh[k][j] - mu) * rs;
-          const float d = g[k][j] * ww[k][j];
-          a += d;
-          bsum += d * xh[k][j];
-          dg[k][j] += g[k][j] * xh[k][j];
-          dbb[k][j] += g[k][j];
+          for (int k = 0; k < NCH; ++k) {
+            load8(xr + k * 256 + lane * 8, xh[p][k]);
+            load8(gr + k * 256 + lane * 8, g[p][k]);
+          }
         }
       }
-      a = warp_sum(a) / C;
-      bsum = warp_sum(bsum) / C;
-      __nv_bfloat16* dr = dx + static_cast<long long>(row) * C;
 #pragma unroll
-      for (int k = 0; k < NCH; ++k) {
-        float o[8];
+      for (int p = 0; p < PR; ++p) {
+        const int row = row0 + p * stride;
+        if (row >= rows) break;
+        float a = 0.f, bsum = 0.f;
 #pragma unroll
-        for (int j = 0; j < 8; ++j) o[j] = rs * (g[k][j] * ww[k][j] - a - xh[k][j] * bsum);
-        store8(dr + k * 256 + lane * 8, o);
+        for (int k = 0; k < NCH; ++k)
+#pragma unroll
+          for (int j = 0; j < 8; ++j) {
+            xh[p][k][j] = (xh[p][k][j] - mu[p]) * rs[p];
+            const float d = g[p][k][j] * ww[k][j];
+            a += d;
+            bsum += d * xh[p][k][j];
+            dg[k][j] += g[p][k][j] * xh[p][k][j];
+            dbb[k][j] += g[p][k][j];
+          }
+        a = warp_sum(a) / C;
+        bsum = warp_sum(bsum) / C;
+        __nv_bfloat16* dr = dx + static_cast<long long>(row) * C;
+#pragma unroll
+        for (int k = 0; k < NCH; ++k) {
+          float o[8];
+#pragma unroll
+          for (int j = 0; j < 8; ++j) o[j] = rs[p] * (g[p][k][j] * ww[k][j] - a - xh[p][k][j] * bsum);
+          store8(dr + k * 256 + lane * 8, o);
+        }
       }
     }
 #pragma unroll
@@ -733,10 +856,23 @@ void layernorm_fwd(torch::Tensor x, torch::Tensor w, torch::Tensor b, torch::Ten
   TORCH_CHECK(C % 8 == 0, "LayerNorm width must be a multiple of 8");
   const int rows = static_cast<int>(x.numel() / C);
   c10::cuda::CUDAGuard g(x.device());
-  layernorm_fwd_kernel<<<(rows + kRowWarps - 1) / kRowWarps, kRowWarps * 32, 0, at::cuda::getCurrentCUDAStream()>>>(
-      reinterpret_cast<const __nv_bfloat16*>(x.data_ptr()), reinterpret_cast<const __nv_bfloat16*>(w.data_ptr()),
-      reinterpret_cast<const __nv_bfloat16*>(b.data_ptr()), reinterpret_cast<__nv_bfloat16*>(y.data_ptr()),
-      mean.data_ptr<float>(), rstd.data_ptr<float>(), rows, C, static_cast<float>(eps));
+  auto stream = at::cuda::getCurrentCUDAStream();
+  const auto* xp = reinterpret_cast<const __nv_bfloat16*>(x.data_ptr());
+  const auto* wp = reinterpret_cast<const __nv_bfloat16*>(w.data_ptr());
+  const auto* bp = reinterpret_cast<const __nv_bfloat16*>(b.data_ptr());
+  auto* yp = reinterpret_cast<__nv_bfloat16*>(y.data_ptr());
+  const float e = static_cast<float>(eps);
+  const int reg_blocks = std::max(1, std::min(148 * 8, (rows + 7) / 8));
+  if (C == 256) layernorm_fwd_reg_kernel<1><<<reg_blocks, 256, 0, stream>>>(xp, wp, bp, yp, mean.data_ptr<float>(), rstd.data_ptr<float>(), rows, e);
+  else if (C == 512) layernorm_fwd_reg_kernel<2><<<reg_blocks, 256, 0, stream>>>(xp, wp, bp, yp, mean.data_ptr<float>(), rstd.data_ptr<float>(), rows, e);
+  else if (C == 768) layernorm_fwd_reg_kernel<3><<<reg_blocks, 256, 0, stream>>>(xp, wp, bp, yp, mean.data_ptr<float>(), rstd.data_ptr<float>(), rows, e);
+  else if (C == 1024) layernorm_fwd_reg_kernel<4><<<reg_blocks, 256, 0, stream>>>(xp, wp, bp, yp, mean.data_ptr<float>(), rstd.data_ptr<float>(), rows, e);
+  else if (C % 256 == 0 && C >= 1536 && C <= 4096)
+    layernorm_fwd_wide_kernel<<<std::max(1, std::min(148 * 4, rows)), C / 8, 0, stream>>>(
+        xp, wp, bp, yp, mean.data_ptr<float>(), rstd.data_ptr<float>(), rows, C, e);
+  else
+    layernorm_fwd_kernel<<<(rows + kRowWarps - 1) / kRowWarps, kRowWarps * 32, 0, stream>>>(
+        xp, wp, bp, yp, mean.data_ptr<float>(), rstd.data_ptr<float>(), rows, C, e);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
