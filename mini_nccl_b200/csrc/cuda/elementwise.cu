@@ -862,11 +862,21 @@ void layernorm_fwd(torch::Tensor x, torch::Tensor w, torch::Tensor b, torch::Ten
   const auto* bp = reinterpret_cast<const __nv_bfloat16*>(b.data_ptr());
   auto* yp = reinterpret_cast<__nv_bfloat16*>(y.data_ptr());
   const float e = static_cast<float>(eps);
-  const int reg_blocks = std::max(1, std::min(148 * 8, (rows + 7) / 8));
-  if (C == 256) layernorm_fwd_reg_kernel<1><<<reg_blocks, 256, 0, stream>>>(xp, wp, bp, yp, mean.data_ptr<float>(), rstd.data_ptr<float>(), rows, e);
-  else if (C == 512) layernorm_fwd_reg_kernel<2><<<reg_blocks, 256, 0, stream>>>(xp, wp, bp, yp, mean.data_ptr<float>(), rstd.data_ptr<float>(), rows, e);
-  else if (C == 768) layernorm_fwd_reg_kernel<3><<<reg_blocks, 256, 0, stream>>>(xp, wp, bp, yp, mean.data_ptr<float>(), rstd.data_ptr<float>(), rows, e);
-  else if (C == 1024) layernorm_fwd_reg_kernel<4><<<reg_blocks, 256, 0, stream>>>(xp, wp, bp, yp, mean.data_ptr<float>(), rstd.data_ptr<float>(), rows, e);
+  // grid-stride kernels: one wave of resident blocks (w and b are loaded once per warp)
+  auto wave_of = [&](auto kern) {
+    int per_sm = 1, sms = 148, dev = 0;
+    C10_CUDA_CHECK(cudaGetDevice(&dev));
+    C10_CUDA_CHECK(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
+    C10_CUDA_CHECK(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, 256, 0));
+    return std::max(1, std::min((rows + 7) / 8, std::max(1, per_sm) * sms));
+  };
+  auto reg = [&](auto kern) {
+    kern<<<wave_of(kern), 256, 0, stream>>>(xp, wp, bp, yp, mean.data_ptr<float>(), rstd.data_ptr<float>(), rows, e);
+  };
+  if (C == 256) reg(layernorm_fwd_reg_kernel<1>);
+  else if (C == 512) reg(layernorm_fwd_reg_kernel<2>);
+  else if (C == 768) reg(layernorm_fwd_reg_kernel<3>);
+  else if (C == 1024) reg(layernorm_fwd_reg_kernel<4>);
   else if (C % 256 == 0 && C >= 1536 && C <= 4096)
     layernorm_fwd_wide_kernel<<<std::max(1, std::min(148 * 4, rows)), C / 8, 0, stream>>>(
         xp, wp, bp, yp, mean.data_ptr<float>(), rstd.data_ptr<float>(), rows, C, e);
@@ -895,7 +905,13 @@ void layernorm_bwd(torch::Tensor dy, torch::Tensor x, torch::Tensor w, torch::Te
   auto launch = [&](auto kern) {
     if (smem > 48 * 1024)
       C10_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
-    kern<<<blocks, kRowWarps * 32, smem, stream>>>(
+    // one wave: as many blocks as can be resident (these kernels grid-stride over rows)
+    int per_sm = 1, sms = 148, dev = 0;
+    C10_CUDA_CHECK(cudaGetDevice(&dev));
+    C10_CUDA_CHECK(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
+    C10_CUDA_CHECK(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, kRowWarps * 32, smem));
+    const int wave = std::max(1, std::min(blocks, std::max(1, per_sm) * sms));
+    kern<<<wave, kRowWarps * 32, smem, stream>>>(
         reinterpret_cast<const __nv_bfloat16*>(dy.data_ptr()), reinterpret_cast<const __nv_bfloat16*>(x.data_ptr()),
         reinterpret_cast<const __nv_bfloat16*>(w.data_ptr()), mean.data_ptr<float>(), rstd.data_ptr<float>(),
         reinterpret_cast<__nv_bfloat16*>(dx.data_ptr()), partials.data_ptr<float>(), rows, C, dw.data_ptr(),
