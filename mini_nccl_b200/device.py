@@ -80,6 +80,7 @@ class DeviceComm:
             self._open(self.impl.staging_segment())
         self.staging_bytes = self.impl.segment_bytes(self.impl.staging_segment())
         self._schedules: dict[tuple, torch.Tensor] = {}
+        self._last_issued: torch.cuda.Event | None = None
         recorder = getattr(comm, "recorder", None)
         if recorder is not None:
             recorder.attach_device_log(self.device_events)
@@ -165,13 +166,29 @@ class DeviceComm:
     # ---- collectives ------------------------------------------------------------------
 
     def _record(self, name: str, algorithm: str, nbytes: int, **detail):
+        self._order_after_previous()
         rec = getattr(self.comm, "recorder", None)
         return rec.start(name, algorithm, channel=-1, nbytes=nbytes, device=True, **detail) if rec is not None else None
 
     def _finish(self, ev) -> None:
+        self._mark_issued()
         rec = getattr(self.comm, "recorder", None)
         if rec is not None:
             rec.finish(ev)
+
+    # Every kernel of this communicator runs in host issue order, whichever
+    # stream it is launched on: the kernels of different ranks wait for one
+    # another, so two of them reordered by the streams on one rank but not on
+    # another would each wait for a peer that is running the other one.
+    def _order_after_previous(self) -> None:
+        last = self._last_issued
+        if last is not None:
+            torch.cuda.current_stream(self.device).wait_event(last)
+
+    def _mark_issued(self) -> None:
+        ev = torch.cuda.Event()
+        ev.record(torch.cuda.current_stream(self.device))
+        self._last_issued = ev
 
     def all_reduce(
         self,

@@ -181,17 +181,27 @@ class _Unit:
             owner._note_released(self.full_bytes)
         return y
 
+    def _regather(self, flat: torch.Tensor, nbytes: int) -> None:
+        flat.untyped_storage().resize_(nbytes)
+        if self.pg.world_size > 1:
+            collectives.all_gather_into(self.pg, flat, self.shard.detach())
+        else:
+            flat.copy_(self.shard.detach().reshape(-1))
+
     def _before_backward(self, grad: torch.Tensor):
         saved = self._saved_flat
+        owner = self.owner
         if saved is not None:
-            flat, nbytes = saved
-            flat.untyped_storage().resize_(nbytes)
-            if self.pg.world_size > 1:
-                collectives.all_gather_into(self.pg, flat, self.shard.detach())
+            ready = owner._bwd_prefetched.pop(id(self), None) if owner is not None else None
+            if ready is not None:
+                cur = torch.cuda.current_stream(self.device)
+                cur.wait_event(ready)  # gathered on the side stream
+                saved[0].record_stream(cur)  # its memory is in use here until this stream is past it
             else:
-                flat.copy_(self.shard.detach().reshape(-1))
-            if self.owner is not None:
-                self.owner._note_materialized(self.full_bytes)
+                self._regather(*saved)
+            if owner is not None:
+                owner._note_materialized(self.full_bytes)
+                owner._prefetch_backward_after(self)
         return grad
 
     def _arm_grad_hooks(self) -> None:
@@ -207,11 +217,29 @@ class _Unit:
             self.finish_backward()
 
     def finish_backward(self) -> None:
-        """Reduce-scatter this unit's gradients into its shard and free everything full-size."""
+        """Reduce-scatter this unit's gradients into its shard and free everything full-size.
+
+        On GPUs with several ranks the reduce-scatter (and the fused AdamW)
+        runs on the owner's comm stream, so the next unit's backward overlaps
+        it; ``sync()`` joins the comm stream back.
+        """
         grads = tuple(p.grad for p in self.params)
         for p in self.params:
             p.grad = None
-        shard_grad = self.reduce_scatter_grads(grads)
+        owner = self.owner
+        side = owner._comm_stream_for(self) if owner is not None else None
+        if side is not None:
+            cur = torch.cuda.current_stream(self.device)
+            side.wait_stream(cur)
+            with torch.cuda.stream(side):
+                shard_grad = self.reduce_scatter_grads(grads)
+            for g in grads:
+                if g is not None:
+                    g.record_stream(side)
+            if shard_grad is not None:
+                shard_grad.record_stream(cur)
+        else:
+            shard_grad = self.reduce_scatter_grads(grads)
         if shard_grad is not None:
             if self.shard.grad is None:
                 self.shard.grad = shard_grad.view_as(self.shard)
@@ -397,6 +425,8 @@ class FullyShardedDataParallel(nn.Module):
         ]
         self._index = {id(u): i for i, u in enumerate(self.units)}
         self._side = None
+        self._comm_stream = None
+        self._bwd_prefetched: dict[int, torch.cuda.Event] = {}
 
     # ---- prefetch (CUDA) -----------------------------------------------------------
 
@@ -417,6 +447,34 @@ class FullyShardedDataParallel(nn.Module):
             done.record(self._side)
         flat.record_stream(cur)
         self._prefetched[i] = (flat, done)
+
+    def _prefetch_backward_after(self, unit: _Unit) -> None:
+        """Gather the unit whose backward comes next (the previous one) on the side stream."""
+        if not self.prefetch or unit.device.type != "cuda" or self.pg.world_size == 1:
+            return
+        i = self._index[id(unit)] - 1
+        if i < 0:
+            return
+        prev = self.units[i]
+        saved = getattr(prev, "_saved_flat", None)
+        if saved is None or id(prev) in self._bwd_prefetched:
+            return
+        if self._side is None:
+            self._side = torch.cuda.Stream(device=unit.device)
+        cur = torch.cuda.current_stream(unit.device)
+        self._side.wait_stream(cur)
+        with torch.cuda.stream(self._side):
+            prev._regather(*saved)
+            done = torch.cuda.Event()
+            done.record(self._side)
+        self._bwd_prefetched[id(prev)] = done
+
+    def _comm_stream_for(self, unit: _Unit):
+        if unit.device.type != "cuda" or self.pg.world_size == 1 or self.recompute:
+            return None
+        if self._comm_stream is None:
+            self._comm_stream = torch.cuda.Stream(device=unit.device)
+        return self._comm_stream
 
     def _take_prefetched(self, unit: _Unit):
         hit = self._prefetched.pop(self._index[id(unit)], None)
@@ -477,6 +535,8 @@ class FullyShardedDataParallel(nn.Module):
         for u in self.units:  # units whose parameters did not all receive gradients
             if getattr(u, "_pending", -1) > 0:
                 u.finish_backward()
+        if self._comm_stream is not None:  # shard gradients / updates made on the comm stream
+            torch.cuda.current_stream(self._comm_stream.device).wait_stream(self._comm_stream)
         if self.pg.world_size == 1 or not self._replicated:
             return
         average_gradients(self.pg, self._replicated)
