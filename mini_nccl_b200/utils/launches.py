@@ -57,7 +57,11 @@ def reset() -> None:
 
 
 class CountingProxy:
-    """Wraps the extension module (or a native object) and counts launches."""
+    """Wraps the extension module (or a native object) and counts launches.
+
+    The counting wrapper of each entry point is built once and cached on the
+    proxy, so a launch costs one dict lookup and one counter update.
+    """
 
     def __init__(self, target) -> None:
         object.__setattr__(self, "_t", target)
@@ -67,13 +71,18 @@ class CountingProxy:
         per = KERNELS_PER_CALL.get(name)
         if per is None or not callable(attr):
             return attr
-
-        def call(*args, **kwargs):
-            out = attr(*args, **kwargs)
-            extra = 0
-            if name == "gemm" and len(args) > 9 and isinstance(args[9], int) and args[9] > 1:
-                extra = 1  # split-K reduction kernel
-            add(per + extra)
-            return out
-
+        if name == "gemm":
+            def call(*args, **kwargs):
+                global _count
+                out = attr(*args, **kwargs)
+                _count += per + (1 if len(args) > 9 and isinstance(args[9], int) and args[9] > 1 else 0)
+                return out
+        else:
+            def call(*args, **kwargs):
+                global _count
+                out = attr(*args, **kwargs)
+                _count += per
+                return out
+        if isinstance(self._t, __import__("types").ModuleType):
+            object.__setattr__(self, name, call)  # module functions are stable: cache the wrapper
         return call
