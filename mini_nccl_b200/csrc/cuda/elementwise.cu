@@ -669,72 +669,56 @@ __global__ void __launch_bounds__(kXentThreads) xent_smem_kernel(__nv_bfloat16* 
                  ::"r"(smem_u32(row_s)), "l"(z), "r"(bytes), "r"(bar_a) : "memory");
   }
   mbar_wait(bar_a, 0, nullptr);
-  float m = -INFINITY, s = 0.f;
-  for (int c = threadIdx.x * 8; c < V; c += kXentThreads * 8) {
-    uint4 raw = ld_v4(row_s + c);
-    float f[8];
-    const uint32_t ws[4] = {raw.x, raw.y, raw.z, raw.w};
-#pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      float2 t = unpack_bf16x2(ws[j]);
-      f[2 * j] = t.x;
-      f[2 * j + 1] = t.y;
-    }
-    float lm = f[0];
-#pragma unroll
-    for (int j = 1; j < 8; ++j) lm = fmaxf(lm, f[j]);
-    const float nm = fmaxf(m, lm);
-    float acc = (m == -INFINITY) ? 0.f : s * __expf(m - nm);
-#pragma unroll
-    for (int j = 0; j < 8; ++j) acc += __expf(f[j] - nm);
-    m = nm;
-    s = acc;
-  }
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) {
-    float om = __shfl_xor_sync(0xffffffffu, m, o);
-    float os = __shfl_xor_sync(0xffffffffu, s, o);
-    float nm = fmaxf(m, om);
-    s = (m == -INFINITY ? 0.f : s * __expf(m - nm)) + (om == -INFINITY ? 0.f : os * __expf(om - nm));
-    m = nm;
-  }
+  // Three passes over the row in shared memory, one exponential per element:
+  // max; e = exp(z - max) with its sum (e written back over the logits, bf16 --
+  // the gradient is rounded to bf16 anyway); gradient = e / sum - onehot.
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
-  if (lane == 0) {
-    sm[warp] = m;
-    ss[warp] = s;
+  const int64_t tgt = targets[row];
+  const bool ignored = tgt == ignore_index;
+  const float z_tgt = ignored ? 0.f : bf16_to_f32(row_s[tgt]);  // read before pass 2 overwrites it
+  float m = -INFINITY;
+  for (int c = threadIdx.x * 8; c < V; c += kXentThreads * 8) {
+    float f[8];
+    load8(row_s + c, f);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) m = fmaxf(m, f[j]);
   }
+  m = warp_max(m);
+  if (lane == 0) sm[warp] = m;
   __syncthreads();
   if (warp == 0) {
-    m = lane < kXentThreads / 32 ? sm[lane] : -INFINITY;
-    s = lane < kXentThreads / 32 ? ss[lane] : 0.f;
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) {
-      float om = __shfl_xor_sync(0xffffffffu, m, o);
-      float os = __shfl_xor_sync(0xffffffffu, s, o);
-      float nm = fmaxf(m, om);
-      s = (m == -INFINITY ? 0.f : s * __expf(m - nm)) + (om == -INFINITY ? 0.f : os * __expf(om - nm));
-      m = nm;
-    }
-    if (lane == 0) {
-      sm[0] = m;
-      ss[0] = s;
-    }
+    m = warp_max(lane < kXentThreads / 32 ? sm[lane] : -INFINITY);
+    if (lane == 0) sm[0] = m;
   }
   __syncthreads();
   const float rmax = sm[0];
-  const float inv = 1.f / ss[0];
-  const int64_t tgt = targets[row];
-  const bool ignored = tgt == ignore_index;
-  if (threadIdx.x == 0) loss[row] = ignored ? 0.f : (rmax + logf(ss[0]) - bf16_to_f32(row_s[tgt]));
-  const float gs = ignored ? 0.f : grad_scale;
+  float s = 0.f;
   for (int c = threadIdx.x * 8; c < V; c += kXentThreads * 8) {
     float f[8];
     load8(row_s + c, f);
 #pragma unroll
     for (int j = 0; j < 8; ++j) {
-      const float p = __expf(f[j] - rmax) * inv;
-      f[j] = (p - ((c + j) == tgt ? 1.f : 0.f)) * gs;
+      f[j] = __expf(f[j] - rmax);
+      s += f[j];
     }
+    store8(row_s + c, f);
+  }
+  s = warp_sum(s);
+  if (lane == 0) ss[warp] = s;
+  __syncthreads();
+  if (warp == 0) {
+    s = warp_sum(lane < kXentThreads / 32 ? ss[lane] : 0.f);
+    if (lane == 0) ss[0] = s;
+  }
+  __syncthreads();
+  const float inv = 1.f / ss[0];
+  if (threadIdx.x == 0) loss[row] = ignored ? 0.f : (rmax + logf(ss[0]) - z_tgt);
+  const float gs = ignored ? 0.f : grad_scale;
+  for (int c = threadIdx.x * 8; c < V; c += kXentThreads * 8) {
+    float f[8];
+    load8(row_s + c, f);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) f[j] = (f[j] * inv - ((c + j) == tgt ? 1.f : 0.f)) * gs;
     store8(z + c, f);
   }
 }
