@@ -28,6 +28,8 @@ namespace mnb {
 
 CUtensorMap make_tma_2d_bf16(const void* base, uint64_t inner, uint64_t outer, uint64_t row_stride_elems,
                              uint32_t box_inner, uint32_t box_outer);
+CUtensorMap make_tma_2d_f32(const void* base, uint64_t inner, uint64_t outer, uint64_t row_stride_elems,
+                            uint32_t box_inner, uint32_t box_outer);
 
 namespace fatc {
 
@@ -333,9 +335,13 @@ __global__ void __launch_bounds__(kThreads, D == 64 ? 2 : 1)
 // The compute warps turn S^T into P^T = exp(S^T*scale - lse) and dP^T into
 // dS^T = scale * P^T (dP^T - delta), both bf16 in 128-byte-swizzled shared
 // memory.  The same dS^T tile is the K-major A operand of dK and, read
-// MN-major (queries contiguous), the A operand of dQ.  dQ_i leaves TMEM as
-// fp32 vector atomics into a [B, T, C] accumulator; dK and dV are written
-// once at the end.  Warp roles as in the forward (producer, MMA, 8 compute).
+// MN-major (queries contiguous), the A operand of dQ.  dQ_i leaves TMEM
+// through a 128-byte-swizzled fp32 staging box in shared memory and is added
+// into a [B, T, C] fp32 accumulator by TMA reduce-add (the adds run at L2, the
+// compute warps do not wait for them); dK and dV are written once at the end.
+// For D = 64 dQ has its own TMEM columns, so dP^T of the next query tile does
+// not wait for dQ to be read out.  Warp roles as in the forward (producer,
+// MMA, 8 compute).
 // ===========================================================================
 constexpr int kBwdThreads = 64 + 32 * 8;
 
@@ -348,31 +354,59 @@ struct BwdSmem {
   static constexpr uint32_t st_off = 2 * tile;
   static constexpr uint32_t p_off = st_off + STAGES * stage_bytes;
   static constexpr uint32_t ds_off = p_off + 128 * 128 * 2;
-  static constexpr uint32_t bar_off = ds_off + 128 * 128 * 2;
-  static constexpr int n_bars = 12 + 2 * STAGES;
+  static constexpr uint32_t dq_off = ds_off + 128 * 128 * 2;  // two [128 x 32] fp32 staging boxes
+  static constexpr uint32_t bar_off = dq_off + 2 * 128 * 128;
+  static constexpr int n_bars = 16 + 2 * STAGES;
   static constexpr uint32_t total = bar_off + n_bars * 8 + 16 + 1024;
-  static_assert(st_off % 1024 == 0 && p_off % 1024 == 0 && ds_off % 1024 == 0, "1 KiB aligned tiles");
+  static_assert(st_off % 1024 == 0 && p_off % 1024 == 0 && ds_off % 1024 == 0 && dq_off % 1024 == 0,
+                "1 KiB aligned tiles");
+  static_assert(total <= 232448, "shared memory per CTA");
 };
 
-// 64 values -> bf16 row `r` of a [128 x 64] 128-byte-swizzled atom, chunk group c (32 values).
-MNB_DEVICE void store_swizzled32(uint8_t* atom, int r, int c, const float* v) {
+MNB_DEVICE float2 ld_shared_f2(uint32_t addr) {
+  float2 v;
+  asm volatile("ld.shared.v2.f32 {%0, %1}, [%2];" : "=f"(v.x), "=f"(v.y) : "r"(addr));
+  return v;
+}
+MNB_DEVICE void st_shared_v4(uint32_t addr, uint32_t a, uint32_t b, uint32_t c, uint32_t d) {
+  asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(a), "r"(b), "r"(c), "r"(d) : "memory");
+}
+// Swizzled row addressing shared by the stores below: row `r` of a [128 x 128 B]
+// atom starts at row_base(r); its 16-byte chunk k sits at slot k ^ (r % 8).
+MNB_DEVICE uint32_t row_base(uint32_t atom, int r) { return atom + (r / 8) * 1024 + (r % 8) * 128; }
+
+// 16 packed bf16 pairs (32 values) -> chunk group c (chunks 4c..4c+3) of a swizzled bf16 row.
+MNB_DEVICE void store_row_words(uint32_t rowb, int x, int c, const uint32_t* w) {
+#pragma unroll
+  for (int q8 = 0; q8 < 4; ++q8)
+    st_shared_v4(rowb + (((c * 4 + q8) ^ x) << 4), w[4 * q8], w[4 * q8 + 1], w[4 * q8 + 2], w[4 * q8 + 3]);
+}
+// 32 floats -> chunk group c of a swizzled bf16 row.
+MNB_DEVICE void store_row_bf16(uint32_t rowb, int x, int c, const float* v) {
 #pragma unroll
   for (int q8 = 0; q8 < 4; ++q8) {
-    const int chunk = c * 4 + q8;
-    const uint32_t off = (r / 8) * 1024 + (r % 8) * 128 + ((chunk ^ (r % 8)) * 16);
     const float* f = v + 8 * q8;
-    *reinterpret_cast<uint4*>(atom + off) = make_uint4(pack_bf16x2(f[0], f[1]), pack_bf16x2(f[2], f[3]),
-                                                       pack_bf16x2(f[4], f[5]), pack_bf16x2(f[6], f[7]));
+    st_shared_v4(rowb + (((c * 4 + q8) ^ x) << 4), pack_bf16x2(f[0], f[1]), pack_bf16x2(f[2], f[3]),
+                 pack_bf16x2(f[4], f[5]), pack_bf16x2(f[6], f[7]));
   }
+}
+// 32 floats -> one swizzled fp32 row (128 bytes, 8 chunks).
+MNB_DEVICE void store_row_f32(uint32_t rowb, int x, const float* v) {
+#pragma unroll
+  for (int k = 0; k < 8; ++k)
+    st_shared_v4(rowb + ((k ^ x) << 4), __float_as_uint(v[4 * k]), __float_as_uint(v[4 * k + 1]),
+                 __float_as_uint(v[4 * k + 2]), __float_as_uint(v[4 * k + 3]));
 }
 
 template <int D, int STAGES>
 __global__ void __launch_bounds__(kBwdThreads, 1)
     fa_bwd_tc_kernel(const __grid_constant__ CUtensorMap map_qkv, const __grid_constant__ CUtensorMap map_do,
-                     const float* __restrict__ lse, const float* __restrict__ delta, float* __restrict__ dq_acc,
-                     __nv_bfloat16* __restrict__ dqkv, int H, int T, float scale, int* status) {
+                     const __grid_constant__ CUtensorMap map_dq, const float* __restrict__ lse,
+                     const float* __restrict__ delta, __nv_bfloat16* __restrict__ dqkv, int H, int T, float scale,
+                     int* status) {
   using S = BwdSmem<D, STAGES>;
   constexpr uint32_t kTmemCols = 512;
+  constexpr bool kOwnDq = 128 + 128 + 3 * D <= 512;  // dQ in its own columns (D = 64)
   constexpr uint32_t kIdSq = idesc_bf16(128, 128, false, false);  // S^T, dP^T
   constexpr uint32_t kIdKV = idesc_bf16(128, D, false, true);     // dV, dK
   constexpr uint32_t kIdQ = idesc_bf16(128, D, true, true);       // dQ
@@ -386,6 +420,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
                  p_free = b0 + 40, ds_full = b0 + 48, ds_free = b0 + 56, dq_full = b0 + 64, dq_free = b0 + 72,
                  acc_full = b0 + 80;
   const uint32_t q_full0 = b0 + 96, q_empty0 = q_full0 + 8 * STAGES;
+  const uint32_t stg_free0 = q_empty0 + 8 * STAGES, stg_full0 = stg_free0 + 16;  // [2] each, one per half
 
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
   const int j = blockIdx.x;  // key tile; j = 0 has the most query tiles, so it starts first
@@ -411,9 +446,14 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       mbar_init(q_full0 + 8 * st, 1);
       mbar_init(q_empty0 + 8 * st, 1);
     }
+    for (int hf = 0; hf < 2; ++hf) {
+      mbar_init(stg_free0 + 8 * hf, 1);
+      mbar_init(stg_full0 + 8 * hf, 128);
+    }
     fence_mbar_init();
     tma_prefetch_desc(&map_qkv);
     tma_prefetch_desc(&map_do);
+    tma_prefetch_desc(&map_dq);
   }
   if (warp == 1) {
     tmem_alloc(smem_u32(tmem_slot), kTmemCols);
@@ -424,6 +464,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
   const uint32_t tS = tmem, tP = tmem + 128, tV = tmem + 256, tK = tmem + 256 + D;
+  const uint32_t tQ = kOwnDq ? tmem + 256 + 2 * D : tP;
 
   if (warp == 0) {
     if (lane == 0) {
@@ -434,6 +475,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
         tma_load_2d(sbase + S::k_off + c * 16384, &map_qkv, C + h * D + c * 64, row0 + j * 128, kv_full);
         tma_load_2d(sbase + S::v_off + c * 16384, &map_qkv, 2 * C + h * D + c * 64, row0 + j * 128, kv_full);
       }
+#pragma unroll 1
       for (int it = 0; it < n_it; ++it) {
         const int i = j + it, st = it % STAGES;
         if (!mbar_wait(q_empty0 + 8 * st, ((it / STAGES) & 1) ^ 1, status)) break;
@@ -456,12 +498,17 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
   } else if (warp == 1) {
     if (lane == 0) {
       bool ok = mbar_wait(kv_full, 0, status);
-      const uint32_t ka = sbase + S::k_off, va = sbase + S::v_off;
-      const uint32_t pa = sbase + S::p_off, dsa = sbase + S::ds_off;
+      const uint32_t ka0 = sbase + S::k_off, va0 = sbase + S::v_off;
+      const uint32_t pa0 = sbase + S::p_off, dsa0 = sbase + S::ds_off;
+#pragma unroll 1
       for (int it = 0; it < n_it && ok; ++it) {
         const int st = it % STAGES;
         const uint32_t par = it & 1;
-        const uint32_t qa = sbase + S::st_off + st * S::stage_bytes, doa = qa + S::tile;
+        uint32_t qa = sbase + S::st_off + st * S::stage_bytes, doa = qa + S::tile;
+        uint32_t ka = ka0, va = va0, pa = pa0, dsa = dsa0;
+        // Opaque per iteration: keeps the ~40 descriptors from being hoisted
+        // out of the loop into registers (and from there into local memory).
+        asm volatile("" : "+r"(ka), "+r"(va), "+r"(pa), "+r"(dsa), "+r"(qa), "+r"(doa));
         ok = mbar_wait(q_full0 + 8 * st, (it / STAGES) & 1, status) && mbar_wait(s_free, par ^ 1, status);
         if (!ok) break;
         tc_fence_after();
@@ -470,8 +517,10 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
           tc_mma(tS, smem_desc_sw128(ka + (kk / 4) * 16384 + (kk % 4) * 32, 16, 1024),
                  smem_desc_sw128(qa + (kk / 4) * 16384 + (kk % 4) * 32, 16, 1024), kIdSq, kk > 0 ? 1u : 0u);
         tc_commit(s_full);
-        if (!(ok = mbar_wait(dq_free, par ^ 1, status))) break;
-        tc_fence_after();
+        if (!kOwnDq) {  // dQ of the previous tile lives in the dP^T columns
+          if (!(ok = mbar_wait(dq_free, par ^ 1, status))) break;
+          tc_fence_after();
+        }
 #pragma unroll
         for (int kk = 0; kk < D / 16; ++kk)  // dP^T = V dO^T
           tc_mma(tP, smem_desc_sw128(va + (kk / 4) * 16384 + (kk % 4) * 32, 16, 1024),
@@ -490,9 +539,13 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
         for (int kk = 0; kk < 8; ++kk)  // dK += dS^T Q
           tc_mma(tK, smem_desc_sw128(dsa + (kk / 4) * 16384 + (kk % 4) * 32, 16, 1024),
                  smem_desc_sw128(qa + kk * 2048, 16384, 1024), kIdKV, (it > 0 || kk > 0) ? 1u : 0u);
+        if (kOwnDq) {
+          if (!(ok = mbar_wait(dq_free, par ^ 1, status))) break;
+          tc_fence_after();
+        }
 #pragma unroll
         for (int kk = 0; kk < 8; ++kk)  // dQ = dS K   (A = dS read MN-major, K = 128 keys)
-          tc_mma(tP, smem_desc_sw128(dsa + kk * 2048, 16384, 1024), smem_desc_sw128(ka + kk * 2048, 16384, 1024),
+          tc_mma(tQ, smem_desc_sw128(dsa + kk * 2048, 16384, 1024), smem_desc_sw128(ka + kk * 2048, 16384, 1024),
                  kIdQ, kk > 0 ? 1u : 0u);
         tc_commit(dq_full);
         tc_commit(ds_free);
@@ -506,16 +559,22 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     const int r = qd * 32 + lane;  // key row (S^T, dP^T, dK, dV) or query row (dQ)
     const uint32_t lane_base = static_cast<uint32_t>(qd * 32) << 16;
     const float sl2 = scale * kLog2e;
-    uint8_t* p_atom = sm + S::p_off + half * 16384;
-    uint8_t* ds_atom = sm + S::ds_off + half * 16384;
+    const int x = r % 8;  // swizzle phase of this row
+    const uint32_t p_row = row_base(sbase + S::p_off + half * 16384, r);
+    const uint32_t ds_row = row_base(sbase + S::ds_off + half * 16384, r);
+    const uint32_t dq_box = sbase + S::dq_off + half * 16384, dq_row = row_base(dq_box, r);
+    const uint32_t stg_free = stg_free0 + 8 * half, stg_full = stg_full0 + 8 * half;
+    const bool leader = warp == 2 + 4 * half && lane == 0;  // issues this half's reduces
+    uint32_t uses = 0;  // staging-box uses of this half so far (mbarrier phase)
     bool ok = true;
+#pragma unroll 1
     for (int it = 0; it < n_it; ++it) {
       const int i = j + it, st = it % STAGES;
       const uint32_t par = it & 1;
-      const float* st_lse = reinterpret_cast<const float*>(sm + S::st_off + st * S::stage_bytes + 2 * S::tile);
-      const float* st_dl = st_lse + 128;
+      const uint32_t st_lse = sbase + S::st_off + st * S::stage_bytes + 2 * S::tile;  // float[128]
+      const uint32_t st_dl = st_lse + 512;
       const bool diag = i == j;
-      float pr[64];
+      uint32_t pk[32];  // this row of P^T as bf16 pairs: the values the dV MMA reads, reused for dS
       // P^T = exp2(S^T * scale * log2e - lse * log2e), causal mask on the diagonal tile
       ok = __all_sync(0xffffffffu, mbar_wait(s_full, par, status));
       if (ok && it > 0) ok = __all_sync(0xffffffffu, mbar_wait(p_free, par ^ 1, status));
@@ -526,13 +585,16 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
         float sv[32];
         tmem_ld_32(tS + lane_base + half * 64 + c * 32, sv);
 #pragma unroll
-        for (int t = 0; t < 32; ++t) {
+        for (int t = 0; t < 32; t += 2) {
           const int qq = half * 64 + c * 32 + t;
-          float pv = fast_exp2(fmaf(sv[t], sl2, -st_lse[qq] * kLog2e));
-          if (diag && qq < r) pv = 0.f;
-          pr[c * 32 + t] = pv;
+          const float2 l2 = ld_shared_f2(st_lse + qq * 4);
+          float p0 = fast_exp2(fmaf(sv[t], sl2, -l2.x * kLog2e));
+          float p1 = fast_exp2(fmaf(sv[t + 1], sl2, -l2.y * kLog2e));
+          if (diag && qq < r) p0 = 0.f;
+          if (diag && qq + 1 < r) p1 = 0.f;
+          pk[c * 16 + t / 2] = pack_bf16x2(p0, p1);
         }
-        store_swizzled32(p_atom, r, c, pr + c * 32);
+        store_row_words(p_row, x, c, pk + c * 16);
       }
       tc_fence_before();
       mbar_arrive(s_free);
@@ -548,51 +610,67 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
         float dv[32];
         tmem_ld_32(tP + lane_base + half * 64 + c * 32, dv);
 #pragma unroll
-        for (int t = 0; t < 32; ++t) {
+        for (int t = 0; t < 32; t += 2) {
           const int qq = half * 64 + c * 32 + t;
-          dv[t] = scale * pr[c * 32 + t] * (dv[t] - st_dl[qq]);
+          const float2 pp = unpack_bf16x2(pk[c * 16 + t / 2]);
+          const float2 d2 = ld_shared_f2(st_dl + qq * 4);
+          dv[t] = scale * pp.x * (dv[t] - d2.x);
+          dv[t + 1] = scale * pp.y * (dv[t + 1] - d2.y);
         }
-        store_swizzled32(ds_atom, r, c, dv);
+        store_row_bf16(ds_row, x, c, dv);
       }
       tc_fence_before();
       fence_async_smem();
       mbar_arrive(ds_full);
-      // dQ_i rows (TMEM lane = query): fp32 vector atomics into the accumulator
+      // dQ_i rows (TMEM lane = query): TMEM -> registers (columns freed at
+      // once) -> swizzled staging box -> one TMA reduce-add per 32 columns.
       ok = __all_sync(0xffffffffu, mbar_wait(dq_full, par, status));
       if (!ok) break;
       tc_fence_after();
-      float* dst = dq_acc + (static_cast<long long>(b) * T + i * 128 + r) * C + h * D + half * (D / 2);
+      float qv[D / 2];
 #pragma unroll
-      for (int c = 0; c < D / 64; ++c) {
-        float qv[32];
-        tmem_ld_32(tP + lane_base + half * (D / 2) + c * 32, qv);
-#pragma unroll
-        for (int t = 0; t < 32; t += 4)
-          atomicAdd(reinterpret_cast<float4*>(dst + c * 32 + t), make_float4(qv[t], qv[t + 1], qv[t + 2], qv[t + 3]));
-      }
+      for (int c = 0; c < D / 64; ++c) tmem_ld_32(tQ + lane_base + half * (D / 2) + c * 32, qv + c * 32);
       tc_fence_before();
       mbar_arrive(dq_free);
+#pragma unroll
+      for (int c = 0; c < D / 64; ++c, ++uses) {
+        if (leader) {  // the box is free once the previous reduce has read it
+          bulk_wait_read<0>();
+          mbar_arrive(stg_free);
+        }
+        ok = __all_sync(0xffffffffu, mbar_wait(stg_free, uses & 1, status));
+        if (!ok) break;
+        store_row_f32(dq_row, x, qv + c * 32);
+        fence_async_smem();
+        mbar_arrive(stg_full);
+        bool staged = true;
+        if (leader && (staged = mbar_wait(stg_full, uses & 1, status))) {
+          tma_reduce_add_2d(&map_dq, dq_box, h * D + half * (D / 2) + c * 32, b * T + i * 128);
+          bulk_commit();
+        }
+        if (!(ok = __all_sync(0xffffffffu, staged))) break;
+      }
+      ok = __all_sync(0xffffffffu, ok);
+      if (!ok) break;
     }
+    if (leader) bulk_wait_all();  // dQ adds complete before the CTA exits
     if (ok) ok = __all_sync(0xffffffffu, mbar_wait(acc_full, 0, status));
     if (ok) {
       tc_fence_after();
       const long long row = static_cast<long long>(b) * T + j * 128 + r;
       __nv_bfloat16* dk = dqkv + row * 3 * C + C + h * D + half * (D / 2);
       __nv_bfloat16* dv = dk + C;
+#pragma unroll 1
+      for (int g = 0; g < 2 * (D / 64); ++g) {  // dK chunks, then dV chunks
+        const int c = g % (D / 64);
+        float kv[32];
+        tmem_ld_32((g < D / 64 ? tK : tV) + lane_base + half * (D / 2) + c * 32, kv);
+        __nv_bfloat16* dst = (g < D / 64 ? dk : dv) + c * 32;
 #pragma unroll
-      for (int c = 0; c < D / 64; ++c) {
-        float kv[32], vv[32];
-        tmem_ld_32(tK + lane_base + half * (D / 2) + c * 32, kv);
-        tmem_ld_32(tV + lane_base + half * (D / 2) + c * 32, vv);
-#pragma unroll
-        for (int t = 0; t < 32; t += 8) {
-          *reinterpret_cast<uint4*>(dk + c * 32 + t) =
+        for (int t = 0; t < 32; t += 8)
+          *reinterpret_cast<uint4*>(dst + t) =
               make_uint4(pack_bf16x2(kv[t], kv[t + 1]), pack_bf16x2(kv[t + 2], kv[t + 3]),
                          pack_bf16x2(kv[t + 4], kv[t + 5]), pack_bf16x2(kv[t + 6], kv[t + 7]));
-          *reinterpret_cast<uint4*>(dv + c * 32 + t) =
-              make_uint4(pack_bf16x2(vv[t], vv[t + 1]), pack_bf16x2(vv[t + 2], vv[t + 3]),
-                         pack_bf16x2(vv[t + 4], vv[t + 5]), pack_bf16x2(vv[t + 6], vv[t + 7]));
-        }
       }
     }
   }
@@ -649,12 +727,14 @@ void flash_attn_bwd_tc_launch(torch::Tensor qkv, torch::Tensor dout, torch::Tens
   c10::cuda::CUDAGuard g(qkv.device());
   CUtensorMap mqkv = make_tma_2d_bf16(qkv.data_ptr(), C3, static_cast<uint64_t>(B) * T, C3, 64, 128);
   CUtensorMap mdo = make_tma_2d_bf16(dout.data_ptr(), C, static_cast<uint64_t>(B) * T, C, 64, 128);
+  TORCH_CHECK(dq_acc.is_contiguous() && dq_acc.numel() == static_cast<int64_t>(B) * T * C, "dq_acc [B, T, C] fp32");
+  CUtensorMap mdq = make_tma_2d_f32(dq_acc.data_ptr(), C, static_cast<uint64_t>(B) * T, C, 32, 128);
   dim3 grid(T / 128, B * H);
   auto stream = at::cuda::getCurrentCUDAStream();
   auto run = [&](auto kern, uint32_t smem) {
     C10_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
     kern<<<grid, fatc::kBwdThreads, smem, stream>>>(
-        mqkv, mdo, lse.data_ptr<float>(), delta.data_ptr<float>(), dq_acc.data_ptr<float>(),
+        mqkv, mdo, mdq, lse.data_ptr<float>(), delta.data_ptr<float>(),
         reinterpret_cast<__nv_bfloat16*>(dqkv.data_ptr()), H, T, static_cast<float>(scale), status.data_ptr<int>());
   };
   if (D == 64) run(fatc::fa_bwd_tc_kernel<64, 2>, fatc::BwdSmem<64, 2>::total);

@@ -270,19 +270,6 @@ MNB_DEVICE void epilogue_store(const GemmArgs& a, int row, int col0, float* v) {
   }
 }
 
-MNB_DEVICE void tma_store_2d(const CUtensorMap* map, uint32_t src, int32_t x, int32_t y) {
-  asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%1, %2}], [%3];" ::"l"(
-                   reinterpret_cast<uint64_t>(map)),
-               "r"(x), "r"(y), "r"(src)
-               : "memory");
-}
-MNB_DEVICE void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
-template <int N>
-MNB_DEVICE void bulk_wait_read() {
-  asm volatile("cp.async.bulk.wait_group.read %0;" ::"n"(N) : "memory");
-}
-MNB_DEVICE void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
-
 // Write 32 bf16 values (one row segment) as 16-byte chunks sub*4.. of a
 // 32-row x 128-byte box laid out in the 128-byte swizzle (conflict-free).
 MNB_DEVICE void stage_row32(uint8_t* box, int row, int sub, const float* v) {
@@ -856,6 +843,24 @@ CUtensorMap make_tma_2d_bf16(const void* base, uint64_t inner, uint64_t outer, u
                            box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
                            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   TORCH_CHECK(r == CUDA_SUCCESS, "cuTensorMapEncodeTiled failed: ", static_cast<int>(r));
+  return map;
+}
+
+// fp32 [outer, inner] matrix, 128-byte swizzle: box_inner * 4 must be <= 128.
+CUtensorMap make_tma_2d_f32(const void* base, uint64_t inner, uint64_t outer, uint64_t row_stride_elems,
+                            uint32_t box_inner, uint32_t box_outer) {
+  TORCH_CHECK(reinterpret_cast<uintptr_t>(base) % 16 == 0, "TMA base address must be 16-byte aligned");
+  TORCH_CHECK((row_stride_elems * 4) % 16 == 0, "TMA row stride must be a multiple of 16 bytes");
+  TORCH_CHECK(box_inner * 4 <= 128, "128-byte swizzle: inner box of at most 32 floats");
+  CUtensorMap map;
+  cuuint64_t dims[2] = {inner, outer};
+  cuuint64_t strides[1] = {row_stride_elems * 4};
+  cuuint32_t box[2] = {box_inner, box_outer};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = encode_fn()(&map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<void*>(base), dims, strides,
+                           box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                           CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  TORCH_CHECK(r == CUDA_SUCCESS, "cuTensorMapEncodeTiled (fp32) failed: ", static_cast<int>(r));
   return map;
 }
 
