@@ -407,6 +407,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
   using S = BwdSmem<D, STAGES>;
   constexpr uint32_t kTmemCols = 512;
   constexpr bool kOwnDq = 128 + 128 + 3 * D <= 512;  // dQ in its own columns (D = 64)
+  constexpr bool kAhead = kOwnDq && STAGES >= 2;      // next tile's S issued before this tile's dK / dQ
   constexpr uint32_t kIdSq = idesc_bf16(128, 128, false, false);  // S^T, dP^T
   constexpr uint32_t kIdKV = idesc_bf16(128, D, false, true);     // dV, dK
   constexpr uint32_t kIdQ = idesc_bf16(128, D, true, true);       // dQ
@@ -500,56 +501,109 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       bool ok = mbar_wait(kv_full, 0, status);
       const uint32_t ka0 = sbase + S::k_off, va0 = sbase + S::v_off;
       const uint32_t pa0 = sbase + S::p_off, dsa0 = sbase + S::ds_off;
-#pragma unroll 1
-      for (int it = 0; it < n_it && ok; ++it) {
-        const int st = it % STAGES;
-        const uint32_t par = it & 1;
-        uint32_t qa = sbase + S::st_off + st * S::stage_bytes, doa = qa + S::tile;
-        uint32_t ka = ka0, va = va0, pa = pa0, dsa = dsa0;
-        // Opaque per iteration: keeps the ~40 descriptors from being hoisted
-        // out of the loop into registers (and from there into local memory).
-        asm volatile("" : "+r"(ka), "+r"(va), "+r"(pa), "+r"(dsa), "+r"(qa), "+r"(doa));
-        ok = mbar_wait(q_full0 + 8 * st, (it / STAGES) & 1, status) && mbar_wait(s_free, par ^ 1, status);
-        if (!ok) break;
-        tc_fence_after();
+      // Shared-memory operand addresses of query tile `it`, opaque to the
+      // compiler so the ~40 descriptors are rebuilt per tile instead of being
+      // hoisted into registers (and from there into local memory).
+      struct Ops { uint32_t ka, va, pa, dsa, qa, doa; };
+      auto ops = [&](int it) {
+        Ops o{ka0, va0, pa0, dsa0, sbase + S::st_off + (it % STAGES) * S::stage_bytes, 0};
+        o.doa = o.qa + S::tile;
+        asm volatile("" : "+r"(o.ka), "+r"(o.va), "+r"(o.pa), "+r"(o.dsa), "+r"(o.qa), "+r"(o.doa));
+        return o;
+      };
+      auto mma_s = [&](const Ops& o) {  // S^T = K Q^T
 #pragma unroll
-        for (int kk = 0; kk < D / 16; ++kk)  // S^T = K Q^T
-          tc_mma(tS, smem_desc_sw128(ka + (kk / 4) * 16384 + (kk % 4) * 32, 16, 1024),
-                 smem_desc_sw128(qa + (kk / 4) * 16384 + (kk % 4) * 32, 16, 1024), kIdSq, kk > 0 ? 1u : 0u);
+        for (int kk = 0; kk < D / 16; ++kk)
+          tc_mma(tS, smem_desc_sw128(o.ka + (kk / 4) * 16384 + (kk % 4) * 32, 16, 1024),
+                 smem_desc_sw128(o.qa + (kk / 4) * 16384 + (kk % 4) * 32, 16, 1024), kIdSq, kk > 0 ? 1u : 0u);
         tc_commit(s_full);
-        if (!kOwnDq) {  // dQ of the previous tile lives in the dP^T columns
-          if (!(ok = mbar_wait(dq_free, par ^ 1, status))) break;
-          tc_fence_after();
-        }
+      };
+      auto mma_dp = [&](const Ops& o) {  // dP^T = V dO^T
 #pragma unroll
-        for (int kk = 0; kk < D / 16; ++kk)  // dP^T = V dO^T
-          tc_mma(tP, smem_desc_sw128(va + (kk / 4) * 16384 + (kk % 4) * 32, 16, 1024),
-                 smem_desc_sw128(doa + (kk / 4) * 16384 + (kk % 4) * 32, 16, 1024), kIdSq, kk > 0 ? 1u : 0u);
+        for (int kk = 0; kk < D / 16; ++kk)
+          tc_mma(tP, smem_desc_sw128(o.va + (kk / 4) * 16384 + (kk % 4) * 32, 16, 1024),
+                 smem_desc_sw128(o.doa + (kk / 4) * 16384 + (kk % 4) * 32, 16, 1024), kIdSq, kk > 0 ? 1u : 0u);
         tc_commit(dp_full);
-        if (!(ok = mbar_wait(p_full, par, status))) break;
-        tc_fence_after();
+      };
+      auto mma_dv = [&](const Ops& o, int it) {  // dV += P^T dO   (K = 128 queries)
 #pragma unroll
-        for (int kk = 0; kk < 8; ++kk)  // dV += P^T dO   (K = 128 queries)
-          tc_mma(tV, smem_desc_sw128(pa + (kk / 4) * 16384 + (kk % 4) * 32, 16, 1024),
-                 smem_desc_sw128(doa + kk * 2048, 16384, 1024), kIdKV, (it > 0 || kk > 0) ? 1u : 0u);
+        for (int kk = 0; kk < 8; ++kk)
+          tc_mma(tV, smem_desc_sw128(o.pa + (kk / 4) * 16384 + (kk % 4) * 32, 16, 1024),
+                 smem_desc_sw128(o.doa + kk * 2048, 16384, 1024), kIdKV, (it > 0 || kk > 0) ? 1u : 0u);
         tc_commit(p_free);
-        if (!(ok = mbar_wait(ds_full, par, status))) break;
-        tc_fence_after();
+      };
+      auto mma_dk = [&](const Ops& o, int it) {  // dK += dS^T Q
 #pragma unroll
-        for (int kk = 0; kk < 8; ++kk)  // dK += dS^T Q
-          tc_mma(tK, smem_desc_sw128(dsa + (kk / 4) * 16384 + (kk % 4) * 32, 16, 1024),
-                 smem_desc_sw128(qa + kk * 2048, 16384, 1024), kIdKV, (it > 0 || kk > 0) ? 1u : 0u);
-        if (kOwnDq) {
-          if (!(ok = mbar_wait(dq_free, par ^ 1, status))) break;
-          tc_fence_after();
-        }
+        for (int kk = 0; kk < 8; ++kk)
+          tc_mma(tK, smem_desc_sw128(o.dsa + (kk / 4) * 16384 + (kk % 4) * 32, 16, 1024),
+                 smem_desc_sw128(o.qa + kk * 2048, 16384, 1024), kIdKV, (it > 0 || kk > 0) ? 1u : 0u);
+      };
+      auto mma_dq = [&](const Ops& o, int it) {  // dQ = dS K   (A = dS read MN-major, K = 128 keys)
 #pragma unroll
-        for (int kk = 0; kk < 8; ++kk)  // dQ = dS K   (A = dS read MN-major, K = 128 keys)
-          tc_mma(tQ, smem_desc_sw128(dsa + kk * 2048, 16384, 1024), smem_desc_sw128(ka + kk * 2048, 16384, 1024),
-                 kIdQ, kk > 0 ? 1u : 0u);
+        for (int kk = 0; kk < 8; ++kk)
+          tc_mma(tQ, smem_desc_sw128(o.dsa + kk * 2048, 16384, 1024),
+                 smem_desc_sw128(o.ka + kk * 2048, 16384, 1024), kIdQ, kk > 0 ? 1u : 0u);
         tc_commit(dq_full);
         tc_commit(ds_free);
-        tc_commit(q_empty0 + 8 * st);
+        tc_commit(q_empty0 + 8 * (it % STAGES));
+      };
+      auto q_ready = [&](int it) { return mbar_wait(q_full0 + 8 * (it % STAGES), (it / STAGES) & 1, status); };
+      if constexpr (kAhead) {
+        // S of the next query tile is issued before dK / dQ of this one, so the
+        // compute warps find it ready when they finish dS; dP of the next tile
+        // follows dQ.  Needs a second Q / dO stage and dQ in its own columns.
+        if (ok && (ok = q_ready(0))) {
+          tc_fence_after();
+          const Ops o = ops(0);
+          mma_s(o);
+          mma_dp(o);
+        }
+#pragma unroll 1
+        for (int it = 0; it < n_it && ok; ++it) {
+          const uint32_t par = it & 1;
+          const Ops o = ops(it);
+          if (!(ok = mbar_wait(p_full, par, status))) break;
+          tc_fence_after();
+          mma_dv(o, it);
+          const bool more = it + 1 < n_it;
+          if (more) {
+            if (!(ok = q_ready(it + 1) && mbar_wait(s_free, par, status))) break;
+            tc_fence_after();
+            mma_s(ops(it + 1));
+          }
+          if (!(ok = mbar_wait(ds_full, par, status))) break;
+          tc_fence_after();
+          mma_dk(o, it);
+          if (!(ok = mbar_wait(dq_free, par ^ 1, status))) break;
+          tc_fence_after();
+          mma_dq(o, it);
+          if (more) mma_dp(ops(it + 1));
+        }
+      } else {
+#pragma unroll 1
+        for (int it = 0; it < n_it && ok; ++it) {
+          const uint32_t par = it & 1;
+          const Ops o = ops(it);
+          if (!(ok = q_ready(it) && mbar_wait(s_free, par ^ 1, status))) break;
+          tc_fence_after();
+          mma_s(o);
+          if (!kOwnDq) {  // dQ of the previous tile lives in the dP^T columns
+            if (!(ok = mbar_wait(dq_free, par ^ 1, status))) break;
+            tc_fence_after();
+          }
+          mma_dp(o);
+          if (!(ok = mbar_wait(p_full, par, status))) break;
+          tc_fence_after();
+          mma_dv(o, it);
+          if (!(ok = mbar_wait(ds_full, par, status))) break;
+          tc_fence_after();
+          mma_dk(o, it);
+          if (kOwnDq) {
+            if (!(ok = mbar_wait(dq_free, par ^ 1, status))) break;
+            tc_fence_after();
+          }
+          mma_dq(o, it);
+        }
       }
       if (ok) tc_commit(acc_full);
     }
@@ -566,20 +620,17 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     const uint32_t stg_free = stg_free0 + 8 * half, stg_full = stg_full0 + 8 * half;
     const bool leader = warp == 2 + 4 * half && lane == 0;  // issues this half's reduces
     uint32_t uses = 0;  // staging-box uses of this half so far (mbarrier phase)
-    bool ok = true;
-#pragma unroll 1
-    for (int it = 0; it < n_it; ++it) {
-      const int i = j + it, st = it % STAGES;
+    uint32_t pk[32];    // this row of P^T as bf16 pairs: the values the dV MMA reads, reused for dS
+    auto lse_of = [&](int it) { return sbase + S::st_off + (it % STAGES) * S::stage_bytes + 2 * S::tile; };
+    // P^T = exp2(S^T * scale * log2e - lse * log2e), causal mask on the diagonal tile
+    auto p_phase = [&](int it) -> bool {
       const uint32_t par = it & 1;
-      const uint32_t st_lse = sbase + S::st_off + st * S::stage_bytes + 2 * S::tile;  // float[128]
-      const uint32_t st_dl = st_lse + 512;
-      const bool diag = i == j;
-      uint32_t pk[32];  // this row of P^T as bf16 pairs: the values the dV MMA reads, reused for dS
-      // P^T = exp2(S^T * scale * log2e - lse * log2e), causal mask on the diagonal tile
-      ok = __all_sync(0xffffffffu, mbar_wait(s_full, par, status));
+      bool ok = __all_sync(0xffffffffu, mbar_wait(s_full, par, status));
       if (ok && it > 0) ok = __all_sync(0xffffffffu, mbar_wait(p_free, par ^ 1, status));
-      if (!ok) break;
+      if (!ok) return false;
       tc_fence_after();
+      const uint32_t st_lse = lse_of(it);  // float[128]
+      const bool diag = it == 0;
 #pragma unroll
       for (int c = 0; c < 2; ++c) {
         float sv[32];
@@ -600,11 +651,16 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       mbar_arrive(s_free);
       fence_async_smem();
       mbar_arrive(p_full);
-      // dS^T = scale * P^T (dP^T - delta)
-      ok = __all_sync(0xffffffffu, mbar_wait(dp_full, par, status));
+      return true;
+    };
+    // dS^T = scale * P^T (dP^T - delta)
+    auto ds_phase = [&](int it) -> bool {
+      const uint32_t par = it & 1;
+      bool ok = __all_sync(0xffffffffu, mbar_wait(dp_full, par, status));
       if (ok && it > 0) ok = __all_sync(0xffffffffu, mbar_wait(ds_free, par ^ 1, status));
-      if (!ok) break;
+      if (!ok) return false;
       tc_fence_after();
+      const uint32_t st_dl = lse_of(it) + 512;  // float[128]
 #pragma unroll
       for (int c = 0; c < 2; ++c) {
         float dv[32];
@@ -622,10 +678,12 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       tc_fence_before();
       fence_async_smem();
       mbar_arrive(ds_full);
-      // dQ_i rows (TMEM lane = query): TMEM -> registers (columns freed at
-      // once) -> swizzled staging box -> one TMA reduce-add per 32 columns.
-      ok = __all_sync(0xffffffffu, mbar_wait(dq_full, par, status));
-      if (!ok) break;
+      return true;
+    };
+    // dQ_i rows (TMEM lane = query): TMEM -> registers (columns freed at
+    // once) -> swizzled staging box -> one TMA reduce-add per 32 columns.
+    auto flush = [&](int it) -> bool {
+      if (!__all_sync(0xffffffffu, mbar_wait(dq_full, it & 1, status))) return false;
       tc_fence_after();
       float qv[D / 2];
 #pragma unroll
@@ -638,20 +696,30 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
           bulk_wait_read<0>();
           mbar_arrive(stg_free);
         }
-        ok = __all_sync(0xffffffffu, mbar_wait(stg_free, uses & 1, status));
-        if (!ok) break;
+        if (!__all_sync(0xffffffffu, mbar_wait(stg_free, uses & 1, status))) return false;
         store_row_f32(dq_row, x, qv + c * 32);
         fence_async_smem();
         mbar_arrive(stg_full);
         bool staged = true;
         if (leader && (staged = mbar_wait(stg_full, uses & 1, status))) {
-          tma_reduce_add_2d(&map_dq, dq_box, h * D + half * (D / 2) + c * 32, b * T + i * 128);
+          tma_reduce_add_2d(&map_dq, dq_box, h * D + half * (D / 2) + c * 32, b * T + (j + it) * 128);
           bulk_commit();
         }
-        if (!(ok = __all_sync(0xffffffffu, staged))) break;
+        if (!__all_sync(0xffffffffu, staged)) return false;
       }
-      ok = __all_sync(0xffffffffu, ok);
-      if (!ok) break;
+      return true;
+    };
+    bool ok = true;
+    if constexpr (kAhead) {
+      // P of the next query tile is computed while dK / dQ of this one run
+      ok = n_it > 0 && p_phase(0);
+#pragma unroll 1
+      for (int it = 0; it < n_it && ok; ++it) {
+        ok = ds_phase(it) && (it + 1 >= n_it || p_phase(it + 1)) && flush(it);
+      }
+    } else {
+#pragma unroll 1
+      for (int it = 0; it < n_it && ok; ++it) ok = p_phase(it) && ds_phase(it) && flush(it);
     }
     if (leader) bulk_wait_all();  // dQ adds complete before the CTA exits
     if (ok) ok = __all_sync(0xffffffffu, mbar_wait(acc_full, 0, status));
