@@ -22,6 +22,8 @@
 #include <c10/cuda/CUDAGuard.h>
 #include <torch/extension.h>
 
+#include <cstdlib>
+
 #include "common.cuh"
 
 namespace mnb {
@@ -396,6 +398,260 @@ MNB_DEVICE void store_row_f32(uint32_t rowb, int x, const float* v) {
   for (int k = 0; k < 8; ++k)
     st_shared_v4(rowb + ((k ^ x) << 4), __float_as_uint(v[4 * k]), __float_as_uint(v[4 * k + 1]),
                  __float_as_uint(v[4 * k + 2]), __float_as_uint(v[4 * k + 3]));
+}
+
+// ===========================================================================
+// Forward, two query tiles per CTA (head dim 64, T % 256 == 0).
+//
+// The CTA owns query tiles A = [q0, q0+128) and B = [q0+128, q0+256) of one
+// (batch, head); each has its own S (TMEM cols [0,128) / [128,256)), O
+// accumulator ([256,320) / [320,384)) and P tile in shared memory, and its own
+// softmax warpgroup (warps 2-5 for A, 6-9 for B) in which every thread owns
+// one full query row, so the row max and sum need no exchange between warps.
+// The MMA warp issues S_A(j), PV_A(j-1), S_B(j), PV_B(j-1): while one
+// warpgroup runs the exponentials of its tile the tensor core works on the
+// other tile's products.  K_j / V_j are loaded once for both tiles.  Same
+// online softmax, outputs and LSE as fa_fwd_tc_kernel.
+// ===========================================================================
+constexpr int kPPThreads = 64 + 256;
+
+struct PPSmem {
+  static constexpr uint32_t tile = 128 * 64 * 2;  // [128 rows x 64] bf16: one 128-byte-swizzle atom
+  static constexpr uint32_t q_off = 0;            // Q_A, Q_B
+  static constexpr uint32_t k_off = 2 * tile;     // two stages
+  static constexpr uint32_t v_off = 4 * tile;     // two stages
+  static constexpr uint32_t p_off = 6 * tile;     // P_A, P_B: [128 x 128 keys] bf16, two atoms each
+  static constexpr uint32_t bar_off = 10 * tile;
+  static constexpr int n_bars = 1 + 12 + 8;
+  static constexpr uint32_t total = bar_off + n_bars * 8 + 16 + 1024;
+};
+
+__global__ void __launch_bounds__(kPPThreads, 1)
+    fa_fwd_pp_kernel(const __grid_constant__ CUtensorMap map_qkv, __nv_bfloat16* __restrict__ o,
+                     float* __restrict__ lse, int H, int T, float scale, int* status) {
+  using S = PPSmem;
+  constexpr int D = 64;
+  constexpr uint32_t kIdescS = idesc_bf16(128, 128, false, false);
+  constexpr uint32_t kIdescO = idesc_bf16(128, D, false, true);
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const uint32_t sbase = smem_u32(sm);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sm + S::bar_off);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + S::n_bars);
+  const uint32_t b0 = smem_u32(bars);
+  const uint32_t q_full = b0;
+  // per tile t: s_full, s_free, p_full, p_free, o_full, o_free
+  auto tb = [&](int k, int t) { return b0 + 8 * (1 + 2 * k + t); };
+  const uint32_t kv0 = b0 + 8 * 13;  // k_full[2], k_empty[2], v_full[2], v_empty[2]
+  auto k_full = [&](int st) { return kv0 + 8 * st; };
+  auto k_empty = [&](int st) { return kv0 + 16 + 8 * st; };
+  auto v_full = [&](int st) { return kv0 + 32 + 8 * st; };
+  auto v_empty = [&](int st) { return kv0 + 48 + 8 * st; };
+
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  const int pair = gridDim.x - 1 - blockIdx.x;  // longest causal rows first
+  const int bh = blockIdx.y;
+  const int b = bh / H, h = bh % H;
+  const int q0 = pair * 256;
+  const int C = H * D;
+  const int n_b = 2 * pair + 2;  // key tiles of tile B; tile A has one fewer
+
+  if (threadIdx.x == 0) {
+    mbar_init(q_full, 1);
+    for (int t = 0; t < 2; ++t) {
+      mbar_init(tb(0, t), 1);    // s_full
+      mbar_init(tb(1, t), 128);  // s_free
+      mbar_init(tb(2, t), 128);  // p_full
+      mbar_init(tb(3, t), 1);    // p_free
+      mbar_init(tb(4, t), 1);    // o_full
+      mbar_init(tb(5, t), 128);  // o_free
+    }
+    for (int st = 0; st < 2; ++st) {
+      mbar_init(k_full(st), 1);
+      mbar_init(k_empty(st), 1);
+      mbar_init(v_full(st), 1);
+      mbar_init(v_empty(st), 1);
+    }
+    fence_mbar_init();
+    tma_prefetch_desc(&map_qkv);
+  }
+  if (warp == 1) {
+    tmem_alloc(smem_u32(tmem_slot), 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      const int row0 = b * T;
+      mbar_arrive_expect_tx(q_full, 2 * S::tile);
+      tma_load_2d(sbase + S::q_off, &map_qkv, h * D, row0 + q0, q_full);
+      tma_load_2d(sbase + S::q_off + S::tile, &map_qkv, h * D, row0 + q0 + 128, q_full);
+      for (int j = 0; j < n_b; ++j) {
+        const int st = j % 2;
+        const uint32_t ph = (j / 2) & 1;
+        if (!mbar_wait(k_empty(st), ph ^ 1, status)) break;
+        mbar_arrive_expect_tx(k_full(st), S::tile);
+        tma_load_2d(sbase + S::k_off + st * S::tile, &map_qkv, C + h * D, row0 + j * 128, k_full(st));
+        if (!mbar_wait(v_empty(st), ph ^ 1, status)) break;
+        mbar_arrive_expect_tx(v_full(st), S::tile);
+        tma_load_2d(sbase + S::v_off + st * S::tile, &map_qkv, 2 * C + h * D, row0 + j * 128, v_full(st));
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      bool ok = mbar_wait(q_full, 0, status);
+      auto mma_s = [&](int t, int j) -> bool {  // S_t = Q_t K_j^T
+        if (!mbar_wait(tb(1, t), (j & 1) ^ 1, status)) return false;
+        tc_fence_after();
+        const uint32_t qa = sbase + S::q_off + t * S::tile, kb = sbase + S::k_off + (j % 2) * S::tile;
+#pragma unroll
+        for (int kk = 0; kk < D / 16; ++kk)
+          tc_mma(tmem + 128 * t, smem_desc_sw128(qa + kk * 32, 16, 1024), smem_desc_sw128(kb + kk * 32, 16, 1024),
+                 kIdescS, kk > 0 ? 1u : 0u);
+        tc_commit(tb(0, t));
+        return true;
+      };
+      auto mma_pv = [&](int t, int j) -> bool {  // O_t = P_t V_j
+        if (!mbar_wait(tb(2, t), j & 1, status) || !mbar_wait(tb(5, t), (j & 1) ^ 1, status)) return false;
+        tc_fence_after();
+        const uint32_t pa = sbase + S::p_off + t * 2 * S::tile, vb = sbase + S::v_off + (j % 2) * S::tile;
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk)
+          tc_mma(tmem + 256 + D * t, smem_desc_sw128(pa + (kk / 4) * S::tile + (kk % 4) * 32, 16, 1024),
+                 smem_desc_sw128(vb + kk * 2048, S::tile, 1024), kIdescO, kk > 0 ? 1u : 0u);
+        tc_commit(tb(4, t));
+        tc_commit(tb(3, t));
+        return true;
+      };
+#pragma unroll 1
+      for (int j = 0; j <= n_b && ok; ++j) {
+        if (j < n_b) {
+          if (!(ok = mbar_wait(k_full(j % 2), (j / 2) & 1, status))) break;
+          tc_fence_after();
+        }
+        if (j >= 1) {
+          if (!(ok = mbar_wait(v_full((j - 1) % 2), ((j - 1) / 2) & 1, status))) break;
+          tc_fence_after();
+        }
+        for (int t = 0; t < 2 && ok; ++t) {
+          const int n_t = n_b - 1 + t;
+          if (j < n_t) ok = mma_s(t, j);
+          if (ok && j >= 1 && j <= n_t) ok = mma_pv(t, j - 1);
+        }
+        if (!ok) break;
+        if (j < n_b) tc_commit(k_empty(j % 2));
+        if (j >= 1) tc_commit(v_empty((j - 1) % 2));
+      }
+    }
+  } else {
+    const int t = (warp - 2) / 4;  // query tile of this warpgroup
+    const int qd = warp & 3;
+    const int r = qd * 32 + lane;
+    const int qrow = q0 + t * 128 + r;
+    const int n = n_b - 1 + t;
+    const int diag = n - 1;  // the one key tile that needs the causal mask
+    const uint32_t lane_base = static_cast<uint32_t>(qd * 32) << 16;
+    const uint32_t s_cols = tmem + 128 * t + lane_base, o_cols = tmem + 256 + D * t + lane_base;
+    const uint32_t s_full = tb(0, t), s_free = tb(1, t), p_full = tb(2, t), p_free = tb(3, t), o_full = tb(4, t),
+                   o_free = tb(5, t);
+    const int x = r % 8;
+    const uint32_t p_row = row_base(sbase + S::p_off + t * 2 * S::tile, r);
+    const float sl2 = scale * kLog2e;
+    float oacc[D];
+#pragma unroll
+    for (int i = 0; i < D; ++i) oacc[i] = 0.f;
+    float m_run = -INFINITY, l_run = 0.f, alpha_prev = 0.f;  // m_run in scaled log2 units
+    auto fold = [&](int j) -> bool {  // oacc = oacc * alpha_prev + O(j)
+      if (!__all_sync(0xffffffffu, mbar_wait(o_full, j & 1, status))) return false;
+      tc_fence_after();
+#pragma unroll
+      for (int c = 0; c < D / 32; ++c) {
+        float ov[32];
+        tmem_ld_32(o_cols + c * 32, ov);
+#pragma unroll
+        for (int i = 0; i < 32; ++i) oacc[c * 32 + i] = fmaf(oacc[c * 32 + i], alpha_prev, ov[i]);
+      }
+      tc_fence_before();
+      mbar_arrive(o_free);
+      return true;
+    };
+    bool ok = true;
+#pragma unroll 1
+    for (int j = 0; j < n; ++j) {
+      if (!(ok = __all_sync(0xffffffffu, mbar_wait(s_full, j & 1, status)))) break;
+      tc_fence_after();
+      const bool masked = j == diag;
+      const int k0 = j * 128;
+      float mx = -INFINITY;
+#pragma unroll 1
+      for (int c = 0; c < 4; ++c) {
+        float sv[32];
+        tmem_ld_32(s_cols + c * 32, sv);
+        if (masked) {
+#pragma unroll
+          for (int i = 0; i < 32; ++i)
+            if (k0 + c * 32 + i <= qrow) mx = fmaxf(mx, sv[i]);
+        } else {
+#pragma unroll
+          for (int i = 0; i < 32; ++i) mx = fmaxf(mx, sv[i]);
+        }
+      }
+      const float m_new = fmaxf(m_run, mx * sl2);
+      const float alpha = m_run == -INFINITY ? 0.f : fast_exp2(m_run - m_new);
+      if (j >= 1 && !(ok = __all_sync(0xffffffffu, mbar_wait(p_free, (j - 1) & 1, status)))) break;
+      float rs = 0.f;
+#pragma unroll 1
+      for (int c = 0; c < 4; ++c) {
+        float sv[32];
+        tmem_ld_32(s_cols + c * 32, sv);
+        uint32_t w[16];
+#pragma unroll
+        for (int i = 0; i < 32; i += 2) {
+          float p0 = fast_exp2(fmaf(sv[i], sl2, -m_new));
+          float p1 = fast_exp2(fmaf(sv[i + 1], sl2, -m_new));
+          if (masked) {
+            if (k0 + c * 32 + i > qrow) p0 = 0.f;
+            if (k0 + c * 32 + i + 1 > qrow) p1 = 0.f;
+          }
+          rs += p0 + p1;
+          w[i / 2] = pack_bf16x2(p0, p1);
+        }
+        store_row_words(p_row + (c / 2) * S::tile, x, c % 2, w);
+      }
+      tc_fence_before();
+      mbar_arrive(s_free);
+      fence_async_smem();
+      mbar_arrive(p_full);
+      l_run = l_run * alpha + rs;
+      if (j >= 1 && !(ok = fold(j - 1))) break;
+      alpha_prev = alpha;
+      m_run = m_new;
+    }
+    if (ok) ok = fold(n - 1);
+    if (ok) {
+      const float inv = l_run > 0.f ? 1.f / l_run : 0.f;
+      __nv_bfloat16* orow = o + (static_cast<long long>(b) * T + qrow) * C + h * D;
+#pragma unroll
+      for (int c = 0; c < D / 8; ++c)
+        *reinterpret_cast<uint4*>(orow + 8 * c) =
+            make_uint4(pack_bf16x2(oacc[8 * c] * inv, oacc[8 * c + 1] * inv),
+                       pack_bf16x2(oacc[8 * c + 2] * inv, oacc[8 * c + 3] * inv),
+                       pack_bf16x2(oacc[8 * c + 4] * inv, oacc[8 * c + 5] * inv),
+                       pack_bf16x2(oacc[8 * c + 6] * inv, oacc[8 * c + 7] * inv));
+      lse[(static_cast<long long>(b) * H + h) * T + qrow] = (m_run + log2f(l_run)) / kLog2e;
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
 }
 
 template <int D, int STAGES>
@@ -773,8 +1029,15 @@ void flash_attn_fwd_tc(torch::Tensor qkv, torch::Tensor o, torch::Tensor lse, in
                                                  lse.data_ptr<float>(), H, T, static_cast<float>(scale),
                                                  status.data_ptr<int>());
   };
-  if (D == 64) run(fatc::fa_fwd_tc_kernel<64, 2>, fatc::Smem<64, 2>::total);
-  else run(fatc::fa_fwd_tc_kernel<128, 2>, fatc::Smem<128, 2>::total);
+  static const bool single = std::getenv("MNB_ATTN_FWD_SINGLE") != nullptr;  // A/B switch for benchmarks
+  if (D == 64 && T % 256 == 0 && !single) {
+    grid.x = T / 256;
+    run(fatc::fa_fwd_pp_kernel, fatc::PPSmem::total);
+  } else if (D == 64) {
+    run(fatc::fa_fwd_tc_kernel<64, 2>, fatc::Smem<64, 2>::total);
+  } else {
+    run(fatc::fa_fwd_tc_kernel<128, 2>, fatc::Smem<128, 2>::total);
+  }
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
