@@ -346,6 +346,123 @@ __global__ void __launch_bounds__(256, 1) layernorm_bwd_kernel(const __nv_bfloat
   fold_into(part, sacc, 2 * C, out_dw, out_db, C, out_f32, accumulate);
 }
 
+// Same result as layernorm_bwd_kernel<NCH> (C = NCH * 256), with the x and dy
+// rows brought into shared memory by bulk (TMA) copies DEPTH rows ahead of
+// each warp: a warp keeps DEPTH rows (DEPTH x 2 x C x 2 bytes) in flight
+// instead of the two it can hold in registers, which is what reaching HBM
+// bandwidth takes at one CTA per SM.  Each warp owns a private ring of DEPTH
+// row slots with one mbarrier per slot; lane 0 refills a slot once the warp
+// has consumed it.  dgamma / dbeta as in the register kernel.
+MNB_DEVICE void ld_shared_bf16x8(uint32_t addr, float* f) {
+  uint32_t w0, w1, w2, w3;
+  asm volatile("ld.shared.v4.b32 {%0, %1, %2, %3}, [%4];" : "=r"(w0), "=r"(w1), "=r"(w2), "=r"(w3) : "r"(addr));
+  const uint32_t ws[4] = {w0, w1, w2, w3};
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const float2 t = unpack_bf16x2(ws[j]);
+    f[2 * j] = t.x;
+    f[2 * j + 1] = t.y;
+  }
+}
+
+template <int NCH, int DEPTH>
+constexpr size_t ln_bwd_bulk_smem() {
+  return static_cast<size_t>(kRowWarps) * DEPTH * 4 * NCH * 256 + 2 * NCH * 256 * 4 + kRowWarps * DEPTH * 8 + 128;
+}
+
+template <int NCH, int DEPTH>
+__global__ void __launch_bounds__(256, 1)
+    layernorm_bwd_bulk_kernel(const __nv_bfloat16* __restrict__ dy, const __nv_bfloat16* __restrict__ x,
+                              const __nv_bfloat16* __restrict__ w, const float* __restrict__ mean,
+                              const float* __restrict__ rstd, __nv_bfloat16* __restrict__ dx,
+                              float* __restrict__ part, int rows, int Cdyn, void* out_dw, void* out_db, int out_f32,
+                              int accumulate) {
+  constexpr int C = NCH * 256;
+  constexpr uint32_t kRowBytes = C * 2;
+  extern __shared__ uint8_t ln_raw[];
+  uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(ln_raw) + 127) & ~uintptr_t(127));
+  float* sacc = reinterpret_cast<float*>(base + kRowWarps * DEPTH * 2 * kRowBytes);  // [2][C]
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sacc + 2 * C);                       // [warps][DEPTH]
+  for (int i = threadIdx.x; i < 2 * C; i += blockDim.x) sacc[i] = 0.f;
+  if (threadIdx.x < kRowWarps * DEPTH) mbar_init(smem_u32(bars + threadIdx.x), 1);
+  fence_mbar_init();
+  __syncthreads();
+  const int lane = threadIdx.x % 32, warp = threadIdx.x / 32;
+  const uint32_t wbuf = smem_u32(base) + warp * DEPTH * 2 * kRowBytes;
+  const uint32_t wbar = smem_u32(bars + warp * DEPTH);
+  const int stride = gridDim.x * kRowWarps;
+  const int first = blockIdx.x * kRowWarps + warp;
+  const int n_mine = first < rows ? (rows - first + stride - 1) / stride : 0;
+  auto issue = [&](int k) {  // lane 0: rows of this warp's k-th turn into slot k % DEPTH
+    const long long row = first + static_cast<long long>(k) * stride;
+    const uint32_t dst = wbuf + (k % DEPTH) * 2 * kRowBytes, bar = wbar + 8 * (k % DEPTH);
+    mbar_arrive_expect_tx(bar, 2 * kRowBytes);
+    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
+                 ::"r"(dst), "l"(x + row * C), "r"(kRowBytes), "r"(bar) : "memory");
+    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
+                 ::"r"(dst + kRowBytes), "l"(dy + row * C), "r"(kRowBytes), "r"(bar) : "memory");
+  };
+  if (lane == 0)
+    for (int k = 0; k < DEPTH && k < n_mine; ++k) issue(k);
+  float dg[NCH][8], dbb[NCH][8], ww[NCH][8];
+#pragma unroll
+  for (int k = 0; k < NCH; ++k) {
+    load8(w + k * 256 + lane * 8, ww[k]);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) dg[k][j] = dbb[k][j] = 0.f;
+  }
+#pragma unroll 1
+  for (int k = 0; k < n_mine; ++k) {
+    const int row = first + k * stride;
+    const float mu = mean[row], rs = rstd[row];
+    if (!__all_sync(0xffffffffu, mbar_wait(wbar + 8 * (k % DEPTH), (k / DEPTH) & 1, nullptr))) break;
+    const uint32_t src = wbuf + (k % DEPTH) * 2 * kRowBytes;
+    float xh[NCH][8], g[NCH][8];
+#pragma unroll
+    for (int c = 0; c < NCH; ++c) {
+      ld_shared_bf16x8(src + (c * 256 + lane * 8) * 2, xh[c]);
+      ld_shared_bf16x8(src + kRowBytes + (c * 256 + lane * 8) * 2, g[c]);
+    }
+    float a = 0.f, bsum = 0.f;
+#pragma unroll
+    for (int c = 0; c < NCH; ++c)
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        xh[c][j] = (xh[c][j] - mu) * rs;
+        const float d = g[c][j] * ww[c][j];
+        a += d;
+        bsum += d * xh[c][j];
+        dg[c][j] += g[c][j] * xh[c][j];
+        dbb[c][j] += g[c][j];
+      }
+    // every lane's reads of this slot are complete (their values were used above)
+    __syncwarp();
+    if (lane == 0 && k + DEPTH < n_mine) {
+      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+      issue(k + DEPTH);
+    }
+    a = warp_sum(a) / C;
+    bsum = warp_sum(bsum) / C;
+    __nv_bfloat16* dr = dx + static_cast<long long>(row) * C;
+#pragma unroll
+    for (int c = 0; c < NCH; ++c) {
+      float o[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) o[j] = rs * (g[c][j] * ww[c][j] - a - xh[c][j] * bsum);
+      store8(dr + c * 256 + lane * 8, o);
+    }
+  }
+#pragma unroll
+  for (int c = 0; c < NCH; ++c)
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      atomicAdd(&sacc[c * 256 + lane * 8 + j], dg[c][j]);
+      atomicAdd(&sacc[C + c * 256 + lane * 8 + j], dbb[c][j]);
+    }
+  __syncthreads();
+  fold_into(part, sacc, 2 * C, out_dw, out_db, C, out_f32, accumulate);
+}
+
 // Wide rows (C = 8 * blockDim.x, e.g. 2048 / 4096): one block per row, each
 // thread owns 8 columns; the two row sums go through a block reduction, and
 // each thread keeps its columns' weight-gradient sums in registers across
@@ -901,7 +1018,27 @@ void layernorm_bwd(torch::Tensor dy, torch::Tensor x, torch::Tensor w, torch::Te
         reinterpret_cast<__nv_bfloat16*>(dx.data_ptr()), partials.data_ptr<float>(), rows, C, dw.data_ptr(),
         db.data_ptr(), f32 ? 1 : 0, accumulate ? 1 : 0);
   };
-  if (C == 256) launch(layernorm_bwd_kernel<1>);
+  // rows reach shared memory by bulk copies: 16-byte aligned row starts needed
+  const bool bulk = reinterpret_cast<uintptr_t>(x.data_ptr()) % 16 == 0 &&
+                    reinterpret_cast<uintptr_t>(dy.data_ptr()) % 16 == 0 && x.is_contiguous() && dy.is_contiguous();
+  auto launch_bulk = [&](auto kern, size_t bytes) {
+    C10_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(bytes)));
+    int per_sm = 1, sms = 148, dev = 0;
+    C10_CUDA_CHECK(cudaGetDevice(&dev));
+    C10_CUDA_CHECK(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
+    C10_CUDA_CHECK(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, kRowWarps * 32, bytes));
+    const int wave = std::max(1, std::min(blocks, std::max(1, per_sm) * sms));
+    kern<<<wave, kRowWarps * 32, bytes, stream>>>(
+        reinterpret_cast<const __nv_bfloat16*>(dy.data_ptr()), reinterpret_cast<const __nv_bfloat16*>(x.data_ptr()),
+        reinterpret_cast<const __nv_bfloat16*>(w.data_ptr()), mean.data_ptr<float>(), rstd.data_ptr<float>(),
+        reinterpret_cast<__nv_bfloat16*>(dx.data_ptr()), partials.data_ptr<float>(), rows, C, dw.data_ptr(),
+        db.data_ptr(), f32 ? 1 : 0, accumulate ? 1 : 0);
+  };
+  if (bulk && C == 256) launch_bulk(layernorm_bwd_bulk_kernel<1, 8>, ln_bwd_bulk_smem<1, 8>());
+  else if (bulk && C == 512) launch_bulk(layernorm_bwd_bulk_kernel<2, 8>, ln_bwd_bulk_smem<2, 8>());
+  else if (bulk && C == 768) launch_bulk(layernorm_bwd_bulk_kernel<3, 6>, ln_bwd_bulk_smem<3, 6>());
+  else if (bulk && C == 1024) launch_bulk(layernorm_bwd_bulk_kernel<4, 4>, ln_bwd_bulk_smem<4, 4>());
+  else if (C == 256) launch(layernorm_bwd_kernel<1>);
   else if (C == 512) launch(layernorm_bwd_kernel<2>);
   else if (C == 768) launch(layernorm_bwd_kernel<3>);
   else if (C == 1024) launch(layernorm_bwd_kernel<4>);
@@ -926,12 +1063,28 @@ __global__ void __launch_bounds__(256) colsum_fold_kernel(const __nv_bfloat16* _
   const int r1 = min(rows, r0 + kColRows);
   float s[8] = {0, 0, 0, 0, 0, 0, 0, 0};
   if (c0 < C) {
-#pragma unroll 4
-    for (int r = r0 + warp; r < r1; r += 8) {
-      float f[8];
-      load8(g + static_cast<long long>(r) * C + c0, f);
+    // all of this warp's kColRows / 8 rows in flight at once (16 x 16 B per
+    // lane): one warp's loads cover the HBM latency instead of four
+    constexpr int kPer = kColRows / 8;
+    uint4 raw[kPer];
+    const __nv_bfloat16* p = g + static_cast<long long>(r0 + warp) * C + c0;
+    if (r1 - r0 == kColRows) {  // full band: unconditional loads, all issued before the first add
 #pragma unroll
-      for (int j = 0; j < 8; ++j) s[j] += f[j];
+      for (int i = 0; i < kPer; ++i) raw[i] = ld_v4(p + static_cast<long long>(8 * i) * C);
+    } else {
+#pragma unroll
+      for (int i = 0; i < kPer; ++i)
+        raw[i] = r0 + warp + 8 * i < r1 ? ld_v4(p + static_cast<long long>(8 * i) * C) : make_uint4(0u, 0u, 0u, 0u);
+    }
+#pragma unroll
+    for (int i = 0; i < kPer; ++i) {
+      const uint32_t ws[4] = {raw[i].x, raw[i].y, raw[i].z, raw[i].w};
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const float2 f = unpack_bf16x2(ws[j]);
+        s[2 * j] += f.x;
+        s[2 * j + 1] += f.y;
+      }
     }
   }
 #pragma unroll

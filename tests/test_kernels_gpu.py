@@ -102,7 +102,8 @@ def test_gemm_split_k_accumulate():
     close(dw, want, 1e-2)
 
 
-@pytest.mark.parametrize("rows,C", [(1000, 768), (777, 2048), (300, 4096), (64, 640)])
+@pytest.mark.parametrize("rows,C", [(1000, 768), (20000, 768), (5000, 256), (3000, 512), (3000, 1024),
+                                    (777, 2048), (300, 4096), (64, 640)])
 def test_layernorm_forward_backward(rows, C):
     x = rnd(rows, C, seed=15).requires_grad_(True)
     w = (1 + 0.1 * rnd(C, seed=16).float()).to(torch.bfloat16).requires_grad_(True)
@@ -117,6 +118,16 @@ def test_layernorm_forward_backward(rows, C):
     close(x.grad, xr.grad, 3e-2)
     close(w.grad, wr.grad, 2e-2)
     close(b.grad, br.grad, 2e-2)
+
+
+@pytest.mark.parametrize("rows,C", [(16384, 768), (16384, 2304), (1000, 3072), (130, 40)])
+def test_bias_grad_column_sums(rows, C):
+    g = rnd(rows, C, seed=30)
+    want = g.float().sum(0)
+    got = K.bias_grad(g, torch.float32)
+    close(got, want, 1e-2)
+    got2 = K.bias_grad(g, torch.float32)  # the fold accumulator re-zeroes itself between calls
+    close(got2, want, 1e-2)
 
 
 def test_gelu_forward_backward():
