@@ -339,8 +339,14 @@ __global__ void __launch_bounds__(kCommThreads) ar_push_one_shot_kernel(CommArgs
 //   identical bits.  Two barriers; no trailing one is needed because a
 //   peer's next phase-1 writes wait for this rank's phase-2 signal.
 // ---------------------------------------------------------------------------
-template <typename TI, typename TW, int OP>
-__global__ void __launch_bounds__(kCommThreads) ar_push_two_shot_kernel(CommArgs a, long long chunk_u) {
+// THREADS / MINB: the default is 512-thread CTAs.  The "beside compute"
+// variant (128 threads, at most 80 registers) leaves room on an SM for one CTA
+// of the persistent tcgen05 GEMM / attention kernels (320 threads x 168
+// registers): comm CTAs that need a whole SM would keep those kernels' CTAs
+// from starting, and each such CTA's fixed share of tiles would then finish
+// late (DDP runs this kernel during the backward pass).
+template <typename TI, typename TW, int OP, int THREADS = kCommThreads, int MINB = 1>
+__global__ void __launch_bounds__(THREADS, MINB) ar_push_two_shot_kernel(CommArgs a, long long chunk_u) {
   using TA = typename Acc<TW>::type;
   constexpr int V = Vec<TW>::n;
   ring_begin(a);
@@ -390,7 +396,9 @@ __global__ void __launch_bounds__(kCommThreads) ar_push_two_shot_kernel(CommArgs
   if (ok) {
     long long lo, hi;
     sub_range(r, &lo, &hi);
-    constexpr int U2 = 4;  // units per thread per pass: U2 independent loads per source rank
+    // units per thread per pass: U2 independent loads per source rank (2 in
+    // the small-CTA variant, whose 80-register budget holds U2 x V accumulators)
+    constexpr int U2 = THREADS >= 512 ? 4 : 2;
     for (long long u0 = lo + threadIdx.x; u0 < hi; u0 += U2 * blockDim.x) {
       TA accs[U2][V];
       // rank order 0..W-1 on every owner: a fixed summation order
@@ -1142,8 +1150,8 @@ class DeviceCommImpl {
     return a;
   }
 
-  int blocks_for(int64_t bytes, int max_blocks) const {
-    int64_t b = (bytes + (64 << 10) - 1) / (64 << 10);  // ~64 KiB per CTA per call
+  int blocks_for(int64_t bytes, int max_blocks, int64_t per_cta = 64 << 10) const {
+    int64_t b = (bytes + per_cta - 1) / per_cta;  // ~64 KiB per 512-thread CTA per call
     return static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(b, std::min(max_blocks, kMaxCommBlocks))));
   }
 
@@ -1281,8 +1289,13 @@ class DeviceCommImpl {
   }
 
   // algorithm: 0 one_shot, 1 two_shot
+  // max_blocks < 0: two-shot sums run as -max_blocks (at most) small CTAs that
+  // fit beside a persistent GEMM CTA on one SM (for all-reduces overlapped
+  // with compute).  Every rank must pass the same value.
   void all_reduce(torch::Tensor in, torch::Tensor out, int op, int algorithm, int wire_bf16, double scale,
                   int max_blocks) {
+    const bool beside = max_blocks < 0;
+    if (beside) max_blocks = -max_blocks;
     c10::cuda::CUDAGuard g(device_);
     TORCH_CHECK(in.is_contiguous() && out.is_contiguous() && in.numel() == out.numel(), "contiguous, same size");
     const auto dt = in.scalar_type();
@@ -1302,8 +1315,20 @@ class DeviceCommImpl {
     const int64_t V = 16 / wsz;
     const long long chunk_u = ((n / V) + world_ - 1) / world_;
     const int64_t n_pad = (n + V - 1) / V * V;
-    const int blocks = blocks_for(algorithm == 1 ? n * wsz / world_ : n * wsz, max_blocks);
+    const int64_t per_rank = algorithm == 1 ? n * wsz / world_ : n * wsz;
     auto stream = at::cuda::getCurrentCUDAStream();
+    if (beside && algorithm == 1 && op == kSum && (dt == at::kBFloat16 || dt == at::kFloat)) {
+      const int nb = blocks_for(per_rank, max_blocks, 16 << 10);
+      if (dt == at::kBFloat16)
+        ar_push_two_shot_kernel<__nv_bfloat16, __nv_bfloat16, kSum, 128, 6><<<nb, 128, 0, stream>>>(a, chunk_u);
+      else if (wire_bf16)
+        ar_push_two_shot_kernel<float, __nv_bfloat16, kSum, 128, 6><<<nb, 128, 0, stream>>>(a, chunk_u);
+      else
+        ar_push_two_shot_kernel<float, float, kSum, 128, 6><<<nb, 128, 0, stream>>>(a, chunk_u);
+      C10_CUDA_KERNEL_LAUNCH_CHECK();
+      return;
+    }
+    const int blocks = blocks_for(per_rank, max_blocks);
 #define MNB_AR1(TI, TW, OPV)                                                                         \
   do {                                                                                              \
     if (algorithm) ar_push_two_shot_kernel<TI, TW, OPV><<<blocks, kCommThreads, 0, stream>>>(a, chunk_u); \

@@ -43,6 +43,8 @@ STAGING_BYTES = int(os.environ.get("MINI_NCCL_STAGING_BYTES", 64 << 20))
 #: CTAs a collective may use (the device meaning of "channels").  Bandwidth
 #: grows with CTAs up to about one per SM; fewer leave SMs to overlapped compute.
 MAX_BLOCKS = int(os.environ.get("MINI_NCCL_DEVICE_BLOCKS", 255))
+#: CTAs (128 threads each) of an all-reduce run beside compute: one per SM.
+BESIDE_BLOCKS = int(os.environ.get("MINI_NCCL_BESIDE_BLOCKS", 148))
 
 _OPS = {"sum": 0, "prod": 1, "max": 2, "min": 3}
 OPNAMES = ["all_reduce", "reduce_scatter", "all_gather", "broadcast", "all_to_all", "barrier", "all_reduce_stepped",
@@ -198,7 +200,15 @@ class DeviceComm:
         wire_dtype: torch.dtype | None = None,
         scale: float = 1.0,
         blocks: int | None = None,
+        beside_compute: bool = False,
     ) -> torch.Tensor:
+        """All-reduce ``tensor`` in place across the communicator.
+
+        ``beside_compute=True`` (two-shot sums of bf16 / fp32) launches small
+        CTAs that fit on an SM next to one CTA of the persistent GEMM and
+        attention kernels, for all-reduces that overlap compute (DDP's
+        buckets); every rank must pass the same value.
+        """
         if op not in _OPS:
             raise ValueError(f"unknown op {op!r}; expected one of {sorted(_OPS)}")
         if not tensor.is_contiguous():
@@ -227,7 +237,9 @@ class DeviceComm:
                 wsz = 2 if wire_bf16 else tensor.element_size()
                 kind = 1 if algorithm == "two_shot" else 0
                 self._ensure_staging(self.impl.staging_need(kind, tensor.numel(), wsz))
-                self.impl.all_reduce(tensor, tensor, _OPS[op], kind, wire_bf16, float(scale), blocks or MAX_BLOCKS)
+                nb = blocks or (BESIDE_BLOCKS if beside_compute else MAX_BLOCKS)
+                self.impl.all_reduce(tensor, tensor, _OPS[op], kind, wire_bf16, float(scale),
+                                     -nb if beside_compute else nb)
             elif algorithm in ("ring", "tree", "halving", "naive"):
                 narrow = tensor.dtype in (torch.bfloat16, torch.float16) and wire_bf16
                 self._ensure_staging(self.impl.staging_need(5, tensor.numel(), 4 if narrow else tensor.element_size()))

@@ -40,6 +40,9 @@ from ..communicator import Communicator
 #: CTAs a bucket all-reduce may use while backward runs beside it (0: the
 #: device communicator's default).
 DDP_COMM_BLOCKS = int(os.environ.get("MINI_NCCL_DDP_BLOCKS", "0"))
+#: Bucket all-reduces run as small CTAs that share SMs with the backward
+#: pass's persistent kernels instead of taking whole SMs from them.
+DDP_BESIDE_COMPUTE = os.environ.get("MINI_NCCL_DDP_BESIDE", "0") != "0"
 
 
 def average_gradients(pg: Communicator, params, algorithm: str = "ring") -> int:
@@ -224,7 +227,7 @@ class DistributedDataParallel(nn.Module):
                 self._comm_stream.wait_event(produced)
                 self._dc.all_reduce(
                     bucket.buffer, op="sum", algorithm="auto", scale=1.0 / self.pg.world_size,
-                    blocks=DDP_COMM_BLOCKS or None,
+                    blocks=DDP_COMM_BLOCKS or None, beside_compute=DDP_BESIDE_COMPUTE,
                 )
                 done = torch.cuda.Event()
                 done.record(self._comm_stream)

@@ -70,6 +70,16 @@ def _battery(pg) -> None:
     dc.all_reduce(sym, algorithm="two_shot", scale=1.0 / W)
     want = expected(W, 1 << 20, torch.bfloat16, "sum", dev) / W
     assert (sym.double() - want).abs().max().item() < 3e-2
+    # the small-CTA variant DDP runs beside the backward pass: same results
+    sym.copy_(seeded(r, 1 << 20, torch.bfloat16, dev))
+    dc.all_reduce(sym, algorithm="two_shot", scale=1.0 / W, beside_compute=True)
+    assert (sym.double() - want).abs().max().item() < 3e-2
+    for dtype, wire in ((torch.float32, None), (torch.float32, torch.bfloat16), (torch.bfloat16, None)):
+        t = seeded(r, 300_017, dtype, dev)
+        dc.all_reduce(t, algorithm="two_shot", wire_dtype=wire, beside_compute=True)
+        assert (t.double() - expected(W, 300_017, dtype, "sum", dev)).abs().max().item() < 0.05
+        everyone = C.all_gather(pg, t)
+        assert all(torch.equal(o, everyone[0]) for o in everyone)
     # narrow wire: fp32 tensor, bf16 on the wire, fp32 accumulation
     t = seeded(r, 100_003, torch.float32, dev)
     C.all_reduce(pg, t, algorithm="two_shot", wire_dtype=torch.bfloat16)
