@@ -11,6 +11,9 @@ void layernorm_fwd(torch::Tensor x, torch::Tensor w, torch::Tensor b, torch::Ten
                    torch::Tensor rstd, double eps);
 void layernorm_bwd(torch::Tensor dy, torch::Tensor x, torch::Tensor w, torch::Tensor mean, torch::Tensor rstd,
                    torch::Tensor dx, torch::Tensor dw, torch::Tensor db, torch::Tensor partials, bool accumulate);
+void layernorm_bwd_add(torch::Tensor dy, torch::Tensor x, torch::Tensor w, torch::Tensor mean, torch::Tensor rstd,
+                       torch::Tensor add, torch::Tensor dx, torch::Tensor dw, torch::Tensor db, torch::Tensor partials,
+                       bool accumulate);
 int ln_bwd_blocks(int rows);
 int colsum_row_blocks(int rows);
 void bias_grad(torch::Tensor g, torch::Tensor out, torch::Tensor partials, bool accumulate);
@@ -42,6 +45,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gemm", &mnb::gemm, "tcgen05 GEMM with fused epilogues");
   m.def("layernorm_fwd", &mnb::layernorm_fwd);
   m.def("layernorm_bwd", &mnb::layernorm_bwd);
+  m.def("layernorm_bwd_add", &mnb::layernorm_bwd_add);
   m.def("ln_bwd_blocks", &mnb::ln_bwd_blocks);
   m.def("colsum_row_blocks", &mnb::colsum_row_blocks);
   m.def("bias_grad", &mnb::bias_grad);

@@ -6,6 +6,9 @@
 // Row kernels use one warp per row with 16-byte vector accesses; reductions
 // over rows (LayerNorm weight grads, bias grads) write per-block fp32 partials
 // that a second small kernel folds, so results do not depend on atomics.
+#include <map>
+#include <mutex>
+#include <tuple>
 #include <ATen/cuda/CUDAContext.h>
 #include <c10/cuda/CUDAGuard.h>
 #include <torch/extension.h>
@@ -365,42 +368,50 @@ MNB_DEVICE void ld_shared_bf16x8(uint32_t addr, float* f) {
   }
 }
 
-template <int NCH, int DEPTH>
+// ADD: dx also receives `add` (the gradient reaching x through a residual
+// branch), so autograd needs no separate accumulation kernel; a slot then
+// holds three rows (x, dy, add).
+template <int NCH, int DEPTH, bool ADD = false>
 constexpr size_t ln_bwd_bulk_smem() {
-  return static_cast<size_t>(kRowWarps) * DEPTH * 4 * NCH * 256 + 2 * NCH * 256 * 4 + kRowWarps * DEPTH * 8 + 128;
+  return static_cast<size_t>(kRowWarps) * DEPTH * (ADD ? 3 : 2) * 2 * NCH * 256 + 2 * NCH * 256 * 4 +
+         kRowWarps * DEPTH * 8 + 128;
 }
 
-template <int NCH, int DEPTH>
+template <int NCH, int DEPTH, bool ADD = false>
 __global__ void __launch_bounds__(256, 1)
     layernorm_bwd_bulk_kernel(const __nv_bfloat16* __restrict__ dy, const __nv_bfloat16* __restrict__ x,
                               const __nv_bfloat16* __restrict__ w, const float* __restrict__ mean,
                               const float* __restrict__ rstd, __nv_bfloat16* __restrict__ dx,
                               float* __restrict__ part, int rows, int Cdyn, void* out_dw, void* out_db, int out_f32,
-                              int accumulate) {
+                              int accumulate, const __nv_bfloat16* __restrict__ add = nullptr) {
   constexpr int C = NCH * 256;
   constexpr uint32_t kRowBytes = C * 2;
+  constexpr int kSlotRows = ADD ? 3 : 2;
   extern __shared__ uint8_t ln_raw[];
   uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(ln_raw) + 127) & ~uintptr_t(127));
-  float* sacc = reinterpret_cast<float*>(base + kRowWarps * DEPTH * 2 * kRowBytes);  // [2][C]
+  float* sacc = reinterpret_cast<float*>(base + kRowWarps * DEPTH * kSlotRows * kRowBytes);  // [2][C]
   uint64_t* bars = reinterpret_cast<uint64_t*>(sacc + 2 * C);                       // [warps][DEPTH]
   for (int i = threadIdx.x; i < 2 * C; i += blockDim.x) sacc[i] = 0.f;
   if (threadIdx.x < kRowWarps * DEPTH) mbar_init(smem_u32(bars + threadIdx.x), 1);
   fence_mbar_init();
   __syncthreads();
   const int lane = threadIdx.x % 32, warp = threadIdx.x / 32;
-  const uint32_t wbuf = smem_u32(base) + warp * DEPTH * 2 * kRowBytes;
+  const uint32_t wbuf = smem_u32(base) + warp * DEPTH * kSlotRows * kRowBytes;
   const uint32_t wbar = smem_u32(bars + warp * DEPTH);
   const int stride = gridDim.x * kRowWarps;
   const int first = blockIdx.x * kRowWarps + warp;
   const int n_mine = first < rows ? (rows - first + stride - 1) / stride : 0;
   auto issue = [&](int k) {  // lane 0: rows of this warp's k-th turn into slot k % DEPTH
     const long long row = first + static_cast<long long>(k) * stride;
-    const uint32_t dst = wbuf + (k % DEPTH) * 2 * kRowBytes, bar = wbar + 8 * (k % DEPTH);
-    mbar_arrive_expect_tx(bar, 2 * kRowBytes);
+    const uint32_t dst = wbuf + (k % DEPTH) * kSlotRows * kRowBytes, bar = wbar + 8 * (k % DEPTH);
+    mbar_arrive_expect_tx(bar, kSlotRows * kRowBytes);
     asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
                  ::"r"(dst), "l"(x + row * C), "r"(kRowBytes), "r"(bar) : "memory");
     asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
                  ::"r"(dst + kRowBytes), "l"(dy + row * C), "r"(kRowBytes), "r"(bar) : "memory");
+    if constexpr (ADD)
+      asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
+                   ::"r"(dst + 2 * kRowBytes), "l"(add + row * C), "r"(kRowBytes), "r"(bar) : "memory");
   };
   if (lane == 0)
     for (int k = 0; k < DEPTH && k < n_mine; ++k) issue(k);
@@ -416,12 +427,13 @@ __global__ void __launch_bounds__(256, 1)
     const int row = first + k * stride;
     const float mu = mean[row], rs = rstd[row];
     if (!__all_sync(0xffffffffu, mbar_wait(wbar + 8 * (k % DEPTH), (k / DEPTH) & 1, nullptr))) break;
-    const uint32_t src = wbuf + (k % DEPTH) * 2 * kRowBytes;
-    float xh[NCH][8], g[NCH][8];
+    const uint32_t src = wbuf + (k % DEPTH) * kSlotRows * kRowBytes;
+    float xh[NCH][8], g[NCH][8], ad[ADD ? NCH : 1][8];
 #pragma unroll
     for (int c = 0; c < NCH; ++c) {
       ld_shared_bf16x8(src + (c * 256 + lane * 8) * 2, xh[c]);
       ld_shared_bf16x8(src + kRowBytes + (c * 256 + lane * 8) * 2, g[c]);
+      if constexpr (ADD) ld_shared_bf16x8(src + 2 * kRowBytes + (c * 256 + lane * 8) * 2, ad[c]);
     }
     float a = 0.f, bsum = 0.f;
 #pragma unroll
@@ -435,7 +447,15 @@ __global__ void __launch_bounds__(256, 1)
         dg[c][j] += g[c][j] * xh[c][j];
         dbb[c][j] += g[c][j];
       }
-    // every lane's reads of this slot are complete (their values were used above)
+    // every lane's reads of this slot are complete (their values were used
+    // above; the add row's values are consumed by the adds below, which the
+    // fence and refill can only follow once those loads have returned)
+    if constexpr (ADD) {
+#pragma unroll
+      for (int c = 0; c < NCH; ++c)
+#pragma unroll
+        for (int j = 0; j < 8; ++j) asm volatile("" ::"f"(ad[c][j]));
+    }
     __syncwarp();
     if (lane == 0 && k + DEPTH < n_mine) {
       asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
@@ -449,6 +469,10 @@ __global__ void __launch_bounds__(256, 1)
       float o[8];
 #pragma unroll
       for (int j = 0; j < 8; ++j) o[j] = rs * (g[c][j] * ww[c][j] - a - xh[c][j] * bsum);
+      if constexpr (ADD) {
+#pragma unroll
+        for (int j = 0; j < 8; ++j) o[j] += ad[c][j];
+      }
       store8(dr + c * 256 + lane * 8, o);
     }
   }
@@ -947,6 +971,28 @@ static void check_bf16(const torch::Tensor& t, const char* n) {
               " must be a contiguous CUDA bf16 tensor");
 }
 
+// Resident blocks per SM x SMs of `kern` at this block size and dynamic shared
+// memory (the one-wave grid of the grid-stride kernels), with the shared-memory
+// opt-in applied: queried once per (kernel, device, smem) instead of per call.
+static int resident_wave(const void* kern, int threads, size_t smem) {
+  static std::mutex mu;
+  static std::map<std::tuple<const void*, int, size_t>, int> cache;
+  int dev = 0;
+  C10_CUDA_CHECK(cudaGetDevice(&dev));
+  std::lock_guard<std::mutex> lock(mu);
+  const auto key = std::make_tuple(kern, dev, smem);
+  auto it = cache.find(key);
+  if (it != cache.end()) return it->second;
+  if (smem > 48 * 1024)
+    C10_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)));
+  int per_sm = 1, sms = 148;
+  C10_CUDA_CHECK(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
+  C10_CUDA_CHECK(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, threads, smem));
+  const int wave = std::max(1, per_sm) * sms;
+  cache.emplace(key, wave);
+  return wave;
+}
+
 void layernorm_fwd(torch::Tensor x, torch::Tensor w, torch::Tensor b, torch::Tensor y, torch::Tensor mean,
                    torch::Tensor rstd, double eps) {
   check_bf16(x, "x");
@@ -965,11 +1011,7 @@ void layernorm_fwd(torch::Tensor x, torch::Tensor w, torch::Tensor b, torch::Ten
   const float e = static_cast<float>(eps);
   // grid-stride kernels: one wave of resident blocks (w and b are loaded once per warp)
   auto wave_of = [&](auto kern) {
-    int per_sm = 1, sms = 148, dev = 0;
-    C10_CUDA_CHECK(cudaGetDevice(&dev));
-    C10_CUDA_CHECK(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
-    C10_CUDA_CHECK(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, 256, 0));
-    return std::max(1, std::min((rows + 7) / 8, std::max(1, per_sm) * sms));
+    return std::max(1, std::min((rows + 7) / 8, resident_wave(reinterpret_cast<const void*>(kern), 256, 0)));
   };
   auto reg = [&](auto kern) {
     kern<<<wave_of(kern), 256, 0, stream>>>(xp, wp, bp, yp, mean.data_ptr<float>(), rstd.data_ptr<float>(), rows, e);
@@ -989,8 +1031,9 @@ void layernorm_fwd(torch::Tensor x, torch::Tensor w, torch::Tensor b, torch::Ten
 
 int ln_bwd_blocks(int rows) { return std::max(1, std::min(148 * 2, (rows + kRowWarps - 1) / kRowWarps)); }
 
-void layernorm_bwd(torch::Tensor dy, torch::Tensor x, torch::Tensor w, torch::Tensor mean, torch::Tensor rstd,
-                   torch::Tensor dx, torch::Tensor dw, torch::Tensor db, torch::Tensor partials, bool accumulate) {
+static void layernorm_bwd_impl(torch::Tensor dy, torch::Tensor x, torch::Tensor w, torch::Tensor mean,
+                               torch::Tensor rstd, torch::Tensor dx, torch::Tensor dw, torch::Tensor db,
+                               torch::Tensor partials, bool accumulate, const torch::Tensor* add) {
   check_bf16(dy, "dy");
   check_bf16(x, "x");
   check_bf16(dx, "dx");
@@ -1004,14 +1047,9 @@ void layernorm_bwd(torch::Tensor dy, torch::Tensor x, torch::Tensor w, torch::Te
   const size_t smem = 2 * C * sizeof(float);
   const bool f32 = dw.scalar_type() == at::kFloat;
   auto launch = [&](auto kern) {
-    if (smem > 48 * 1024)
-      C10_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
     // one wave: as many blocks as can be resident (these kernels grid-stride over rows)
-    int per_sm = 1, sms = 148, dev = 0;
-    C10_CUDA_CHECK(cudaGetDevice(&dev));
-    C10_CUDA_CHECK(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
-    C10_CUDA_CHECK(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, kRowWarps * 32, smem));
-    const int wave = std::max(1, std::min(blocks, std::max(1, per_sm) * sms));
+    const int wave =
+        std::max(1, std::min(blocks, resident_wave(reinterpret_cast<const void*>(kern), kRowWarps * 32, smem)));
     kern<<<wave, kRowWarps * 32, smem, stream>>>(
         reinterpret_cast<const __nv_bfloat16*>(dy.data_ptr()), reinterpret_cast<const __nv_bfloat16*>(x.data_ptr()),
         reinterpret_cast<const __nv_bfloat16*>(w.data_ptr()), mean.data_ptr<float>(), rstd.data_ptr<float>(),
@@ -1020,21 +1058,23 @@ void layernorm_bwd(torch::Tensor dy, torch::Tensor x, torch::Tensor w, torch::Te
   };
   // rows reach shared memory by bulk copies: 16-byte aligned row starts needed
   const bool bulk = reinterpret_cast<uintptr_t>(x.data_ptr()) % 16 == 0 &&
-                    reinterpret_cast<uintptr_t>(dy.data_ptr()) % 16 == 0 && x.is_contiguous() && dy.is_contiguous();
+                    reinterpret_cast<uintptr_t>(dy.data_ptr()) % 16 == 0 && x.is_contiguous() && dy.is_contiguous() &&
+                    (add == nullptr || (add->is_contiguous() && reinterpret_cast<uintptr_t>(add->data_ptr()) % 16 == 0));
+  const __nv_bfloat16* add_p = add ? reinterpret_cast<const __nv_bfloat16*>(add->data_ptr()) : nullptr;
   auto launch_bulk = [&](auto kern, size_t bytes) {
-    C10_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(bytes)));
-    int per_sm = 1, sms = 148, dev = 0;
-    C10_CUDA_CHECK(cudaGetDevice(&dev));
-    C10_CUDA_CHECK(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
-    C10_CUDA_CHECK(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, kRowWarps * 32, bytes));
-    const int wave = std::max(1, std::min(blocks, std::max(1, per_sm) * sms));
+    const int wave =
+        std::max(1, std::min(blocks, resident_wave(reinterpret_cast<const void*>(kern), kRowWarps * 32, bytes)));
     kern<<<wave, kRowWarps * 32, bytes, stream>>>(
         reinterpret_cast<const __nv_bfloat16*>(dy.data_ptr()), reinterpret_cast<const __nv_bfloat16*>(x.data_ptr()),
         reinterpret_cast<const __nv_bfloat16*>(w.data_ptr()), mean.data_ptr<float>(), rstd.data_ptr<float>(),
         reinterpret_cast<__nv_bfloat16*>(dx.data_ptr()), partials.data_ptr<float>(), rows, C, dw.data_ptr(),
-        db.data_ptr(), f32 ? 1 : 0, accumulate ? 1 : 0);
+        db.data_ptr(), f32 ? 1 : 0, accumulate ? 1 : 0, add_p);
   };
-  if (bulk && C == 256) launch_bulk(layernorm_bwd_bulk_kernel<1, 8>, ln_bwd_bulk_smem<1, 8>());
+  if (add != nullptr && bulk && C == 256) launch_bulk(layernorm_bwd_bulk_kernel<1, 8, true>, ln_bwd_bulk_smem<1, 8, true>());
+  else if (add != nullptr && bulk && C == 512) launch_bulk(layernorm_bwd_bulk_kernel<2, 8, true>, ln_bwd_bulk_smem<2, 8, true>());
+  else if (add != nullptr && bulk && C == 768) launch_bulk(layernorm_bwd_bulk_kernel<3, 5, true>, ln_bwd_bulk_smem<3, 5, true>());
+  else if (add != nullptr && bulk && C == 1024) launch_bulk(layernorm_bwd_bulk_kernel<4, 3, true>, ln_bwd_bulk_smem<4, 3, true>());
+  else if (bulk && C == 256) launch_bulk(layernorm_bwd_bulk_kernel<1, 8>, ln_bwd_bulk_smem<1, 8>());
   else if (bulk && C == 512) launch_bulk(layernorm_bwd_bulk_kernel<2, 8>, ln_bwd_bulk_smem<2, 8>());
   else if (bulk && C == 768) launch_bulk(layernorm_bwd_bulk_kernel<3, 6>, ln_bwd_bulk_smem<3, 6>());
   else if (bulk && C == 1024) launch_bulk(layernorm_bwd_bulk_kernel<4, 4>, ln_bwd_bulk_smem<4, 4>());
@@ -1050,6 +1090,23 @@ void layernorm_bwd(torch::Tensor dy, torch::Tensor x, torch::Tensor w, torch::Te
         db.data_ptr(), f32 ? 1 : 0, accumulate ? 1 : 0);
   else launch(layernorm_bwd_kernel<0>);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
+  const bool fused = add != nullptr && bulk && (C == 256 || C == 512 || C == 768 || C == 1024);
+  if (add != nullptr && !fused) dx.add_(*add);
+}
+
+void layernorm_bwd(torch::Tensor dy, torch::Tensor x, torch::Tensor w, torch::Tensor mean, torch::Tensor rstd,
+                   torch::Tensor dx, torch::Tensor dw, torch::Tensor db, torch::Tensor partials, bool accumulate) {
+  layernorm_bwd_impl(dy, x, w, mean, rstd, dx, dw, db, partials, accumulate, nullptr);
+}
+
+// dx = LayerNorm backward + add (the gradient x also receives through a
+// residual branch), dgamma / dbeta as layernorm_bwd.
+void layernorm_bwd_add(torch::Tensor dy, torch::Tensor x, torch::Tensor w, torch::Tensor mean, torch::Tensor rstd,
+                       torch::Tensor add, torch::Tensor dx, torch::Tensor dw, torch::Tensor db, torch::Tensor partials,
+                       bool accumulate) {
+  check_bf16(add, "add");
+  TORCH_CHECK(add.numel() == x.numel(), "add must match x");
+  layernorm_bwd_impl(dy, x, w, mean, rstd, dx, dw, db, partials, accumulate, &add);
 }
 
 // Bias gradient in one kernel: column sums of a 128-row band per block,

@@ -77,11 +77,13 @@ class Block(nn.Module):
     def _forward_cuda(self, x: torch.Tensor) -> torch.Tensor:
         K = _kernels()
         B, T, C = x.shape
-        h = K.LayerNorm.apply(x, self.ln1.weight, self.ln1.bias, self.ln1.eps)
+        # x feeds both the norm and the residual add: LayerNormResidual hands the
+        # residual branch its own alias so the two gradients meet in one kernel
+        h, x = K.LayerNormResidual.apply(x, self.ln1.weight, self.ln1.bias, self.ln1.eps)
         qkv = K.Linear.apply(h, self.qkv.weight, self.qkv.bias)
         y = K.FlashAttention.apply(qkv, self.n_head)
         x = K.Linear.apply(y.view(B, T, C), self.proj.weight, self.proj.bias, x)
-        h = K.LayerNorm.apply(x, self.ln2.weight, self.ln2.bias, self.ln2.eps)
+        h, x = K.LayerNormResidual.apply(x, self.ln2.weight, self.ln2.bias, self.ln2.eps)
         fc, out = self.mlp[0], self.mlp[2]
         return K.MLP.apply(h, fc.weight, fc.bias, out.weight, out.bias, x)
 

@@ -274,6 +274,42 @@ class LayerNorm(torch.autograd.Function):
         return dx, dw, db, None
 
 
+class LayerNormResidual(torch.autograd.Function):
+    """``(LayerNorm(x), x)``: the second output is the residual branch's copy of x.
+
+    Its gradient and the LayerNorm's input gradient are summed inside the
+    LayerNorm backward kernel, instead of by autograd with a separate add
+    kernel (x feeds both the norm and the block's residual connection).
+    """
+
+    @staticmethod
+    def forward(ctx, x, weight, bias, eps: float):
+        xc = x.contiguous()
+        rows = xc.numel() // xc.shape[-1]
+        y = torch.empty_like(xc)
+        mean = torch.empty(rows, dtype=torch.float32, device=x.device)
+        rstd = torch.empty(rows, dtype=torch.float32, device=x.device)
+        ext().layernorm_fwd(xc, weight, bias, y, mean, rstd, eps)
+        ctx.save_for_backward(xc, weight, mean, rstd)
+        return y, x.view_as(x)
+
+    @staticmethod
+    def backward(ctx, gy, gres):
+        x, w, mean, rstd = ctx.saved_tensors
+        C = x.shape[-1]
+        dx = torch.empty_like(x)
+        dw = torch.empty_like(w)
+        db = torch.empty_like(w)
+        acc = fold_accumulator(x.device, 2 * C)
+        if gy is None:
+            gy = torch.zeros_like(x)
+        if gres is None:
+            ext().layernorm_bwd(gy.contiguous(), x, w, mean, rstd, dx, dw, db, acc, False)
+        else:
+            ext().layernorm_bwd_add(gy.contiguous(), x, w, mean, rstd, gres.contiguous(), dx, dw, db, acc, False)
+        return dx, dw, db, None
+
+
 class FlashAttention(torch.autograd.Function):
     """Causal attention straight out of a fused ``[B, T, 3*H*D]`` QKV tensor.
 

@@ -18,6 +18,7 @@ KERNELS_PER_CALL = {
     "gemm": 1,
     "layernorm_fwd": 1,
     "layernorm_bwd": 1,
+    "layernorm_bwd_add": 1,
     "bias_grad": 1,
     "gelu_fwd": 1,
     "gelu_bwd": 1,

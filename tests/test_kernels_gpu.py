@@ -120,6 +120,23 @@ def test_layernorm_forward_backward(rows, C):
     close(b.grad, br.grad, 2e-2)
 
 
+@pytest.mark.parametrize("rows,C", [(20000, 768), (3000, 1024), (500, 2048)])
+def test_layernorm_residual_gradients_meet_in_one_kernel(rows, C):
+    x = rnd(rows, C, seed=40).requires_grad_(True)
+    w = (1 + 0.1 * rnd(C, seed=41).float()).to(torch.bfloat16).requires_grad_(True)
+    b = rnd(C, seed=42, scale=0.1).requires_grad_(True)
+    gy, gr = rnd(rows, C, seed=43), rnd(rows, C, seed=44)
+    y, x_alias = K.LayerNormResidual.apply(x, w, b, 1e-5)
+    torch.autograd.backward([y, x_alias], [gy, gr])
+    xf, wf, bf = (t.detach().float().requires_grad_(True) for t in (x, w, b))
+    yf = F.layer_norm(xf, (C,), wf, bf, 1e-5)
+    torch.autograd.backward([yf, xf * 1.0], [gy.float(), gr.float()])
+    close(y, yf, 2e-2)
+    close(x.grad, xf.grad, 3e-2)
+    close(w.grad, wf.grad, 2e-2)
+    close(b.grad, bf.grad, 2e-2)
+
+
 @pytest.mark.parametrize("rows,C", [(16384, 768), (16384, 2304), (1000, 3072), (130, 40)])
 def test_bias_grad_column_sums(rows, C):
     g = rnd(rows, C, seed=30)
