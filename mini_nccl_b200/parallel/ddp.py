@@ -42,7 +42,7 @@ from ..communicator import Communicator
 DDP_COMM_BLOCKS = int(os.environ.get("MINI_NCCL_DDP_BLOCKS", "0"))
 #: Bucket all-reduces run as small CTAs that share SMs with the backward
 #: pass's persistent kernels instead of taking whole SMs from them.
-DDP_BESIDE_COMPUTE = os.environ.get("MINI_NCCL_DDP_BESIDE", "0") != "0"
+DDP_BESIDE_COMPUTE = os.environ.get("MINI_NCCL_DDP_BESIDE", "1") != "0"
 
 
 def average_gradients(pg: Communicator, params, algorithm: str = "ring") -> int:
