@@ -28,6 +28,8 @@ from __future__ import annotations
 
 from dataclasses import dataclass
 
+import os
+
 import torch
 import torch.nn.functional as F
 from torch import nn
@@ -52,6 +54,11 @@ def _kernels():
     from ..ops import kernels
 
     return kernels
+
+
+#: The LayerNorm backward also adds the residual branch's gradient (one kernel
+#: instead of LayerNorm backward + an autograd accumulation add).
+_FUSED_RESIDUAL_GRAD = os.environ.get("MNB_FUSED_RESIDUAL_GRAD", "1") != "0"
 
 
 class Block(nn.Module):
@@ -79,11 +86,26 @@ class Block(nn.Module):
         B, T, C = x.shape
         # x feeds both the norm and the residual add: LayerNormResidual hands the
         # residual branch its own alias so the two gradients meet in one kernel
+        if not _FUSED_RESIDUAL_GRAD:
+            return self._forward_cuda_unfused(x)
         h, x = K.LayerNormResidual.apply(x, self.ln1.weight, self.ln1.bias, self.ln1.eps)
         qkv = K.Linear.apply(h, self.qkv.weight, self.qkv.bias)
         y = K.FlashAttention.apply(qkv, self.n_head)
         x = K.Linear.apply(y.view(B, T, C), self.proj.weight, self.proj.bias, x)
         h, x = K.LayerNormResidual.apply(x, self.ln2.weight, self.ln2.bias, self.ln2.eps)
+        fc, out = self.mlp[0], self.mlp[2]
+        return K.MLP.apply(h, fc.weight, fc.bias, out.weight, out.bias, x)
+
+
+    def _forward_cuda_unfused(self, x: torch.Tensor) -> torch.Tensor:
+        """Same block; autograd sums the residual and LayerNorm input gradients."""
+        K = _kernels()
+        B, T, C = x.shape
+        h = K.LayerNorm.apply(x, self.ln1.weight, self.ln1.bias, self.ln1.eps)
+        qkv = K.Linear.apply(h, self.qkv.weight, self.qkv.bias)
+        y = K.FlashAttention.apply(qkv, self.n_head)
+        x = K.Linear.apply(y.view(B, T, C), self.proj.weight, self.proj.bias, x)
+        h = K.LayerNorm.apply(x, self.ln2.weight, self.ln2.bias, self.ln2.eps)
         fc, out = self.mlp[0], self.mlp[2]
         return K.MLP.apply(h, fc.weight, fc.bias, out.weight, out.bias, x)
 
