@@ -422,10 +422,18 @@ __global__ void __launch_bounds__(256, 1)
 #pragma unroll
     for (int j = 0; j < 8; ++j) dg[k][j] = dbb[k][j] = 0.f;
   }
+  // lane i holds the statistics of this warp's turn 32 * m + i: one load
+  // latency per 32 rows instead of one per row
+  float mu_l = 0.f, rs_l = 0.f;
 #pragma unroll 1
   for (int k = 0; k < n_mine; ++k) {
     const int row = first + k * stride;
-    const float mu = mean[row], rs = rstd[row];
+    if (k % 32 == 0 && k + lane < n_mine) {
+      const int r = first + (k + lane) * stride;
+      mu_l = mean[r];
+      rs_l = rstd[r];
+    }
+    const float mu = __shfl_sync(0xffffffffu, mu_l, k % 32), rs = __shfl_sync(0xffffffffu, rs_l, k % 32);
     if (!__all_sync(0xffffffffu, mbar_wait(wbar + 8 * (k % DEPTH), (k / DEPTH) & 1, nullptr))) break;
     const uint32_t src = wbuf + (k % DEPTH) * kSlotRows * kRowBytes;
     float xh[NCH][8], g[NCH][8], ad[ADD ? NCH : 1][8];
