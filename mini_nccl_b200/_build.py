@@ -31,6 +31,7 @@ PKG = Path(__file__).resolve().parent
 BUILD = PKG / "_build"
 HOST_SRC = sorted((PKG / "csrc" / "host").glob("*.cpp"))
 CUDA_DIR = PKG / "csrc" / "cuda"
+INCLUDE_DIR = PKG / "csrc" / "include"
 
 SM100A = ["-gencode", "arch=compute_100a,code=sm_100a"]
 NVCC_FLAGS = [
@@ -142,7 +143,7 @@ def cuda_sources() -> list[Path]:
 
 
 def cuda_headers() -> list[Path]:
-    return sorted(CUDA_DIR.glob("*.cuh")) + sorted(CUDA_DIR.glob("*.h"))
+    return sorted(CUDA_DIR.glob("*.cuh")) + sorted(CUDA_DIR.glob("*.h")) + sorted(INCLUDE_DIR.glob("*.h"))
 
 
 def build_cuda(force: bool = False, verbose: bool = False) -> Path:

@@ -21,10 +21,13 @@
 //     clipped.
 //   * the array's name is only a host-side stand-in: host code must not
 //     hand it to a kernel.  The device address is obtained with
-//     cudaGetSymbolAddress once per device, with that device current, on the
-//     first call made on that device.  That first call therefore does the
-//     set-up (and may initialise the CUDA context); make it before any
-//     latency-sensitive section.
+//     cudaGetSymbolAddress once per CUDA context (each device's primary
+//     context, or a context the host runtime created), with that context
+//     current, on the first call made in it.  That first call therefore does
+//     the set-up (and may initialise the device's primary context); make it
+//     before any latency-sensitive section.
+//   * problems with more than 65,535 bands of 128 rows are handled by CTAs
+//     that walk several bands; the scratch need and the limit are the same.
 //   * every call shares the one array, and each call overwrites every
 //     partial it reads before reading it, so nothing has to start at zero.
 //     Calls whose kernels can overlap on the GPU (different streams, or
@@ -32,29 +35,38 @@
 //     issuing them on one stream.
 //   * no cudaMalloc, cudaFree or allocating library routine is called.
 //
-// C signature (exported, unmangled):
-//   int mnb_bias_grad_noalloc(const void* grad, void* out, int rows, int cols,
-//                             int out_is_fp32, int accumulate, void* stream);
-//   grad: bf16 [rows, cols] row-major (device); out: [cols] bf16 or fp32
-//   (device); accumulate != 0 adds into out.  Returns 0 on success, 1 for an
-//   invalid argument, 2 when the problem needs more scratch than the array
-//   holds, 3 for a CUDA error.  mnb_noalloc_last_error() returns the message
-//   of the last failure on the calling thread.
+// The exported C interface (prototypes, return codes, the scratch limit) is
+// declared in csrc/include/mnb_noalloc.h, which this file includes so the
+// definitions below are checked against it.
+#include <cuda.h>
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
 
 #include <cstdio>
 #include <mutex>
 
+#include "../include/mnb_noalloc.h"
+
 namespace {
 
-constexpr long long kMaxScratchFloats = 1LL << 21;  // 8 MiB
+constexpr long long kMaxScratchFloats = MNB_NOALLOC_MAX_SCRATCH_FLOATS;  // 8 MiB
 constexpr int kRowsPerBlock = 128;
-constexpr int kMaxDevices = 64;
+// gridDim.y limit: problems with more 128-row bands than this run each CTA
+// row over several bands (one partial per band, as with fewer bands).
+constexpr long long kMaxGridY = 65535;
+constexpr int kMaxContexts = 64;
 
 static __device__ __align__(256) float g_colsum_scratch[kMaxScratchFloats];
 
-float* g_scratch_addr[kMaxDevices] = {nullptr};
+// The array has its own device address in every CUDA context (the primary
+// context of each device, and any context a host runtime creates with
+// cuCtxCreate), so the looked-up address is cached per context.
+struct ScratchAddr {
+  CUcontext ctx;
+  float* addr;
+};
+ScratchAddr g_scratch_addr[kMaxContexts] = {};
+int g_scratch_count = 0;
 std::mutex g_setup_mutex;
 thread_local char g_last_error[256] = "";
 
@@ -75,31 +87,37 @@ __device__ __forceinline__ void load8_bf16(const __nv_bfloat16* p, float* f) {
   }
 }
 
-// Partial column sums: block (x, y) covers 256 columns of rows [128y, 128y+128).
+// Partial column sums: band b covers rows [128b, 128b+128); block (x, y)
+// handles 256 columns of bands y, y + gridDim.y, ... and writes one partial
+// row per band, so the scratch layout does not depend on the grid.
 __global__ void __launch_bounds__(256) noalloc_colsum_partials(const __nv_bfloat16* __restrict__ g,
-                                                               float* __restrict__ scratch, int rows, int cols) {
+                                                               float* __restrict__ scratch, int rows, int cols,
+                                                               int bands) {
   __shared__ float red[8][256];
   const int lane = threadIdx.x % 32, warp = threadIdx.x / 32;
   const int c0 = blockIdx.x * 256 + lane * 8;
-  const int r0 = blockIdx.y * kRowsPerBlock;
-  const int r1 = min(rows, r0 + kRowsPerBlock);
-  float s[8] = {0, 0, 0, 0, 0, 0, 0, 0};
-  if (c0 < cols) {
-    for (int r = r0 + warp; r < r1; r += 8) {
-      float f[8];
-      load8_bf16(g + static_cast<long long>(r) * cols + c0, f);
+  for (int band = blockIdx.y; band < bands; band += gridDim.y) {
+    const int r0 = band * kRowsPerBlock;
+    const int r1 = min(rows, r0 + kRowsPerBlock);
+    float s[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+    if (c0 < cols) {
+      for (int r = r0 + warp; r < r1; r += 8) {
+        float f[8];
+        load8_bf16(g + static_cast<long long>(r) * cols + c0, f);
 #pragma unroll
-      for (int j = 0; j < 8; ++j) s[j] += f[j];
+        for (int j = 0; j < 8; ++j) s[j] += f[j];
+      }
     }
+    __syncthreads();  // the previous band's reads of `red` are done
+#pragma unroll
+    for (int j = 0; j < 8; ++j) red[warp][lane * 8 + j] = s[j];
+    __syncthreads();
+    float t = 0.f;
+#pragma unroll
+    for (int w = 0; w < 8; ++w) t += red[w][threadIdx.x];
+    const int c = blockIdx.x * 256 + threadIdx.x;
+    if (c < cols) scratch[static_cast<long long>(band) * cols + c] = t;
   }
-#pragma unroll
-  for (int j = 0; j < 8; ++j) red[warp][lane * 8 + j] = s[j];
-  __syncthreads();
-  float t = 0.f;
-#pragma unroll
-  for (int w = 0; w < 8; ++w) t += red[w][threadIdx.x];
-  const int c = blockIdx.x * 256 + threadIdx.x;
-  if (c < cols) scratch[static_cast<long long>(blockIdx.y) * cols + c] = t;
 }
 
 __global__ void noalloc_fold(const float* __restrict__ scratch, int parts, int cols, void* out, int out_f32,
@@ -117,20 +135,50 @@ __global__ void noalloc_fold(const float* __restrict__ scratch, int parts, int c
   }
 }
 
-// Device address of the scratch array on the current device (set up once).
-int scratch_for_current_device(float** out) {
-  int dev = 0;
-  cudaError_t e = cudaGetDevice(&dev);
-  if (e != cudaSuccess) return fail(3, cudaGetErrorString(e));
-  if (dev < 0 || dev >= kMaxDevices) return fail(3, "device index out of range");
-  std::lock_guard<std::mutex> lock(g_setup_mutex);
-  if (g_scratch_addr[dev] == nullptr) {
+// Device address of the scratch array in the current CUDA context, looked up
+// once per context with that context current.
+// cuCtxGetCurrent, resolved through the runtime (the library does not link
+// libcuda directly, so it still loads on a machine without a driver).
+using CtxGetCurrentFn = CUresult (*)(CUcontext*);
+CtxGetCurrentFn ctx_get_current() {
+  static CtxGetCurrentFn fn = [] {
     void* p = nullptr;
-    e = cudaGetSymbolAddress(&p, g_colsum_scratch);
-    if (e != cudaSuccess || p == nullptr) return fail(3, cudaGetErrorString(e));
-    g_scratch_addr[dev] = static_cast<float*>(p);
+    cudaDriverEntryPointQueryResult q{};
+    if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &p, cudaEnableDefault, &q) != cudaSuccess ||
+        q != cudaDriverEntryPointSuccess)
+      p = nullptr;
+    return reinterpret_cast<CtxGetCurrentFn>(p);
+  }();
+  return fn;
+}
+
+int scratch_for_current_context(float** out) {
+  const CtxGetCurrentFn get_ctx = ctx_get_current();
+  if (get_ctx == nullptr) return fail(3, "cuCtxGetCurrent is not available from the CUDA driver");
+  CUcontext ctx = nullptr;
+  if (get_ctx(&ctx) != CUDA_SUCCESS) return fail(3, "cuCtxGetCurrent failed");
+  if (ctx == nullptr) {
+    // No context yet on this thread: make the current device's primary
+    // context current (cudaSetDevice initialises it), as the runtime would.
+    int dev = 0;
+    cudaError_t e0 = cudaGetDevice(&dev);
+    if (e0 == cudaSuccess) e0 = cudaSetDevice(dev);
+    if (e0 != cudaSuccess) return fail(3, cudaGetErrorString(e0));
+    if (get_ctx(&ctx) != CUDA_SUCCESS || ctx == nullptr) return fail(3, "no current CUDA context");
   }
-  *out = g_scratch_addr[dev];
+  std::lock_guard<std::mutex> lock(g_setup_mutex);
+  for (int i = 0; i < g_scratch_count; ++i) {
+    if (g_scratch_addr[i].ctx == ctx) {
+      *out = g_scratch_addr[i].addr;
+      return 0;
+    }
+  }
+  if (g_scratch_count == kMaxContexts) return fail(3, "too many CUDA contexts for the scratch address cache");
+  void* p = nullptr;
+  const cudaError_t e = cudaGetSymbolAddress(&p, g_colsum_scratch);
+  if (e != cudaSuccess || p == nullptr) return fail(3, cudaGetErrorString(e));
+  g_scratch_addr[g_scratch_count++] = {ctx, static_cast<float*>(p)};
+  *out = static_cast<float*>(p);
   return 0;
 }
 
@@ -157,11 +205,12 @@ extern "C" __attribute__((visibility("default"))) int mnb_bias_grad_noalloc(cons
     return fail(2, msg);
   }
   float* scratch = nullptr;
-  const int rc = scratch_for_current_device(&scratch);
+  const int rc = scratch_for_current_context(&scratch);
   if (rc != 0) return rc;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  noalloc_colsum_partials<<<dim3((cols + 255) / 256, static_cast<unsigned>(parts)), 256, 0, s>>>(
-      static_cast<const __nv_bfloat16*>(grad), scratch, rows, cols);
+  const unsigned grid_y = static_cast<unsigned>(parts < kMaxGridY ? parts : kMaxGridY);
+  noalloc_colsum_partials<<<dim3((cols + 255) / 256, grid_y), 256, 0, s>>>(
+      static_cast<const __nv_bfloat16*>(grad), scratch, rows, cols, static_cast<int>(parts));
   noalloc_fold<<<(cols + 255) / 256, 256, 0, s>>>(scratch, static_cast<int>(parts), cols, out, out_is_fp32 ? 1 : 0,
                                                   accumulate ? 1 : 0);
   const cudaError_t e = cudaGetLastError();

@@ -64,6 +64,37 @@ def test_no_alloc_entry_matches_allocating_entry(rows, cols, dtype):
         assert err <= 1e-2 * (want.abs().max().item() + 1e-6), f"call {call}: max err {err}"
 
 
+def test_no_alloc_entry_bf16_accumulate_and_near_limit():
+    """Accumulate into a bf16 output, on a shape that uses most of the scratch."""
+    lib = _lib()
+    limit = lib.mnb_noalloc_max_scratch_floats()
+    cols = 4096
+    rows = (limit // cols) * 128 - 5  # ceil(rows/128) * cols is just inside the limit
+    g = (torch.randn(rows, cols, device=DEV) * 0.25).to(torch.bfloat16)
+    base = (torch.randn(cols, device=DEV)).to(torch.bfloat16)
+    want = base.float() + K.bias_grad(g, torch.float32)
+    for call in range(2):
+        out = base.clone()
+        assert _call(lib, g, out, accumulate=True) == 0, lib.mnb_noalloc_last_error().decode()
+        torch.cuda.synchronize()
+        err = (out.float() - want).abs().max().item()
+        assert err <= 1e-2 * want.abs().max().item(), f"call {call}: max err {err}"
+
+
+def test_no_alloc_entry_more_bands_than_grid_rows():
+    """More than 65,535 bands of 128 rows: CTAs walk several bands each."""
+    lib = _lib()
+    cols = 8
+    rows = 65535 * 128 + 3 * 128 + 17  # 65,539 bands
+    g = (torch.rand(rows, cols, device=DEV) - 0.5).to(torch.bfloat16)
+    want = g.float().sum(0)
+    out = torch.zeros(cols, dtype=torch.float32, device=DEV)
+    rc = _call(lib, g, out)
+    torch.cuda.synchronize()
+    assert rc == 0, lib.mnb_noalloc_last_error().decode()
+    assert (out - want).abs().max().item() <= 1e-3 * rows ** 0.5
+
+
 def test_no_alloc_entry_accumulates_and_rejects_oversize():
     lib = _lib()
     g = torch.randn(512, 256, device=DEV).to(torch.bfloat16)
