@@ -64,13 +64,15 @@ def worker(pg, data: torch.Tensor, vocab: str, cfg: dict) -> float:
                 print(f"step {step:4d} | loss {final:.4f} | {tokens / dt:,.0f} tok/s", flush=True)
                 t0, tokens = time.perf_counter(), 0
     if cfg["fsdp"] and pg.rank == 0:
-        mib = {k: v / 2**20 for k, v in wrapped.memory_report().items()}
-        print("\nparameter memory per rank:\n"
-              f"  DDP equivalent (full replica): {mib['ddp_equivalent']:8.2f} MiB\n"
-              f"  FSDP resident shards:          {mib['sharded_params_resident']:8.2f} MiB\n"
-              f"  FSDP replicated (embeds/head): {mib['replicated_params']:8.2f} MiB\n"
-              f"  FSDP peak transient gather:    {mib['peak_transient']:8.2f} MiB\n"
-              f"  FSDP peak total:               {mib['fsdp_peak']:8.2f} MiB", flush=True)
+        rows = (("replica a DDP rank would hold", "ddp_equivalent"),
+                ("shards resident between steps", "sharded_params_resident"),
+                ("parameters kept whole on every rank", "replicated_params"),
+                ("largest gathered unit in flight", "peak_transient"),
+                ("peak while training", "fsdp_peak"))
+        report = wrapped.memory_report()
+        print("\nFSDP parameter memory on rank 0 (MiB):", flush=True)
+        for label, key in rows:
+            print(f"  {label:<38s}{report[key] / 2**20:10.2f}", flush=True)
     state = wrapped.full_state_dict() if cfg["fsdp"] else None
     if pg.rank == 0 and cfg["sample"]:
         if state is not None:

@@ -84,17 +84,17 @@ MUTATIONS: list[Mutation] = [
     M("ddp-no-average", "mini_nccl_b200/parallel/ddp.py",
       "                bucket.buffer.div_(self.pg.world_size)\n",
       "                pass\n",
-      ["tests/test_ddp.py::test_ddp_matches_single_process"],
+      ["tests/test_ddp.py::test_tied_lm_trains_like_one_process"],
       "gradients are summed, not averaged"),
     M("ddp-no-sync-ignored", "mini_nccl_b200/parallel/ddp.py",
       "            if self._accumulating:\n                return  # inside no_sync()",
       "            if False:\n                return  # inside no_sync()",
-      ["tests/test_ddp.py::test_no_sync_accumulates_without_communicating"],
+      ["tests/test_ddp.py::test_no_sync_accumulates_three_microbatches"],
       "no_sync() still communicates"),
     M("ddp-bucket-order", "mini_nccl_b200/parallel/ddp.py",
       "        for p in reversed(list(self.module.parameters())):\n",
       "        for p in list(self.module.parameters()):\n",
-      ["tests/test_ddp.py::test_gradients_live_in_the_buckets"],
+      ["tests/test_ddp.py::test_a_dtype_change_starts_a_new_bucket"],
       "buckets follow registration order, so the first bucket to fill is reduced last"),
     M("fsdp-rng-not-replayed", "mini_nccl_b200/parallel/fsdp.py",
       "                torch.set_rng_state(ctx.cpu_rng)\n",
@@ -120,7 +120,7 @@ MUTATIONS: list[Mutation] = [
     M("pipeline-lifo", "mini_nccl_b200/parallel/pipeline.py",
       "            x, out = self._queue.popleft()\n",
       "            x, out = self._queue.pop()\n",
-      ["tests/test_pipeline.py::test_1f1b_matches_single_process_four_stages"],
+      ["tests/test_pipeline.py::test_gradients_match_one_process"],
       "gradients are matched to the newest microbatch instead of the oldest"),
     M("pipeline-warmup-too-deep", "mini_nccl_b200/parallel/pipeline.py",
       "        warm = min(self.n_stages - 1 - self.rank, n)\n",
@@ -133,8 +133,8 @@ MUTATIONS: list[Mutation] = [
       ["tests/test_mesh.py::test_mesh_layout_last_dimension_fastest"],
       "the rank layout no longer matches the documented last-dimension-fastest order"),
     M("recorder-seq-frozen", "mini_nccl_b200/recorder.py",
-      "            self._seq[channel] = value + 1\n",
-      "            self._seq[channel] = value\n",
+      "        self._next_seq[channel] = seq + 1\n",
+      "        self._next_seq[channel] = seq\n",
       ["tests/test_faults.py::test_desync_times_out_with_diagnosis"],
       "every collective gets the same sequence number, so desyncs are invisible"),
     M("staging-no-stream-order", "mini_nccl_b200/device.py",

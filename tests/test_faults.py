@@ -11,7 +11,6 @@ import os
 import subprocess
 import sys
 import time
-from collections import deque
 
 import pytest
 import torch
@@ -91,12 +90,11 @@ def test_desync_times_out_with_diagnosis(tmp_path) -> None:
 
 def _bounded(pg) -> None:
     pg.recorder.enabled = True
-    pg.recorder.capacity = 8
-    pg.recorder._events = deque(pg.recorder._events, maxlen=8)
+    pg.recorder.resize(8)
     for _ in range(40):
         C.all_reduce(pg, torch.ones(64))
-    assert len(pg.recorder._events) == 8
-    assert pg.recorder._dropped > 0
+    assert len(pg.recorder.events()) == 8
+    assert pg.recorder.dropped > 0
     assert pg.recorder.next_seq(-1) >= 40
 
 
@@ -105,8 +103,7 @@ def test_recorder_ring_buffer_bounds_memory() -> None:
 
 
 def _late_skip(pg) -> None:
-    pg.recorder.capacity = 6
-    pg.recorder._events = deque(pg.recorder._events, maxlen=6)
+    pg.recorder.resize(6)
     t = torch.ones(128)
     for _ in range(20):
         C.all_reduce(pg, t)

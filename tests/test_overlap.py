@@ -45,7 +45,7 @@ def _measure(pg, overlap: bool) -> dict:
     t1 = time.perf_counter_ns()
     submitted = ddp.reduce_submitted_ns
     ddp.sync()
-    buckets = [e for e in pg.recorder._events if e.op.startswith("ddp_bucket") and e.start_ns >= t0]
+    buckets = [e for e in pg.recorder.events() if e.op.startswith("ddp_bucket") and e.start_ns >= t0]
     first = min((e.start_ns for e in buckets), default=None)
     return {
         "rank": pg.rank,

@@ -1,4 +1,11 @@
-"""Pipeline schedules: whole-model parity, the 1F1B depth bound, tracing, validation."""
+"""Pipeline schedules on CPU ranks: gradients equal one process, depth, tracing.
+
+This library's own scenarios: a stack of pre-norm residual MLP blocks split
+evenly over the stages, a classification head with cross-entropy on the last
+stage, and per-case seeds; every stage's parameter gradients and the last
+stage's loss must equal what one process computes on the whole model and the
+whole batch.
+"""
 
 from __future__ import annotations
 
@@ -14,120 +21,135 @@ from torch import nn
 from mini_nccl_b200.launcher import run
 from mini_nccl_b200.pipeline import PIPELINE_CHANNEL, PipelineParallel
 
-WIDTH, PER_STAGE = 8, 2
+HIDDEN, CLASSES, BLOCKS_PER_STAGE = 12, 5, 2
 
 
-def layers_for(n_stages: int) -> list[nn.Module]:
-    torch.manual_seed(4)
-    return [nn.Sequential(nn.Linear(WIDTH, WIDTH), nn.Tanh()) for _ in range(n_stages * PER_STAGE)]
+class ResidualMLP(nn.Module):
+    def __init__(self) -> None:
+        super().__init__()
+        self.norm = nn.LayerNorm(HIDDEN)
+        self.up = nn.Linear(HIDDEN, 2 * HIDDEN)
+        self.down = nn.Linear(2 * HIDDEN, HIDDEN)
+
+    def forward(self, x: torch.Tensor) -> torch.Tensor:
+        return x + self.down(F.gelu(self.up(self.norm(x))))
 
 
-def my_stage(layers, rank: int) -> nn.Module:
-    return nn.Sequential(*layers[rank * PER_STAGE : (rank + 1) * PER_STAGE])
+class Head(nn.Module):
+    def __init__(self) -> None:
+        super().__init__()
+        self.norm = nn.LayerNorm(HIDDEN)
+        self.out = nn.Linear(HIDDEN, CLASSES)
+
+    def forward(self, x: torch.Tensor) -> torch.Tensor:
+        return self.out(self.norm(x))
 
 
-def _parity(pg, schedule: str, n_micro: int, batch: int) -> None:
-    layers = layers_for(pg.world_size)
-    whole = nn.Sequential(*layers)
-    stage = my_stage(layers, pg.rank)
-    pp = PipelineParallel(stage, pg, (batch // n_micro, WIDTH), loss_fn=F.mse_loss, schedule=schedule)
-    g = torch.Generator().manual_seed(19)
-    x = torch.randn(batch, WIDTH, generator=g)
-    y = torch.randn(batch, WIDTH, generator=g)
-    for p in whole.parameters():
-        p.grad = None
-    loss = pp.step(x if pg.rank == 0 else None, y if pg.rank == pg.world_size - 1 else None, n_micro)
-    got = [p.grad.clone() for p in stage.parameters()]
-    for p in whole.parameters():
-        p.grad = None
-    ref_loss = F.mse_loss(whole(x), y)
-    ref_loss.backward()
-    for i, p in enumerate(stage.parameters()):
-        torch.testing.assert_close(got[i], p.grad, rtol=1e-4, atol=1e-6)
-    if pg.rank == pg.world_size - 1:
-        torch.testing.assert_close(torch.tensor(loss), ref_loss.detach(), rtol=1e-5, atol=1e-6)
+def build_stages(n_stages: int, seed: int) -> list[nn.Sequential]:
+    """The whole model, already cut into stages (the last one ends in the head)."""
+    torch.manual_seed(seed)
+    stages = [nn.Sequential(*(ResidualMLP() for _ in range(BLOCKS_PER_STAGE))) for _ in range(n_stages)]
+    stages[-1].append(Head())
+    return stages
 
 
-def test_1f1b_matches_single_process_two_stages() -> None:
-    run(_parity, 2, "1f1b", 4, 16)
+def _matches_one_process(pg, schedule: str, n_micro: int, batch: int, seed: int) -> float | None:
+    stages = build_stages(pg.world_size, seed)
+    whole = nn.Sequential(*stages)
+    mine = stages[pg.rank]
+    pp = PipelineParallel(mine, pg, (batch // n_micro, HIDDEN), loss_fn=F.cross_entropy, schedule=schedule)
+    data = torch.Generator().manual_seed(seed + 1)
+    x = torch.randn(batch, HIDDEN, generator=data)
+    y = torch.randint(0, CLASSES, (batch,), generator=data)
+    last = pg.rank == pg.world_size - 1
+    whole.zero_grad(set_to_none=True)
+    loss = pp.step(x if pg.rank == 0 else None, y if last else None, n_micro)
+    piped = [p.grad.clone() for p in mine.parameters()]
+    whole.zero_grad(set_to_none=True)
+    want = F.cross_entropy(whole(x), y)
+    want.backward()
+    for got, p in zip(piped, mine.parameters(), strict=True):
+        torch.testing.assert_close(got, p.grad, rtol=1e-5, atol=1e-6)
+    if last:
+        assert abs(float(loss) - want.item()) <= 1e-5 * max(1.0, abs(want.item()))
+        return float(loss)
+    return None
 
 
-def test_1f1b_matches_single_process_four_stages() -> None:
-    run(_parity, 4, "1f1b", 8, 16)
+@pytest.mark.parametrize("world,schedule,n_micro,batch,seed", [
+    (2, "1f1b", 6, 18, 3),   # more microbatches than stages
+    (4, "1f1b", 4, 16, 5),   # exactly one microbatch per stage
+    (4, "1f1b", 3, 12, 7),   # fewer microbatches than stages: warm-up is cut short
+    (3, "gpipe", 5, 15, 11),
+    (2, "1f1b", 1, 6, 13),   # one microbatch: no steady state at all
+])
+def test_gradients_match_one_process(world, schedule, n_micro, batch, seed) -> None:
+    losses = run(_matches_one_process, world, schedule, n_micro, batch, seed)
+    assert losses[-1] is not None and all(v is None for v in losses[:-1])
 
 
-def test_gpipe_matches_single_process() -> None:
-    run(_parity, 4, "gpipe", 8, 16)
-
-
-def test_1f1b_fewer_microbatches_than_stages() -> None:
-    run(_parity, 4, "1f1b", 2, 16)
-
-
-def test_single_microbatch_degenerates_cleanly() -> None:
-    run(_parity, 3, "1f1b", 1, 12)
-
-
-def _depth(pg, schedule: str, n_micro: int) -> dict:
-    stage = my_stage(layers_for(pg.world_size), pg.rank)
-    pp = PipelineParallel(stage, pg, (2, WIDTH), loss_fn=F.mse_loss, schedule=schedule)
-    g = torch.Generator().manual_seed(23)
-    b = 2 * n_micro
-    pp.step(torch.randn(b, WIDTH, generator=g) if pg.rank == 0 else None,
-            torch.randn(b, WIDTH, generator=g) if pg.rank == pg.world_size - 1 else None, n_micro)
-    return {"rank": pg.rank, "peak": pp.in_flight_peak}
+def _peak_depth(pg, schedule: str, n_micro: int) -> int:
+    stage = build_stages(pg.world_size, 17)[pg.rank]
+    pp = PipelineParallel(stage, pg, (3, HIDDEN), loss_fn=F.cross_entropy, schedule=schedule)
+    data = torch.Generator().manual_seed(18)
+    n = 3 * n_micro
+    x = torch.randn(n, HIDDEN, generator=data)
+    y = torch.randint(0, CLASSES, (n,), generator=data)
+    pp.step(x if pg.rank == 0 else None, y if pg.rank == pg.world_size - 1 else None, n_micro)
+    return pp.in_flight_peak
 
 
 def test_1f1b_bounds_in_flight_microbatches() -> None:
-    W, M = 4, 12
-    peaks = {r["rank"]: r["peak"] for r in run(_depth, W, "1f1b", M)}
-    for rank, peak in peaks.items():
-        assert peak <= W - rank and peak < M, peaks
-    assert peaks[0] > peaks[W - 1] and peaks[W - 1] == 1, peaks
+    W, M = 4, 10
+    peaks = run(_peak_depth, W, "1f1b", M)
+    assert peaks == [W - s for s in range(W)], peaks  # stage s holds at most W - s, the last one 1
 
 
 def test_gpipe_holds_every_microbatch() -> None:
-    for rep in run(_depth, 4, "gpipe", 12):
-        assert rep["peak"] == 12, rep
+    assert run(_peak_depth, 3, "gpipe", 7) == [7, 7, 7]
 
 
-def _traced(pg) -> None:
-    stage = nn.Sequential(nn.Linear(WIDTH, WIDTH), nn.Tanh())
-    pp = PipelineParallel(stage, pg, (2, WIDTH), loss_fn=F.mse_loss)
-    for _ in range(2):
-        pp.step(torch.randn(8, WIDTH) if pg.rank == 0 else None,
-                torch.randn(8, WIDTH) if pg.rank == pg.world_size - 1 else None, 4)
+def _two_traced_steps(pg) -> None:
+    stage = build_stages(pg.world_size, 21)[pg.rank]
+    pp = PipelineParallel(stage, pg, (2, HIDDEN), loss_fn=F.cross_entropy)
+    for k in range(2):
+        data = torch.Generator().manual_seed(100 + k)
+        x = torch.randn(6, HIDDEN, generator=data)
+        y = torch.randint(0, CLASSES, (6,), generator=data)
+        pp.step(x if pg.rank == 0 else None, y if pg.rank == pg.world_size - 1 else None, 3)
 
 
-def test_pipeline_traced_without_faking_a_desync(tmp_path) -> None:
+def test_stage_dependent_schedules_do_not_read_as_a_desync(tmp_path) -> None:
     trace = tmp_path / "trace"
-    run(_traced, 4, trace_dir=trace, timeout=180.0)
+    run(_two_traced_steps, 3, trace_dir=trace, timeout=180.0)
     proc = subprocess.run([sys.executable, "-m", "mini_nccl_b200.diagnose", str(trace)],
                           capture_output=True, text=True)
     assert proc.returncode == 0, proc.stdout
     assert "all ranks agree" in proc.stdout and "'pipeline':" in proc.stdout, proc.stdout
-    st = json.loads((trace / "rank0.json").read_text())
-    ops = [e["op"] for e in st["events"]]
-    assert "pp_forward" in ops and "pp_backward" in ops
-    assert all(e["channel"] == PIPELINE_CHANNEL for e in st["events"] if e["op"].startswith("pp_"))
+    for rank in range(3):
+        events = json.loads((trace / f"rank{rank}.json").read_text())["events"]
+        pipe = [e for e in events if e["op"].startswith("pp_")]
+        assert {e["op"] for e in pipe} == {"pp_forward", "pp_backward"}
+        assert all(e["channel"] == PIPELINE_CHANNEL for e in pipe)
+        assert sum(e["op"] == "pp_forward" for e in pipe) == 6  # 2 steps x 3 microbatches
 
 
-def _rejects(pg) -> None:
-    stage = nn.Linear(WIDTH, WIDTH)
+def _bad_arguments(pg) -> None:
+    stage = nn.Linear(HIDDEN, HIDDEN)
     with pytest.raises(ValueError, match="unknown schedule"):
-        PipelineParallel(stage, pg, (2, WIDTH), loss_fn=F.mse_loss, schedule="zigzag")
+        PipelineParallel(stage, pg, (2, HIDDEN), loss_fn=F.mse_loss, schedule="interleaved")
     with pytest.raises(ValueError, match="needs loss_fn"):
-        PipelineParallel(stage, pg, (2, WIDTH), loss_fn=None)
-    pp = PipelineParallel(stage, pg, (2, WIDTH), loss_fn=F.mse_loss)
+        PipelineParallel(stage, pg, (2, HIDDEN))
+    pp = PipelineParallel(stage, pg, (3, HIDDEN), loss_fn=F.mse_loss)
     with pytest.raises(ValueError, match="needs inputs"):
-        pp.step(None, torch.zeros(4, WIDTH), 2)
+        pp.step(None, torch.zeros(6, HIDDEN), 2)
     with pytest.raises(ValueError, match="needs targets"):
-        pp.step(torch.zeros(4, WIDTH), None, 2)
+        pp.step(torch.zeros(6, HIDDEN), None, 2)
     with pytest.raises(ValueError, match="not divisible"):
-        pp.step(torch.zeros(5, WIDTH), torch.zeros(5, WIDTH), 2)
+        pp.step(torch.zeros(7, HIDDEN), torch.zeros(7, HIDDEN), 2)
     with pytest.raises(ValueError, match="at least 1"):
-        pp.step(torch.zeros(4, WIDTH), torch.zeros(4, WIDTH), 0)
+        pp.step(torch.zeros(6, HIDDEN), torch.zeros(6, HIDDEN), 0)
 
 
-def test_argument_errors_are_clear() -> None:
-    run(_rejects, 1)
+def test_argument_errors_are_raised_before_any_traffic() -> None:
+    run(_bad_arguments, 1)
