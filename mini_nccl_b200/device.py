@@ -35,6 +35,7 @@ import torch
 
 from . import collectives as _hostc
 from .errors import CollectiveTimeoutError, DeviceCommError
+from .utils import nvtx as _nvtx
 
 #: Below this many bytes ``auto`` uses the one-shot all-reduce.
 ONE_SHOT_MAX_BYTES = int(os.environ.get("MINI_NCCL_ONE_SHOT_MAX_BYTES", 512 << 10))
@@ -83,6 +84,7 @@ class DeviceComm:
         self.staging_bytes = self.impl.segment_bytes(self.impl.staging_segment())
         self._schedules: dict[tuple, torch.Tensor] = {}
         self._last_issued: torch.cuda.Event | None = None
+        self._nvtx_open: list[bool] = []
         recorder = getattr(comm, "recorder", None)
         if recorder is not None:
             recorder.attach_device_log(self.device_events)
@@ -169,6 +171,7 @@ class DeviceComm:
 
     def _record(self, name: str, algorithm: str, nbytes: int, **detail):
         self._order_after_previous()
+        self._nvtx_open.append(_nvtx.push(_nvtx.label(name, algorithm, nbytes)))
         rec = getattr(self.comm, "recorder", None)
         return rec.start(name, algorithm, channel=-1, nbytes=nbytes, device=True, **detail) if rec is not None else None
 
@@ -177,6 +180,7 @@ class DeviceComm:
         rec = getattr(self.comm, "recorder", None)
         if rec is not None:
             rec.finish(ev)
+        _nvtx.pop(self._nvtx_open.pop() if self._nvtx_open else False)
 
     # Every kernel of this communicator runs in host issue order, whichever
     # stream it is launched on: the kernels of different ranks wait for one

@@ -484,6 +484,37 @@ class FusedAdamW(torch.optim.Optimizer):
         self._tables[gi] = (key, *out)
         return out
 
+    def state_dict(self) -> dict:
+        """torch's optimizer state dict plus the shared step count.
+
+        Moments and master weights are saved as fp32, whatever the
+        parameters' dtype."""
+        sd = super().state_dict()
+        sd["fused_adamw_step"] = self._step
+        return sd
+
+    def load_state_dict(self, state_dict: dict) -> None:
+        """Restore a :meth:`state_dict`, keeping moments and masters in fp32.
+
+        (``torch.optim.Optimizer.load_state_dict`` would cast them to each
+        parameter's dtype, rounding fp32 masters of bf16 parameters.)"""
+        saved_groups = state_dict["param_groups"]
+        if len(saved_groups) != len(self.param_groups):
+            raise ValueError("the state dict has a different number of parameter groups")
+        by_index = {}
+        for group, saved in zip(self.param_groups, saved_groups, strict=True):
+            if len(group["params"]) != len(saved["params"]):
+                raise ValueError("a parameter group has a different number of parameters")
+            by_index.update(zip(saved["params"], group["params"], strict=True))
+            group.update({k: v for k, v in saved.items() if k != "params"})
+        self.state.clear()
+        for index, st in state_dict["state"].items():
+            p = by_index[index]
+            self.state[p] = {k: v.detach().to(device=p.device, dtype=torch.float32).clone().contiguous()
+                             if torch.is_tensor(v) else v for k, v in st.items()}
+        self._step = int(state_dict.get("fused_adamw_step", 0))
+        self._tables.clear()  # the cached pointer tables name the old state tensors
+
     @torch.no_grad()
     def step(self, closure=None, grad_scale: float = 1.0):
         loss = closure() if closure is not None else None

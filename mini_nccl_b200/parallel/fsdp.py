@@ -266,18 +266,34 @@ class ShardAdamW:
     def __init__(self, lr: float = 3e-4, betas: tuple[float, float] = (0.9, 0.95), eps: float = 1e-8,
                  weight_decay: float = 0.1) -> None:
         self.hp = {"lr": lr, "betas": tuple(betas), "eps": eps, "weight_decay": weight_decay}
-        self.state: dict[int, dict] = {}
+        #: unit name -> {"step", "m", "v"[, "master"]}; names are stable across
+        #: processes, so a checkpoint written by one run loads into the next.
+        self.state: dict[str, dict] = {}
 
     def _state(self, unit: _Unit) -> dict:
-        st = self.state.get(id(unit))
+        st = self.state.get(unit.name)
         if st is None:
             shard = unit.shard.detach()
             st = {"step": 0, "m": torch.zeros(shard.numel(), dtype=torch.float32, device=shard.device),
                   "v": torch.zeros(shard.numel(), dtype=torch.float32, device=shard.device)}
             if shard.dtype != torch.float32:
                 st["master"] = shard.float().clone()
-            self.state[id(unit)] = st
+            self.state[unit.name] = st
         return st
+
+    def state_dict(self) -> dict:
+        """Hyper-parameters and every unit's moments, master shard and step (this rank's shards)."""
+        return {"hp": dict(self.hp),
+                "state": {name: {k: (v.detach().clone() if torch.is_tensor(v) else v) for k, v in st.items()}
+                          for name, st in self.state.items()}}
+
+    def load_state_dict(self, sd: dict, device: torch.device | None = None) -> None:
+        self.hp = dict(sd["hp"])
+        self.hp["betas"] = tuple(self.hp["betas"])
+        self.state = {}
+        for name, st in sd["state"].items():
+            self.state[name] = {k: (v.to(device=device or v.device, dtype=torch.float32).clone().contiguous()
+                                    if torch.is_tensor(v) else int(v)) for k, v in st.items()}
 
     @torch.no_grad()
     def step_unit(self, unit: _Unit, flat_grad: torch.Tensor) -> None:
@@ -489,6 +505,13 @@ class FullyShardedDataParallel(nn.Module):
     def shard_parameters(self) -> list[nn.Parameter]:
         return [u.shard for u in self.units]
 
+    def replicated_parameters(self) -> list[nn.Parameter]:
+        """Parameters outside every unit (kept whole on each rank, averaged in ``sync``).
+
+        With ``optimizer_in_backward`` these are all the user's optimizer has
+        to step: the shards are updated inside the reduce-scatter."""
+        return list(self._replicated)
+
     def parameters(self, recurse: bool = True):
         """Shards and replicated parameters only (never the transient full ones)."""
         return iter(self.shard_parameters() + self._replicated)
@@ -568,9 +591,18 @@ class FullyShardedDataParallel(nn.Module):
             state[name] = b.detach().clone()
         return state
 
-    def sharded_state_dict(self) -> dict[str, object]:
-        """This rank's shards plus the metadata to re-assemble them (per-rank file)."""
-        return {
+    def sharded_state_dict(self, optimizer: torch.optim.Optimizer | None = None) -> dict[str, object]:
+        """Everything this rank needs to resume, as one per-rank checkpoint.
+
+        Holds this rank's shards, the replicated parameters and buffers, the
+        fused shard optimizer's state (fp32 master shards, moments and step
+        counts) when ``optimizer_in_backward`` is on, and the ``state_dict`` of
+        ``optimizer`` (the user's optimizer over shards and replicated
+        parameters) when given.  Save it with ``torch.save`` to one file per
+        rank; :meth:`load_sharded_state_dict` restores it on the same layout,
+        after which training continues bit for bit as if never interrupted.
+        """
+        sd: dict[str, object] = {
             "rank": self.pg.rank,
             "world_size": self.pg.world_size,
             "shards": {u.name: u.shard.detach().clone() for u in self.units},
@@ -578,9 +610,16 @@ class FullyShardedDataParallel(nn.Module):
                 self._param_names.get(id(p), f"replicated{i}"): p.detach().clone()
                 for i, p in enumerate(self._replicated)
             },
+            "buffers": {name: b.detach().clone() for name, b in self.module.named_buffers()},
         }
+        if self.shard_optimizer is not None:
+            sd["shard_optimizer"] = self.shard_optimizer.state_dict()
+        if optimizer is not None:
+            sd["optimizer"] = optimizer.state_dict()
+        return sd
 
-    def load_sharded_state_dict(self, state: dict[str, object]) -> None:
+    def load_sharded_state_dict(self, state: dict[str, object],
+                                optimizer: torch.optim.Optimizer | None = None) -> None:
         if state["world_size"] != self.pg.world_size or state["rank"] != self.pg.rank:
             raise ValueError("sharded checkpoint was written by a different rank layout")
         shards = state["shards"]
@@ -590,3 +629,14 @@ class FullyShardedDataParallel(nn.Module):
                 u.shard.copy_(shards[u.name])  # type: ignore[index]
             for i, p in enumerate(self._replicated):
                 p.copy_(replicated[self._param_names.get(id(p), f"replicated{i}")])  # type: ignore[index]
+            for name, b in self.module.named_buffers():
+                saved = state.get("buffers", {}).get(name)  # type: ignore[union-attr]
+                if saved is not None:
+                    b.copy_(saved)
+        if self.shard_optimizer is not None and "shard_optimizer" in state:
+            device = self.units[0].shard.device
+            self.shard_optimizer.load_state_dict(state["shard_optimizer"], device=device)  # type: ignore[arg-type]
+        if optimizer is not None:
+            if "optimizer" not in state:
+                raise ValueError("the checkpoint holds no optimizer state")
+            optimizer.load_state_dict(state["optimizer"])  # type: ignore[arg-type]

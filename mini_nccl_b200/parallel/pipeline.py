@@ -24,6 +24,7 @@ import torch
 from torch import nn
 
 from ..communicator import Communicator
+from ..utils import nvtx as _nvtx
 
 SCHEDULES = ("1f1b", "gpipe")
 
@@ -58,6 +59,7 @@ class PipelineParallel:
             first = next(iter(stage.parameters()), None)
             device = first.device if first is not None else torch.device("cpu")
         self.device = torch.device(device)
+        self._gpu = self.device.type == "cuda"
         self.rank = pg.rank
         self.n_stages = pg.world_size
         self.is_first = self.rank == 0
@@ -104,6 +106,7 @@ class PipelineParallel:
             "pp_forward", self.schedule, channel=PIPELINE_CHANNEL,
             nbytes=self._activation_bytes, stage=self.rank, depth=len(self._queue),
         )
+        opened = _nvtx.push(_nvtx.label("pp_forward", self.schedule, self._activation_bytes)) if self._gpu else False
         try:
             x = None if self.is_first else self._recv_activation()
             out = self.stage(micro_input if self.is_first else x)
@@ -114,6 +117,7 @@ class PipelineParallel:
             return out
         finally:
             self.pg.recorder.finish(ev)
+            _nvtx.pop(opened)
 
     def _backward(self, grad: torch.Tensor | None) -> None:
         """Backward of the *oldest* queued microbatch (FIFO: the next stage lags)."""
@@ -121,6 +125,7 @@ class PipelineParallel:
             "pp_backward", self.schedule, channel=PIPELINE_CHANNEL,
             nbytes=self._activation_bytes, stage=self.rank, depth=len(self._queue),
         )
+        opened = _nvtx.push(_nvtx.label("pp_backward", self.schedule, self._activation_bytes)) if self._gpu else False
         try:
             x, out = self._queue.popleft()
             if self.is_last:
@@ -132,6 +137,7 @@ class PipelineParallel:
                 self._send_gradient(x.grad)
         finally:
             self.pg.recorder.finish(ev)
+            _nvtx.pop(opened)
 
     # ---- schedules ----------------------------------------------------------------------
 

@@ -218,3 +218,60 @@ def test_optimizer_in_backward_matches_single_process() -> None:
 
 def test_optimizer_in_backward_without_recompute() -> None:
     run(_opt_in_backward, 2, 4, False)
+
+
+def _train(fsdp, opt, pg, steps: int, first_step: int) -> None:
+    W, per = pg.world_size, 5
+    for k in range(first_step, first_step + steps):
+        gen = torch.Generator().manual_seed(900 + k)  # batch k is the same however the run was split
+        x = torch.randn(W * per, 8, generator=gen)
+        y = torch.randn(W * per, 1, generator=gen)
+        mine = slice(pg.rank * per, (pg.rank + 1) * per)
+        fsdp.zero_grad()
+        F.mse_loss(fsdp(x[mine]), y[mine]).backward()
+        fsdp.sync()
+        opt.step()
+
+
+def _resume_bit_exact(pg, path, fused: bool) -> None:
+    hp = dict(lr=3e-2, betas=(0.9, 0.95), eps=1e-8, weight_decay=0.1)
+
+    def fresh():
+        torch.manual_seed(3)
+        fsdp = FullyShardedDataParallel(Model(), pg, unit_cls=Block,
+                                        optimizer_in_backward=hp if fused else None)
+        # With the shard optimizer fused into backward the user's optimizer only
+        # sees the replicated parameters; otherwise it steps shards too.
+        params = fsdp.replicated_parameters() if fused else list(fsdp.parameters())
+        return fsdp, torch.optim.AdamW(params, **hp)
+
+    straight, straight_opt = fresh()
+    _train(straight, straight_opt, pg, 4, 0)
+
+    first, first_opt = fresh()
+    _train(first, first_opt, pg, 2, 0)
+    ckpt = path / f"rank{pg.rank}.pt"
+    torch.save(first.sharded_state_dict(optimizer=first_opt), ckpt)
+    del first, first_opt
+
+    resumed, resumed_opt = fresh()
+    resumed.load_sharded_state_dict(torch.load(ckpt, weights_only=False), optimizer=resumed_opt)
+    _train(resumed, resumed_opt, pg, 2, 2)
+
+    for (name, a), b in zip(straight.full_state_dict().items(), resumed.full_state_dict().values(), strict=True):
+        assert torch.equal(a, b), f"{name} differs after resuming"
+    if fused:
+        for name, st in straight.shard_optimizer.state.items():
+            other = resumed.shard_optimizer.state[name]
+            assert st["step"] == other["step"] == 4
+            assert torch.equal(st["m"], other["m"]) and torch.equal(st["v"], other["v"])
+
+
+def test_resume_from_sharded_checkpoint_is_bit_exact(tmp_path) -> None:
+    """2 steps, save, load into a fresh model, 2 more steps == 4 uninterrupted steps."""
+    run(_resume_bit_exact, 2, tmp_path, False)
+
+
+def test_resume_with_fused_shard_optimizer_is_bit_exact(tmp_path) -> None:
+    """The fused reduce-scatter + AdamW keeps its moments and step count across a resume."""
+    run(_resume_bit_exact, 2, tmp_path, True)
