@@ -142,6 +142,27 @@ MUTATIONS: list[Mutation] = [
       "    pass\n",
       ["tests/test_device_staging.py::test_every_exchange_orders_the_copy_stream_behind_compute"],
       "the copy stream may read a block before the compute stream has reduced into it"),
+    M("ddp-comm-stream-no-producer-wait", "mini_nccl_b200/parallel/ddp.py",
+      "                self._comm_stream.wait_event(produced)\n",
+      "                pass\n",
+      ["tests/test_stream_order_gpu.py::test_ddp_comm_stream_waits_for_every_bucket"],
+      "a bucket's all-reduce may read the bucket before backward finished writing it", needs_gpu=True),
+    M("fsdp-prefetch-no-wait", "mini_nccl_b200/parallel/fsdp.py",
+      "        self._side.wait_stream(cur)\n        with torch.cuda.stream(self._side):\n"
+      "            flat = nxt._gather(nxt.shard)\n",
+      "        with torch.cuda.stream(self._side):\n            flat = nxt._gather(nxt.shard)\n",
+      ["tests/test_stream_order_gpu.py::test_fsdp_side_and_comm_streams_wait_for_their_producers"],
+      "the prefetched gather may run ahead of the compute stream it must follow", needs_gpu=True),
+    M("fsdp-prefetched-used-unawaited", "mini_nccl_b200/parallel/fsdp.py",
+      "        torch.cuda.current_stream(unit.device).wait_event(done)\n        return flat\n",
+      "        return flat\n",
+      ["tests/test_stream_order_gpu.py::test_fsdp_side_and_comm_streams_wait_for_their_producers"],
+      "the compute stream may read prefetched parameters before their gather finished", needs_gpu=True),
+    M("fsdp-reduce-scatter-no-wait", "mini_nccl_b200/parallel/fsdp.py",
+      "            side.wait_stream(cur)\n            with torch.cuda.stream(side):\n",
+      "            with torch.cuda.stream(side):\n",
+      ["tests/test_stream_order_gpu.py::test_fsdp_side_and_comm_streams_wait_for_their_producers"],
+      "a unit's gradient reduce-scatter may read gradients backward has not written yet", needs_gpu=True),
     M("control-docstring", "mini_nccl_b200/collectives.py",
       "    \"\"\"Deterministic contiguous split; the first ``n % parts`` pieces get one extra.\"\"\"\n",
       "    \"\"\"Deterministic contiguous split (the first n % parts pieces get one extra).\"\"\"\n",

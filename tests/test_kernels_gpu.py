@@ -29,9 +29,23 @@ def rnd(*shape, scale=1.0, seed=0):
 
 
 def close(got, want, tol):
-    err = (got.float() - want.float()).abs().max().item()
-    ref = want.float().abs().max().item() + 1e-6
-    assert err <= tol * ref, f"max abs err {err:.4g} vs max |ref| {ref:.4g} (rel {err / ref:.3g} > {tol})"
+    """Element-wise: |got - want| <= tol * |want| + (tol / 4) * max|want|.
+
+    The relative term bounds every entry by its own magnitude (bf16 rounding
+    of the result plus the error fp32 accumulation lets through); the small
+    absolute floor, a quarter of the tolerance at the tensor's largest entry,
+    covers entries that are near zero only because of cancellation.
+    """
+    g, w = got.float(), want.float()
+    scale = w.abs().max().item() + 1e-6
+    err = (g - w).abs()
+    bound = tol * w.abs() + 0.25 * tol * scale
+    bad = err > bound
+    if bool(bad.any()):
+        i = int(torch.argmax((err - bound).flatten()).item())
+        raise AssertionError(
+            f"{int(bad.sum())} of {err.numel()} entries out of tolerance; worst at flat index {i}: "
+            f"got {g.flatten()[i].item():.5g}, want {w.flatten()[i].item():.5g} (tol {tol}, max |want| {scale:.4g})")
 
 
 def test_extension_is_the_in_tree_build():
@@ -159,7 +173,8 @@ def test_gelu_forward_backward():
 
 
 @pytest.mark.parametrize("B,T,H,D", [(2, 64, 2, 64), (2, 200, 3, 64), (1, 256, 2, 128), (2, 130, 2, 32),
-                                     (2, 512, 3, 64), (1, 1024, 2, 64), (2, 384, 2, 128)])
+                                     (2, 512, 3, 64), (1, 1024, 2, 64), (2, 384, 2, 128),
+                                     (1, 2048, 2, 128)])  # the FSDP / 3D configs' head dim and length
 def test_flash_attention(B, T, H, D):
     C = H * D
     qkv = rnd(B, T, 3 * C, seed=21).requires_grad_(True)
@@ -252,7 +267,7 @@ def test_gpt_block_matches_cpu_reference():
             continue
         err = (pg.grad.float().cpu() - pc.grad).abs().max().item()
         ref = pc.grad.abs().max().item() + 1e-8
-        assert err <= 0.08 * ref, f"{name}: grad err {err:.3g} vs {ref:.3g}"
+        assert err <= 0.06 * ref, f"{name}: grad err {err:.3g} vs {ref:.3g}"
 
 
 def test_gemm_throughput_is_tensor_core_class():
