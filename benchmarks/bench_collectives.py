@@ -19,7 +19,11 @@ from baseline/_ref) for all-reduce up to ``--reference-max-bytes``.
 ``two_shot_sym`` is the two-shot all-reduce on a tensor in symmetric memory
 (every peer has it mapped, like a DDP gradient bucket): results are stored
 straight into every rank's copy, with no copy-out (NCCL's counterpart is a
-registered user buffer).
+registered user buffer).  ``nvls`` reduces through the NVSwitch (multimem
+loads and stores) via a staging buffer; ``nvls_sym`` does it in place on a
+tensor bound to the multicast object (how DDP's buckets are reduced).
+Reduce-scatter, all-gather and broadcast are timed on both of this
+library's paths: ``direct`` (peer stores) and ``nvls``.
 Rank 0 prints one JSON line per measurement and writes the CSV.
 """
 
@@ -53,7 +57,7 @@ def main() -> None:
     ap.add_argument("--iters", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--ops", default="all_reduce,reduce_scatter,all_gather,broadcast,all_to_all")
-    ap.add_argument("--algorithms", default="auto,one_shot,two_shot,two_shot_sym,ring,tree,halving,naive")
+    ap.add_argument("--algorithms", default="auto,one_shot,two_shot,two_shot_sym,nvls,nvls_sym,ring,tree,halving,naive")
     ap.add_argument("--dtypes", default="float32,bfloat16,float32+bf16wire")
     ap.add_argument("--no-nccl", action="store_true")
     ap.add_argument("--reference", action="store_true")
@@ -97,11 +101,17 @@ def main() -> None:
 
     rows = []
     sym_bufs: dict = {}
+    dc = pg.device_comm()
+    nvls_paths = ("direct", "nvls") if dc.nvls else ("direct",)
+    if rank == 0:
+        print(json.dumps({"nvls": dc.nvls, "nvls_reason": dc.nvls_reason}), flush=True)
 
-    def sym_view(dtype, n):
-        buf = sym_bufs.get(dtype)
+    def sym_view(dtype, n, nvls=False):
+        key = (dtype, nvls)
+        buf = sym_bufs.get(key)
         if buf is None:
-            buf = sym_bufs[dtype] = pg.device_comm().symmetric_zeros(args.max_bytes // torch.empty(0, dtype=dtype).element_size(), dtype)
+            numel = args.max_bytes // torch.empty(0, dtype=dtype).element_size()
+            buf = sym_bufs[key] = dc.symmetric_zeros(numel, dtype, nvls=nvls)
         return buf[:n]
 
     def record(op, impl, algo, dtype, nbytes, ms):
@@ -129,12 +139,15 @@ def main() -> None:
                     continue
                 if op == "all_reduce":
                     for algo in args.algorithms.split(","):
-                        if algo == "two_shot_sym":
+                        if algo in ("nvls", "nvls_sym") and (not dc.nvls or wire is not None):
+                            continue
+                        if algo in ("two_shot_sym", "nvls_sym"):
                             if wire is None:
-                                sv = sym_view(dtype, n)
+                                sv = sym_view(dtype, n, nvls=algo == "nvls_sym")
                                 sv.copy_(x)
+                                a = algo[: -len("_sym")]
                                 record(op, "ours", algo, dname, size,
-                                       time_it(lambda: pg.device_comm().all_reduce(sv, algorithm="two_shot")))
+                                       time_it(lambda a=a: dc.all_reduce(sv, algorithm=a)))
                             continue
                         if algo == "halving" and world & (world - 1):
                             continue
@@ -148,7 +161,9 @@ def main() -> None:
                         record(op, "reference", "staged-ring", dname, size,
                                time_it(lambda: rdev.all_reduce_staged(ref_pg, x)))
                 elif op == "reduce_scatter":
-                    record(op, "ours", "direct", dname, size, time_it(lambda: C.reduce_scatter(pg, x)))
+                    for path in nvls_paths:
+                        record(op, "ours", path, dname, size,
+                               time_it(lambda p=path: dc.reduce_scatter(x, algorithm=p)))
                     if not args.no_nccl:
                         o = torch.empty(n // world, dtype=dtype, device=dev)
                         record(op, "nccl", "nccl", dname, size,
@@ -156,13 +171,20 @@ def main() -> None:
                 elif op == "all_gather":
                     shard = x[: n // world]
                     out = torch.empty(n, dtype=dtype, device=dev)
-                    record(op, "ours", "direct", dname, size,
-                           time_it(lambda: C.all_gather_into(pg, out, shard)))
+                    for path in nvls_paths:
+                        if path == "nvls" and (shard.numel() * shard.element_size()) % 16:
+                            continue
+                        record(op, "ours", path, dname, size,
+                               time_it(lambda p=path: dc.all_gather(shard, out.view(world, -1), algorithm=p)))
                     if not args.no_nccl:
                         record(op, "nccl", "nccl", dname, size,
                                time_it(lambda: dist.all_gather_into_tensor(out, shard)))
                 elif op == "broadcast":
-                    record(op, "ours", "direct", dname, size, time_it(lambda: C.broadcast(pg, x, src=0)))
+                    for path in nvls_paths:
+                        if path == "nvls" and size % 16:
+                            continue
+                        record(op, "ours", path, dname, size,
+                               time_it(lambda p=path: dc.broadcast(x, src=0, algorithm=p)))
                     if not args.no_nccl:
                         record(op, "nccl", "nccl", dname, size, time_it(lambda: dist.broadcast(x, src=0)))
                 elif op == "all_to_all":

@@ -13,8 +13,9 @@ Two engines sit behind that surface:
   (:mod:`mini_nccl_b200.device`): one sm_100a kernel per collective that
   loads and stores peer HBM over NVLink directly.  On the device the same
   algorithm names select the same *schedules* over peer memory, plus
-  ``one_shot`` / ``two_shot`` (what ``auto`` picks on a switch where every
-  peer is one hop away).
+  ``one_shot`` / ``two_shot`` (peer stores; every peer is one hop away on a
+  switch) and ``nvls`` (the NVSwitch adds the ranks' copies itself;
+  multimem loads and stores).  ``auto`` picks among the last three.
 * **CPU tensors** run the schedules below over the host TCP mesh.  They are
   the parity/testing path and what multi-host CPU runs use.
 
@@ -45,7 +46,7 @@ MAX_SLICES = int(os.environ.get("MINI_NCCL_MAX_SLICES", "1"))
 #: Host-path algorithms, in the order benchmarks report them.
 ALGORITHMS = ("ring", "tree", "halving", "naive")
 #: Extra schedules only the device path implements.
-DEVICE_ALGORITHMS = ALGORITHMS + ("one_shot", "two_shot")
+DEVICE_ALGORITHMS = ALGORITHMS + ("one_shot", "two_shot", "nvls")
 
 #: Dtypes too narrow to accumulate many terms in.
 LOW_PRECISION = (torch.bfloat16, torch.float16)
@@ -156,7 +157,7 @@ def all_reduce(
     nbytes = tensor.numel() * tensor.element_size()
     if algorithm == "auto":
         algorithm = "tree" if nbytes <= RING_THRESHOLD_BYTES else "ring"
-    elif algorithm in ("one_shot", "two_shot"):
+    elif algorithm in ("one_shot", "two_shot", "nvls"):
         # Device-only schedules; on the host their closest analogues.
         algorithm = "naive" if algorithm == "one_shot" else "ring"
     if algorithm == "halving" and (pg.world_size & (pg.world_size - 1)):

@@ -40,10 +40,12 @@
 #include <torch/extension.h>
 
 #include <cstring>
+#include <memory>
 #include <string>
 #include <vector>
 
 #include "common.cuh"
+#include "nvls.h"
 #include "peer.cuh"
 
 namespace cg = cooperative_groups;
@@ -892,6 +894,349 @@ __global__ void __launch_bounds__(kCommThreads) bcast_scatter_gather_kernel(Comm
   ring_end(a, ok);
 }
 
+// ===========================================================================
+// NVLS collectives: multimem loads and stores through an NVSwitch multicast
+// address (nvls.h).  `uc` / `mc` are the unicast and multicast addresses of
+// the same bytes of this call's region: a symmetric NVLS tensor (in place) or
+// the NVLS staging buffer (one parity half per call, like the peer staging).
+//
+// Work split: the message is W slices; block b of every rank owns sub-range
+// b of every slice, so a block-level barrier (block b of every rank) orders
+// exactly the bytes that block touches.  Rank r reduces slice r:
+//   multimem.ld_reduce  the NVSwitch reads slice r from every rank's memory
+//                       and returns the sum (bf16 / f16 accumulated in fp32);
+//   multimem.st         writes the result into every rank's memory at once.
+// Each element is reduced once, by one rank, so every rank holds identical
+// bits.  Per GPU that moves about (1 + 1/W) x the message over NVLink in each
+// direction, against 2 (W-1)/W for the peer two-shot kernel.
+// Accesses through the unicast and the multicast address of the same memory
+// are ordered with fence.proxy.alias around every barrier.
+// ===========================================================================
+MNB_DEVICE void fence_proxy_alias() { asm volatile("fence.proxy.alias;" ::: "memory"); }
+
+MNB_DEVICE bool nvls_barrier(const CommArgs& a, uint32_t value) {
+  fence_proxy_alias();
+  const bool ok = peer_barrier(a, value);
+  fence_proxy_alias();
+  return ok;
+}
+
+template <typename T> struct Multimem;
+template <> struct Multimem<float> {
+  static MNB_DEVICE uint4 ld_reduce(const void* p) {
+    float4 f;
+    asm volatile("multimem.ld_reduce.relaxed.sys.global.add.v4.f32 {%0,%1,%2,%3}, [%4];"
+                 : "=f"(f.x), "=f"(f.y), "=f"(f.z), "=f"(f.w)
+                 : "l"(p)
+                 : "memory");
+    return make_uint4(__float_as_uint(f.x), __float_as_uint(f.y), __float_as_uint(f.z), __float_as_uint(f.w));
+  }
+  static MNB_DEVICE void unpack(uint4 v, float* f) {
+    f[0] = __uint_as_float(v.x); f[1] = __uint_as_float(v.y); f[2] = __uint_as_float(v.z); f[3] = __uint_as_float(v.w);
+  }
+  static MNB_DEVICE uint4 pack(const float* f) {
+    return make_uint4(__float_as_uint(f[0]), __float_as_uint(f[1]), __float_as_uint(f[2]), __float_as_uint(f[3]));
+  }
+};
+template <> struct Multimem<__nv_bfloat16> {
+  static MNB_DEVICE uint4 ld_reduce(const void* p) {
+    uint4 v;
+    asm volatile("multimem.ld_reduce.relaxed.sys.global.add.acc::f32.v4.bf16x2 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+                 : "l"(p)
+                 : "memory");
+    return v;
+  }
+  static MNB_DEVICE void unpack(uint4 v, float* f) {
+    const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const float2 t = unpack_bf16x2(w[j]);
+      f[2 * j] = t.x;
+      f[2 * j + 1] = t.y;
+    }
+  }
+  static MNB_DEVICE uint4 pack(const float* f) {
+    return make_uint4(pack_bf16x2(f[0], f[1]), pack_bf16x2(f[2], f[3]), pack_bf16x2(f[4], f[5]),
+                      pack_bf16x2(f[6], f[7]));
+  }
+};
+template <> struct Multimem<__half> {
+  static MNB_DEVICE uint4 ld_reduce(const void* p) {
+    uint4 v;
+    asm volatile("multimem.ld_reduce.relaxed.sys.global.add.acc::f32.v4.f16x2 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+                 : "l"(p)
+                 : "memory");
+    return v;
+  }
+  static MNB_DEVICE void unpack(uint4 v, float* f) {
+    const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const float2 t = __half22float2(*reinterpret_cast<const __half2*>(&w[j]));
+      f[2 * j] = t.x;
+      f[2 * j + 1] = t.y;
+    }
+  }
+  static MNB_DEVICE uint4 pack(const float* f) {
+    uint32_t w[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const __half2 h = __floats2half2_rn(f[2 * j], f[2 * j + 1]);
+      w[j] = *reinterpret_cast<const uint32_t*>(&h);
+    }
+    return make_uint4(w[0], w[1], w[2], w[3]);
+  }
+};
+
+// 16 bytes into every rank's memory (raw bits: a store does no arithmetic).
+MNB_DEVICE void multimem_st16(void* p, uint4 v) {
+  asm volatile("multimem.st.relaxed.sys.global.v4.f32 [%0], {%1,%2,%3,%4};" ::"l"(p), "f"(__uint_as_float(v.x)),
+               "f"(__uint_as_float(v.y)), "f"(__uint_as_float(v.z)), "f"(__uint_as_float(v.w))
+               : "memory");
+}
+
+// Sub-range of slice c owned by this block, in 16-byte units.
+struct SliceSplit {
+  long long units, per_slice, per_block;
+  MNB_DEVICE void range(int c, long long* lo, long long* hi) const {
+    const long long c0 = min(units, c * per_slice), c1 = min(units, c0 + per_slice);
+    *lo = min(c1, c0 + per_block * blockIdx.x);
+    *hi = min(c1, *lo + per_block);
+  }
+};
+MNB_DEVICE SliceSplit slice_split(long long units, int slices) {
+  SliceSplit s;
+  s.units = units;
+  s.per_slice = (units + slices - 1) / slices;
+  s.per_block = (s.per_slice + gridDim.x - 1) / gridDim.x;
+  return s;
+}
+
+// Copy 16-byte units [lo, hi) of an n-element array; the last unit may be
+// partial: into the staging region it is zero-padded, out of it only the
+// n elements are written.
+template <typename T>
+MNB_DEVICE void copy_units(const T* src, T* dst, long long lo, long long hi, long long n, bool pad) {
+  constexpr int V = 16 / sizeof(T);
+  constexpr int U = 4;
+  for (long long u0 = lo + threadIdx.x; u0 < hi; u0 += U * blockDim.x) {
+    uint4 w[U];
+#pragma unroll
+    for (int j = 0; j < U; ++j) {
+      const long long u = u0 + j * blockDim.x;
+      if (u < hi && (u + 1) * V <= n) w[j] = ld_v4_cg(src + u * V);
+    }
+#pragma unroll
+    for (int j = 0; j < U; ++j) {
+      const long long u = u0 + j * blockDim.x;
+      if (u >= hi) continue;
+      if ((u + 1) * V <= n) {
+        st_v4(dst + u * V, w[j]);
+      } else {
+        for (int i = 0; i < V; ++i) {
+          const long long e = u * V + i;
+          if (e < n) dst[e] = src[e];
+          else if (pad) dst[e] = T(0.0f);
+        }
+      }
+    }
+  }
+}
+
+// Copy 16-byte units [lo, hi) (byte moves; sizes are 16-byte multiples).
+MNB_DEVICE void copy16(const void* src, void* dst, long long lo, long long hi) {
+  const uint8_t* s8 = reinterpret_cast<const uint8_t*>(src);
+  uint8_t* d8 = reinterpret_cast<uint8_t*>(dst);
+  constexpr int U = 4;
+  for (long long u0 = lo + threadIdx.x; u0 < hi; u0 += U * blockDim.x) {
+    uint4 w[U];
+#pragma unroll
+    for (int j = 0; j < U; ++j)
+      if (u0 + j * blockDim.x < hi) w[j] = ld_v4_cg(s8 + 16 * (u0 + j * blockDim.x));
+#pragma unroll
+    for (int j = 0; j < U; ++j)
+      if (u0 + j * blockDim.x < hi) st_v4(d8 + 16 * (u0 + j * blockDim.x), w[j]);
+  }
+}
+
+// all-reduce (sum).  staged: copy the input into the region first and the
+// result out of it last; otherwise the tensor is the region (in place).
+template <typename T, int THREADS, int MINB>
+__global__ void __launch_bounds__(THREADS, MINB) nvls_all_reduce_kernel(CommArgs a, char* uc, char* mc, int staged) {
+  constexpr int V = 16 / sizeof(T);
+  ring_begin(a);
+  const int W = a.world, r = a.rank;
+  const long long n = a.n;
+  const SliceSplit sp = slice_split((n + V - 1) / V, W);
+  long long lo, hi;
+  if (staged) {
+    for (int c = 0; c < W; ++c) {
+      sp.range(c, &lo, &hi);
+      copy_units<T>(reinterpret_cast<const T*>(a.in), reinterpret_cast<T*>(uc), lo, hi, n, true);
+    }
+  }
+  bool ok = nvls_barrier(a, a.epoch + 1);
+  if (ok) {
+    sp.range(r, &lo, &hi);
+    constexpr int U = 4;  // independent multimem loads in flight per thread
+    for (long long u0 = lo + threadIdx.x; u0 < hi; u0 += U * THREADS) {
+      uint4 v[U];
+#pragma unroll
+      for (int j = 0; j < U; ++j)
+        if (u0 + j * THREADS < hi) v[j] = Multimem<T>::ld_reduce(mc + 16 * (u0 + j * THREADS));
+#pragma unroll
+      for (int j = 0; j < U; ++j) {
+        if (u0 + j * THREADS >= hi) continue;
+        if (a.scale != 1.0f) {
+          float f[V];
+          Multimem<T>::unpack(v[j], f);
+#pragma unroll
+          for (int i = 0; i < V; ++i) f[i] *= a.scale;
+          v[j] = Multimem<T>::pack(f);
+        }
+        multimem_st16(mc + 16 * (u0 + j * THREADS), v[j]);
+      }
+    }
+    ok = nvls_barrier(a, a.epoch + 2);
+  }
+  if (ok && staged) {
+    for (int c = 0; c < W; ++c) {
+      sp.range(c, &lo, &hi);
+      copy_units<T>(reinterpret_cast<const T*>(uc), reinterpret_cast<T*>(a.out), lo, hi, n, false);
+    }
+  }
+  ring_end(a, ok);
+}
+
+// reduce-scatter (sum): out[chunk] = scale * sum over ranks of chunk r of the
+// input.  a.n = chunk elements (16-byte multiple).  The trailing barrier keeps
+// a fast rank from refilling its input while a peer's reduction still reads it.
+template <typename T>
+__global__ void __launch_bounds__(kCommThreads) nvls_reduce_scatter_kernel(CommArgs a, char* uc, char* mc, int staged) {
+  constexpr int V = 16 / sizeof(T);
+  ring_begin(a);
+  const int W = a.world, r = a.rank;
+  const long long chunk_u = a.n / V;
+  const SliceSplit sp = slice_split(chunk_u * W, W);
+  long long lo, hi;
+  if (staged) {
+    for (int c = 0; c < W; ++c) {
+      sp.range(c, &lo, &hi);
+      copy_units<T>(reinterpret_cast<const T*>(a.in), reinterpret_cast<T*>(uc), lo, hi, a.n * W, true);
+    }
+  }
+  bool ok = nvls_barrier(a, a.epoch + 1);
+  if (ok) {
+    sp.range(r, &lo, &hi);
+    T* out = reinterpret_cast<T*>(a.out);
+    constexpr int U = 4;
+    for (long long u0 = lo + threadIdx.x; u0 < hi; u0 += U * kCommThreads) {
+      uint4 v[U];
+#pragma unroll
+      for (int j = 0; j < U; ++j)
+        if (u0 + j * kCommThreads < hi) v[j] = Multimem<T>::ld_reduce(mc + 16 * (u0 + j * kCommThreads));
+#pragma unroll
+      for (int j = 0; j < U; ++j) {
+        const long long u = u0 + j * kCommThreads;
+        if (u >= hi) continue;
+        if (a.scale != 1.0f) {
+          float f[V];
+          Multimem<T>::unpack(v[j], f);
+#pragma unroll
+          for (int i = 0; i < V; ++i) f[i] *= a.scale;
+          v[j] = Multimem<T>::pack(f);
+        }
+        st_v4(out + (u - r * chunk_u) * V, v[j]);
+      }
+    }
+    ok = nvls_barrier(a, a.epoch + 2);
+  }
+  ring_end(a, ok);
+}
+
+// reduce-scatter fused with AdamW on the owned shard: the switch returns the
+// summed gradient slice and it feeds the update directly (see rs_adamw_kernel).
+template <typename TG, bool P_BF16>
+__global__ void __launch_bounds__(kCommThreads) nvls_rs_adamw_kernel(CommArgs a, AdamArgs o, char* uc, char* mc,
+                                                                    int staged) {
+  constexpr int V = 16 / sizeof(TG);
+  ring_begin(a);
+  const int W = a.world, r = a.rank;
+  const long long chunk_u = a.n / V;
+  const SliceSplit sp = slice_split(chunk_u * W, W);
+  long long lo, hi;
+  if (staged) {
+    for (int c = 0; c < W; ++c) {
+      sp.range(c, &lo, &hi);
+      copy_units<TG>(reinterpret_cast<const TG*>(a.in), reinterpret_cast<TG*>(uc), lo, hi, a.n * W, true);
+    }
+  }
+  bool ok = nvls_barrier(a, a.epoch + 1);
+  if (ok) {
+    sp.range(r, &lo, &hi);
+    for (long long u = lo + threadIdx.x; u < hi; u += kCommThreads) {
+      float g[8];
+      Multimem<TG>::unpack(Multimem<TG>::ld_reduce(mc + 16 * u), g);
+#pragma unroll
+      for (int i = 0; i < V; ++i) g[i] *= a.scale;
+      const long long e0 = (u - r * chunk_u) * V;
+      if constexpr (V == 8) {
+        adam_update8<P_BF16>(o, e0, g);
+      } else {
+#pragma unroll
+        for (int i = 0; i < V; ++i) adam_update<P_BF16>(o, e0 + i, g[i]);
+      }
+    }
+    ok = nvls_barrier(a, a.epoch + 2);
+  }
+  ring_end(a, ok);
+}
+
+// all-gather (kind 0: every rank stores its shard into slot r of every rank)
+// and broadcast (kind 1: the root stores the message into every rank), by
+// multimem stores; a.n = bytes per slot (16-byte multiple).  A first barrier
+// makes sure every rank is inside this collective before any store reaches
+// its memory (no multimem access ever targets a rank that has not launched
+// the same kernel); after the second one each rank copies the region out.
+__global__ void __launch_bounds__(kCommThreads) nvls_move_kernel(CommArgs a, char* uc, char* mc, int kind) {
+  ring_begin(a);
+  const int W = a.world, r = a.rank;
+  const long long units = a.n / 16;
+  const int slots = kind == 0 ? W : 1;
+  const SliceSplit sp = slice_split(units, 1);
+  long long lo, hi;
+  sp.range(0, &lo, &hi);
+  const uint8_t* in = reinterpret_cast<const uint8_t*>(a.in);
+  bool ok = nvls_barrier(a, a.epoch + 1);
+  if (ok && (kind == 0 || r == a.root)) {
+    char* dst = mc + (kind == 0 ? r * a.n : 0);
+    constexpr int U = 4;
+    for (long long u0 = lo + threadIdx.x; u0 < hi; u0 += U * kCommThreads) {
+      uint4 w[U];
+#pragma unroll
+      for (int j = 0; j < U; ++j)
+        if (u0 + j * kCommThreads < hi) w[j] = ld_v4(in + 16 * (u0 + j * kCommThreads));
+#pragma unroll
+      for (int j = 0; j < U; ++j)
+        if (u0 + j * kCommThreads < hi) multimem_st16(dst + 16 * (u0 + j * kCommThreads), w[j]);
+    }
+  }
+  if (ok) ok = nvls_barrier(a, a.epoch + 2);
+  if (ok) {
+    uint8_t* out = reinterpret_cast<uint8_t*>(a.out);
+    for (int s = 0; s < slots; ++s) {
+      if (kind == 1 && r == a.root) {
+        if (a.out != a.in) copy16(in, out, lo, hi);
+        break;
+      }
+      copy16(uc + s * a.n, out + s * a.n, lo, hi);
+    }
+  }
+  ring_end(a, ok);
+}
+
 __global__ void barrier_kernel(CommArgs a) {
   ring_begin(a);
   const bool ok = peer_barrier(a, a.epoch + 1);
@@ -984,6 +1329,11 @@ void gemm_fused(int fuse, torch::Tensor a, torch::Tensor b, torch::Tensor out, b
                 c10::optional<torch::Tensor> resid, int64_t epi, torch::Tensor status, const PeerCtx& ctx,
                 uint32_t* ag_base, c10::optional<torch::Tensor> stamps);
 
+// FSDP weight all-gather fused with the GEMM that consumes it; gemm.cu.
+void gemm_agw(torch::Tensor x, torch::Tensor flat, int64_t w_off, int64_t N, c10::optional<torch::Tensor> bias,
+              torch::Tensor out, const std::vector<const void*>& shards, int64_t shard, torch::Tensor counters,
+              torch::Tensor status, const PeerCtx& ctx, uint32_t* ag_base);
+
 struct Segment {
   void* local = nullptr;
   int64_t bytes = 0;
@@ -1022,6 +1372,9 @@ class DeviceCommImpl {
     closed_ = true;
     c10::cuda::CUDAGuard g(device_);
     cudaDeviceSynchronize();
+    for (auto& o : nvls_) o->release();  // the Python layer synchronised every rank first
+    nvls_.clear();
+    nvls_staging_ = -1;
     for (auto& s : segs_) {
       for (int r = 0; r < world_; ++r)
         if (r != rank_ && s.opened && s.peers[r]) cudaIpcCloseMemHandle(s.peers[r]);
@@ -1243,6 +1596,25 @@ class DeviceCommImpl {
     }
   }
 
+  // FSDP: out = x @ W^T (+ bias) with W = rows [0, N) of the weight at
+  // w_off in the unit's flat parameter buffer, gathering that buffer from
+  // every rank's shard (a symmetric tensor) into `flat` in the same launch.
+  void gemm_agw(torch::Tensor x, torch::Tensor shard, torch::Tensor flat, int64_t w_off, int64_t N,
+                c10::optional<torch::Tensor> bias, torch::Tensor out, torch::Tensor status) {
+    c10::cuda::CUDAGuard g(device_);
+    TORCH_CHECK(shard.is_contiguous() && shard.scalar_type() == at::kBFloat16, "shard: contiguous bf16");
+    const int64_t n = shard.numel();
+    auto loc = locate(shard.data_ptr(), n * 2);
+    TORCH_CHECK(loc.first >= 0, "the shard must be a symmetric tensor of this communicator");
+    std::vector<const void*> shards(world_);
+    for (int r = 0; r < world_; ++r)
+      shards[r] = static_cast<const uint8_t*>(segs_[loc.first].peers[r]) + loc.second;
+    if (!agw_cnt_.defined())
+      agw_cnt_ = torch::zeros({kMaxRanks * 16 + 1}, torch::TensorOptions().dtype(torch::kInt).device(torch::kCUDA, device_));
+    CommArgs a = base_args(staging_, 0, x.data_ptr(), out.data_ptr(), n * world_, 10, n * world_ * 2, 1);
+    mnb::gemm_agw(x, flat, w_off, N, bias, out, shards, n, agw_cnt_, status, peer_ctx(a), &ag_base_);
+  }
+
   // shard of sum_r(grad_r) * scale fed straight into AdamW on this rank's shard
   void reduce_scatter_adamw(torch::Tensor grad, torch::Tensor param, c10::optional<torch::Tensor> master,
                             torch::Tensor m, torch::Tensor v, double lr, double b1, double b2, double eps, double wd,
@@ -1457,6 +1829,199 @@ class DeviceCommImpl {
 #undef MNB_ST
   }
 
+
+  // ---- NVLS multicast objects (collective set-up driven from Python) --------
+  std::string nvls_reason() const { return nvls_unsupported_reason(device_); }
+  int nvls_create(int64_t bytes) {
+    c10::cuda::CUDAGuard g(device_);
+    nvls_.push_back(std::make_unique<NvlsObject>(rank_, world_, device_, bytes));
+    return static_cast<int>(nvls_.size()) - 1;
+  }
+  py::bytes nvls_socket_name(int id) { return py::bytes(nvls_.at(id)->socket_name()); }
+  void nvls_exchange(int id, std::vector<std::string> names, double timeout_s) {
+    c10::cuda::CUDAGuard g(device_);
+    nvls_.at(id)->exchange(names, timeout_s);
+  }
+  void nvls_bind(int id) {
+    c10::cuda::CUDAGuard g(device_);
+    nvls_.at(id)->bind_and_map();
+  }
+  // Every rank's kernels on the object must have finished (the caller
+  // synchronises all ranks first).
+  void nvls_release(int id) {
+    c10::cuda::CUDAGuard g(device_);
+    cudaDeviceSynchronize();
+    nvls_.at(id)->release();
+    if (nvls_staging_ == id) nvls_staging_ = -1;
+  }
+  int64_t nvls_bytes(int id) { return nvls_.at(id)->bytes(); }
+  void set_nvls_staging(int id) {
+    TORCH_CHECK(id >= 0 && id < static_cast<int>(nvls_.size()) && nvls_[id]->mapped(), "bad NVLS staging object");
+    nvls_staging_ = id;
+  }
+  torch::Tensor nvls_tensor(int id, int64_t numel, at::ScalarType dtype) {
+    const NvlsObject& o = *nvls_.at(id);
+    TORCH_CHECK(o.mapped(), "NVLS object not mapped");
+    TORCH_CHECK(numel * static_cast<int64_t>(c10::elementSize(dtype)) <= o.bytes(), "NVLS object too small");
+    auto opts = torch::TensorOptions().dtype(dtype).device(torch::kCUDA, device_);
+    return torch::from_blob(o.uc(), {numel}, [](void*) {}, opts);
+  }
+  std::pair<int, int64_t> locate_nvls(const void* p, int64_t bytes) const {
+    const auto a = reinterpret_cast<uintptr_t>(p);
+    for (size_t i = 0; i < nvls_.size(); ++i) {
+      if (!nvls_[i]->mapped()) continue;
+      const auto b = reinterpret_cast<uintptr_t>(nvls_[i]->uc());
+      if (a >= b && a + bytes <= b + nvls_[i]->bytes()) return {static_cast<int>(i), static_cast<int64_t>(a - b)};
+    }
+    return {-1, 0};
+  }
+  bool is_nvls(torch::Tensor t) {
+    return locate_nvls(t.data_ptr(), (t.numel() * t.element_size() + 15) / 16 * 16).first >= 0;
+  }
+
+  struct NvlsRegion {
+    char* uc;
+    char* mc;
+    bool staged;
+  };
+  // The call's region: the tensor itself when it lives (16-byte aligned) in an
+  // NVLS object and in-place use is allowed, else this call's parity half of
+  // the NVLS staging object.
+  NvlsRegion nvls_region(const CommArgs& a, const void* p, int64_t bytes, int64_t need, bool in_place_ok) {
+    if (in_place_ok) {
+      auto loc = locate_nvls(p, bytes);
+      if (loc.first >= 0 && loc.second % 16 == 0) {
+        const NvlsObject& o = *nvls_[loc.first];
+        return {static_cast<char*>(o.uc()) + loc.second, static_cast<char*>(o.mc()) + loc.second, false};
+      }
+    }
+    TORCH_CHECK(nvls_staging_ >= 0, "NVLS staging buffer not set up");
+    const NvlsObject& o = *nvls_[nvls_staging_];
+    const int64_t half = (o.bytes() / 2) / 256 * 256;
+    TORCH_CHECK(need <= half, "NVLS staging buffer too small for this message");
+    const int64_t off = static_cast<int64_t>(a.seq & 1) * half;
+    return {static_cast<char*>(o.uc()) + off, static_cast<char*>(o.mc()) + off, true};
+  }
+  int64_t nvls_staging_half() const {
+    return nvls_staging_ < 0 ? 0 : (nvls_[nvls_staging_]->bytes() / 2) / 256 * 256;
+  }
+
+  // Sum all-reduce through the switch.  max_blocks < 0: 128-thread CTAs that
+  // fit beside a persistent GEMM / attention CTA (all-reduces overlapped with
+  // compute); every rank must pass the same value.
+  void nvls_all_reduce(torch::Tensor in, torch::Tensor out, double scale, int max_blocks) {
+    const bool beside = max_blocks < 0;
+    if (beside) max_blocks = -max_blocks;
+    c10::cuda::CUDAGuard g(device_);
+    TORCH_CHECK(in.is_contiguous() && out.is_contiguous() && in.numel() == out.numel(), "contiguous, same size");
+    const auto dt = in.scalar_type();
+    TORCH_CHECK(dt == at::kFloat || dt == at::kBFloat16 || dt == at::kHalf, "NVLS all-reduce: fp32, bf16 or fp16");
+    const int64_t n = in.numel();
+    const int64_t bytes = (n * in.element_size() + 15) / 16 * 16;
+    CommArgs a = base_args(staging_, 0, in.data_ptr(), out.data_ptr(), n, 0, n * in.element_size(), 2);
+    a.scale = static_cast<float>(scale);
+    const NvlsRegion rg = nvls_region(a, in.data_ptr(), bytes, bytes, in.data_ptr() == out.data_ptr());
+    auto stream = at::cuda::getCurrentCUDAStream();
+    const int staged = rg.staged ? 1 : 0;
+    if (beside) {
+      const int nb = blocks_for(bytes / world_, max_blocks, 16 << 10);
+      if (dt == at::kFloat) nvls_all_reduce_kernel<float, 128, 6><<<nb, 128, 0, stream>>>(a, rg.uc, rg.mc, staged);
+      else if (dt == at::kBFloat16)
+        nvls_all_reduce_kernel<__nv_bfloat16, 128, 6><<<nb, 128, 0, stream>>>(a, rg.uc, rg.mc, staged);
+      else nvls_all_reduce_kernel<__half, 128, 6><<<nb, 128, 0, stream>>>(a, rg.uc, rg.mc, staged);
+    } else {
+      const int nb = blocks_for(bytes / world_, max_blocks);
+      if (dt == at::kFloat)
+        nvls_all_reduce_kernel<float, kCommThreads, 1><<<nb, kCommThreads, 0, stream>>>(a, rg.uc, rg.mc, staged);
+      else if (dt == at::kBFloat16)
+        nvls_all_reduce_kernel<__nv_bfloat16, kCommThreads, 1><<<nb, kCommThreads, 0, stream>>>(a, rg.uc, rg.mc,
+                                                                                                staged);
+      else nvls_all_reduce_kernel<__half, kCommThreads, 1><<<nb, kCommThreads, 0, stream>>>(a, rg.uc, rg.mc, staged);
+    }
+    C10_CUDA_KERNEL_LAUNCH_CHECK();
+  }
+
+  void nvls_reduce_scatter(torch::Tensor in, torch::Tensor out, double scale, int max_blocks) {
+    c10::cuda::CUDAGuard g(device_);
+    TORCH_CHECK(in.is_contiguous() && out.is_contiguous(), "contiguous tensors required");
+    const auto dt = in.scalar_type();
+    TORCH_CHECK(dt == at::kFloat || dt == at::kBFloat16 || dt == at::kHalf, "NVLS reduce-scatter: fp32, bf16 or fp16");
+    const int64_t chunk = out.numel();
+    TORCH_CHECK(in.numel() == chunk * world_ && (chunk * in.element_size()) % 16 == 0,
+                "NVLS reduce-scatter: W chunks of a 16-byte multiple");
+    const int64_t bytes = in.numel() * in.element_size();
+    CommArgs a = base_args(staging_, 0, in.data_ptr(), out.data_ptr(), chunk, 1, bytes, 2);
+    a.scale = static_cast<float>(scale);
+    const NvlsRegion rg = nvls_region(a, in.data_ptr(), bytes, bytes, true);
+    const int nb = blocks_for(bytes / world_, max_blocks);
+    auto stream = at::cuda::getCurrentCUDAStream();
+    const int staged = rg.staged ? 1 : 0;
+    if (dt == at::kFloat) nvls_reduce_scatter_kernel<float><<<nb, kCommThreads, 0, stream>>>(a, rg.uc, rg.mc, staged);
+    else if (dt == at::kBFloat16)
+      nvls_reduce_scatter_kernel<__nv_bfloat16><<<nb, kCommThreads, 0, stream>>>(a, rg.uc, rg.mc, staged);
+    else nvls_reduce_scatter_kernel<__half><<<nb, kCommThreads, 0, stream>>>(a, rg.uc, rg.mc, staged);
+    C10_CUDA_KERNEL_LAUNCH_CHECK();
+  }
+
+  // kind 0 all-gather (in = shard, out = W shards), 1 broadcast from `root`.
+  void nvls_move(torch::Tensor in, torch::Tensor out, int kind, int root, int max_blocks) {
+    c10::cuda::CUDAGuard g(device_);
+    TORCH_CHECK(in.is_contiguous() && out.is_contiguous(), "contiguous tensors required");
+    const int64_t nb = in.numel() * in.element_size();
+    TORCH_CHECK(nb % 16 == 0, "NVLS all-gather / broadcast: a 16-byte multiple per rank");
+    const int64_t need = kind == 0 ? nb * world_ : nb;
+    TORCH_CHECK(out.numel() * out.element_size() == need, "output size does not match");
+    CommArgs a = base_args(staging_, 0, in.data_ptr(), out.data_ptr(), nb, 2 + kind, need, 2);
+    a.root = root;
+    const NvlsRegion rg = nvls_region(a, nullptr, 0, need, false);
+    const int blocks = blocks_for(nb, max_blocks);
+    nvls_move_kernel<<<blocks, kCommThreads, 0, at::cuda::getCurrentCUDAStream()>>>(a, rg.uc, rg.mc, kind);
+    C10_CUDA_KERNEL_LAUNCH_CHECK();
+  }
+
+  void nvls_rs_adamw(torch::Tensor grad, torch::Tensor param, c10::optional<torch::Tensor> master, torch::Tensor m,
+                     torch::Tensor v, double lr, double b1, double b2, double eps, double wd, double bc1, double bc2,
+                     double scale, int max_blocks) {
+    c10::cuda::CUDAGuard g(device_);
+    TORCH_CHECK(grad.is_contiguous() && param.is_contiguous(), "contiguous grad and param shard");
+    const int64_t n = grad.numel();
+    const int64_t chunk = n / world_;
+    TORCH_CHECK(n % world_ == 0 && (chunk * grad.element_size()) % 16 == 0, "NVLS: chunks of a 16-byte multiple");
+    TORCH_CHECK(param.numel() == chunk && m.numel() == chunk && v.numel() == chunk, "shard sizes disagree");
+    const auto gt = grad.scalar_type(), pt = param.scalar_type();
+    TORCH_CHECK(gt == at::kBFloat16 || gt == at::kFloat, "gradient must be bf16 or fp32");
+    TORCH_CHECK(pt == at::kBFloat16 || pt == at::kFloat, "parameters must be bf16 or fp32");
+    const int64_t bytes = n * grad.element_size();
+    CommArgs a = base_args(staging_, 0, grad.data_ptr(), param.data_ptr(), chunk, 9, bytes, 2);
+    a.scale = static_cast<float>(scale);
+    AdamArgs o{};
+    if (master) o.master = master->data_ptr<float>();
+    o.m = m.data_ptr<float>();
+    o.v = v.data_ptr<float>();
+    o.param = param.data_ptr();
+    o.lr = static_cast<float>(lr);
+    o.b1 = static_cast<float>(b1);
+    o.b2 = static_cast<float>(b2);
+    o.eps = static_cast<float>(eps);
+    o.wd = static_cast<float>(wd);
+    o.c1 = static_cast<float>(1.0 / bc1);
+    o.c2 = static_cast<float>(1.0 / bc2);
+    const NvlsRegion rg = nvls_region(a, grad.data_ptr(), bytes, bytes, true);
+    const int blocks = blocks_for(bytes / world_, max_blocks);
+    auto stream = at::cuda::getCurrentCUDAStream();
+    const int staged = rg.staged ? 1 : 0;
+    if (gt == at::kBFloat16) {
+      if (pt == at::kBFloat16)
+        nvls_rs_adamw_kernel<__nv_bfloat16, true><<<blocks, kCommThreads, 0, stream>>>(a, o, rg.uc, rg.mc, staged);
+      else nvls_rs_adamw_kernel<__nv_bfloat16, false><<<blocks, kCommThreads, 0, stream>>>(a, o, rg.uc, rg.mc, staged);
+    } else {
+      if (pt == at::kBFloat16)
+        nvls_rs_adamw_kernel<float, true><<<blocks, kCommThreads, 0, stream>>>(a, o, rg.uc, rg.mc, staged);
+      else nvls_rs_adamw_kernel<float, false><<<blocks, kCommThreads, 0, stream>>>(a, o, rg.uc, rg.mc, staged);
+    }
+    C10_CUDA_KERNEL_LAUNCH_CHECK();
+  }
+
   int rank() const { return rank_; }
   int world() const { return world_; }
 
@@ -1477,6 +2042,9 @@ class DeviceCommImpl {
   uint32_t seq_ = 0;
   unsigned long long timeout_ns_ = 300ull * 1000000000ull;
   bool closed_ = false;
+  std::vector<std::unique_ptr<NvlsObject>> nvls_;
+  int nvls_staging_ = -1;
+  torch::Tensor agw_cnt_;  // chunk counters of the FSDP gather-GEMM (zeroed per launch)
 };
 
 void register_comm(py::module_& m) {
@@ -1507,6 +2075,22 @@ void register_comm(py::module_& m) {
       .def("gemm_rs", &DeviceCommImpl::gemm_rs)
       .def("reduce_scatter_adamw", &DeviceCommImpl::reduce_scatter_adamw)
       .def("ag_gemm", &DeviceCommImpl::ag_gemm)
+      .def("gemm_agw", &DeviceCommImpl::gemm_agw)
+      .def("nvls_reason", &DeviceCommImpl::nvls_reason)
+      .def("nvls_create", &DeviceCommImpl::nvls_create)
+      .def("nvls_socket_name", &DeviceCommImpl::nvls_socket_name)
+      .def("nvls_exchange", &DeviceCommImpl::nvls_exchange)
+      .def("nvls_bind", &DeviceCommImpl::nvls_bind)
+      .def("nvls_release", &DeviceCommImpl::nvls_release)
+      .def("nvls_bytes", &DeviceCommImpl::nvls_bytes)
+      .def("set_nvls_staging", &DeviceCommImpl::set_nvls_staging)
+      .def("nvls_staging_half", &DeviceCommImpl::nvls_staging_half)
+      .def("nvls_tensor", &DeviceCommImpl::nvls_tensor)
+      .def("is_nvls", &DeviceCommImpl::is_nvls)
+      .def("nvls_all_reduce", &DeviceCommImpl::nvls_all_reduce)
+      .def("nvls_reduce_scatter", &DeviceCommImpl::nvls_reduce_scatter)
+      .def("nvls_move", &DeviceCommImpl::nvls_move)
+      .def("nvls_rs_adamw", &DeviceCommImpl::nvls_rs_adamw)
       .def("close", &DeviceCommImpl::close)
       .def_property_readonly("rank", &DeviceCommImpl::rank)
       .def_property_readonly("world", &DeviceCommImpl::world);

@@ -16,11 +16,24 @@ Replaces the reference's pinned-host staging path (mini_nccl/device.py:
    mapped.  DDP buckets and FSDP shards live there, so their collectives are
    zero-copy (the two-shot all-reduce runs in place on the bucket).
 
+4. **NVLS (NVLink SHARP)**, where the GPUs and the driver support multicast
+   objects: at set-up the ranks build a multicast object over NVSwitch (rank
+   0 creates it and hands it to the others as a file descriptor over a Unix
+   socket; each rank binds its own memory), and sum reductions run as
+   ``multimem.ld_reduce`` (the switch adds every rank's copy and returns the
+   sum) plus ``multimem.st`` (one store reaches every rank).  A tensor made by
+   :meth:`symmetric_zeros` with ``nvls=True`` (DDP's buckets) is reduced in
+   place; other tensors go through an NVLS staging buffer.
+
 Algorithm names: ``auto`` picks ``one_shot`` for small messages (one round of
-peer reads; lowest latency) and ``two_shot`` (reduce-scatter + all-gather;
-bandwidth-optimal) above :data:`ONE_SHOT_MAX_BYTES`.  ``ring``, ``tree``,
-``halving`` and ``naive`` run the reference's schedules step by step over
-peer memory (for parity and the narrow-wire precision study).
+peer stores; lowest latency), ``nvls`` for sum reductions of fp32 / bf16 /
+fp16 from :data:`NVLS_MIN_BYTES` on (and always for tensors that live in NVLS
+memory), and ``two_shot`` (reduce-scatter + all-gather by peer stores) for
+the rest above :data:`ONE_SHOT_MAX_BYTES`.  ``ring``, ``tree``, ``halving``
+and ``naive`` run the reference's schedules step by step over peer memory
+(for parity and the narrow-wire precision study).  The cut-over sizes come
+from the measured sweep in ``results/`` (``benchmarks/bench_collectives.py``)
+and can be overridden by environment variables.
 
 A kernel that waits past the op timeout records the stuck peer in a
 host-mapped status block; :meth:`check` turns that into
@@ -46,10 +59,24 @@ STAGING_BYTES = int(os.environ.get("MINI_NCCL_STAGING_BYTES", 64 << 20))
 MAX_BLOCKS = int(os.environ.get("MINI_NCCL_DEVICE_BLOCKS", 255))
 #: CTAs (128 threads each) of an all-reduce run beside compute: one per SM.
 BESIDE_BLOCKS = int(os.environ.get("MINI_NCCL_BESIDE_BLOCKS", 148))
+#: NVLS collectives on (where the hardware and driver support them).
+NVLS_ENABLED = os.environ.get("MINI_NCCL_NVLS", "1") != "0"
+#: From this many bytes on ``auto`` sends sum reductions through the switch.
+NVLS_MIN_BYTES = int(os.environ.get("MINI_NCCL_NVLS_MIN_BYTES", 1 << 20))
+#: CTAs an NVLS collective may use (each multimem access is one 16-byte request
+#: the switch serves, so far fewer CTAs than the peer kernels need).
+NVLS_BLOCKS = int(os.environ.get("MINI_NCCL_NVLS_BLOCKS", 64))
+#: CTAs (128 threads) of an NVLS all-reduce that runs beside compute.
+NVLS_BESIDE_BLOCKS = int(os.environ.get("MINI_NCCL_NVLS_BESIDE_BLOCKS", 64))
+#: Initial NVLS staging buffer per rank (grows on demand, collectively).
+NVLS_STAGING_BYTES = int(os.environ.get("MINI_NCCL_NVLS_STAGING_BYTES", 64 << 20))
+#: Seconds the multicast set-up waits for a peer (socket hand-off).
+NVLS_SETUP_TIMEOUT = float(os.environ.get("MINI_NCCL_NVLS_SETUP_TIMEOUT", 60.0))
+_NVLS_DTYPES = (torch.float32, torch.bfloat16, torch.float16)
 
 _OPS = {"sum": 0, "prod": 1, "max": 2, "min": 3}
 OPNAMES = ["all_reduce", "reduce_scatter", "all_gather", "broadcast", "all_to_all", "barrier", "all_reduce_stepped",
-           "gemm_reduce_scatter", "all_gather_gemm", "reduce_scatter_adamw"]
+           "gemm_reduce_scatter", "all_gather_gemm", "reduce_scatter_adamw", "gather_weight_gemm"]
 
 
 def _ext():
@@ -82,6 +109,13 @@ class DeviceComm:
             self.impl.open_signals(self._all_gather_bytes(bytes(self.impl.signal_handle())))
             self._open(self.impl.staging_segment())
         self.staging_bytes = self.impl.segment_bytes(self.impl.staging_segment())
+        #: Whether NVLS collectives are available; :attr:`nvls_reason` says why not.
+        self.nvls = False
+        self.nvls_reason = "disabled (MINI_NCCL_NVLS=0)" if not NVLS_ENABLED else "single rank"
+        self._nvls_objects: list[int] = []
+        self._nvls_staging = -1
+        if self.world_size > 1 and NVLS_ENABLED:
+            self._init_nvls()
         self._schedules: dict[tuple, torch.Tensor] = {}
         self._last_issued: torch.cuda.Event | None = None
         self._nvtx_open: list[bool] = []
@@ -107,15 +141,88 @@ class DeviceComm:
             self._open(seg)
         return seg
 
-    def symmetric_zeros(self, numel: int, dtype: torch.dtype) -> torch.Tensor:
+    def symmetric_zeros(self, numel: int, dtype: torch.dtype, nvls: bool = False) -> torch.Tensor:
         """A zeroed tensor every peer has mapped (collective: same size on all ranks).
 
-        The memory belongs to this communicator and stays valid until
-        :meth:`close`.
+        ``nvls=True`` puts it in memory bound to an NVLS multicast object
+        (when NVLS is available), so sum all-reduces on it run in place
+        through the switch; otherwise peers map it through CUDA IPC.  The
+        memory belongs to this communicator and stays valid until :meth:`close`.
         """
         nbytes = max(16, numel * torch.empty(0, dtype=dtype).element_size())
+        if nvls and self.nvls:
+            oid = self._nvls_new((nbytes + 255) // 256 * 256)
+            return self.impl.nvls_tensor(oid, numel, dtype)
         seg = self._new_segment((nbytes + 255) // 256 * 256)
         return self.impl.segment_tensor(seg, numel, dtype)
+
+    # ---- NVLS multicast objects -------------------------------------------------------
+
+    def _agree(self, ok: bool) -> bool:
+        """True when every rank passes True (a host collective, so also a barrier)."""
+        return all(f == b"\x01" for f in self._all_gather_bytes(b"\x01" if ok else b"\x00"))
+
+    def _nvls_new(self, nbytes: int) -> int:
+        """Build one multicast object over every rank (collective).
+
+        Each step ends with every rank agreeing that it worked, so a failure
+        on one rank leaves every rank releasing its part and raising."""
+        oid, err = None, ""
+        try:
+            oid = self.impl.nvls_create(int(nbytes))
+        except RuntimeError as exc:
+            err = str(exc)
+        steps = (
+            lambda: self.impl.nvls_exchange(oid, [bytes(n).decode() for n in self._all_gather_bytes(
+                bytes(self.impl.nvls_socket_name(oid)) if oid is not None else b"")], NVLS_SETUP_TIMEOUT),
+            lambda: self.impl.nvls_bind(oid),
+        )
+        if self._agree(oid is not None):
+            for step in steps:
+                ok = True
+                try:
+                    step()
+                except RuntimeError as exc:
+                    ok, err = False, str(exc)
+                if not self._agree(ok):
+                    break
+            else:
+                self._nvls_objects.append(oid)
+                return oid
+        if oid is not None:
+            self.impl.nvls_release(oid)
+        raise DeviceCommError(f"rank {self.rank}: NVLS set-up failed: {err or 'a peer failed'}")
+
+    def _init_nvls(self) -> None:
+        reasons = [bytes(r).decode() for r in self._all_gather_bytes(self.impl.nvls_reason().encode())]
+        bad = [f"rank {r}: {why}" for r, why in enumerate(reasons) if why]
+        if bad:
+            self.nvls_reason = "; ".join(bad)
+            return
+        try:
+            self._nvls_staging = self._nvls_new(2 * NVLS_STAGING_BYTES)
+        except DeviceCommError as exc:
+            self.nvls_reason = str(exc)
+            return
+        self.impl.set_nvls_staging(self._nvls_staging)
+        self.nvls = True
+        self.nvls_reason = ""
+
+    def _ensure_nvls_staging(self, nbytes: int) -> None:
+        """Grow the NVLS staging buffer (collectively: every rank makes the same call)."""
+        if nbytes <= self.impl.nvls_staging_half():
+            return
+        size = 2 * max(nbytes, 2 * self.impl.nvls_staging_half())
+        torch.cuda.synchronize(self.device)
+        self._agree(True)  # nobody still runs a kernel on the old buffer
+        old = self._nvls_staging
+        self._nvls_staging = self._nvls_new(size)
+        self.impl.set_nvls_staging(self._nvls_staging)
+        self.impl.nvls_release(old)
+        self._nvls_objects.remove(old)
+
+    def _nvls_sum_ok(self, tensor: torch.Tensor, op: str) -> bool:
+        return self.nvls and op == "sum" and tensor.dtype in _NVLS_DTYPES
 
     def scratch_zeros(self, numel: int, dtype: torch.dtype) -> torch.Tensor:
         """A zeroed tensor inside the staging buffer's tail is not safe to hand out
@@ -222,10 +329,6 @@ class DeviceComm:
                 tensor.mul_(scale)
             return tensor
         nbytes = tensor.numel() * tensor.element_size()
-        if algorithm == "auto":
-            algorithm = "one_shot" if nbytes <= ONE_SHOT_MAX_BYTES else "two_shot"
-        if algorithm == "halving" and (self.world_size & (self.world_size - 1)):
-            algorithm = "ring"
         wire_bf16 = 0
         if wire_dtype is not None:
             if wire_dtype.itemsize > tensor.element_size():
@@ -233,10 +336,27 @@ class DeviceComm:
             if wire_dtype not in (torch.bfloat16, tensor.dtype):
                 raise ValueError("the device wire type must be bfloat16")
             wire_bf16 = int(wire_dtype == torch.bfloat16)
+        # the switch reads the tensor's own type: a narrower wire needs the peer kernels
+        nvls_ok = self._nvls_sum_ok(tensor, op) and not (wire_bf16 and tensor.dtype != torch.bfloat16)
+        if algorithm == "auto":
+            if nvls_ok and (nbytes >= NVLS_MIN_BYTES or self.impl.is_nvls(tensor)):
+                algorithm = "nvls"
+            else:
+                algorithm = "one_shot" if nbytes <= ONE_SHOT_MAX_BYTES else "two_shot"
+        if algorithm == "nvls" and not nvls_ok:
+            raise ValueError(f"nvls all-reduce needs NVLS ({self.nvls_reason or 'available'}), op='sum', "
+                             f"an fp32 / bf16 / fp16 tensor and no narrower wire type")
+        if algorithm == "halving" and (self.world_size & (self.world_size - 1)):
+            algorithm = "ring"
         ev = self._record("all_reduce", algorithm, nbytes, op=op,
                           wire=str(wire_dtype) if wire_dtype else "native")
         try:
-            if algorithm in ("one_shot", "two_shot"):
+            if algorithm == "nvls":
+                if not self.impl.is_nvls(tensor):
+                    self._ensure_nvls_staging((nbytes + 15) // 16 * 16)
+                nb = blocks or (NVLS_BESIDE_BLOCKS if beside_compute else NVLS_BLOCKS)
+                self.impl.nvls_all_reduce(tensor, tensor, float(scale), -nb if beside_compute else nb)
+            elif algorithm in ("one_shot", "two_shot"):
                 wire_bf16 = wire_bf16 if tensor.dtype == torch.float32 else 0
                 wsz = 2 if wire_bf16 else tensor.element_size()
                 kind = 1 if algorithm == "two_shot" else 0
@@ -256,7 +376,9 @@ class DeviceComm:
         return tensor
 
     def reduce_scatter(self, flat: torch.Tensor, op: str = "sum", scale: float = 1.0,
-                       blocks: int | None = None) -> torch.Tensor:
+                       blocks: int | None = None, algorithm: str = "auto") -> torch.Tensor:
+        """This rank's chunk of the sum (op) over ranks; ``algorithm``: ``auto``,
+        ``nvls`` (through the switch) or ``direct`` (peer stores)."""
         W = self.world_size
         if flat.numel() % W:
             raise ValueError(f"numel {flat.numel()} not divisible by world_size {W}")
@@ -265,10 +387,19 @@ class DeviceComm:
             out.copy_(flat)
             return out.mul_(scale) if scale != 1.0 else out
         nbytes = flat.numel() * flat.element_size()
-        self._ensure_staging(self.impl.staging_need(2, flat.numel(), flat.element_size()))
-        ev = self._record("reduce_scatter", "direct", nbytes, op=op)
+        nvls = _pick(algorithm, self._nvls_sum_ok(flat, op) and (out.numel() * out.element_size()) % 16 == 0,
+                     nbytes >= NVLS_MIN_BYTES or self.impl.is_nvls(flat), "reduce_scatter")
+        if nvls:
+            if not self.impl.is_nvls(flat):
+                self._ensure_nvls_staging(nbytes)
+        else:
+            self._ensure_staging(self.impl.staging_need(2, flat.numel(), flat.element_size()))
+        ev = self._record("reduce_scatter", "nvls" if nvls else "direct", nbytes, op=op)
         try:
-            self.impl.reduce_scatter(flat, out, _OPS[op], float(scale), blocks or MAX_BLOCKS)
+            if nvls:
+                self.impl.nvls_reduce_scatter(flat, out, float(scale), blocks or NVLS_BLOCKS)
+            else:
+                self.impl.reduce_scatter(flat, out, _OPS[op], float(scale), blocks or MAX_BLOCKS)
         finally:
             self._finish(ev)
         return out
@@ -288,17 +419,27 @@ class DeviceComm:
         if flat_grad.numel() % W:
             raise ValueError(f"gradient length {flat_grad.numel()} not divisible by world_size {W}")
         b1, b2 = betas
-        self._ensure_staging(self.impl.staging_need(2, flat_grad.numel(), flat_grad.element_size()))
-        ev = self._record("reduce_scatter_adamw", "fused", flat_grad.numel() * flat_grad.element_size())
+        nbytes = flat_grad.numel() * flat_grad.element_size()
+        nvls = (self._nvls_sum_ok(flat_grad, "sum") and flat_grad.dtype != torch.float16
+                and (nbytes // W) % 16 == 0 and (nbytes >= NVLS_MIN_BYTES or self.impl.is_nvls(flat_grad)))
+        if nvls:
+            if not self.impl.is_nvls(flat_grad):
+                self._ensure_nvls_staging(nbytes)
+        else:
+            self._ensure_staging(self.impl.staging_need(2, flat_grad.numel(), flat_grad.element_size()))
+        ev = self._record("reduce_scatter_adamw", "nvls" if nvls else "fused", nbytes)
+        args = (flat_grad, param_shard, state.get("master"), state["m"], state["v"], float(lr), float(b1), float(b2),
+                float(eps), float(weight_decay), 1.0 - b1 ** step, 1.0 - b2 ** step, float(scale))
         try:
-            self.impl.reduce_scatter_adamw(flat_grad, param_shard, state.get("master"), state["m"], state["v"],
-                                           float(lr), float(b1), float(b2), float(eps), float(weight_decay),
-                                           1.0 - b1 ** step, 1.0 - b2 ** step, float(scale), blocks or MAX_BLOCKS)
+            if nvls:
+                self.impl.nvls_rs_adamw(*args, blocks or NVLS_BLOCKS)
+            else:
+                self.impl.reduce_scatter_adamw(*args, blocks or MAX_BLOCKS)
         finally:
             self._finish(ev)
 
     def all_gather(self, shard: torch.Tensor, out: torch.Tensor | None = None,
-                   blocks: int | None = None) -> torch.Tensor:
+                   blocks: int | None = None, algorithm: str = "auto") -> torch.Tensor:
         W = self.world_size
         if out is None:
             out = torch.empty((W, shard.numel()), dtype=shard.dtype, device=shard.device)
@@ -306,22 +447,36 @@ class DeviceComm:
             out.view(-1).copy_(shard.reshape(-1))
             return out
         nbytes = shard.numel() * shard.element_size()
-        self._ensure_staging(self.impl.staging_need(3, nbytes, 1))
-        ev = self._record("all_gather", "direct", nbytes)
+        nvls = _pick(algorithm, self.nvls and nbytes % 16 == 0, nbytes * W >= NVLS_MIN_BYTES, "all_gather")
+        if nvls:
+            self._ensure_nvls_staging(nbytes * W)
+        else:
+            self._ensure_staging(self.impl.staging_need(3, nbytes, 1))
+        ev = self._record("all_gather", "nvls" if nvls else "direct", nbytes)
         try:
-            self.impl.move(shard.contiguous(), out, 0, 0, blocks or MAX_BLOCKS)
+            if nvls:
+                self.impl.nvls_move(shard.contiguous(), out, 0, 0, blocks or NVLS_BLOCKS)
+            else:
+                self.impl.move(shard.contiguous(), out, 0, 0, blocks or MAX_BLOCKS)
         finally:
             self._finish(ev)
         return out
 
-    def broadcast(self, tensor: torch.Tensor, src: int = 0) -> torch.Tensor:
+    def broadcast(self, tensor: torch.Tensor, src: int = 0, algorithm: str = "auto") -> torch.Tensor:
         if self.world_size == 1:
             return tensor
         nbytes = tensor.numel() * tensor.element_size()
-        self._ensure_staging(self.impl.staging_need(4, nbytes, 1))
-        ev = self._record("broadcast", "direct", nbytes, root=src)
+        nvls = _pick(algorithm, self.nvls and nbytes % 16 == 0, nbytes >= NVLS_MIN_BYTES, "broadcast")
+        if nvls:
+            self._ensure_nvls_staging(nbytes)
+        else:
+            self._ensure_staging(self.impl.staging_need(4, nbytes, 1))
+        ev = self._record("broadcast", "nvls" if nvls else "direct", nbytes, root=src)
         try:
-            self.impl.move(tensor, tensor, 1, int(src), MAX_BLOCKS)
+            if nvls:
+                self.impl.nvls_move(tensor, tensor, 1, int(src), NVLS_BLOCKS)
+            else:
+                self.impl.move(tensor, tensor, 1, int(src), MAX_BLOCKS)
         finally:
             self._finish(ev)
         return tensor
@@ -440,6 +595,33 @@ class DeviceComm:
             self._finish(ev)
         return out, gathered
 
+    def gather_weight_gemm(self, x: torch.Tensor, shard: torch.Tensor, flat: torch.Tensor, w_off: int, n_rows: int,
+                           bias: torch.Tensor | None = None) -> torch.Tensor:
+        """FSDP's first GEMM fused with the all-gather of its parameters, as one kernel.
+
+        ``shard`` is this rank's shard (a :meth:`symmetric_zeros` tensor) of a
+        flattened parameter buffer of ``world * shard.numel()`` elements;
+        ``flat`` (local, that many elements) receives the whole gathered
+        buffer.  Returns ``x @ W^T (+ bias)`` for the ``[n_rows, K]`` weight at
+        element offset ``w_off`` of the buffer.  Inside the kernel two warps
+        per CTA copy the buffer in from every rank's shard -- this weight's
+        chunks first -- and each output tile starts as soon as the chunks
+        holding its weight rows have arrived, so the gather runs under the
+        MMAs (the reference materialises the buffer with ``torch.cat`` before
+        the unit runs: mini_nccl/fsdp.py:113-127).
+        """
+        from .ops import kernels as K
+
+        x2 = x.reshape(-1, x.shape[-1])
+        out = torch.empty(x2.shape[0], n_rows, dtype=torch.bfloat16, device=x.device)
+        ev = self._record("gather_weight_gemm", "fused", shard.numel() * shard.element_size() * self.world_size)
+        try:
+            self.impl.gemm_agw(x2.contiguous(), shard, flat, int(w_off), int(n_rows), bias, out,
+                               K.status_word(x.device))
+        finally:
+            self._finish(ev)
+        return out
+
     # ---- parity schedules -------------------------------------------------------------
 
     def _schedule(self, algorithm: str, n: int) -> torch.Tensor:
@@ -454,9 +636,35 @@ class DeviceComm:
         return hit
 
     def close(self) -> None:
+        """Free the communicator's memory (collective when NVLS objects exist).
+
+        A rank that unbinds its memory from a multicast object while a peer's
+        kernel still reads through the switch faults that peer, so with NVLS
+        every rank first finishes its work and the ranks meet on the host."""
         if not self._closed:
             self._closed = True
+            if self._nvls_objects:
+                torch.cuda.synchronize(self.device)
+                try:
+                    self._agree(True)
+                except Exception:  # the host communicator is gone: release anyway
+                    pass
             self.impl.close()
+
+
+def _pick(algorithm: str, eligible: bool, preferred: bool, op: str) -> bool:
+    """Whether a collective goes through the switch: ``auto`` when it can and
+    the size favours it; ``nvls`` / ``direct`` force one path."""
+    if algorithm == "auto":
+        return eligible and preferred
+    if algorithm == "direct":
+        return False
+    if algorithm == "nvls":
+        if not eligible:
+            raise ValueError(f"{op}: the NVLS path needs NVLS, a 16-byte-multiple message (and for reductions "
+                             f"op='sum' on fp32 / bf16 / fp16)")
+        return True
+    raise ValueError(f"unknown {op} algorithm {algorithm!r}; expected auto, nvls or direct")
 
 
 def _split_bounds(n: int, parts: int) -> list[int]:

@@ -12,8 +12,10 @@ suppresses communication for gradient accumulation; ``sync()`` waits.
 Two engines:
 
 * **CUDA parameters.**  Bucket buffers are allocated in the group's
-  *symmetric* device memory, so the all-reduce kernel reads every peer's
-  bucket over NVLink with no copy-in.  There is no communication thread: the
+  *symmetric* device memory -- bound to an NVLS multicast object where the
+  GPUs support it, so the switch sums the ranks' buckets in place
+  (``multimem.ld_reduce`` / ``multimem.st``), else mapped by every peer, so
+  the two-shot kernel stores into them over NVLink -- with no copy-in.  There is no communication thread: the
   hook that completes bucket ``i`` records a CUDA event on the compute stream,
   the communication stream waits on it and the fused all-reduce kernel (sum in
   fp32, ``1/W`` scale, bf16 or fp32 in and out) is launched there, while
@@ -43,6 +45,8 @@ DDP_COMM_BLOCKS = int(os.environ.get("MINI_NCCL_DDP_BLOCKS", "0"))
 #: Bucket all-reduces run as small CTAs that share SMs with the backward
 #: pass's persistent kernels instead of taking whole SMs from them.
 DDP_BESIDE_COMPUTE = os.environ.get("MINI_NCCL_DDP_BESIDE", "1") != "0"
+#: Buckets live in NVLS multicast memory where available (in-place switch reduction).
+DDP_NVLS = os.environ.get("MINI_NCCL_DDP_NVLS", "1") != "0"
 
 
 def average_gradients(pg: Communicator, params, algorithm: str = "ring") -> int:
@@ -145,6 +149,14 @@ class DistributedDataParallel(nn.Module):
         #: ``perf_counter_ns`` at which this iteration's first reduction was
         #: dispatched (None until then) -- lets tests check overlap mechanically.
         self.reduce_submitted_ns: int | None = None
+        #: Per-step timeline (CUDA): when an int64 CUDA tensor is set here, each
+        #: bucket's launch stamps ``%globaltimer`` into ``timeline[bucket.index]``
+        #: on the compute stream (the moment its last gradient is written) and
+        #: appends the device collective sequence number of its all-reduce to
+        #: ``timeline_seqs``; the device event ring holds that all-reduce's
+        #: start and end on the same clock (benchmarks/ddp_timeline.py).
+        self.timeline: torch.Tensor | None = None
+        self.timeline_seqs: list[int] = []
         params = [p for p in module.parameters()]
         self._cuda = bool(params) and params[0].is_cuda
 
@@ -190,7 +202,9 @@ class DistributedDataParallel(nn.Module):
         for i, ps in enumerate(groups):
             numel = sum(p.numel() for p in ps)
             if self._cuda:
-                buf = self.pg.device_comm().symmetric_zeros(numel, ps[0].dtype)
+                # NVLS memory when the GPUs have it: the bucket all-reduce then
+                # runs in place through the switch
+                buf = self.pg.device_comm().symmetric_zeros(numel, ps[0].dtype, nvls=DDP_NVLS)
             else:
                 buf = torch.zeros(numel, dtype=ps[0].dtype, device=ps[0].device)
             self._buckets.append(_Bucket(i, ps, buf))
@@ -217,6 +231,11 @@ class DistributedDataParallel(nn.Module):
         if self.reduce_submitted_ns is None:
             self.reduce_submitted_ns = time.perf_counter_ns()
         produced = torch.cuda.Event()
+        if self.timeline is not None:
+            from ..ops.kernels import ext
+
+            ext().stamp(self.timeline, bucket.index)
+            self.timeline_seqs.append(int(self._dc.impl.seq()))
         produced.record(torch.cuda.current_stream(bucket.buffer.device))
         ev = self.pg.recorder.start(
             f"ddp_bucket{bucket.index}", self.algorithm, channel=-1,

@@ -190,9 +190,149 @@ def _timeout(pg) -> str:
 
 @needs2
 def test_device_wait_times_out_without_hanging(monkeypatch):
+    # No multicast objects in a failure test: a rank that leaves while its
+    # memory is bound to one can fault the other GPUs.
     monkeypatch.setenv("NCCL_NVLS_ENABLE", "0")
+    monkeypatch.setenv("MINI_NCCL_NVLS", "0")
     results = run(_timeout, 2, devices="cuda", timeout=300.0, op_timeout=60.0)
     assert results[0] == "timeout", results
+
+
+def _nvls_battery(pg) -> str:
+    """Every NVLS collective against values each rank recomputes from seeds."""
+    dev = torch.device("cuda", torch.cuda.current_device())
+    W, r = pg.world_size, pg.rank
+    dc = pg.device_comm()
+    if not dc.nvls:
+        return "unavailable: " + dc.nvls_reason
+    tol = {torch.float32: 1e-5, torch.bfloat16: 2e-2, torch.float16: 2e-3}
+    for dtype in (torch.float32, torch.bfloat16, torch.float16):
+        for numel in (1, 3, 1000, 262_147, (3 << 20) + 5):
+            t = seeded(r, numel, dtype, dev)
+            dc.all_reduce(t, algorithm="nvls")
+            want = expected(W, numel, dtype, "sum", dev)
+            err = (t.double() - want).abs().max().item()
+            assert err <= tol[dtype] * (want.abs().max().item() + 1), (dtype, numel, err)
+            everyone = C.all_gather(pg, t)  # one reduction per element: identical bits everywhere
+            assert all(torch.equal(o, everyone[0]) for o in everyone), (dtype, numel)
+    # in place on NVLS memory (DDP's buckets), with the 1/W scale, both CTA shapes
+    n = (5 << 20) + 3
+    sym = dc.symmetric_zeros(n, torch.bfloat16, nvls=True)
+    assert dc.impl.is_nvls(sym)
+    want = expected(W, n, torch.bfloat16, "sum", dev) / W
+    for beside in (False, True):
+        sym.copy_(seeded(r, n, torch.bfloat16, dev))
+        dc.all_reduce(sym, scale=1.0 / W, beside_compute=beside)  # auto -> nvls
+        assert (sym.double() - want).abs().max().item() < 3e-2, beside
+    # reduce-scatter through the switch (input untouched, 1/W fused)
+    n = (1 << 20) * W
+    for dtype in (torch.float32, torch.bfloat16):
+        t = seeded(r, n, dtype, dev)
+        before = t.clone()
+        mine = dc.reduce_scatter(t, scale=1.0 / W)
+        want = expected(W, n, dtype, "sum", dev).view(W, -1)[r] / W
+        assert (mine.double() - want).abs().max().item() < tol[dtype] * 10, dtype
+        assert torch.equal(t, before)
+    # all-gather and broadcast by multimem stores
+    shard = seeded(r, 1 << 19, torch.bfloat16, dev)
+    got = dc.all_gather(shard)
+    for i in range(W):
+        assert torch.equal(got[i], seeded(i, 1 << 19, torch.bfloat16, dev)), i
+    for src in range(W):
+        t = seeded(r, 1 << 20, torch.float32, dev)
+        dc.broadcast(t, src=src)
+        assert torch.equal(t, seeded(src, 1 << 20, torch.float32, dev)), src
+    # reduce-scatter fused with AdamW, the summed gradient taken from the switch
+    n = (1 << 19) * W
+    grad = seeded(r, n, torch.bfloat16, dev)
+    w0 = seeded(100 + r, n // W, torch.float32, dev)
+    param = w0.to(torch.bfloat16)
+    state = {"m": torch.zeros(n // W, device=dev), "v": torch.zeros(n // W, device=dev), "master": w0.clone()}
+    lr, b1, b2, eps, wd = 1e-2, 0.9, 0.95, 1e-8, 0.1
+    dc.reduce_scatter_adamw(grad, param, state, lr=lr, betas=(b1, b2), eps=eps, weight_decay=wd, step=1,
+                            scale=1.0 / W)
+    g = (expected(W, n, torch.bfloat16, "sum", dev).view(W, -1)[r] / W).float()
+    m, v = (1 - b1) * g, (1 - b2) * g * g
+    w = w0 * (1 - lr * wd) - lr * (m / (1 - b1)) / ((v / (1 - b2)).sqrt() + eps)
+    assert (state["master"] - w).abs().max().item() < 1e-4
+    # a message larger than the staging buffer grows it (collectively)
+    big = seeded(r, 100 << 20, torch.bfloat16, dev)
+    C.all_reduce(pg, big)
+    want = expected(W, 100 << 20, torch.bfloat16, "sum", dev)
+    assert (big.double() - want).abs().max().item() < 0.1
+    dc.synchronize()
+    return "ok"
+
+
+@needs2
+def test_nvls_collectives_two_ranks():
+    out = run(_nvls_battery, 2, devices="cuda", timeout=600.0, op_timeout=60.0)
+    if out[0].startswith("unavailable"):
+        pytest.skip(out[0])
+    assert out == ["ok", "ok"], out
+
+
+def _gather_weight_gemm(pg) -> None:
+    """FSDP's fused gather + first GEMM == a plain all-gather followed by the GEMM."""
+    from mini_nccl_b200.ops import kernels as K
+
+    dev = torch.device("cuda", torch.cuda.current_device())
+    W, r = pg.world_size, pg.rank
+    dc = pg.device_comm()
+    for shard_n, w_off, N, Kd, M in ((40_000, 8, 384, 64, 300), (262_144, 4096, 1536, 256, 1024)):
+        shard = dc.symmetric_zeros(shard_n, torch.bfloat16)
+        shard.copy_(seeded(r, shard_n, torch.bfloat16, dev))
+        x = seeded(50 + r, M * Kd, torch.bfloat16, dev).view(M, Kd)
+        bias = seeded(77, N, torch.bfloat16, dev)
+        flat = torch.full((W * shard_n,), float("nan"), dtype=torch.bfloat16, device=dev)
+        for _ in range(2):  # twice: the chunk counters are reset per launch
+            out = dc.gather_weight_gemm(x, shard, flat, w_off, N, bias=bias)
+        dc.synchronize()
+        want_flat = torch.cat([seeded(i, shard_n, torch.bfloat16, dev) for i in range(W)])
+        assert torch.equal(flat, want_flat)
+        w = want_flat[w_off : w_off + N * Kd].view(N, Kd)
+        ref = K.gemm(x, w, bias=bias)
+        assert torch.equal(out, ref), (out.float() - ref.float()).abs().max().item()
+
+
+@needs2
+def test_fsdp_gather_weight_gemm_two_ranks():
+    run(_gather_weight_gemm, 2, devices="cuda", timeout=300.0, op_timeout=60.0)
+
+
+def _fsdp_fused_vs_plain(pg) -> None:
+    from mini_nccl_b200.fsdp import FullyShardedDataParallel
+    from mini_nccl_b200.models.gpt import GPT, Block
+
+    dev = torch.device("cuda", torch.cuda.current_device())
+    states = []
+    for fused in (False, True):
+        torch.manual_seed(0)
+        model = GPT(vocab_size=512, block_size=256, n_layer=2, n_head=4, n_embd=256).to(dev, torch.bfloat16)
+        fsdp = FullyShardedDataParallel(model, pg, unit_cls=Block, recompute=False, fuse_gather_gemm=fused)
+        opt = torch.optim.SGD(fsdp.parameters(), lr=0.5)
+        g = torch.Generator().manual_seed(5 + pg.rank)
+        losses = []
+        for _ in range(2):
+            idx = torch.randint(0, 512, (4, 256), generator=g).to(dev)
+            tgt = torch.randint(0, 512, (4, 256), generator=g).to(dev)
+            fsdp.zero_grad()
+            _, loss = fsdp(idx, tgt)
+            loss.backward()
+            fsdp.sync()
+            opt.step()
+            losses.append(float(loss))
+        states.append((losses, {k: v.float() for k, v in fsdp.full_state_dict().items()}))
+    (l0, s0), (l1, s1) = states
+    assert abs(l0[0] - l1[0]) < 1e-3 and abs(l0[1] - l1[1]) < 2e-2, (l0, l1)
+    for name, v in s0.items():
+        err = (v - s1[name]).abs().max().item()
+        assert err <= 2e-2 * (v.abs().max().item() + 1e-3), (name, err)
+
+
+@needs2
+def test_fsdp_fused_gather_trains_like_plain_gather():
+    run(_fsdp_fused_vs_plain, 2, devices="cuda", timeout=600.0, op_timeout=60.0)
 
 
 def _host_staged(pg) -> None:
@@ -344,3 +484,96 @@ needs4 = pytest.mark.skipif(n_gpus() < 4, reason="needs at least 4 GPUs")
 def test_device_collective_battery_four_ranks():
     """W=4 reaches the scatter + all-gather broadcast and 4-way push schedules."""
     run(_battery, 4, devices="cuda", timeout=900.0, op_timeout=60.0)
+
+
+needs8 = pytest.mark.skipif(n_gpus() < 8, reason="needs 8 GPUs")
+
+
+@needs8
+def test_device_collective_battery_eight_ranks():
+    """The whole battery on one 8-GPU NVSwitch box (every schedule, W=8)."""
+    run(_battery, 8, devices="cuda", timeout=1200.0, op_timeout=60.0)
+
+
+@needs8
+def test_nvls_collectives_eight_ranks():
+    out = run(_nvls_battery, 8, devices="cuda", timeout=900.0, op_timeout=60.0)
+    if out[0].startswith("unavailable"):
+        pytest.skip(out[0])
+    assert all(o == "ok" for o in out), out
+
+
+@needs8
+def test_fused_gemm_collectives_eight_ranks():
+    run(_fused_tp, 8, timeout=900.0, devices="cuda", op_timeout=60.0)
+
+
+@needs8
+def test_fsdp_fused_gather_eight_ranks():
+    run(_fsdp_fused_vs_plain, 8, devices="cuda", timeout=900.0, op_timeout=60.0)
+
+
+def _gpt_3d_gpu(pg) -> None:
+    """The 3D configuration's model (fused sequence-parallel TP kernels, 1F1B over
+    NCCL p2p, DP replicas) on 8 GPUs against one fp32 CPU process, same weights."""
+    import types
+
+    import mini_nccl_b200 as mn
+    from mini_nccl_b200.models.tp_gpt import GPTStage, sync_tensor_parallel_grads
+
+    dev = torch.device("cuda", torch.cuda.current_device())
+    V, T, L, H, Cw = 512, 128, 2, 4, 256
+    mesh = mn.ParallelMesh(pg, dp=2, pp=2, tp=2)
+    dp, pp, tp = mesh.group("dp"), mesh.group("pp"), mesh.group("tp")
+    d, s = mesh.coordinate("dp"), mesh.coordinate("pp")
+    torch.manual_seed(123)
+    solo = types.SimpleNamespace(world_size=1, rank=0)
+    ref = GPTStage(V, T, L, H, Cw, solo, 0, 1, sequence_parallel=False)
+    stage = GPTStage(V, T, L, H, Cw, tp, s, 2, sequence_parallel=True)
+    per = L // 2
+    with torch.no_grad():
+        if s == 0:
+            stage.tok_emb.weight.copy_(ref.tok_emb.weight)
+            stage.pos_emb.copy_(ref.pos_emb)
+        else:
+            stage.ln_f.load_state_dict(ref.ln_f.state_dict())
+            stage.head.weight.copy_(ref.head.weight)
+        for j, blk in enumerate(stage.blocks):
+            rb = ref.blocks[s * per + j]
+            blk.ln1.load_state_dict(rb.ln1.state_dict())
+            blk.ln2.load_state_dict(rb.ln2.state_dict())
+            blk.attn.qkv.load_full_weight(rb.attn.qkv.weight, rb.attn.qkv.bias)
+            blk.attn.proj.load_full_weight(rb.attn.proj.weight, rb.attn.proj.bias)
+            blk.mlp.up.load_full_weight(rb.mlp.up.weight, rb.mlp.up.bias)
+            blk.mlp.down.load_full_weight(rb.mlp.down.weight, rb.mlp.down.bias)
+    stage = stage.to(dev, torch.bfloat16)
+    g = torch.Generator().manual_seed(7)
+    idx = torch.randint(0, V, (8, T), generator=g)  # 2 replicas x 2 microbatches x 2 sequences
+    tgt = torch.randint(0, V, (8, T), generator=g)
+    ref.loss(ref(idx), tgt).backward()
+    pipe = mn.PipelineParallel(stage, pp, activation_shape=(T // 2, 2, Cw),
+                               loss_fn=stage.loss if s == 1 else None, dtype=torch.bfloat16, device=dev)
+    mine = slice(4 * d, 4 * d + 4)
+    pipe.step(idx[mine].to(dev) if s == 0 else None, tgt[mine].to(dev) if s == 1 else None, n_microbatches=2)
+    sync_tensor_parallel_grads(stage, tp)
+    mn.average_gradients(dp, list(stage.parameters()))
+
+    def check(got, want, what):
+        got, want = got.float().cpu(), want.float()
+        err = (got - want).abs().max().item()
+        assert err <= 0.08 * want.abs().max().item() + 1e-4, (what, err, want.abs().max().item())
+
+    for j, blk in enumerate(stage.blocks):
+        rb = ref.blocks[s * per + j]
+        check(blk.ln1.weight.grad, rb.ln1.weight.grad, f"block{j}.ln1")
+        a, n = blk.mlp.up.shard_start, blk.mlp.up.shard_size
+        check(blk.mlp.up.weight.grad, rb.mlp.up.weight.grad[a: a + n], f"block{j}.mlp.up")
+        rows = blk.attn.qkv.shard_rows.cpu()
+        check(blk.attn.qkv.weight.grad, rb.attn.qkv.weight.grad.index_select(0, rows), f"block{j}.qkv")
+    if s == 1:
+        check(stage.head.weight.grad, ref.head.weight.grad, "head")
+
+
+@needs8
+def test_gpt_3d_fused_tp_matches_single_process_on_eight_gpus():
+    run(_gpt_3d_gpu, 8, devices="cuda", timeout=900.0, op_timeout=120.0)
