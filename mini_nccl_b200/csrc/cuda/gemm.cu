@@ -45,6 +45,20 @@
 //            Tiles of the own rows come first, so the exchange runs under
 //            them; every remote row crosses NVLink once and the TMA unit only
 //            reads local memory.
+//   kFuseAGW all-gather of the weight -> GEMM (FSDP).  B is a weight inside
+//            a flattened parameter buffer that every rank holds one shard of.
+//            Two extra warps per CTA first meet every other rank's CTAs (so
+//            no shard is read before its owner has entered the collective),
+//            then claim parts of chunks from one work counter -- the chunks
+//            that hold this GEMM's weight first, in row order, then the rest
+//            of the buffer -- and copy them from the owner's shard (peer
+//            loads) into the local gathered buffer, counting every copied part
+//            on its chunk.  The TMA producer waits only for the chunks that
+//            hold the B rows of its tile, so the first tiles start after the
+//            first chunks arrive and the rest of the gather runs under the
+//            MMAs.  When the launch ends the whole buffer is gathered (the
+//            unit's later GEMMs read it).  Parts are claimed dynamically, so
+//            progress never depends on one particular CTA being resident.
 #include <ATen/cuda/CUDAContext.h>
 #include <c10/cuda/CUDAGuard.h>
 #include <cudaTypedefs.h>
@@ -89,9 +103,20 @@ struct GemmArgs {
   uint32_t rs_target;               // RS: counter value meaning "every CTA of that rank has stored its tiles"
   int ag_own_map;                   // AG: own rows are read through map_own from the input (rows % 128 == 0)
   unsigned long long* stamps;       // optional %globaltimer phase stamps (CTA 0 / slowest CTA), or null
+  // kFuseAGW: B = rows of a weight inside the gathered flat parameter buffer
+  const __nv_bfloat16* agw_src[kMaxRanks];  // every rank's shard (peer addresses; own = local)
+  __nv_bfloat16* agw_flat;                  // local gathered buffer [world * agw_shard]
+  long long agw_shard;                      // shard elements (multiple of 8)
+  long long agw_chunk;                      // chunk elements (multiple of 8)
+  long long agw_w_off;                      // flat offset of B's row 0 (B is [N, K], row stride K)
+  long long agw_bias_off;                   // flat offset of the bias, or -1
+  int agw_nch;                              // chunks per shard
+  int agw_parts;                            // parts per chunk (the unit of claimed work)
+  int agw_pri_first, agw_pri_last;          // chunk range holding B (and its bias): gathered first
+  uint32_t* agw_cnt;                        // [world * nch] per-chunk part counts, then the work counter
 };
 
-enum : int { kFuseNone = 0, kFuseRS = 1, kFuseAG = 2 };
+enum : int { kFuseNone = 0, kFuseRS = 1, kFuseAG = 2, kFuseAGW = 3 };
 
 constexpr int kBM = 128;
 constexpr int kBK = 64;
@@ -99,7 +124,7 @@ constexpr int kEpiWarps = 8;  // two warps per TMEM lane quadrant, each owning h
 constexpr int kGemmThreads = 64 + 32 * kEpiWarps;
 constexpr int kGatherThreads = 64;  // kFuseAG: two gather warps after the epilogue warps
 template <int FUSE>
-constexpr int gemm_threads() { return kGemmThreads + (FUSE == kFuseAG ? kGatherThreads : 0); }
+constexpr int gemm_threads() { return kGemmThreads + ((FUSE == kFuseAG || FUSE == kFuseAGW) ? kGatherThreads : 0); }
 
 MNB_DEVICE uint32_t ld_acquire_gpu(const int* p) {
   uint32_t v;
@@ -110,12 +135,18 @@ MNB_DEVICE void red_release_gpu_add(int* p, int v) {
   asm volatile("red.release.gpu.global.add.s32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
 MNB_DEVICE void fence_proxy_async_global() { asm volatile("fence.proxy.async.global;" ::: "memory"); }
+// 16-byte load that bypasses L1 (another GPU's memory, rewritten between launches).
+MNB_DEVICE uint4 ld_v4_cg_peer(const void* p) {
+  uint4 v;
+  asm volatile("ld.global.cg.v4.u32 {%0,%1,%2,%3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "l"(p));
+  return v;
+}
 
 // Output tile visiting order.  RS: start with the next rank's rows and end
 // with our own (their transfer is local); AG: our own rows first (no wait).
 template <int FUSE>
 MNB_DEVICE int remap_mblock(int mb, int m_tiles, const GemmArgs& a, const PeerCtx& ctx) {
-  if constexpr (FUSE == kFuseNone) {
+  if constexpr (FUSE == kFuseNone || FUSE == kFuseAGW) {
     return mb;
   } else {
     if (a.rows_per_rank % kBM != 0) return mb;
@@ -443,6 +474,98 @@ MNB_DEVICE void push_shard(const GemmArgs& a, const PeerCtx& ctx, int gt) {
   }
 }
 
+
+// ---- kFuseAGW ---------------------------------------------------------------
+// Order in which chunks are gathered: the chunks holding B first, in flat
+// (= weight row) order, then the chunks before them, then those after them.
+MNB_DEVICE int agw_chunk_at(const GemmArgs& a, int o) {
+  const int n_pri = a.agw_pri_last - a.agw_pri_first + 1;
+  if (o < n_pri) return a.agw_pri_first + o;
+  const int q = o - n_pri;
+  return q < a.agw_pri_first ? q : q + n_pri;
+}
+
+MNB_DEVICE int agw_chunk_of(const GemmArgs& a, long long f) {
+  const int s = static_cast<int>(f / a.agw_shard);
+  return s * a.agw_nch + static_cast<int>((f - s * a.agw_shard) / a.agw_chunk);
+}
+
+// Producer side: wait until every chunk overlapping flat elements [f0, f1) is
+// gathered.  Bounded; false on timeout or when another wait already failed.
+MNB_DEVICE bool agw_wait_range(const GemmArgs& a, const PeerCtx& ctx, long long f0, long long f1) {
+  if (f1 <= f0) return true;
+  const int g1 = agw_chunk_of(a, f1 - 1);
+  const uint64_t t0 = globaltimer_ns();
+  for (int g = agw_chunk_of(a, f0); g <= g1; ++g) {
+    const int* c = reinterpret_cast<const int*>(a.agw_cnt + g);
+    uint32_t spins = 0;
+    while (static_cast<int>(ld_acquire_gpu(c)) < a.agw_parts) {
+      if ((++spins & 255u) == 0) {
+        if (*reinterpret_cast<volatile int*>(a.status) != 0) return false;
+        if (globaltimer_ns() - t0 > ctx.timeout_ns) {
+          atomicCAS(a.status, 0, kErrPeerTimeout);
+          return false;
+        }
+        __nanosleep(128);
+      }
+    }
+  }
+  return true;
+}
+
+// Gather warps (64 threads).
+MNB_DEVICE void agw_gather(const GemmArgs& a, const PeerCtx& ctx, int gt) {
+  const int W = ctx.world, r = ctx.rank;
+  __shared__ int agw_flag;
+  if (gt == 0) {
+    // Meet every rank: its shard is final once it has entered this launch,
+    // and it is only written again after a later collective this rank joins.
+    __threadfence_system();
+    for (int k = 0; k < W; ++k) red_release_sys_add(ctx.sig[k] + kCountRow * kMaxRanks + r, 1u);
+    bool ok = true;
+    const uint64_t t0 = globaltimer_ns();
+    for (int p = 0; ok && p < W; ++p)
+      ok = wait_signal(ctx.sig[r] + kCountRow * kMaxRanks + p, a.ag_target, ctx.status, p, blockIdx.x, ctx.seq,
+                       ctx.timeout_ns, t0);
+    if (!ok) atomicCAS(a.status, 0, kErrPeerTimeout);
+    agw_flag = ok ? 1 : 0;
+  }
+  asm volatile("bar.sync 2, %0;" ::"n"(kGatherThreads) : "memory");
+  if (!agw_flag) return;
+  const int total = W * a.agw_nch;
+  const int claims = total * a.agw_parts;
+  for (;;) {
+    if (gt == 0) agw_flag = static_cast<int>(atomicAdd(a.agw_cnt + total, 1u));
+    asm volatile("bar.sync 2, %0;" ::"n"(kGatherThreads) : "memory");
+    const int w = agw_flag;
+    if (w >= claims) break;
+    const int g = agw_chunk_at(a, w / a.agw_parts), part = w % a.agw_parts;
+    const int src = g / a.agw_nch;
+    const long long c0 = static_cast<long long>(g % a.agw_nch) * a.agw_chunk;
+    const long long c1 = min(a.agw_shard, c0 + a.agw_chunk);
+    const long long units = c0 < c1 ? (c1 - c0) / 8 : 0;
+    const long long per = (units + a.agw_parts - 1) / a.agw_parts;
+    const long long lo = min(units, part * per), hi = min(units, lo + per);
+    const __nv_bfloat16* from = a.agw_src[src] + c0;
+    __nv_bfloat16* to = a.agw_flat + static_cast<long long>(src) * a.agw_shard + c0;
+    constexpr int U = 8;
+    for (long long u0 = lo + gt; u0 < hi; u0 += U * kGatherThreads) {
+      uint4 v[U];
+#pragma unroll
+      for (int j = 0; j < U; ++j)
+        if (u0 + j * kGatherThreads < hi) v[j] = ld_v4_cg_peer(from + 8 * (u0 + j * kGatherThreads));
+#pragma unroll
+      for (int j = 0; j < U; ++j)
+        if (u0 + j * kGatherThreads < hi) st_v4(to + 8 * (u0 + j * kGatherThreads), v[j]);
+    }
+    asm volatile("bar.sync 2, %0;" ::"n"(kGatherThreads) : "memory");  // part copied; agw_flag free again
+    if (gt == 0) {
+      __threadfence();
+      red_release_gpu_add(reinterpret_cast<int*>(a.agw_cnt + g), 1);
+    }
+  }
+}
+
 // kFuseRS tail (all threads): announce that this CTA's tiles have landed,
 // wait for every CTA of every rank, then reduce this rank's rows.
 MNB_DEVICE void rs_finish(const GemmArgs& a, const PeerCtx& ctx) {
@@ -591,6 +714,15 @@ __global__ void __launch_bounds__(gemm_threads<FUSE>(), 1)
           }
           fence_proxy_async_global();  // generic-proxy (peer) writes -> TMA reads
         }
+        if constexpr (FUSE == kFuseAGW) {
+          // B rows of this tile (and, before the first tile, the bias the
+          // epilogue reads) must have been gathered
+          if (u == static_cast<int>(blockIdx.x) && args.agw_bias_off >= 0)
+            ok = agw_wait_range(args, ctx, args.agw_bias_off, args.agw_bias_off + args.N);
+          const long long r0 = static_cast<long long>(nb) * BN, r1 = min(static_cast<long long>(args.N), r0 + BN);
+          if (ok) ok = agw_wait_range(args, ctx, args.agw_w_off + r0 * args.K, args.agw_w_off + r1 * args.K);
+          fence_proxy_async_global();  // generic-proxy writes of the gather warps -> TMA reads
+        }
         for (int kb = kb0; kb < kb1 && ok; ++kb) {
           if (!mbar_wait(empty0 + 8 * stage, phase ^ 1, status)) { ok = false; break; }
           const uint32_t full = full0 + 8 * stage;
@@ -684,6 +816,7 @@ __global__ void __launch_bounds__(gemm_threads<FUSE>(), 1)
         a.out = reinterpret_cast<float*>(args.out) + static_cast<long long>(split) * args.split_stride;
       const int row = mb * kBM + row_in_tile;
       const uint32_t lane_addr = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + acc * BN;
+      bool released = false;  // accumulator handed back early (TMA-store path)
       if (FUSE == kFuseRS) {
         // 32 rows x 64 columns at a time: registers -> swizzled smem box ->
         // 128-byte row segments stored into the owner's slot (a warp store
@@ -710,21 +843,30 @@ __global__ void __launch_bounds__(gemm_threads<FUSE>(), 1)
         uint8_t* box_out = staging + (warp - 2) * (S::boxes * 4096);
         uint8_t* box_aux = box_out + (S::boxes - 1) * 4096;  // == box_out with one box
         const bool gelu = (a.epi & kEpiGelu) != 0;
+        const int g_end = (half + 1) * (BN / 128);
 #pragma unroll 1
-        for (int g = half * (BN / 128); g < (half + 1) * (BN / 128); ++g) {
+        for (int g = half * (BN / 128); g < g_end; ++g) {
           const int colg = nb * BN + g * 64;
           if (colg >= a.N) break;
           // with two boxes and a single output, alternate them (double buffer)
           uint8_t* bo = (!gelu && S::boxes == 2 && (g & 1)) ? box_aux : box_out;
-          if (lane == 0) {
+          float v64[64];
+          tmem_ld_64(lane_addr + g * 64, v64);  // both 32-column halves, one wait
+          if (g + 1 == g_end || colg + 64 >= a.N) {
+            // this warp's last columns are in registers: hand the accumulator
+            // back to the MMA warp before the math and the stores
+            tc_fence_before();
+            mbar_arrive(tempty0 + 8 * acc);
+            released = true;
+          }
+          if (lane == 0) {  // the staging box is free once the previous store has read it
             if (gelu || S::boxes == 1) bulk_wait_read<0>();
             else bulk_wait_read<1>();
           }
           __syncwarp();
 #pragma unroll
           for (int sub = 0; sub < 2; ++sub) {
-            float v[32];
-            tmem_ld_32(lane_addr + g * 64 + sub * 32, v);
+            float* v = v64 + sub * 32;
             const int k = (g - half * (BN / 128)) * 2 + sub;  // warp-local chunk
             const int col0 = colg + sub * 32;
             if (fast && col0 + 32 <= a.N) {
@@ -760,13 +902,17 @@ __global__ void __launch_bounds__(gemm_threads<FUSE>(), 1)
           if (col0 < a.N) epilogue_store(a, row, col0, v);
         }
       }
-      tc_fence_before();
-      mbar_arrive(tempty0 + 8 * acc);
+      if (!released) {
+        tc_fence_before();
+        mbar_arrive(tempty0 + 8 * acc);
+      }
       acc ^= 1;
       if (acc == 0) acc_phase ^= 1;
     }
   } else if constexpr (FUSE == kFuseAG) {
     push_shard(args, ctx, threadIdx.x - kGemmThreads);
+  } else if constexpr (FUSE == kFuseAGW) {
+    agw_gather(args, ctx, threadIdx.x - kGemmThreads);
   }
 
   if (warp >= 2 && warp < 2 + kEpiWarps && lane == 0) bulk_wait_all();  // staging boxes drained before exit
@@ -1134,6 +1280,76 @@ void gemm_fused(int fuse, torch::Tensor a, torch::Tensor b, torch::Tensor out, b
   }
 #undef MNB_FUSED
   TORCH_CHECK(false, "unsupported fused GEMM configuration");
+}
+
+
+// FSDP: out [M, N] = x [M, K] @ B^T (+ bias), where B = rows [0, N) of a [N, K]
+// weight at element offset w_off of a flattened parameter buffer that the
+// ranks hold one shard each of (shards[p]: rank p's shard, `shard` elements).
+// The launch also gathers the whole buffer into `flat` (kFuseAGW above).
+// `counters`: uint32 [world * 16 + 1] of scratch (zeroed here).
+void gemm_agw(torch::Tensor x, torch::Tensor flat, int64_t w_off, int64_t N, c10::optional<torch::Tensor> bias,
+              torch::Tensor out, const std::vector<const void*>& shards, int64_t shard, torch::Tensor counters,
+              torch::Tensor status, const PeerCtx& ctx, uint32_t* ag_base) {
+  c10::cuda::CUDAGuard guard(x.device());
+  const int W = ctx.world;
+  TORCH_CHECK(static_cast<int>(shards.size()) == W, "one shard address per rank");
+  TORCH_CHECK(x.dim() == 2 && x.is_contiguous() && x.scalar_type() == at::kBFloat16, "x: contiguous bf16 [M, K]");
+  const int M = static_cast<int>(x.size(0)), K = static_cast<int>(x.size(1));
+  TORCH_CHECK(K % 8 == 0 && N % 8 == 0 && N > 0, "N and K must be multiples of 8");
+  TORCH_CHECK(shard % 8 == 0 && shard > 0, "shards must be a positive multiple of 8 elements");
+  TORCH_CHECK(flat.is_contiguous() && flat.scalar_type() == at::kBFloat16 && flat.numel() == shard * W,
+              "flat: contiguous bf16 [world * shard]");
+  TORCH_CHECK(w_off % 8 == 0 && w_off >= 0 && w_off + N * K <= shard * W, "the weight must lie in the buffer");
+  TORCH_CHECK(out.scalar_type() == at::kBFloat16 && out.size(0) == M && out.size(1) == N && out.stride(1) == 1 &&
+                  out.stride(0) % 8 == 0,
+              "out: bf16 [M, N] with 16-byte rows");
+  TORCH_CHECK(counters.scalar_type() == at::kInt && counters.numel() >= W * 16 + 1, "counters: int32 [world*16+1]");
+  GemmArgs args{};
+  args.M = M;
+  args.N = static_cast<int>(N);
+  args.K = K;
+  args.status = status.data_ptr<int>();
+  args.k_blocks_per_split = (K + kBK - 1) / kBK;
+  args.splits = 1;
+  args.out = out.data_ptr();
+  args.ldo = out.stride(0);
+  args.tma_out = 1;
+  args.epi = 0;
+  if (bias) {
+    TORCH_CHECK(bias->scalar_type() == at::kBFloat16 && bias->numel() == N && bias->is_contiguous(),
+                "bias must be bf16 [N]");
+    args.bias = reinterpret_cast<const __nv_bfloat16*>(bias->data_ptr());
+    args.epi |= kEpiBias;
+  }
+  for (int p = 0; p < W; ++p) args.agw_src[p] = static_cast<const __nv_bfloat16*>(shards[p]);
+  args.agw_flat = reinterpret_cast<__nv_bfloat16*>(flat.data_ptr());
+  args.agw_shard = shard;
+  const int64_t chunk = ((shard + 15) / 16 + 7) / 8 * 8;  // at most 16 chunks per shard
+  args.agw_chunk = chunk;
+  args.agw_nch = static_cast<int>((shard + chunk - 1) / chunk);
+  args.agw_parts = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(64, chunk * 2 / 8192)));
+  args.agw_w_off = w_off;
+  args.agw_bias_off = -1;  // the bias is an ordinary tensor here
+  auto chunk_of = [&](int64_t f) {
+    const int64_t s = f / shard;
+    return static_cast<int>(s * args.agw_nch + (f - s * shard) / chunk);
+  };
+  args.agw_pri_first = chunk_of(w_off);
+  args.agw_pri_last = chunk_of(w_off + N * K - 1);
+  args.agw_cnt = reinterpret_cast<uint32_t*>(counters.data_ptr());
+  cudaStream_t stream = at::cuda::getCurrentCUDAStream();
+  C10_CUDA_CHECK(cudaMemsetAsync(counters.data_ptr(), 0, (W * args.agw_nch + 1) * sizeof(uint32_t), stream));
+  const int BN = N >= 256 ? 256 : 128;
+  CUtensorMap ma = make_tma_2d_bf16(x.data_ptr(), K, M, K, 64, kBM);
+  CUtensorMap mb = make_tma_2d_bf16(args.agw_flat + w_off, K, static_cast<int>(N), K, 64, BN);
+  CUtensorMap mo = make_tma_2d_bf16(out.data_ptr(), static_cast<int>(N), M, out.stride(0), 64, 32);
+  const int units = ((M + kBM - 1) / kBM) * ((static_cast<int>(N) + BN - 1) / BN);
+  // one start signal per CTA of each rank (the kCountRow counters it shares with kFuseAG)
+  *ag_base += static_cast<uint32_t>(std::min(units, num_sms()));
+  args.ag_target = *ag_base;
+  if (BN == 256) launch_gemm<256, false, false, 4, kFuseAGW>(ma, mb, mo, mo, args, units, stream, ctx, &ma);
+  else launch_gemm<128, false, false, 4, kFuseAGW>(ma, mb, mo, mo, args, units, stream, ctx, &ma);
 }
 
 }  // namespace mnb

@@ -97,6 +97,32 @@ class Block(nn.Module):
         return K.MLP.apply(h, fc.weight, fc.bias, out.weight, out.bias, x)
 
 
+    # ---- FSDP: the QKV projection is the block's first GEMM over its parameters --------
+
+    def fsdp_forward_with_gathered_gemm(self, x: torch.Tensor, gather_gemm) -> torch.Tensor:
+        """The CUDA forward, with the QKV GEMM computed by ``gather_gemm``.
+
+        FullyShardedDataParallel(fuse_gather_gemm=True) passes a callable that
+        runs the QKV projection as one kernel with the all-gather of this
+        block's sharded parameters (its 1-D parameters -- LayerNorm scales and
+        biases, linear biases -- stay whole on every rank, so LayerNorm runs
+        before anything is gathered).  Every later GEMM reads the gathered
+        weights.
+        """
+        K = _kernels()
+        B, T, C = x.shape
+        h, x = K.LayerNormResidual.apply(x, self.ln1.weight, self.ln1.bias, self.ln1.eps)
+        qkv = K.GatheredLinear.apply(h, self.qkv.weight, self.qkv.bias, gather_gemm)
+        y = K.FlashAttention.apply(qkv, self.n_head)
+        x = K.Linear.apply(y.view(B, T, C), self.proj.weight, self.proj.bias, x)
+        h, x = K.LayerNormResidual.apply(x, self.ln2.weight, self.ln2.bias, self.ln2.eps)
+        fc, out = self.mlp[0], self.mlp[2]
+        return K.MLP.apply(h, fc.weight, fc.bias, out.weight, out.bias, x)
+
+    def fsdp_first_gemm(self) -> tuple[nn.Parameter, nn.Parameter]:
+        """(weight, bias) of the first GEMM ``fsdp_forward_with_gathered_gemm`` runs."""
+        return self.qkv.weight, self.qkv.bias
+
     def _forward_cuda_unfused(self, x: torch.Tensor) -> torch.Tensor:
         """Same block; autograd sums the residual and LayerNorm input gradients."""
         K = _kernels()

@@ -179,6 +179,31 @@ class Linear(torch.autograd.Function):
         return dx, dw, db, dr
 
 
+class GatheredLinear(torch.autograd.Function):
+    """``y = x W^T + b`` where computing it also gathers W's sharded parameter buffer.
+
+    ``gather_gemm(x2)`` runs the fused kernel (FSDP's first GEMM of a unit,
+    :meth:`DeviceComm.gather_weight_gemm`) and returns ``x2 W^T + b``; by the
+    time it returns (in stream order) ``weight`` -- a view into the gathered
+    buffer -- holds its values.  The backward is :class:`Linear`'s.
+    """
+
+    @staticmethod
+    def forward(ctx, x, weight, bias, gather_gemm):
+        x2 = _rows(x)
+        y = gather_gemm(x2)
+        ctx.save_for_backward(x2, weight)
+        ctx.has_bias = bias is not None
+        ctx.has_resid = False
+        ctx.x_shape = x.shape
+        return y.view(*x.shape[:-1], weight.shape[0])
+
+    @staticmethod
+    def backward(ctx, gy):
+        dx, dw, db, _ = Linear.backward(ctx, gy)
+        return dx, dw, db, None
+
+
 class LinearGelu(torch.autograd.Function):
     """``gelu(x W^T + b)``: GELU in the forward epilogue, GELU' in the backward one."""
 

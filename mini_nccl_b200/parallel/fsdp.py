@@ -27,6 +27,15 @@ valid; each unit's gradients are reduce-scattered as soon as all of them
 have accumulated.  Peak memory then holds activations rather than extra
 compute.
 
+``fuse_gather_gemm=True`` (with ``recompute=False``, on GPUs) gathers each
+unit's parameters inside its first GEMM: one kernel whose extra warps copy
+the unit's flat buffer in from every rank's shard -- the first GEMM's weight
+first -- while its MMAs start on the tiles whose weight rows have arrived
+(:meth:`DeviceComm.gather_weight_gemm`).  The unit provides the hook
+(``fsdp_first_gemm`` / ``fsdp_forward_with_gathered_gemm``, as the GPT block
+does); its 1-D parameters stay whole on every rank so that its LayerNorm can
+run before anything is gathered.
+
 ``optimizer_in_backward=dict(lr=..., betas=..., eps=..., weight_decay=...)``
 fuses the shard's AdamW step into the gradient reduce-scatter: on CUDA one
 kernel pushes every gradient chunk to its owner, sums the W slots in rank
@@ -54,7 +63,7 @@ _RELEASED = torch.empty(0)
 class _Unit:
     """One module whose parameters are sharded across ranks."""
 
-    def __init__(self, module: nn.Module, pg: Communicator, name: str) -> None:
+    def __init__(self, module: nn.Module, pg: Communicator, name: str, keep_vectors_whole: bool = False) -> None:
         self.module = module
         self.pg = pg
         self.name = name
@@ -65,7 +74,7 @@ class _Unit:
         seen: set[int] = set()
         for sub in module.modules():
             for attr, p in list(sub.named_parameters(recurse=False)):
-                if id(p) in seen:
+                if id(p) in seen or (keep_vectors_whole and p.dim() < 2):
                     continue
                 seen.add(id(p))
                 self.entries.append((sub, attr, p.shape, p.numel()))
@@ -158,17 +167,50 @@ class _Unit:
 
     # ---- no-recompute mode: activations saved, parameters resharded in between ----
 
+    def _offset_of(self, param: nn.Parameter) -> int:
+        at = 0
+        for p, (_, _, _, n) in zip(self.params, self.entries, strict=True):
+            if p is param:
+                return at
+            at += n
+        raise ValueError("the first GEMM's weight is not one of the unit's sharded parameters")
+
+    def fused_gather_ok(self, x: torch.Tensor) -> bool:
+        owner = self.owner
+        return (owner is not None and owner.fuse_gather_gemm and x.is_cuda and self.pg.world_size > 1
+                and self.dtype == torch.bfloat16 and hasattr(self.module, "fsdp_forward_with_gathered_gemm"))
+
+    def _forward_gathering_in_first_gemm(self, x: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
+        """Bind the parameters to a fresh buffer that the unit's first GEMM fills."""
+        flat = torch.empty(self.padded_numel, dtype=self.dtype, device=self.device)
+        self._bind(flat)  # views now; their values arrive inside the first GEMM's kernel
+        if self.owner is not None:
+            self.owner._note_materialized(self.full_bytes)
+        weight, bias = self.module.fsdp_first_gemm()
+        w_off = self._offset_of(weight)
+        dc = self.pg.device_comm()
+        shard = self.shard.detach()
+
+        def gather_gemm(x2: torch.Tensor) -> torch.Tensor:
+            return dc.gather_weight_gemm(x2, shard, flat, w_off, weight.shape[0], bias=bias)
+
+        return self.module.fsdp_forward_with_gathered_gemm(x, gather_gemm), flat
+
     def forward_saving_activations(self, x: torch.Tensor) -> torch.Tensor:
         """Forward with the autograd graph kept; the gathered parameters are freed
         right after it (their storage shrinks to 0 bytes) and gathered again into
-        the same storage just before this unit's backward runs."""
+        the same storage just before this unit's backward runs.  With
+        ``fuse_gather_gemm`` the gather happens inside the unit's first GEMM."""
         owner = self.owner
-        flat = owner._take_prefetched(self) if owner is not None else None
-        flat = self.materialize(self.shard, flat)
-        if owner is not None:
-            owner._prefetch_after(self)
         self._arm_grad_hooks()
-        y = self.module(x)
+        if self.fused_gather_ok(x):
+            y, flat = self._forward_gathering_in_first_gemm(x)
+        else:
+            flat = owner._take_prefetched(self) if owner is not None else None
+            flat = self.materialize(self.shard, flat)
+            if owner is not None:
+                owner._prefetch_after(self)
+            y = self.module(x)
         if self.pg.world_size > 1 or flat.untyped_storage().data_ptr() != self.shard.untyped_storage().data_ptr():
             nbytes = flat.untyped_storage().nbytes()
             flat.untyped_storage().resize_(0)
@@ -397,10 +439,17 @@ class FullyShardedDataParallel(nn.Module):
         prefetch: bool = False,
         optimizer_in_backward: dict | None = None,
         recompute: bool = True,
+        fuse_gather_gemm: bool = False,
     ) -> None:
         super().__init__()
         if unit_cls is None and units is None:
             raise ValueError("pass unit_cls or units to say what should be sharded")
+        if fuse_gather_gemm and recompute:
+            raise ValueError("fuse_gather_gemm needs recompute=False (activations kept)")
+        #: Gather each unit's parameters inside its first GEMM (one kernel;
+        #: units that provide ``fsdp_forward_with_gathered_gemm``).  Units then
+        #: keep their 1-D parameters whole on every rank (averaged in ``sync``).
+        self.fuse_gather_gemm = fuse_gather_gemm
         self.pg = pg
         self.shard_optimizer = ShardAdamW(**optimizer_in_backward) if optimizer_in_backward is not None else None
         self.recompute = recompute
@@ -426,7 +475,8 @@ class FullyShardedDataParallel(nn.Module):
                 hit = id(child) in chosen or (unit_cls is not None and isinstance(child, unit_cls))
                 if not hit or not any(True for _ in child.parameters()):
                     continue
-                unit = _Unit(child, pg, name=f"{type(child).__name__.lower()}{len(self.units)}")
+                unit = _Unit(child, pg, name=f"{type(child).__name__.lower()}{len(self.units)}",
+                             keep_vectors_whole=fuse_gather_gemm)
                 unit.owner = self
                 self.units.append(unit)
                 parent._modules[key] = _UnitWrapper(unit)
@@ -448,6 +498,8 @@ class FullyShardedDataParallel(nn.Module):
 
     def _prefetch_after(self, unit: _Unit) -> None:
         if not self.prefetch or unit.device.type != "cuda" or self.pg.world_size == 1:
+            return
+        if self.fuse_gather_gemm:  # the next unit gathers inside its own first GEMM
             return
         i = self._index[id(unit)] + 1
         if i >= len(self.units) or i in self._prefetched:
