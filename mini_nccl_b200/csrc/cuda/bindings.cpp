@@ -25,6 +25,7 @@ void xent_fwd_bwd(torch::Tensor logits, torch::Tensor targets, torch::Tensor los
                   int64_t ignore_index);
 void adamw_step(torch::Tensor table, torch::Tensor chunks, bool param_bf16, bool grad_bf16, double lr, double beta1,
                 double beta2, double eps, double wd, double bc1, double bc2, double grad_scale);
+void stamp(torch::Tensor out, int64_t idx);
 // attention.cu
 void flash_attn_fwd(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tensor o, torch::Tensor lse,
                     int64_t n_head, double scale);
@@ -36,6 +37,7 @@ void flash_attn_fwd_tc(torch::Tensor qkv, torch::Tensor o, torch::Tensor lse, in
                        torch::Tensor status);
 void flash_attn_bwd_tc(torch::Tensor qkv, torch::Tensor o, torch::Tensor dout, torch::Tensor lse, torch::Tensor dqkv,
                        torch::Tensor dq_acc, torch::Tensor delta, int64_t n_head, double scale, torch::Tensor status);
+void exp2_poly_eval(torch::Tensor x, torch::Tensor y);
 // comm.cu
 void register_comm(pybind11::module_& m);
 }  // namespace mnb
@@ -55,9 +57,11 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("embed_bwd", &mnb::embed_bwd);
   m.def("xent_fwd_bwd", &mnb::xent_fwd_bwd);
   m.def("adamw_step", &mnb::adamw_step);
+  m.def("stamp", &mnb::stamp, "write %globaltimer into out[idx] in stream order");
   m.def("flash_attn_fwd", &mnb::flash_attn_fwd);
   m.def("flash_attn_bwd", &mnb::flash_attn_bwd);
   m.def("flash_attn_fwd_tc", &mnb::flash_attn_fwd_tc, "tcgen05 flash attention forward");
   m.def("flash_attn_bwd_tc", &mnb::flash_attn_bwd_tc, "tcgen05 flash attention backward");
+  m.def("exp2_poly_eval", &mnb::exp2_poly_eval, "the attention softmax's FMA-pipe exp2, over a tensor");
   mnb::register_comm(m);
 }

@@ -1037,6 +1037,16 @@ void layernorm_fwd(torch::Tensor x, torch::Tensor w, torch::Tensor b, torch::Ten
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
+// A fold launch that fails leaves its accumulator in an unknown state (the
+// partial sums and arrival counter of blocks that ran); every later fold of
+// that size would carry them.  Clear it before reporting the error.
+static void check_fold_launch(const torch::Tensor& acc, int64_t n_values, cudaStream_t stream) {
+  const cudaError_t e = cudaGetLastError();
+  if (e == cudaSuccess) return;
+  cudaMemsetAsync(acc.data_ptr(), 0, static_cast<size_t>(n_values + 1) * sizeof(float), stream);
+  TORCH_CHECK(false, "column-sum fold launch failed (accumulator cleared): ", cudaGetErrorString(e));
+}
+
 int ln_bwd_blocks(int rows) { return std::max(1, std::min(148 * 2, (rows + kRowWarps - 1) / kRowWarps)); }
 
 static void layernorm_bwd_impl(torch::Tensor dy, torch::Tensor x, torch::Tensor w, torch::Tensor mean,
@@ -1097,7 +1107,7 @@ static void layernorm_bwd_impl(torch::Tensor dy, torch::Tensor x, torch::Tensor 
         reinterpret_cast<__nv_bfloat16*>(dx.data_ptr()), partials.data_ptr<float>(), rows, C, dw.data_ptr(),
         db.data_ptr(), f32 ? 1 : 0, accumulate ? 1 : 0);
   else launch(layernorm_bwd_kernel<0>);
-  C10_CUDA_KERNEL_LAUNCH_CHECK();
+  check_fold_launch(partials, 2LL * C, stream);
   const bool fused = add != nullptr && bulk && (C == 256 || C == 512 || C == 768 || C == 1024);
   if (add != nullptr && !fused) dx.add_(*add);
 }
@@ -1178,7 +1188,7 @@ void bias_grad(torch::Tensor g, torch::Tensor out, torch::Tensor partials, bool 
   colsum_fold_kernel<<<dim3((C + 255) / 256, yb), 256, 0, stream>>>(
       reinterpret_cast<const __nv_bfloat16*>(g.data_ptr()), partials.data_ptr<float>(), rows, C, out.data_ptr(),
       out.scalar_type() == at::kFloat ? 1 : 0, accumulate ? 1 : 0);
-  C10_CUDA_KERNEL_LAUNCH_CHECK();
+  check_fold_launch(partials, C, stream);
 }
 
 static int elementwise_blocks(long long n8) {
@@ -1280,6 +1290,25 @@ void adamw_step(torch::Tensor table, torch::Tensor chunks, bool param_bf16, bool
       n_chunks, param_bf16, grad_bf16, static_cast<float>(lr), static_cast<float>(beta1), static_cast<float>(beta2),
       static_cast<float>(eps), static_cast<float>(wd), static_cast<float>(bc1), static_cast<float>(bc2),
       static_cast<float>(grad_scale));
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+}  // namespace mnb
+
+namespace mnb {
+
+// One %globaltimer reading (ns) into out[idx], in stream order: places host-
+// side events (a DDP bucket becoming ready, the end of backward) on the same
+// clock as the device event ring's collective start / end stamps.
+__global__ void stamp_kernel(unsigned long long* out, int idx) {
+  if (threadIdx.x == 0) out[idx] = globaltimer_ns();
+}
+
+void stamp(torch::Tensor out, int64_t idx) {
+  TORCH_CHECK(out.is_cuda() && out.scalar_type() == at::kLong && idx >= 0 && idx < out.numel(),
+              "stamp: int64 CUDA tensor and an index inside it");
+  stamp_kernel<<<1, 32, 0, at::cuda::getCurrentCUDAStream()>>>(
+      reinterpret_cast<unsigned long long*>(out.data_ptr()), static_cast<int>(idx));
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 

@@ -189,6 +189,18 @@ def test_flash_attention(B, T, H, D):
     close(qkv.grad, ref_in.grad, 3e-2)
 
 
+def test_softmax_polynomial_exp2_against_exp2():
+    """The FMA-pipe exp2 of the attention softmax stays within bf16's half-ulp of exp2."""
+    x = torch.cat([torch.linspace(-126.0, 0.0, 1 << 20, device=DEV),
+                   -torch.rand(1 << 20, device=DEV) * 30.0, torch.tensor([0.0, -1.0, -0.5, -125.999], device=DEV)])
+    y = torch.empty_like(x)
+    K.ext().exp2_poly_eval(x, y)
+    want = torch.exp2(x.double())
+    rel = ((y.double() - want).abs() / want).max().item()
+    assert rel < 2.0 ** -9, rel
+    assert torch.all(y[-4:-2] == torch.tensor([1.0, 0.5], device=DEV))  # exact at integers
+
+
 def test_cross_entropy_and_fused_head():
     M, V, C = 512, 1000, 256
     logits = rnd(M, V, seed=23, scale=2.0).requires_grad_(True)
