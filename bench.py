@@ -94,6 +94,9 @@ def parse_args():
                     help="ddp: config 3 (default); fsdp: config 4; 3d: config 5 (N in 1, 2, 4, 8)")
     ap.add_argument("--micro-batch", type=int, default=None)
     ap.add_argument("--no-e2e", action="store_true", help="skip the end-to-end phase")
+    ap.add_argument("--fsdp-gather", choices=["fused", "prefetch"], default="fused",
+                    help="--mode fsdp: gather each block's parameters inside its first GEMM (fused) or "
+                         "with a separate all-gather prefetched on a side stream")
     return ap.parse_args()
 
 
@@ -367,8 +370,11 @@ def run_ours(args):
         # one unit per block; each block's AdamW runs inside its gradient reduce-scatter
         # activations saved (as torch FSDP2 does by default); parameters still freed after each
         # block's forward and gathered again for its backward
+        # fused: each block's parameter all-gather runs inside its QKV GEMM (one kernel);
+        # prefetch: a separate all-gather of the next block on a side stream
         ddp = mn.FullyShardedDataParallel(model, pg, unit_cls=Block, prefetch=True, recompute=False,
-                                          optimizer_in_backward=dict(hp, eps=1e-8))
+                                          optimizer_in_backward=dict(hp, eps=1e-8),
+                                          fuse_gather_gemm=args.fsdp_gather == "fused" and world > 1)
         shard_ids = {id(u.shard) for u in ddp.units}
         opt = FusedAdamW([p for p in ddp.parameters() if id(p) not in shard_ids], **hp)
     else:
@@ -535,10 +541,7 @@ def run_torch(args):
     import torch.distributed as dist
 
     if args.mode == "3d":
-        if env_rank()[0] == 0:
-            print(json.dumps({"impl": "torch", "unavailable": "no stock-torch tensor x pipeline parallel GPT is "
-                              "provided for config 5; compare against --impl ours with --mode ddp/fsdp arms"}))
-        return
+        return run_torch_3d(args)
 
     sys.path.insert(0, str(ROOT))
     from mini_nccl_b200.models.gpt import GPT
@@ -631,6 +634,251 @@ def run_torch(args):
     ms, e2e_ms, _ = run_phases(torch, args, step, barrier, reduce_max, dev, clocks, e2e_step)
     if rank == 0:
         emit(args, world, "torch", ms, e2e_ms, clocks, None)
+    if world > 1:
+        dist.destroy_process_group()
+
+
+
+def run_torch_3d(args):
+    """Config 5 on stock torch + NCCL: the Megatron-style baseline.
+
+    Same mesh, model shape, microbatching and optimizer as ``run_ours_3d``;
+    every op is stock PyTorch under bf16 autocast (cuBLAS GEMMs, SDPA flash
+    attention, fused AdamW) and every transfer is NCCL through
+    torch.distributed: tensor parallelism as Megatron's column / row split
+    with an all-reduce after each row-parallel GEMM (forward) and before each
+    column-parallel one (backward), 1F1B over NCCL send / recv on the pp
+    group, and a data-parallel all-reduce of the gradients after the
+    pipeline drains.
+    """
+    import torch
+    import torch.distributed as dist
+    import torch.nn.functional as F
+    from torch import nn
+
+    rank, world, local = env_rank()
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    dp, pp, tp = mesh_dims(world)
+    if world > 1:
+        dist.init_process_group("nccl", device_id=dev, timeout=timedelta(seconds=300))
+    # rank = (d * pp + s) * tp + t  (last dimension fastest, as ParallelMesh lays it out)
+    d, s, t = rank // (pp * tp), (rank // tp) % pp, rank % tp
+    groups = {}
+    if world > 1:
+        for name, members in (("tp", [[(dd * pp + ss) * tp + tt for tt in range(tp)] for dd in range(dp)
+                                      for ss in range(pp)]),
+                              ("pp", [[(dd * pp + ss) * tp + tt for ss in range(pp)] for dd in range(dp)
+                                      for tt in range(tp)]),
+                              ("dp", [[(dd * pp + ss) * tp + tt for dd in range(dp)] for ss in range(pp)
+                                      for tt in range(tp)])):
+            for m in members:
+                g = dist.new_group(m)  # every rank creates every group, in the same order
+                if rank in m:
+                    groups[name] = (g, m)
+
+    class ToTP(torch.autograd.Function):  # identity forward, all-reduce of the input gradient
+        @staticmethod
+        def forward(ctx, x):
+            return x
+
+        @staticmethod
+        def backward(ctx, g):
+            g = g.contiguous()
+            dist.all_reduce(g, group=groups["tp"][0])
+            return g
+
+    class FromTP(torch.autograd.Function):  # all-reduce of the partial sums, identity backward
+        @staticmethod
+        def forward(ctx, x):
+            x = x.contiguous()
+            dist.all_reduce(x, group=groups["tp"][0])
+            return x
+
+        @staticmethod
+        def backward(ctx, g):
+            return g
+
+    C, H = EMBD, HEADS
+    hl = H // tp  # heads on this rank
+
+    class TPBlock(nn.Module):
+        def __init__(self):
+            super().__init__()
+            self.ln1, self.ln2 = nn.LayerNorm(C), nn.LayerNorm(C)
+            self.qkv = nn.Linear(C, 3 * C // tp)           # column parallel: this rank's q, k, v heads
+            self.proj = nn.Linear(C // tp, C, bias=False)  # row parallel (bias added once, after the sum)
+            self.proj_b = nn.Parameter(torch.zeros(C))
+            self.fc1 = nn.Linear(C, 4 * C // tp)
+            self.fc2 = nn.Linear(4 * C // tp, C, bias=False)
+            self.fc2_b = nn.Parameter(torch.zeros(C))
+
+        def forward(self, h):  # h [B, T, C], replicated over the tp group
+            Bq, T, _ = h.shape
+            x = self.ln1(h)
+            if tp > 1:
+                x = ToTP.apply(x)
+            q, k, v = self.qkv(x).view(Bq, T, 3, hl, C // H).permute(2, 0, 3, 1, 4)
+            a = F.scaled_dot_product_attention(q, k, v, is_causal=True).transpose(1, 2).reshape(Bq, T, C // tp)
+            y = self.proj(a)
+            h = h + (FromTP.apply(y) if tp > 1 else y) + self.proj_b
+            x = self.ln2(h)
+            if tp > 1:
+                x = ToTP.apply(x)
+            y = self.fc2(F.gelu(self.fc1(x)))
+            return h + (FromTP.apply(y) if tp > 1 else y) + self.fc2_b
+
+    class Stage(nn.Module):
+        def __init__(self):
+            super().__init__()
+            self.first, self.last = s == 0, s == pp - 1
+            if self.first:
+                self.tok_emb = nn.Embedding(VOCAB, C)
+                self.pos_emb = nn.Parameter(torch.zeros(1, SEQ, C))
+            self.blocks = nn.ModuleList(TPBlock() for _ in range(LAYERS // pp))
+            if self.last:
+                self.ln_f = nn.LayerNorm(C)
+                self.head = nn.Linear(C, VOCAB, bias=False)
+
+        def forward(self, x):
+            h = self.tok_emb(x) + self.pos_emb if self.first else x
+            for blk in self.blocks:
+                h = blk(h)
+            return self.head(self.ln_f(h)) if self.last else h
+
+    torch.manual_seed(1000 + s)  # replicated parameters identical across the tp group and the replicas
+    torch.cuda.manual_seed(1000 + s)
+    with torch.device(dev):
+        stage = Stage()
+    for p in stage.parameters():  # N(0, 0.02) like the model of the other arms; LayerNorm stays (1, 0)
+        if p.dim() > 1:
+            nn.init.normal_(p, 0.0, 0.02)
+    opt = torch.optim.AdamW(stage.parameters(), lr=3e-4, betas=(0.9, 0.95), weight_decay=0.1, fused=True)
+    B = args.micro_batch
+    M = MICROBATCHES
+    n_seq = M * B
+    xs, ys = batches_on_device(torch, 2, n_seq, dev, seed=1000 + d)
+    params = [p for p in stage.parameters()]
+    pp_group, pp_ranks = groups.get("pp", (None, [rank]))
+    prev_rank = pp_ranks[s - 1] if s > 0 else None
+    next_rank = pp_ranks[s + 1] if s < pp - 1 else None
+    act_shape = (B, SEQ, C)
+
+    def p2p(send=None, to=None, recv_from=None):
+        ops, buf = [], None
+        if send is not None:
+            ops.append(dist.P2POp(dist.isend, send.contiguous(), to, group=pp_group))
+        if recv_from is not None:
+            buf = torch.empty(act_shape, dtype=torch.bfloat16, device=dev)
+            ops.append(dist.P2POp(dist.irecv, buf, recv_from, group=pp_group))
+        if ops:
+            for w in dist.batch_isend_irecv(ops):
+                w.wait()
+        return buf
+
+    first, last = s == 0, s == pp - 1
+
+    # Paired NCCL point-to-point steps of the 1F1B schedule (every send is
+    # posted together with the receive its neighbour pairs it with).
+    def recv_forward():
+        return None if first else p2p(recv_from=prev_rank)
+
+    def send_forward(out):
+        if not last:
+            p2p(send=out.detach().to(torch.bfloat16), to=next_rank)
+
+    def send_forward_recv_backward(out):
+        return None if last else p2p(send=out.detach().to(torch.bfloat16), to=next_rank, recv_from=next_rank)
+
+    def send_backward_recv_forward(g):
+        return None if first else p2p(send=g.to(torch.bfloat16), to=prev_rank, recv_from=prev_rank)
+
+    def send_backward(g):
+        if not first:
+            p2p(send=g.to(torch.bfloat16), to=prev_rank)
+
+    def recv_backward():
+        return None if last else p2p(recv_from=next_rank)
+
+    def train(x, y):
+        opt.zero_grad(set_to_none=True)
+        queue = []
+        losses = []
+
+        def forward(k, inp):
+            if inp is not None:
+                inp.requires_grad_(True)
+            with torch.autocast("cuda", dtype=torch.bfloat16):
+                out = stage(x[k * B:(k + 1) * B] if first else inp)
+                if last:
+                    out = F.cross_entropy(out.float().view(-1, VOCAB), y[k * B:(k + 1) * B].reshape(-1)) / M
+                    losses.append(out.detach())
+            queue.append((inp, out))
+            return out
+
+        def backward(grad):
+            inp, out = queue.pop(0)  # the oldest microbatch in flight
+            if last:
+                out.backward()
+            else:
+                out.backward(grad.to(out.dtype))
+            return inp.grad if inp is not None else None
+
+        warm = min(pp - 1 - s, M)
+        for k in range(warm):
+            send_forward(forward(k, recv_forward()))
+        inp = recv_forward() if warm < M else None
+        for k in range(warm, M):
+            g_out = send_forward_recv_backward(forward(k, inp))
+            g_in = backward(g_out)
+            if k == M - 1:
+                send_backward(g_in)
+                inp = None
+            else:
+                inp = send_backward_recv_forward(g_in)
+        for _ in range(warm):
+            send_backward(backward(recv_backward()))
+        if dp > 1:  # average over the data-parallel replicas: NCCL all-reduces queued back to back
+            works = [dist.all_reduce(p.grad, group=groups["dp"][0], async_op=True) for p in params
+                     if p.grad is not None]
+            for w in works:
+                w.wait()
+            torch._foreach_div_([p.grad for p in params if p.grad is not None], float(dp))
+        opt.step()
+        return torch.stack(losses).sum() if losses else None
+
+    def step(i):
+        train(xs[i % 2], ys[i % 2])
+
+    hx = torch.empty((n_seq, SEQ), dtype=torch.int64).pin_memory()
+    hy = torch.empty((n_seq, SEQ), dtype=torch.int64).pin_memory()
+    gen = torch.Generator().manual_seed(77 + d)
+    final = [0.0]
+
+    def e2e_step(i):
+        torch.randint(0, VOCAB, (n_seq, SEQ), generator=gen, out=hx)
+        torch.randint(0, VOCAB, (n_seq, SEQ), generator=gen, out=hy)
+        loss = train(hx.to(dev, non_blocking=True) if s == 0 else None,
+                     hy.to(dev, non_blocking=True) if s == pp - 1 else None)
+        if loss is not None:
+            final[0] = float(loss.item())
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    def reduce_max(v):
+        if world == 1:
+            return v
+        tt = torch.tensor([v], dtype=torch.float64, device=dev)
+        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+        return float(tt.item())
+
+    clocks = ClockSampler(dev.index)
+    ms, e2e_ms, _ = run_phases(torch, args, step, barrier, reduce_max, dev, clocks, e2e_step)
+    loss_max = reduce_max(final[0])
+    if rank == 0:
+        emit(args, world, "torch", ms, e2e_ms, clocks, None, {"final_loss": round(loss_max, 4)})
     if world > 1:
         dist.destroy_process_group()
 
