@@ -94,6 +94,9 @@ def parse_args():
                     help="ddp: config 3 (default); fsdp: config 4; 3d: config 5 (N in 1, 2, 4, 8)")
     ap.add_argument("--micro-batch", type=int, default=None)
     ap.add_argument("--no-e2e", action="store_true", help="skip the end-to-end phase")
+    ap.add_argument("--ddp-optimizer", choices=["fused", "separate"], default="separate",
+                    help="--mode ddp, N > 1: AdamW inside each gradient bucket's reduction on 1/N of the "
+                         "parameters per rank (fused), or one AdamW step over all parameters after backward")
     ap.add_argument("--fsdp-gather", choices=["fused", "prefetch"], default="fused",
                     help="--mode fsdp: gather each block's parameters inside its first GEMM (fused) or "
                          "with a separate all-gather prefetched on a side stream")
@@ -239,7 +242,10 @@ def emit(args, world, impl, ms, e2e_ms, clocks, launches, extra=None):
                 *mesh_dims(world), MICROBATCHES)) if args.mode == "3d"
                 else f"{args.mode if args.mode != 'ddp' else 'dp'}{world}"),
             "bucket_mb": BUCKET_MB if args.mode == "ddp" else None,
-            "optimizer": "AdamW(0.9,0.95,wd0.1), fp32 master",
+            "optimizer": "AdamW(0.9,0.95,wd0.1), fp32 master" + (
+                ", inside each bucket's reduction on 1/N of the parameters per rank"
+                if args.mode == "ddp" and getattr(args, "ddp_optimizer", "") == "fused" and world > 1
+                and impl == "ours" else ""),
             "l2": "no flush: per-step working set (activations, params, grads, Adam state) >> 126 MB L2",
         },
         "clocks": clocks.summary(),
@@ -377,6 +383,12 @@ def run_ours(args):
                                           fuse_gather_gemm=args.fsdp_gather == "fused" and world > 1)
         shard_ids = {id(u.shard) for u in ddp.units}
         opt = FusedAdamW([p for p in ddp.parameters() if id(p) not in shard_ids], **hp)
+    elif args.ddp_optimizer == "fused" and world > 1:
+        # AdamW inside each bucket's reduction: every rank updates its 1/W slice, new parameters by all-gather
+        ddp = mn.DistributedDataParallel(model, pg, bucket_cap_mb=BUCKET_MB, overlap=True, algorithm="auto",
+                                         optimizer_in_backward=dict(hp, eps=1e-8))
+        rest = ddp.unbucketed_parameters()
+        opt = FusedAdamW(rest, **hp) if rest else None
     else:
         ddp = mn.DistributedDataParallel(model, pg, bucket_cap_mb=BUCKET_MB, overlap=True, algorithm="auto")
         opt = FusedAdamW(model.parameters(), **hp)
@@ -388,7 +400,8 @@ def run_ours(args):
         _, loss = ddp(xs[i % 4], ys[i % 4])
         loss.backward()
         ddp.sync()
-        opt.step()
+        if opt is not None:
+            opt.step()
         return loss
 
     hx = torch.empty((B, SEQ), dtype=torch.int64).pin_memory()
@@ -405,7 +418,8 @@ def run_ours(args):
         _, loss = ddp(x, y)
         loss.backward()
         ddp.sync()
-        opt.step()
+        if opt is not None:
+            opt.step()
         losses.append(loss.item())
 
     def barrier():

@@ -1237,6 +1237,128 @@ __global__ void __launch_bounds__(kCommThreads) nvls_move_kernel(CommArgs a, cha
   ring_end(a, ok);
 }
 
+// ===========================================================================
+// DDP with the optimizer inside the gradient reduction (one kernel per
+// bucket; ZeRO-1 layout): rank r owns elements [r*slice, (r+1)*slice) of the
+// bucket -- it reduces their gradients, applies AdamW to them with fp32
+// master weights and moments held for that slice only, and writes the new
+// parameters (the bucket's type) into every rank's parameter bucket.  The
+// traffic is a reduce-scatter of gradients plus an all-gather of parameters,
+// the same bytes as the all-reduce it replaces, and the optimizer work and
+// state shrink W-fold.  a.n = slice (elements, a multiple of 16 / sizeof(T)).
+// ===========================================================================
+template <typename T> struct Pack;
+template <> struct Pack<__nv_bfloat16> {
+  static constexpr int V = 8;
+  static MNB_DEVICE void unpack(uint4 v, float* f) { Multimem<__nv_bfloat16>::unpack(v, f); }
+  static MNB_DEVICE uint4 pack(const float* f) { return Multimem<__nv_bfloat16>::pack(f); }
+};
+template <> struct Pack<float> {
+  static constexpr int V = 4;
+  static MNB_DEVICE void unpack(uint4 v, float* f) { Multimem<float>::unpack(v, f); }
+  static MNB_DEVICE uint4 pack(const float* f) { return Multimem<float>::pack(f); }
+};
+
+// AdamW on V consecutive slice elements starting at e0 (state arrays index
+// the slice); g holds the reduced, scaled gradients; w receives the new weights.
+template <int V>
+MNB_DEVICE void adamw_slice(const AdamArgs& o, long long e0, const float* g, float* w) {
+#pragma unroll
+  for (int i = 0; i < V; ++i) {
+    const long long e = e0 + i;
+    const float m = o.b1 * o.m[e] + (1.f - o.b1) * g[i];
+    const float v = o.b2 * o.v[e] + (1.f - o.b2) * g[i] * g[i];
+    o.m[e] = m;
+    o.v[e] = v;
+    float x = o.master[e];
+    x -= o.lr * o.wd * x;
+    x -= o.lr * (m * o.c1) / (sqrtf(v * o.c2) + o.eps);
+    o.master[e] = x;
+    w[i] = x;
+  }
+}
+
+// Peer-memory version: phase 1 pushes gradient chunk c into rank c's staging
+// slot r; phase 2 sums the owned chunk in rank order (identical bits on every
+// rank), updates it and stores the parameters into every rank's bucket
+// (a.dst[p] = rank p's parameter bucket).
+template <typename T, int THREADS, int MINB>
+__global__ void __launch_bounds__(THREADS, MINB) ar_adamw_push_kernel(CommArgs a, AdamArgs o) {
+  constexpr int V = Pack<T>::V;
+  ring_begin(a);
+  const int W = a.world, r = a.rank;
+  const long long slice_u = a.n / V;
+  const SliceSplit sp = slice_split(slice_u * W, W);
+  const T* in = reinterpret_cast<const T*>(a.in);
+  long long lo, hi;
+  for (int k = 1; k < W; ++k) {  // my copy of chunk c -> slot r of rank c
+    const int c = (r + k) % W;
+    sp.range(c, &lo, &hi);
+    const uint4* src = reinterpret_cast<const uint4*>(in) + c * slice_u;
+    uint4* dst = reinterpret_cast<uint4*>(a.data[c]) + r * slice_u;
+    constexpr int U = 4;
+    for (long long u0 = lo - c * slice_u + threadIdx.x; u0 < hi - c * slice_u; u0 += U * THREADS) {
+      uint4 w[U];
+#pragma unroll
+      for (int j = 0; j < U; ++j)
+        if (u0 + j * THREADS < hi - c * slice_u) w[j] = ld_v4(src + u0 + j * THREADS);
+#pragma unroll
+      for (int j = 0; j < U; ++j)
+        if (u0 + j * THREADS < hi - c * slice_u) st_v4(dst + u0 + j * THREADS, w[j]);
+    }
+  }
+  bool ok = peer_barrier(a, a.epoch + 1);
+  if (ok) {
+    sp.range(r, &lo, &hi);
+    for (long long u = lo + threadIdx.x; u < hi; u += THREADS) {
+      const long long e = (u - r * slice_u) * V;  // index inside the slice
+      float g[V], x[V];
+      for (int q = 0; q < W; ++q) {  // rank order
+        const uint4 raw = q == r ? ld_v4(in + u * V) : ld_v4_cg(reinterpret_cast<const T*>(a.data[r]) +
+                                                               static_cast<long long>(q) * a.n + e);
+        Pack<T>::unpack(raw, x);
+#pragma unroll
+        for (int i = 0; i < V; ++i) g[i] = q == 0 ? x[i] : g[i] + x[i];
+      }
+#pragma unroll
+      for (int i = 0; i < V; ++i) g[i] *= a.scale;
+      float w[V];
+      adamw_slice<V>(o, e, g, w);
+      const uint4 pw = Pack<T>::pack(w);
+      for (int k = 0; k < W; ++k) st_v4(reinterpret_cast<T*>(a.dst[(r + k) % W]) + u * V, pw);
+    }
+    ok = peer_barrier(a, a.epoch + 2);
+  }
+  ring_end(a, ok);
+}
+
+// NVLS version: the switch returns the summed gradient slice, the new
+// parameters go to every rank with one multimem store.
+template <typename T, int THREADS, int MINB>
+__global__ void __launch_bounds__(THREADS, MINB) nvls_ar_adamw_kernel(CommArgs a, AdamArgs o, char* g_mc,
+                                                                       char* p_mc) {
+  constexpr int V = Pack<T>::V;
+  ring_begin(a);
+  const int W = a.world, r = a.rank;
+  const long long slice_u = a.n / V;
+  const SliceSplit sp = slice_split(slice_u * W, W);
+  bool ok = nvls_barrier(a, a.epoch + 1);
+  if (ok) {
+    long long lo, hi;
+    sp.range(r, &lo, &hi);
+    for (long long u = lo + threadIdx.x; u < hi; u += THREADS) {
+      float g[V], w[V];
+      Multimem<T>::unpack(Multimem<T>::ld_reduce(g_mc + 16 * u), g);
+#pragma unroll
+      for (int i = 0; i < V; ++i) g[i] *= a.scale;
+      adamw_slice<V>(o, (u - r * slice_u) * V, g, w);
+      multimem_st16(p_mc + 16 * u, Pack<T>::pack(w));
+    }
+    ok = nvls_barrier(a, a.epoch + 2);
+  }
+  ring_end(a, ok);
+}
+
 __global__ void barrier_kernel(CommArgs a) {
   ring_begin(a);
   const bool ok = peer_barrier(a, a.epoch + 1);
@@ -2022,6 +2144,70 @@ class DeviceCommImpl {
     C10_CUDA_KERNEL_LAUNCH_CHECK();
   }
 
+  // DDP bucket with the optimizer inside its reduction: reduce `grad`, apply
+  // AdamW to this rank's 1/W slice (fp32 master / m / v hold that slice) and
+  // write the new parameters into every rank's `param` bucket.  Both buckets
+  // are NVLS tensors (switch reduction, multicast store) or peer-mapped
+  // symmetric tensors (push kernel).  max_blocks < 0: 128-thread CTAs that
+  // fit beside compute.
+  void all_reduce_adamw(torch::Tensor grad, torch::Tensor param, torch::Tensor master, torch::Tensor m,
+                        torch::Tensor v, double lr, double b1, double b2, double eps, double wd, double bc1,
+                        double bc2, double scale, int max_blocks) {
+    const bool beside = max_blocks < 0;
+    if (beside) max_blocks = -max_blocks;
+    c10::cuda::CUDAGuard g(device_);
+    const auto dt = grad.scalar_type();
+    TORCH_CHECK(dt == param.scalar_type() && (dt == at::kBFloat16 || dt == at::kFloat),
+                "gradient and parameter buckets: both bf16 or both fp32");
+    TORCH_CHECK(grad.is_contiguous() && param.is_contiguous() && grad.numel() == param.numel(), "bucket shapes");
+    const int64_t V = 16 / grad.element_size();
+    const int64_t n = grad.numel();
+    TORCH_CHECK(n % (world_ * V) == 0, "bucket length must be a multiple of world_size x 16 bytes");
+    const int64_t slice = n / world_;
+    for (const torch::Tensor* t : {&master, &m, &v})
+      TORCH_CHECK(t->scalar_type() == at::kFloat && t->is_contiguous() && t->numel() == slice,
+                  "master / m / v: fp32 [bucket / world_size]");
+    const int64_t bytes = n * grad.element_size();
+    CommArgs a = base_args(staging_, 0, grad.data_ptr(), param.data_ptr(), slice, 11, bytes, 2);
+    a.scale = static_cast<float>(scale);
+    AdamArgs o{};
+    o.master = master.data_ptr<float>();
+    o.m = m.data_ptr<float>();
+    o.v = v.data_ptr<float>();
+    o.param = param.data_ptr();
+    o.lr = static_cast<float>(lr);
+    o.b1 = static_cast<float>(b1);
+    o.b2 = static_cast<float>(b2);
+    o.eps = static_cast<float>(eps);
+    o.wd = static_cast<float>(wd);
+    o.c1 = static_cast<float>(1.0 / bc1);
+    o.c2 = static_cast<float>(1.0 / bc2);
+    auto stream = at::cuda::getCurrentCUDAStream();
+    const int threads = beside ? 128 : kCommThreads;
+    const int nb = blocks_for(bytes / world_, max_blocks, beside ? (16 << 10) : (64 << 10));
+    const auto lg = locate_nvls(grad.data_ptr(), bytes), lp = locate_nvls(param.data_ptr(), bytes);
+    if (lg.first >= 0 && lp.first >= 0 && lg.second % 16 == 0 && lp.second % 16 == 0) {
+      char* gmc = static_cast<char*>(nvls_[lg.first]->mc()) + lg.second;
+      char* pmc = static_cast<char*>(nvls_[lp.first]->mc()) + lp.second;
+#define MNB_NA(T)                                                                                     \
+  if (beside) nvls_ar_adamw_kernel<T, 128, 6><<<nb, threads, 0, stream>>>(a, o, gmc, pmc);            \
+  else nvls_ar_adamw_kernel<T, kCommThreads, 1><<<nb, threads, 0, stream>>>(a, o, gmc, pmc);
+      if (dt == at::kBFloat16) { MNB_NA(__nv_bfloat16) } else { MNB_NA(float) }
+#undef MNB_NA
+    } else {
+      const auto sg = locate(grad.data_ptr(), bytes), spm = locate(param.data_ptr(), bytes);
+      TORCH_CHECK(sg.first >= 0 && spm.first >= 0, "both buckets must be symmetric tensors of this communicator");
+      TORCH_CHECK(bytes <= (segs_[staging_].bytes / 2) / 256 * 256, "staging buffer too small for the bucket");
+      for (int r = 0; r < world_; ++r) a.dst[r] = static_cast<uint8_t*>(segs_[spm.first].peers[r]) + spm.second;
+#define MNB_PA(T)                                                                                     \
+  if (beside) ar_adamw_push_kernel<T, 128, 6><<<nb, threads, 0, stream>>>(a, o);                      \
+  else ar_adamw_push_kernel<T, kCommThreads, 1><<<nb, threads, 0, stream>>>(a, o);
+      if (dt == at::kBFloat16) { MNB_PA(__nv_bfloat16) } else { MNB_PA(float) }
+#undef MNB_PA
+    }
+    C10_CUDA_KERNEL_LAUNCH_CHECK();
+  }
+
   int rank() const { return rank_; }
   int world() const { return world_; }
 
@@ -2091,6 +2277,7 @@ void register_comm(py::module_& m) {
       .def("nvls_reduce_scatter", &DeviceCommImpl::nvls_reduce_scatter)
       .def("nvls_move", &DeviceCommImpl::nvls_move)
       .def("nvls_rs_adamw", &DeviceCommImpl::nvls_rs_adamw)
+      .def("all_reduce_adamw", &DeviceCommImpl::all_reduce_adamw)
       .def("close", &DeviceCommImpl::close)
       .def_property_readonly("rank", &DeviceCommImpl::rank)
       .def_property_readonly("world", &DeviceCommImpl::world);

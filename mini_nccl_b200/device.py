@@ -76,7 +76,8 @@ _NVLS_DTYPES = (torch.float32, torch.bfloat16, torch.float16)
 
 _OPS = {"sum": 0, "prod": 1, "max": 2, "min": 3}
 OPNAMES = ["all_reduce", "reduce_scatter", "all_gather", "broadcast", "all_to_all", "barrier", "all_reduce_stepped",
-           "gemm_reduce_scatter", "all_gather_gemm", "reduce_scatter_adamw", "gather_weight_gemm"]
+           "gemm_reduce_scatter", "all_gather_gemm", "reduce_scatter_adamw", "gather_weight_gemm",
+           "all_reduce_adamw"]
 
 
 def _ext():
@@ -435,6 +436,34 @@ class DeviceComm:
                 self.impl.nvls_rs_adamw(*args, blocks or NVLS_BLOCKS)
             else:
                 self.impl.reduce_scatter_adamw(*args, blocks or MAX_BLOCKS)
+        finally:
+            self._finish(ev)
+
+    def all_reduce_adamw(self, grad_bucket: torch.Tensor, param_bucket: torch.Tensor, state: dict, *, lr: float,
+                         betas: tuple[float, float], eps: float, weight_decay: float, step: int, scale: float = 1.0,
+                         beside_compute: bool = False, blocks: int | None = None) -> None:
+        """One DDP bucket's gradient average and AdamW step as one kernel (ZeRO-1 layout).
+
+        Rank r reduces the gradients of its 1/W slice of the bucket, applies
+        AdamW to that slice (``state``: fp32 ``master``, ``m``, ``v`` of the
+        slice's length) and writes the new parameters into every rank's
+        ``param_bucket``: a reduce-scatter of gradients and an all-gather of
+        parameters, the bytes of the all-reduce it replaces.  Both buckets are
+        symmetric tensors of this communicator (NVLS ones reduce in the
+        switch and store by multicast).  ``step`` is the 1-based update count.
+        """
+        b1, b2 = betas
+        nbytes = grad_bucket.numel() * grad_bucket.element_size()
+        nvls = self.impl.is_nvls(grad_bucket) and self.impl.is_nvls(param_bucket)
+        if not nvls:
+            self._ensure_staging(2 * nbytes)
+        ev = self._record("all_reduce_adamw", "nvls" if nvls else "two_shot", nbytes)
+        try:
+            nb = blocks or ((NVLS_BESIDE_BLOCKS if beside_compute else NVLS_BLOCKS) if nvls
+                            else (BESIDE_BLOCKS if beside_compute else MAX_BLOCKS))
+            self.impl.all_reduce_adamw(grad_bucket, param_bucket, state["master"], state["m"], state["v"], float(lr),
+                                       float(b1), float(b2), float(eps), float(weight_decay), 1.0 - b1 ** step,
+                                       1.0 - b2 ** step, float(scale), -nb if beside_compute else nb)
         finally:
             self._finish(ev)
 

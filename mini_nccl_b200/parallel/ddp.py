@@ -23,6 +23,18 @@ Two engines:
   compute stream wait on the communication stream; the host never blocks.
 * **CPU parameters.**  A one-thread executor runs the host collectives while
   autograd continues, exactly as the reference does.
+
+``optimizer_in_backward=dict(lr=..., betas=..., eps=..., weight_decay=...)``
+(CUDA, world size > 1) moves the AdamW step into each bucket's reduction:
+the parameters are re-homed into symmetric parameter buckets next to the
+gradient buckets, and one kernel per bucket reduces this rank's 1/W slice of
+the gradients, updates that slice (fp32 master weights and moments held for
+the slice only: ZeRO-1) and writes the new parameters into every rank's
+bucket.  The optimizer then runs during backward, on 1/W of the parameters
+per rank, and its state shrinks W-fold; ``sync()`` leaves the parameters
+updated, so no separate ``optimizer.step()`` is needed for bucketed
+parameters.  Gradient clipping by global norm is not available in this mode
+(each slice is updated as soon as its gradients are reduced).
 """
 
 from __future__ import annotations
@@ -106,6 +118,23 @@ class _Bucket:
         for p, v in zip(self.params, self.views, strict=True):
             p.grad = v
 
+    def home_parameters(self, store: torch.Tensor, rank: int, world: int) -> None:
+        """Move the parameters into ``store`` (views) and create this rank's slice of
+        optimizer state: fp32 master weights, first and second moments."""
+        self.param_buffer = store
+        offset = 0
+        with torch.no_grad():
+            for p in self.params:
+                n = p.numel()
+                view = store[offset : offset + n].view(p.shape)
+                view.copy_(p.data)
+                p.data = view
+                offset += n
+        slice_n = store.numel() // world
+        mine = store[rank * slice_n : (rank + 1) * slice_n]
+        self.opt_state = {"master": mine.float().clone(), "m": torch.zeros(slice_n, device=store.device),
+                          "v": torch.zeros(slice_n, device=store.device)}
+
     def mark_ready(self) -> bool:
         """Count one parameter in; True when the bucket just became complete."""
         with self.lock:
@@ -137,10 +166,14 @@ class DistributedDataParallel(nn.Module):
         overlap: bool = True,
         algorithm: str = "ring",
         broadcast_buffers: bool = True,
+        optimizer_in_backward: dict | None = None,
     ) -> None:
         super().__init__()
         self.module = module
         self.pg = pg
+        #: AdamW hyper-parameters of the fused optimizer (read at every step), or None.
+        self.optimizer_hp = None
+        self._opt_step = 0
         self.algorithm = algorithm
         self._overlap = overlap and pg.world_size > 1
         self._buckets: list[_Bucket] = []
@@ -159,6 +192,13 @@ class DistributedDataParallel(nn.Module):
         self.timeline_seqs: list[int] = []
         params = [p for p in module.parameters()]
         self._cuda = bool(params) and params[0].is_cuda
+        if optimizer_in_backward is not None:
+            if not self._cuda or pg.world_size < 2:
+                raise ValueError("optimizer_in_backward needs CUDA parameters and world_size > 1")
+            hp = dict(lr=3e-4, betas=(0.9, 0.95), eps=1e-8, weight_decay=0.1)
+            hp.update(optimizer_in_backward)
+            hp["betas"] = tuple(hp["betas"])
+            self.optimizer_hp = hp
 
         if pg.world_size > 1:
             with torch.no_grad():
@@ -202,12 +242,20 @@ class DistributedDataParallel(nn.Module):
         for i, ps in enumerate(groups):
             numel = sum(p.numel() for p in ps)
             if self._cuda:
+                dc = self.pg.device_comm()
+                if self.optimizer_hp is not None:  # W equal slices of whole 16-byte units
+                    quantum = self.pg.world_size * (16 // ps[0].element_size())
+                    numel = -(-numel // quantum) * quantum
                 # NVLS memory when the GPUs have it: the bucket all-reduce then
                 # runs in place through the switch
-                buf = self.pg.device_comm().symmetric_zeros(numel, ps[0].dtype, nvls=DDP_NVLS)
+                buf = dc.symmetric_zeros(numel, ps[0].dtype, nvls=DDP_NVLS)
             else:
                 buf = torch.zeros(numel, dtype=ps[0].dtype, device=ps[0].device)
-            self._buckets.append(_Bucket(i, ps, buf))
+            bucket = _Bucket(i, ps, buf)
+            if self.optimizer_hp is not None:
+                bucket.home_parameters(dc.symmetric_zeros(numel, ps[0].dtype, nvls=DDP_NVLS),
+                                       self.pg.rank, self.pg.world_size)
+            self._buckets.append(bucket)
 
     def _make_hook(self, bucket: _Bucket):
         def hook(_param: nn.Parameter) -> None:
@@ -244,10 +292,18 @@ class DistributedDataParallel(nn.Module):
         try:
             with torch.cuda.stream(self._comm_stream):
                 self._comm_stream.wait_event(produced)
-                self._dc.all_reduce(
-                    bucket.buffer, op="sum", algorithm="auto", scale=1.0 / self.pg.world_size,
-                    blocks=DDP_COMM_BLOCKS or None, beside_compute=DDP_BESIDE_COMPUTE,
-                )
+                if self.optimizer_hp is not None:
+                    hp = self.optimizer_hp
+                    self._dc.all_reduce_adamw(
+                        bucket.buffer, bucket.param_buffer, bucket.opt_state, lr=hp["lr"], betas=hp["betas"],
+                        eps=hp["eps"], weight_decay=hp["weight_decay"], step=self._opt_step + 1,
+                        scale=1.0 / self.pg.world_size, blocks=DDP_COMM_BLOCKS or None,
+                        beside_compute=DDP_BESIDE_COMPUTE)
+                else:
+                    self._dc.all_reduce(
+                        bucket.buffer, op="sum", algorithm="auto", scale=1.0 / self.pg.world_size,
+                        blocks=DDP_COMM_BLOCKS or None, beside_compute=DDP_BESIDE_COMPUTE,
+                    )
                 done = torch.cuda.Event()
                 done.record(self._comm_stream)
                 self._last_done = done
@@ -312,6 +368,8 @@ class DistributedDataParallel(nn.Module):
                 for b in self._buckets:
                     b.ready.set()
             self._sync_cuda()
+            if self.optimizer_hp is not None:
+                self._opt_step += 1
         elif self._overlap:
             if self._future is not None:
                 self._future.result()
@@ -338,3 +396,30 @@ class DistributedDataParallel(nn.Module):
     def grad_buffers(self) -> list[torch.Tensor]:
         """The flat bucket buffers, in bucket order (for fused optimizers)."""
         return [b.buffer for b in self._buckets]
+
+    def unbucketed_parameters(self) -> list[nn.Parameter]:
+        """Parameters outside every bucket (frozen ones): what a separate optimizer
+        still has to step when ``optimizer_in_backward`` is on."""
+        bucketed = {id(p) for b in self._buckets for p in b.params}
+        return [p for p in self.module.parameters() if id(p) not in bucketed and p.requires_grad]
+
+    def optimizer_state_dict(self) -> dict:
+        """This rank's slice of the fused optimizer's state (one file per rank)."""
+        if self.optimizer_hp is None:
+            raise ValueError("no fused optimizer (optimizer_in_backward is off)")
+        return {"hp": dict(self.optimizer_hp), "step": self._opt_step, "rank": self.pg.rank,
+                "world_size": self.pg.world_size,
+                "buckets": [{k: t.detach().clone() for k, t in b.opt_state.items()} for b in self._buckets]}
+
+    def load_optimizer_state_dict(self, sd: dict) -> None:
+        if self.optimizer_hp is None:
+            raise ValueError("no fused optimizer (optimizer_in_backward is off)")
+        if sd["rank"] != self.pg.rank or sd["world_size"] != self.pg.world_size:
+            raise ValueError("optimizer state was written by a different rank layout")
+        self.optimizer_hp = dict(sd["hp"])
+        self.optimizer_hp["betas"] = tuple(self.optimizer_hp["betas"])
+        self._opt_step = int(sd["step"])
+        with torch.no_grad():
+            for b, st in zip(self._buckets, sd["buckets"], strict=True):
+                for k, t in st.items():
+                    b.opt_state[k].copy_(t)

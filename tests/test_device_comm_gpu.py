@@ -335,6 +335,54 @@ def test_fsdp_fused_gather_trains_like_plain_gather():
     run(_fsdp_fused_vs_plain, 2, devices="cuda", timeout=600.0, op_timeout=60.0)
 
 
+def _ddp_fused_optimizer(pg) -> str:
+    """DDP with AdamW inside each bucket's reduction == DDP followed by FusedAdamW."""
+    from mini_nccl_b200.ddp import DistributedDataParallel
+    from mini_nccl_b200.models.gpt import GPT
+    from mini_nccl_b200.ops.kernels import FusedAdamW
+
+    dev = torch.device("cuda", torch.cuda.current_device())
+    hp = dict(lr=1e-3, betas=(0.9, 0.95), eps=1e-8, weight_decay=0.1)
+    finals, kinds = [], []
+    for fused in (False, True):
+        torch.manual_seed(0)
+        model = GPT(vocab_size=512, block_size=128, n_layer=2, n_head=4, n_embd=256).to(dev, torch.bfloat16)
+        ddp = DistributedDataParallel(model, pg, bucket_cap_mb=1.0, optimizer_in_backward=hp if fused else None)
+        opt = None if fused else FusedAdamW(model.parameters(), **hp)
+        g = torch.Generator().manual_seed(11 + pg.rank)
+        for _ in range(3):
+            idx = torch.randint(0, 512, (4, 128), generator=g).to(dev)
+            tgt = torch.randint(0, 512, (4, 128), generator=g).to(dev)
+            ddp.zero_grad()
+            _, loss = ddp(idx, tgt)
+            loss.backward()
+            ddp.sync()
+            if opt is not None:
+                opt.step()
+        torch.cuda.synchronize()
+        kinds.append(pg.device_comm().impl.is_nvls(ddp._buckets[0].buffer))
+        finals.append({n: p.detach().float().clone() for n, p in model.named_parameters()})
+        if fused:
+            assert ddp.unbucketed_parameters() == []
+            st = ddp.optimizer_state_dict()
+            assert st["step"] == 3 and len(st["buckets"]) == len(ddp._buckets)
+    for name, a in finals[0].items():
+        err = (a - finals[1][name]).abs().max().item()
+        assert err <= 1e-2 * (a.abs().max().item() + 1e-3), (name, err)
+    flat = torch.cat([t.reshape(-1) for t in finals[1].values()])
+    everyone = C.all_gather(pg, flat)
+    assert all(torch.equal(o, everyone[0]) for o in everyone)  # identical replicas
+    return "nvls" if kinds[1] else "peer"
+
+
+@needs2
+@pytest.mark.parametrize("nvls", ["1", "0"])
+def test_ddp_optimizer_in_backward_matches_separate_optimizer(monkeypatch, nvls):
+    monkeypatch.setenv("MINI_NCCL_DDP_NVLS", nvls)
+    out = run(_ddp_fused_optimizer, 2, devices="cuda", timeout=600.0, op_timeout=60.0)
+    assert out[0] in ("nvls", "peer"), out
+
+
 def _host_staged(pg) -> None:
     from mini_nccl_b200 import device as D
 
