@@ -37,13 +37,15 @@ class Model(nn.Module):
         return self.head(h)
 
 
-def _parity(pg, steps: int = 5, recompute: bool = True) -> dict:
+def _parity(pg, steps: int = 5, recompute: bool = True, fuse_gather_gemm: bool = False) -> dict:
     W, per = pg.world_size, 6
     torch.manual_seed(0)
     model = Model()
     ref = copy.deepcopy(model)
-    fsdp = FullyShardedDataParallel(model, pg, unit_cls=Block, recompute=recompute)
+    fsdp = FullyShardedDataParallel(model, pg, unit_cls=Block, recompute=recompute, fuse_gather_gemm=fuse_gather_gemm)
     assert len(fsdp.units) == 3
+    if fuse_gather_gemm:  # 1-D parameters (LayerNorm, biases) stay whole; only matrices are sharded
+        assert all(len(u.entries) == 2 and all(len(e[2]) == 2 for e in u.entries) for u in fsdp.units)
     assert all(u.shard.numel() < u.padded_numel or W == 1 for u in fsdp.units)
     opt = torch.optim.SGD(fsdp.parameters(), lr=0.05, momentum=0.9)
     ref_opt = torch.optim.SGD(ref.parameters(), lr=0.05, momentum=0.9)
@@ -75,6 +77,24 @@ def test_fsdp_without_recompute_matches_single_process() -> None:
     reports = run(_parity, 2, 5, False)
     assert reports[0] == reports[1]
     run(_parity, 3, 3, False)
+
+
+def test_fsdp_units_keeping_vectors_whole_match_single_process() -> None:
+    """The layout fuse_gather_gemm uses (on CPU the gather itself is the plain one):
+    vectors replicated and averaged in sync(), matrices sharded."""
+    reports = run(_parity, 2, 4, False, True)
+    assert reports[0] == reports[1]
+
+
+def test_fuse_gather_gemm_needs_saved_activations() -> None:
+    import pytest
+
+    with pytest.raises(RuntimeError, match="fuse_gather_gemm needs recompute=False"):
+        run(_fused_with_recompute, 1)  # the worker's ValueError comes back through the launcher
+
+
+def _fused_with_recompute(pg) -> None:
+    FullyShardedDataParallel(Model(), pg, unit_cls=Block, recompute=True, fuse_gather_gemm=True)
 
 
 def test_fsdp_matches_single_process_world4() -> None:
