@@ -15,6 +15,11 @@ x [8192, 2048] @ W_qkv^T, W_qkv = the first [6144, 2048] of the buffer.
 * ``ours``  : this library's all-gather kernel, then its GEMM kernel;
 * ``nccl``  : NCCL all-gather (torch.distributed), then ``torch.matmul`` (cuBLAS).
 
+``--single`` runs the fused kernel on one GPU (the gather copies the own
+shard only), which is what an ncu capture can see:
+
+    python benchmarks/bench_fsdp_gather_gemm.py --single --iters 1 --warmup 1
+
 Each is timed with CUDA events over ``--iters`` calls after ``--warmup``,
 with a >126 MB L2 flush enqueued before every call and its own time
 subtracted; the reported time is the max over ranks.  The roofline target is
@@ -55,9 +60,14 @@ def main() -> None:
     ap.add_argument("--iters", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impls", default="fused,ours,nccl")
+    ap.add_argument("--single", action="store_true", help="one GPU, the fused kernel only (for ncu)")
     ap.add_argument("--out")
     args = ap.parse_args()
 
+    if args.single:
+        os.environ.update(RANK="0", WORLD_SIZE="1", MASTER_ADDR="127.0.0.1",
+                          MASTER_PORT=os.environ.get("MASTER_PORT", "29731"))
+        args.impls = "fused"
     rank, world = int(os.environ["RANK"]), int(os.environ["WORLD_SIZE"])
     dev = torch.device("cuda", int(os.environ.get("LOCAL_RANK", rank)))
     torch.cuda.set_device(dev)

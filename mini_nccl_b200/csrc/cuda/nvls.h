@@ -58,6 +58,7 @@ class NvlsObject {
 
   int rank_, world_, device_;
   int64_t bytes_ = 0;
+  int64_t gran_ = 0;  // mapping granularity (multicast and allocation)
   CUmemGenericAllocationHandle mc_handle_ = 0;
   CUmemGenericAllocationHandle mem_handle_ = 0;
   bool have_mc_ = false, have_mem_ = false, added_ = false, bound_ = false, mapped_ = false;

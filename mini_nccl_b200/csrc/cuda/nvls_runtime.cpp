@@ -212,6 +212,7 @@ void NvlsObject::create(int64_t bytes) {
   size_t mem_gran = 0;
   cu_check(d.mem_granularity(&mem_gran, &ap, CU_MEM_ALLOC_GRANULARITY_MINIMUM), "cuMemGetAllocationGranularity");
   const int64_t gran = static_cast<int64_t>(std::max(mc_gran, mem_gran));
+  gran_ = gran;
   bytes_ = round_up(std::max<int64_t>(bytes, 1), gran);
   mp.size = static_cast<size_t>(bytes_);
   if (rank_ == 0) {
@@ -260,11 +261,13 @@ void NvlsObject::bind_and_map() {
   access.location.id = dev;
   access.flags = CU_MEM_ACCESS_FLAGS_PROT_READWRITE;
   CUdeviceptr uc = 0, mc = 0;
-  cu_check(d.addr_reserve(&uc, static_cast<size_t>(bytes_), 0, 0, 0), "cuMemAddressReserve(unicast)");
+  cu_check(d.addr_reserve(&uc, static_cast<size_t>(bytes_), static_cast<size_t>(gran_), 0, 0),
+           "cuMemAddressReserve(unicast)");
   uc_ = reinterpret_cast<void*>(uc);
   cu_check(d.mem_map(uc, static_cast<size_t>(bytes_), 0, mem_handle_, 0), "cuMemMap(unicast)");
   cu_check(d.mem_set_access(uc, static_cast<size_t>(bytes_), &access, 1), "cuMemSetAccess(unicast)");
-  cu_check(d.addr_reserve(&mc, static_cast<size_t>(bytes_), 0, 0, 0), "cuMemAddressReserve(multicast)");
+  cu_check(d.addr_reserve(&mc, static_cast<size_t>(bytes_), static_cast<size_t>(gran_), 0, 0),
+           "cuMemAddressReserve(multicast)");
   mc_ = reinterpret_cast<void*>(mc);
   cu_check(d.mem_map(mc, static_cast<size_t>(bytes_), 0, mc_handle_, 0), "cuMemMap(multicast)");
   cu_check(d.mem_set_access(mc, static_cast<size_t>(bytes_), &access, 1), "cuMemSetAccess(multicast)");

@@ -86,6 +86,25 @@ def _ext():
     return cuda_ext()
 
 
+def all_gather_blobs(comm, blob: bytes) -> list[bytes]:
+    """Every rank's byte string, in rank order, over the host communicator.
+
+    Blobs may differ in length (socket names, error messages) and may be
+    empty: the lengths are gathered first, then every blob padded to the
+    longest one, and each is cut back to its own length.
+    """
+    sizes = _hostc.all_gather(comm, torch.tensor([len(blob)], dtype=torch.int64))
+    lengths = [int(s.item()) for s in sizes]
+    longest = max(lengths)
+    if longest == 0:
+        return [b"" for _ in lengths]
+    padded = torch.zeros(longest, dtype=torch.uint8)
+    if blob:
+        padded[: len(blob)] = torch.frombuffer(bytearray(blob), dtype=torch.uint8)
+    parts = _hostc.all_gather(comm, padded)
+    return [bytes(part[:n].numpy().tobytes()) for part, n in zip(parts, lengths, strict=True)]
+
+
 class DeviceComm:
     """Peer-memory collectives among the ranks of one host communicator."""
 
@@ -128,9 +147,7 @@ class DeviceComm:
     # ---- bootstrap ------------------------------------------------------------------
 
     def _all_gather_bytes(self, blob: bytes) -> list[bytes]:
-        t = torch.frombuffer(bytearray(blob), dtype=torch.uint8).clone()
-        parts = _hostc.all_gather(self.comm, t)
-        return [bytes(p.numpy().tobytes()) for p in parts]
+        return all_gather_blobs(self.comm, blob)
 
     def _open(self, seg: int) -> None:
         handles = self._all_gather_bytes(bytes(self.impl.segment_handle(seg)))
