@@ -1310,22 +1310,38 @@ __global__ void __launch_bounds__(THREADS, MINB) ar_adamw_push_kernel(CommArgs a
   bool ok = peer_barrier(a, a.epoch + 1);
   if (ok) {
     sp.range(r, &lo, &hi);
-    for (long long u = lo + threadIdx.x; u < hi; u += THREADS) {
-      const long long e = (u - r * slice_u) * V;  // index inside the slice
-      float g[V], x[V];
+    constexpr int U = 2;  // units per thread with all their slot loads in flight
+    for (long long u0 = lo + threadIdx.x; u0 < hi; u0 += U * THREADS) {
+      float g[U][V];
       for (int q = 0; q < W; ++q) {  // rank order
-        const uint4 raw = q == r ? ld_v4(in + u * V) : ld_v4_cg(reinterpret_cast<const T*>(a.data[r]) +
-                                                               static_cast<long long>(q) * a.n + e);
-        Pack<T>::unpack(raw, x);
+        uint4 raw[U];
 #pragma unroll
-        for (int i = 0; i < V; ++i) g[i] = q == 0 ? x[i] : g[i] + x[i];
+        for (int j = 0; j < U; ++j) {
+          const long long u = u0 + j * THREADS;
+          if (u < hi)
+            raw[j] = q == r ? ld_v4(in + u * V)
+                            : ld_v4_cg(reinterpret_cast<const T*>(a.data[r]) + static_cast<long long>(q) * a.n +
+                                       (u - r * slice_u) * V);
+        }
+#pragma unroll
+        for (int j = 0; j < U; ++j) {
+          float x[V];
+          Pack<T>::unpack(raw[j], x);
+#pragma unroll
+          for (int i = 0; i < V; ++i) g[j][i] = q == 0 ? x[i] : g[j][i] + x[i];
+        }
       }
 #pragma unroll
-      for (int i = 0; i < V; ++i) g[i] *= a.scale;
-      float w[V];
-      adamw_slice<V>(o, e, g, w);
-      const uint4 pw = Pack<T>::pack(w);
-      for (int k = 0; k < W; ++k) st_v4(reinterpret_cast<T*>(a.dst[(r + k) % W]) + u * V, pw);
+      for (int j = 0; j < U; ++j) {
+        const long long u = u0 + j * THREADS;
+        if (u >= hi) continue;
+#pragma unroll
+        for (int i = 0; i < V; ++i) g[j][i] *= a.scale;
+        float w[V];
+        adamw_slice<V>(o, (u - r * slice_u) * V, g[j], w);
+        const uint4 pw = Pack<T>::pack(w);
+        for (int k = 0; k < W; ++k) st_v4(reinterpret_cast<T*>(a.dst[(r + k) % W]) + u * V, pw);
+      }
     }
     ok = peer_barrier(a, a.epoch + 2);
   }
@@ -1333,11 +1349,13 @@ __global__ void __launch_bounds__(THREADS, MINB) ar_adamw_push_kernel(CommArgs a
 }
 
 // NVLS version: the switch returns the summed gradient slice, the new
-// parameters go to every rank with one multimem store.
+// parameters go to every rank with one multimem store.  U switch loads per
+// thread are in flight before the first update (each waits a round trip).
 template <typename T, int THREADS, int MINB>
 __global__ void __launch_bounds__(THREADS, MINB) nvls_ar_adamw_kernel(CommArgs a, AdamArgs o, char* g_mc,
                                                                        char* p_mc) {
   constexpr int V = Pack<T>::V;
+  constexpr int U = 4;
   ring_begin(a);
   const int W = a.world, r = a.rank;
   const long long slice_u = a.n / V;
@@ -1346,13 +1364,22 @@ __global__ void __launch_bounds__(THREADS, MINB) nvls_ar_adamw_kernel(CommArgs a
   if (ok) {
     long long lo, hi;
     sp.range(r, &lo, &hi);
-    for (long long u = lo + threadIdx.x; u < hi; u += THREADS) {
-      float g[V], w[V];
-      Multimem<T>::unpack(Multimem<T>::ld_reduce(g_mc + 16 * u), g);
+    for (long long u0 = lo + threadIdx.x; u0 < hi; u0 += U * THREADS) {
+      uint4 raw[U];
 #pragma unroll
-      for (int i = 0; i < V; ++i) g[i] *= a.scale;
-      adamw_slice<V>(o, (u - r * slice_u) * V, g, w);
-      multimem_st16(p_mc + 16 * u, Pack<T>::pack(w));
+      for (int j = 0; j < U; ++j)
+        if (u0 + j * THREADS < hi) raw[j] = Multimem<T>::ld_reduce(g_mc + 16 * (u0 + j * THREADS));
+#pragma unroll
+      for (int j = 0; j < U; ++j) {
+        const long long u = u0 + j * THREADS;
+        if (u >= hi) continue;
+        float g[V], w[V];
+        Multimem<T>::unpack(raw[j], g);
+#pragma unroll
+        for (int i = 0; i < V; ++i) g[i] *= a.scale;
+        adamw_slice<V>(o, (u - r * slice_u) * V, g, w);
+        multimem_st16(p_mc + 16 * u, Pack<T>::pack(w));
+      }
     }
     ok = nvls_barrier(a, a.epoch + 2);
   }
@@ -2184,7 +2211,7 @@ class DeviceCommImpl {
     o.c2 = static_cast<float>(1.0 / bc2);
     auto stream = at::cuda::getCurrentCUDAStream();
     const int threads = beside ? 128 : kCommThreads;
-    const int nb = blocks_for(bytes / world_, max_blocks, beside ? (16 << 10) : (64 << 10));
+    const int nb = blocks_for(bytes / world_, max_blocks, beside ? (8 << 10) : (32 << 10));
     const auto lg = locate_nvls(grad.data_ptr(), bytes), lp = locate_nvls(param.data_ptr(), bytes);
     if (lg.first >= 0 && lp.first >= 0 && lg.second % 16 == 0 && lp.second % 16 == 0) {
       char* gmc = static_cast<char*>(nvls_[lg.first]->mc()) + lg.second;

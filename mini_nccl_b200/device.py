@@ -61,8 +61,13 @@ MAX_BLOCKS = int(os.environ.get("MINI_NCCL_DEVICE_BLOCKS", 255))
 BESIDE_BLOCKS = int(os.environ.get("MINI_NCCL_BESIDE_BLOCKS", 148))
 #: NVLS collectives on (where the hardware and driver support them).
 NVLS_ENABLED = os.environ.get("MINI_NCCL_NVLS", "1") != "0"
-#: From this many bytes on ``auto`` sends sum reductions through the switch.
+#: From this many bytes on ``auto`` sends collectives through the switch ...
 NVLS_MIN_BYTES = int(os.environ.get("MINI_NCCL_NVLS_MIN_BYTES", 1 << 20))
+#: ... on communicators of at least this many ranks.  With W ranks an NVLS
+#: all-reduce moves about (1 + 1/W) x the message per GPU each way against
+#: 2 (W-1)/W for two-shot: at W = 2 that is 1.5 vs 1 and the measured sweep
+#: has two-shot ahead at every size; from W = 4 on the switch moves less.
+NVLS_MIN_WORLD = int(os.environ.get("MINI_NCCL_NVLS_MIN_WORLD", 4))
 #: CTAs an NVLS collective may use (each multimem access is one 16-byte request
 #: the switch serves, so far fewer CTAs than the peer kernels need).
 NVLS_BLOCKS = int(os.environ.get("MINI_NCCL_NVLS_BLOCKS", 64))
@@ -242,6 +247,10 @@ class DeviceComm:
     def _nvls_sum_ok(self, tensor: torch.Tensor, op: str) -> bool:
         return self.nvls and op == "sum" and tensor.dtype in _NVLS_DTYPES
 
+    def _nvls_preferred(self, nbytes: int) -> bool:
+        """Whether ``auto`` should use the switch for a message of ``nbytes``."""
+        return self.world_size >= NVLS_MIN_WORLD and nbytes >= NVLS_MIN_BYTES
+
     def scratch_zeros(self, numel: int, dtype: torch.dtype) -> torch.Tensor:
         """A zeroed tensor inside the staging buffer's tail is not safe to hand out
         (collectives reuse it), so scratch is ordinary device memory."""
@@ -357,7 +366,7 @@ class DeviceComm:
         # the switch reads the tensor's own type: a narrower wire needs the peer kernels
         nvls_ok = self._nvls_sum_ok(tensor, op) and not (wire_bf16 and tensor.dtype != torch.bfloat16)
         if algorithm == "auto":
-            if nvls_ok and (nbytes >= NVLS_MIN_BYTES or self.impl.is_nvls(tensor)):
+            if nvls_ok and (self._nvls_preferred(nbytes) or self.impl.is_nvls(tensor)):
                 algorithm = "nvls"
             else:
                 algorithm = "one_shot" if nbytes <= ONE_SHOT_MAX_BYTES else "two_shot"
@@ -406,7 +415,7 @@ class DeviceComm:
             return out.mul_(scale) if scale != 1.0 else out
         nbytes = flat.numel() * flat.element_size()
         nvls = _pick(algorithm, self._nvls_sum_ok(flat, op) and (out.numel() * out.element_size()) % 16 == 0,
-                     nbytes >= NVLS_MIN_BYTES or self.impl.is_nvls(flat), "reduce_scatter")
+                     self._nvls_preferred(nbytes) or self.impl.is_nvls(flat), "reduce_scatter")
         if nvls:
             if not self.impl.is_nvls(flat):
                 self._ensure_nvls_staging(nbytes)
@@ -438,6 +447,8 @@ class DeviceComm:
             raise ValueError(f"gradient length {flat_grad.numel()} not divisible by world_size {W}")
         b1, b2 = betas
         nbytes = flat_grad.numel() * flat_grad.element_size()
+        # overlapped with backward: the switch path wins at every world size here
+        # (it leaves the SMs and most of the HBM bandwidth to the compute)
         nvls = (self._nvls_sum_ok(flat_grad, "sum") and flat_grad.dtype != torch.float16
                 and (nbytes // W) % 16 == 0 and (nbytes >= NVLS_MIN_BYTES or self.impl.is_nvls(flat_grad)))
         if nvls:
@@ -476,8 +487,8 @@ class DeviceComm:
             self._ensure_staging(2 * nbytes)
         ev = self._record("all_reduce_adamw", "nvls" if nvls else "two_shot", nbytes)
         try:
-            nb = blocks or ((NVLS_BESIDE_BLOCKS if beside_compute else NVLS_BLOCKS) if nvls
-                            else (BESIDE_BLOCKS if beside_compute else MAX_BLOCKS))
+            # the optimizer's state traffic and arithmetic ride along: one small CTA per SM
+            nb = blocks or (BESIDE_BLOCKS if beside_compute else MAX_BLOCKS)
             self.impl.all_reduce_adamw(grad_bucket, param_bucket, state["master"], state["m"], state["v"], float(lr),
                                        float(b1), float(b2), float(eps), float(weight_decay), 1.0 - b1 ** step,
                                        1.0 - b2 ** step, float(scale), -nb if beside_compute else nb)
@@ -493,7 +504,7 @@ class DeviceComm:
             out.view(-1).copy_(shard.reshape(-1))
             return out
         nbytes = shard.numel() * shard.element_size()
-        nvls = _pick(algorithm, self.nvls and nbytes % 16 == 0, nbytes * W >= NVLS_MIN_BYTES, "all_gather")
+        nvls = _pick(algorithm, self.nvls and nbytes % 16 == 0, self._nvls_preferred(nbytes * W), "all_gather")
         if nvls:
             self._ensure_nvls_staging(nbytes * W)
         else:
@@ -512,7 +523,7 @@ class DeviceComm:
         if self.world_size == 1:
             return tensor
         nbytes = tensor.numel() * tensor.element_size()
-        nvls = _pick(algorithm, self.nvls and nbytes % 16 == 0, nbytes >= NVLS_MIN_BYTES, "broadcast")
+        nvls = _pick(algorithm, self.nvls and nbytes % 16 == 0, self._nvls_preferred(nbytes), "broadcast")
         if nvls:
             self._ensure_nvls_staging(nbytes)
         else:

@@ -366,9 +366,13 @@ def _ddp_fused_optimizer(pg) -> str:
             assert ddp.unbucketed_parameters() == []
             st = ddp.optimizer_state_dict()
             assert st["step"] == 3 and len(st["buckets"]) == len(ddp._buckets)
+    # Adam's first steps move an element by about lr whatever its gradient's size,
+    # so a near-zero gradient whose sign flips under bf16 rounding (the fused
+    # kernel does not round the reduced gradient to bf16) moves that element by
+    # 2 lr: compare whole tensors by relative norm, not element by element.
     for name, a in finals[0].items():
-        err = (a - finals[1][name]).abs().max().item()
-        assert err <= 1e-2 * (a.abs().max().item() + 1e-3), (name, err)
+        rel = ((a - finals[1][name]).norm() / (a.norm() + 1e-12)).item()
+        assert rel <= 2e-2, (name, rel)
     flat = torch.cat([t.reshape(-1) for t in finals[1].values()])
     everyone = C.all_gather(pg, flat)
     assert all(torch.equal(o, everyone[0]) for o in everyone)  # identical replicas
