@@ -64,7 +64,9 @@
 #include <cudaTypedefs.h>
 #include <torch/extension.h>
 
+#include <cstdlib>
 #include <mutex>
+#include <string>
 
 #include "common.cuh"
 #include "peer.cuh"
@@ -1126,10 +1128,22 @@ void gemm(torch::Tensor a, torch::Tensor b, torch::Tensor out, bool a_mn, bool b
     launch_gemm<BNV, AM, BMJ, ST>(ma, mb, mo, mx, args, units, stream);    \
   } else
   const bool gelu_out = (args.epi & kEpiGelu) != 0;
+  // TMA-store epilogues of K-major-A GEMMs can trade one pipeline stage for a
+  // second staging box per epilogue warp (double-buffered stores): chosen by
+  // MNB_GEMM_STAGES=3 (measured A/B switch; 4 stages by default).
+  static const bool three_stage = [] {
+    const char* e = std::getenv("MNB_GEMM_STAGES");
+    return e != nullptr && std::string(e) == "3";
+  }();
   if (gelu_out) {
     TORCH_CHECK(!a_mn && !b_mn, "the GELU epilogue is for the forward (K-major) layout");
     if (BN == 256) launch_gemm<256, false, false, 3>(ma, mb, mo, mx, args, units, stream);
     else launch_gemm<128, false, false, 3>(ma, mb, mo, mx, args, units, stream);
+  } else if (three_stage && args.tma_out && !a_mn) {
+    if (BN == 256 && !b_mn) launch_gemm<256, false, false, 3>(ma, mb, mo, mx, args, units, stream);
+    else if (BN == 256) launch_gemm<256, false, true, 3>(ma, mb, mo, mx, args, units, stream);
+    else if (!b_mn) launch_gemm<128, false, false, 3>(ma, mb, mo, mx, args, units, stream);
+    else launch_gemm<128, false, true, 3>(ma, mb, mo, mx, args, units, stream);
   } else
   MNB_GEMM_CASE(256, false, false, 4)
   MNB_GEMM_CASE(256, false, true, 4)
