@@ -50,8 +50,12 @@ from . import collectives as _hostc
 from .errors import CollectiveTimeoutError, DeviceCommError
 from .utils import nvtx as _nvtx
 
-#: Below this many bytes ``auto`` uses the one-shot all-reduce.
-ONE_SHOT_MAX_BYTES = int(os.environ.get("MINI_NCCL_ONE_SHOT_MAX_BYTES", 512 << 10))
+#: Up to this many bytes ``auto`` uses the one-shot all-reduce (when NVLS is
+#: not chosen).  Measured cut-over against the two-shot kernel on a
+#: non-symmetric buffer: one-shot is ahead through 8 MiB and behind from
+#: 16 MiB on, at W = 2 (results/collectives_w2.csv) and at W = 8
+#: (results/collectives_w8_bf16.csv).
+ONE_SHOT_MAX_BYTES = int(os.environ.get("MINI_NCCL_ONE_SHOT_MAX_BYTES", 8 << 20))
 #: Initial staging buffer per rank (grows on demand, collectively).
 STAGING_BYTES = int(os.environ.get("MINI_NCCL_STAGING_BYTES", 64 << 20))
 #: CTAs a collective may use (the device meaning of "channels").  Bandwidth
