@@ -7,9 +7,9 @@
 
 For every op (all_reduce per algorithm, reduce_scatter, all_gather,
 broadcast, all_to_all), dtype (fp32, bf16, and fp32 with a bf16 wire) and
-message size (powers of two), each rank times ``--iters`` back-to-back calls
-with CUDA events after ``--warmup`` calls; the reported time is the **max
-over ranks** and bus bandwidth follows nccl-tests
+message size (powers of ``--size-factor``, default 2), each rank times
+``--iters`` back-to-back calls with CUDA events after ``--warmup`` calls;
+the reported time is the **max over ranks** and bus bandwidth follows nccl-tests
 (``busbw = algbw * 2(W-1)/W`` for all-reduce, ``(W-1)/W`` for reduce-scatter,
 all-gather and all-to-all, ``1`` for broadcast).  Messages are larger than L2
 above 128 MiB; below that the same buffer is reused (as nccl-tests does).
@@ -54,6 +54,7 @@ def main() -> None:
     ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
     ap.add_argument("--min-bytes", type=int, default=4096)
     ap.add_argument("--max-bytes", type=int, default=1 << 30)
+    ap.add_argument("--size-factor", type=int, default=2, help="ratio of consecutive message sizes")
     ap.add_argument("--iters", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--ops", default="all_reduce,reduce_scatter,all_gather,broadcast,all_to_all")
@@ -193,7 +194,7 @@ def main() -> None:
                         o = torch.empty_like(x)
                         record(op, "nccl", "nccl", dname, size, time_it(lambda: dist.all_to_all_single(o, x)))
             del x
-        size *= 2
+        size *= args.size_factor
     pg.device_comm().synchronize()
     if rank == 0 and args.out:
         Path(args.out).parent.mkdir(parents=True, exist_ok=True)

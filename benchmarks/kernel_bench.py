@@ -64,6 +64,7 @@ def main() -> None:
     ap.add_argument("--k", type=int, default=768)
     ap.add_argument("--layout", choices=["tn", "dgrad", "wgrad"], default="tn")
     ap.add_argument("--epi", choices=["none", "bias", "gelu", "gelu_grad", "resid"], default="none")
+    ap.add_argument("--splits", type=int, default=0, help="GEMM split-K factor (0: the library's choice)")
     ap.add_argument("--b", type=int, default=16)
     ap.add_argument("--h", type=int, default=12)
     ap.add_argument("--t", type=int, default=1024)
@@ -99,6 +100,8 @@ def main() -> None:
             kw["gelu_grad_aux"] = r(M, N)
         elif args.epi == "resid":
             kw["resid"] = r(M, N)
+        if args.splits > 0:
+            kw["splits"] = args.splits
         fn = lambda: K.gemm(a, b, out, **kw)  # noqa: E731
         flops = 2.0 * M * N * Kd
     elif args.kernel in ("attn_fwd", "attn_bwd"):

@@ -48,22 +48,27 @@ MNB_DEVICE float fast_exp2(float x) {
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
   return y;
 }
-// 2^x for x <= 0 on the FMA pipe, to take part of the softmax's
-// exponentials off the MUFU unit (the forward's bottleneck): x = n + f with
-// n = floor(x), f in [0, 1); 2^f from the cubic 1 + f + f (f - 1)(a + b f),
-// exact at f = 0 and 1 so the pieces join, with a and b a least-squares fit
-// of 2^f on [0, 1] weighted for relative error (computed for this library:
-// maximum relative error 1.1e-4, under bf16's half-ulp of 2^-9); 2^n by adding
-// n to the exponent field.  Inputs below -126 give 2^-126 (the probabilities
-// are rounded to bf16 next, where such values are zero for practical purposes).
+// 2^x for x <= 0 on the FMA and integer pipes, to take part of the
+// softmax's exponentials off the MUFU unit (the forward's bottleneck).
+// x = n + f with n = round(x) (adding and subtracting 1.5 * 2^23 rounds to
+// the nearest integer in plain float adds; the integer is read off the sum's
+// low mantissa bits) and f in [-1/2, 1/2]; 2^f from the cubic
+// 1 + c1 f + c2 f^2 + c3 f^3 with c1..c3 an iteratively reweighted least-
+// squares fit of 2^f on [-1/2, 1/2] for relative error (computed for this
+// library: maximum relative error 1.0e-4, under bf16's half-ulp of 2^-9);
+// 2^n by adding n to the exponent field.  Inputs below -126 give about
+// 2^-126 (the probabilities are rounded to bf16 next).
 MNB_DEVICE float exp2_poly(float x) {
-  constexpr float c1 = 0.6955020102552258f, c2 = 0.22626981564297854f, c3 = 0.07822817410179568f;
+  constexpr float c1 = 0.6932827186256372f, c2 = 0.2422078019971109f, c3 = 0.055007628266016344f;
+  constexpr float kRound = 12582912.0f;  // 1.5 * 2^23
   x = fmaxf(x, -126.f);
-  const float n = floorf(x);
-  const float f = x - n;
+  const float t = x + kRound;
+  const int n = __float_as_int(t) - 0x4B400000;
+  const float f = x - (t - kRound);
   const float p = fmaf(fmaf(fmaf(c3, f, c2), f, c1), f, 1.0f);
-  return __int_as_float(__float_as_int(p) + (static_cast<int>(n) << 23));
+  return __int_as_float(__float_as_int(p) + (n << 23));
 }
+
 MNB_DEVICE void softmax_barrier() { asm volatile("bar.sync 1, %0;" ::"n"(kSoftThreads) : "memory"); }
 
 template <int D, int KV_STAGES>
@@ -358,10 +363,14 @@ __global__ void __launch_bounds__(kThreads, D == 64 ? 2 : 1)
 // into a [B, T, C] fp32 accumulator by TMA reduce-add (the adds run at L2, the
 // compute warps do not wait for them); dK and dV are written once at the end.
 // For D = 64 dQ has its own TMEM columns, so dP^T of the next query tile does
-// not wait for dQ to be read out.  Warp roles as in the forward (producer,
-// MMA, 8 compute).
+// not wait for dQ to be read out.  Warp roles: producer, MMA, then PARTS x 4
+// compute warps; compute warp w serves TMEM lanes 32 (w % 4) .. +31 and the
+// column part (w - 2) / 4 of every tile it reads (S^T, dP^T: 128 / PARTS
+// columns; dQ, dK, dV: D / PARTS).  PARTS = 4 puts four warps on each
+// scheduler to hide the TMEM, shared-memory and MUFU latencies of the
+// exponentials and dS; PARTS = 2 needs fewer registers per thread.
 // ===========================================================================
-constexpr int kBwdThreads = 64 + 32 * 8;
+constexpr int bwd_threads(int parts) { return 64 + 128 * parts; }
 
 template <int D, int STAGES>
 struct BwdSmem {
@@ -442,6 +451,11 @@ struct PPSmem {
   static constexpr uint32_t total = bar_off + n_bars * 8 + 16 + 1024;
 };
 
+// kPoly: half of the softmax's exponentials as exp2_poly on the FMA pipe
+// (true), or all of them on MUFU (false).  kPacked: the row max with
+// three-input max and the scaling, row sums and O rescaling in f32x2 pairs
+// (half the instructions; same rounding), or all scalar (the A/B reference).
+template <bool kPoly, bool kPacked>
 __global__ void __launch_bounds__(kPPThreads, 1)
     fa_fwd_pp_kernel(const __grid_constant__ CUtensorMap map_qkv, __nv_bfloat16* __restrict__ o,
                      float* __restrict__ lse, int H, int T, float scale, int* status) {
@@ -588,8 +602,18 @@ __global__ void __launch_bounds__(kPPThreads, 1)
       for (int c = 0; c < D / 32; ++c) {
         float ov[32];
         tmem_ld_32(o_cols + c * 32, ov);
+        if constexpr (kPacked) {
 #pragma unroll
-        for (int i = 0; i < 32; ++i) oacc[c * 32 + i] = fmaf(oacc[c * 32 + i], alpha_prev, ov[i]);
+          for (int i = 0; i < 32; i += 2) {
+            const float2 r = fma2(make_float2(oacc[c * 32 + i], oacc[c * 32 + i + 1]), splat2(alpha_prev),
+                                  make_float2(ov[i], ov[i + 1]));
+            oacc[c * 32 + i] = r.x;
+            oacc[c * 32 + i + 1] = r.y;
+          }
+        } else {
+#pragma unroll
+          for (int i = 0; i < 32; ++i) oacc[c * 32 + i] = fmaf(oacc[c * 32 + i], alpha_prev, ov[i]);
+        }
       }
       tc_fence_before();
       mbar_arrive(o_free);
@@ -611,6 +635,9 @@ __global__ void __launch_bounds__(kPPThreads, 1)
 #pragma unroll
           for (int i = 0; i < 32; ++i)
             if (k0 + c * 32 + i <= qrow) mx = fmaxf(mx, sv[i]);
+        } else if constexpr (kPacked) {
+#pragma unroll
+          for (int i = 0; i < 32; i += 2) mx = max3f(mx, sv[i], sv[i + 1]);
         } else {
 #pragma unroll
           for (int i = 0; i < 32; ++i) mx = fmaxf(mx, sv[i]);
@@ -620,6 +647,7 @@ __global__ void __launch_bounds__(kPPThreads, 1)
       const float alpha = m_run == -INFINITY ? 0.f : fast_exp2(m_run - m_new);
       if (j >= 1 && !(ok = __all_sync(0xffffffffu, mbar_wait(p_free, (j - 1) & 1, status)))) break;
       float rs = 0.f;
+      float2 rs2 = make_float2(0.f, 0.f);
 #pragma unroll 1
       for (int c = 0; c < 4; ++c) {
         float sv[32];
@@ -627,14 +655,27 @@ __global__ void __launch_bounds__(kPPThreads, 1)
         uint32_t w[16];
 #pragma unroll
         for (int i = 0; i < 32; i += 2) {
-          // half of the exponentials on MUFU, half as a polynomial on the FMA pipe
-          float p0 = fast_exp2(fmaf(sv[i], sl2, -m_new));
-          float p1 = exp2_poly(fmaf(sv[i + 1], sl2, -m_new));
+          float x0, x1;
+          if constexpr (kPacked) {
+            const float2 xs = fma2(make_float2(sv[i], sv[i + 1]), splat2(sl2), splat2(-m_new));
+            x0 = xs.x;
+            x1 = xs.y;
+          } else {
+            x0 = fmaf(sv[i], sl2, -m_new);
+            x1 = fmaf(sv[i + 1], sl2, -m_new);
+          }
+          // with kPoly, every second exponential as a polynomial on the FMA pipe
+          float p0 = fast_exp2(x0);
+          float p1 = kPoly ? exp2_poly(x1) : fast_exp2(x1);
           if (masked) {
             if (k0 + c * 32 + i > qrow) p0 = 0.f;
             if (k0 + c * 32 + i + 1 > qrow) p1 = 0.f;
           }
-          rs += p0 + p1;
+          if constexpr (kPacked) {
+            rs2 = add2(rs2, make_float2(p0, p1));
+          } else {
+            rs += p0 + p1;
+          }
           w[i / 2] = pack_bf16x2(p0, p1);
         }
         store_row_words(p_row + (c / 2) * S::tile, x, c % 2, w);
@@ -643,6 +684,7 @@ __global__ void __launch_bounds__(kPPThreads, 1)
       mbar_arrive(s_free);
       fence_async_smem();
       mbar_arrive(p_full);
+      if constexpr (kPacked) rs = rs2.x + rs2.y;
       l_run = l_run * alpha + rs;
       if (j >= 1 && !(ok = fold(j - 1))) break;
       alpha_prev = alpha;
@@ -671,8 +713,8 @@ __global__ void __launch_bounds__(kPPThreads, 1)
   }
 }
 
-template <int D, int STAGES>
-__global__ void __launch_bounds__(kBwdThreads, 1)
+template <int D, int STAGES, int PARTS>
+__global__ void __launch_bounds__(bwd_threads(PARTS), 1)
     fa_bwd_tc_kernel(const __grid_constant__ CUtensorMap map_qkv, const __grid_constant__ CUtensorMap map_do,
                      const __grid_constant__ CUtensorMap map_dq, const float* __restrict__ lse,
                      const float* __restrict__ delta, __nv_bfloat16* __restrict__ dqkv, int H, int T, float scale,
@@ -681,6 +723,14 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
   constexpr uint32_t kTmemCols = 512;
   constexpr bool kOwnDq = 128 + 128 + 3 * D <= 512;  // dQ in its own columns (D = 64)
   constexpr bool kAhead = kOwnDq && STAGES >= 2;      // next tile's S issued before this tile's dK / dQ
+  constexpr int kCompute = 128 * PARTS;                // compute threads
+  constexpr int kSCols = 128 / PARTS;                  // S^T / dP^T columns of one part
+  constexpr int kDCols = D / PARTS;                    // dQ / dK / dV columns of one part
+  constexpr int kFill = kDCols < 32 ? kDCols : 32;     // dQ columns per staging-box fill
+  constexpr int kPerBox = 32 / kFill;                  // parts sharing one [128 x 32] fp32 box
+  static_assert(PARTS == 2 || PARTS == 4, "two or four column parts");
+  static_assert(kSCols % 32 == 0 && kDCols % 16 == 0, "whole TMEM loads");
+  static_assert(PARTS / kPerBox == 2, "two dQ staging boxes");
   constexpr uint32_t kIdSq = idesc_bf16(128, 128, false, false);  // S^T, dP^T
   constexpr uint32_t kIdKV = idesc_bf16(128, D, false, true);     // dV, dK
   constexpr uint32_t kIdQ = idesc_bf16(128, D, true, true);       // dQ
@@ -694,7 +744,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
                  p_free = b0 + 40, ds_full = b0 + 48, ds_free = b0 + 56, dq_full = b0 + 64, dq_free = b0 + 72,
                  acc_full = b0 + 80;
   const uint32_t q_full0 = b0 + 96, q_empty0 = q_full0 + 8 * STAGES;
-  const uint32_t stg_free0 = q_empty0 + 8 * STAGES, stg_full0 = stg_free0 + 16;  // [2] each, one per half
+  const uint32_t stg_free0 = q_empty0 + 8 * STAGES, stg_full0 = stg_free0 + 16;  // [2] each, one per dQ staging box
 
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
   const int j = blockIdx.x;  // key tile; j = 0 has the most query tiles, so it starts first
@@ -707,14 +757,14 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
   if (threadIdx.x == 0) {
     mbar_init(kv_full, 1);
     mbar_init(s_full, 1);
-    mbar_init(s_free, 256);
+    mbar_init(s_free, kCompute);
     mbar_init(dp_full, 1);
-    mbar_init(p_full, 256);
+    mbar_init(p_full, kCompute);
     mbar_init(p_free, 1);
-    mbar_init(ds_full, 256);
+    mbar_init(ds_full, kCompute);
     mbar_init(ds_free, 1);
     mbar_init(dq_full, 1);
-    mbar_init(dq_free, 256);
+    mbar_init(dq_free, kCompute);
     mbar_init(acc_full, 1);
     for (int st = 0; st < STAGES; ++st) {
       mbar_init(q_full0 + 8 * st, 1);
@@ -722,7 +772,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     }
     for (int hf = 0; hf < 2; ++hf) {
       mbar_init(stg_free0 + 8 * hf, 1);
-      mbar_init(stg_full0 + 8 * hf, 128);
+      mbar_init(stg_full0 + 8 * hf, 128 * kPerBox);
     }
     fence_mbar_init();
     tma_prefetch_desc(&map_qkv);
@@ -882,19 +932,22 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     }
   } else {
     const int qd = warp & 3;
-    const int half = (warp - 2) / 4;
+    const int part = (warp - 2) / 4;
     const int r = qd * 32 + lane;  // key row (S^T, dP^T, dK, dV) or query row (dQ)
     const uint32_t lane_base = static_cast<uint32_t>(qd * 32) << 16;
     const float sl2 = scale * kLog2e;
     const int x = r % 8;  // swizzle phase of this row
-    const uint32_t p_row = row_base(sbase + S::p_off + half * 16384, r);
-    const uint32_t ds_row = row_base(sbase + S::ds_off + half * 16384, r);
-    const uint32_t dq_box = sbase + S::dq_off + half * 16384, dq_row = row_base(dq_box, r);
-    const uint32_t stg_free = stg_free0 + 8 * half, stg_full = stg_full0 + 8 * half;
-    const bool leader = warp == 2 + 4 * half && lane == 0;  // issues this half's reduces
-    uint32_t uses = 0;  // staging-box uses of this half so far (mbarrier phase)
-    uint32_t pk[32];    // this row of P^T as bf16 pairs: the values the dV MMA reads, reused for dS
+    const int box = part / kPerBox;                       // dQ staging box of this part
+    const int box_chunk = (part % kPerBox) * (kFill / 4);  // first 16-byte chunk of this part in a box row
+    const uint32_t dq_box = sbase + S::dq_off + box * 16384, dq_row = row_base(dq_box, r);
+    const uint32_t stg_free = stg_free0 + 8 * box, stg_full = stg_full0 + 8 * box;
+    const bool leader = warp == 2 + 4 * part && part % kPerBox == 0 && lane == 0;  // issues this box's reduces
+    uint32_t uses = 0;  // staging-box uses so far (mbarrier phase)
+    uint32_t pk[kSCols / 2];  // this row of P^T as bf16 pairs: the values the dV MMA reads, reused for dS
     auto lse_of = [&](int it) { return sbase + S::st_off + (it % STAGES) * S::stage_bytes + 2 * S::tile; };
+    // 32-column group c of this part: its bf16 row in a [128 x 64] swizzled atom
+    auto col_of = [&](int c) { return part * kSCols + c * 32; };
+    auto atom_row = [&](uint32_t off, int col0) { return row_base(sbase + off + (col0 / 64) * 16384, r); };
     // P^T = exp2(S^T * scale * log2e - lse * log2e), causal mask on the diagonal tile
     auto p_phase = [&](int it) -> bool {
       const uint32_t par = it & 1;
@@ -905,20 +958,22 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       const uint32_t st_lse = lse_of(it);  // float[128]
       const bool diag = it == 0;
 #pragma unroll
-      for (int c = 0; c < 2; ++c) {
+      for (int c = 0; c < kSCols / 32; ++c) {
+        const int col0 = col_of(c);
         float sv[32];
-        tmem_ld_32(tS + lane_base + half * 64 + c * 32, sv);
+        tmem_ld_32(tS + lane_base + col0, sv);
 #pragma unroll
         for (int t = 0; t < 32; t += 2) {
-          const int qq = half * 64 + c * 32 + t;
+          const int qq = col0 + t;
           const float2 l2 = ld_shared_f2(st_lse + qq * 4);
-          float p0 = fast_exp2(fmaf(sv[t], sl2, -l2.x * kLog2e));
-          float p1 = fast_exp2(fmaf(sv[t + 1], sl2, -l2.y * kLog2e));
+          const float2 xs = fma2(make_float2(sv[t], sv[t + 1]), splat2(sl2), mul2(l2, splat2(-kLog2e)));
+          float p0 = fast_exp2(xs.x);
+          float p1 = fast_exp2(xs.y);
           if (diag && qq < r) p0 = 0.f;
           if (diag && qq + 1 < r) p1 = 0.f;
           pk[c * 16 + t / 2] = pack_bf16x2(p0, p1);
         }
-        store_row_words(p_row, x, c, pk + c * 16);
+        store_row_words(atom_row(S::p_off, col0), x, (col0 % 64) / 32, pk + c * 16);
       }
       tc_fence_before();
       mbar_arrive(s_free);
@@ -935,18 +990,20 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       tc_fence_after();
       const uint32_t st_dl = lse_of(it) + 512;  // float[128]
 #pragma unroll
-      for (int c = 0; c < 2; ++c) {
+      for (int c = 0; c < kSCols / 32; ++c) {
+        const int col0 = col_of(c);
         float dv[32];
-        tmem_ld_32(tP + lane_base + half * 64 + c * 32, dv);
+        tmem_ld_32(tP + lane_base + col0, dv);
 #pragma unroll
         for (int t = 0; t < 32; t += 2) {
-          const int qq = half * 64 + c * 32 + t;
+          const int qq = col0 + t;
           const float2 pp = unpack_bf16x2(pk[c * 16 + t / 2]);
           const float2 d2 = ld_shared_f2(st_dl + qq * 4);
-          dv[t] = scale * pp.x * (dv[t] - d2.x);
-          dv[t + 1] = scale * pp.y * (dv[t + 1] - d2.y);
+          const float2 ds = mul2(mul2(splat2(scale), pp), sub2(make_float2(dv[t], dv[t + 1]), d2));
+          dv[t] = ds.x;
+          dv[t + 1] = ds.y;
         }
-        store_row_bf16(ds_row, x, c, dv);
+        store_row_bf16(atom_row(S::ds_off, col0), x, (col0 % 64) / 32, dv);
       }
       tc_fence_before();
       fence_async_smem();
@@ -958,24 +1015,33 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     auto flush = [&](int it) -> bool {
       if (!__all_sync(0xffffffffu, mbar_wait(dq_full, it & 1, status))) return false;
       tc_fence_after();
-      float qv[D / 2];
+      float qv[kDCols];
+      if constexpr (kDCols == 16) {
+        tmem_ld_16(tQ + lane_base + part * kDCols, qv);
+      } else {
 #pragma unroll
-      for (int c = 0; c < D / 64; ++c) tmem_ld_32(tQ + lane_base + half * (D / 2) + c * 32, qv + c * 32);
+        for (int c = 0; c < kDCols / 32; ++c) tmem_ld_32(tQ + lane_base + part * kDCols + c * 32, qv + c * 32);
+      }
       tc_fence_before();
       mbar_arrive(dq_free);
 #pragma unroll
-      for (int c = 0; c < D / 64; ++c, ++uses) {
+      for (int f = 0; f < kDCols / kFill; ++f, ++uses) {
         if (leader) {  // the box is free once the previous reduce has read it
           bulk_wait_read<0>();
           mbar_arrive(stg_free);
         }
         if (!__all_sync(0xffffffffu, mbar_wait(stg_free, uses & 1, status))) return false;
-        store_row_f32(dq_row, x, qv + c * 32);
+#pragma unroll
+        for (int k = 0; k < kFill / 4; ++k) {
+          const float* v = qv + f * kFill + 4 * k;
+          st_shared_v4(dq_row + (((box_chunk + k) ^ x) << 4), __float_as_uint(v[0]), __float_as_uint(v[1]),
+                       __float_as_uint(v[2]), __float_as_uint(v[3]));
+        }
         fence_async_smem();
         mbar_arrive(stg_full);
         bool staged = true;
         if (leader && (staged = mbar_wait(stg_full, uses & 1, status))) {
-          tma_reduce_add_2d(&map_dq, dq_box, h * D + half * (D / 2) + c * 32, b * T + (j + it) * 128);
+          tma_reduce_add_2d(&map_dq, dq_box, h * D + box * (kPerBox * kDCols) + f * 32, b * T + (j + it) * 128);
           bulk_commit();
         }
         if (!__all_sync(0xffffffffu, staged)) return false;
@@ -999,16 +1065,20 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     if (ok) {
       tc_fence_after();
       const long long row = static_cast<long long>(b) * T + j * 128 + r;
-      __nv_bfloat16* dk = dqkv + row * 3 * C + C + h * D + half * (D / 2);
+      __nv_bfloat16* dk = dqkv + row * 3 * C + C + h * D + part * kDCols;
       __nv_bfloat16* dv = dk + C;
+      constexpr int kChunk = kDCols < 32 ? kDCols : 32;  // columns per TMEM load
+      constexpr int kPer = kDCols / kChunk;
 #pragma unroll 1
-      for (int g = 0; g < 2 * (D / 64); ++g) {  // dK chunks, then dV chunks
-        const int c = g % (D / 64);
-        float kv[32];
-        tmem_ld_32((g < D / 64 ? tK : tV) + lane_base + half * (D / 2) + c * 32, kv);
-        __nv_bfloat16* dst = (g < D / 64 ? dk : dv) + c * 32;
+      for (int g = 0; g < 2 * kPer; ++g) {  // dK chunks, then dV chunks
+        const int c = g % kPer;
+        float kv[kChunk];
+        const uint32_t src = (g < kPer ? tK : tV) + lane_base + part * kDCols + c * kChunk;
+        if constexpr (kChunk == 16) tmem_ld_16(src, kv);
+        else tmem_ld_32(src, kv);
+        __nv_bfloat16* dst = (g < kPer ? dk : dv) + c * kChunk;
 #pragma unroll
-        for (int t = 0; t < 32; t += 8)
+        for (int t = 0; t < kChunk; t += 8)
           *reinterpret_cast<uint4*>(dst + t) =
               make_uint4(pack_bf16x2(kv[t], kv[t + 1]), pack_bf16x2(kv[t + 2], kv[t + 3]),
                          pack_bf16x2(kv[t + 4], kv[t + 5]), pack_bf16x2(kv[t + 6], kv[t + 7]));
@@ -1047,9 +1117,18 @@ void flash_attn_fwd_tc(torch::Tensor qkv, torch::Tensor o, torch::Tensor lse, in
                                                  status.data_ptr<int>());
   };
   static const bool single = std::getenv("MNB_ATTN_FWD_SINGLE") != nullptr;  // A/B switch for benchmarks
+  // MNB_ATTN_POLY=1: half of the exponentials as exp2_poly (measured 12 %
+  // slower at B16 H12 T1024 D64 than all on MUFU, so off by default)
+  static const bool poly = std::getenv("MNB_ATTN_POLY") != nullptr;
+  static const bool scalar = std::getenv("MNB_ATTN_SCALAR") != nullptr;  // A/B switch: no f32x2 pairs
   if (D == 64 && T % 256 == 0 && !single) {
     grid.x = T / 256;
-    run(fatc::fa_fwd_pp_kernel, fatc::PPSmem::total);
+    if (poly)
+      run(fatc::fa_fwd_pp_kernel<true, true>, fatc::PPSmem::total);
+    else if (scalar)
+      run(fatc::fa_fwd_pp_kernel<false, false>, fatc::PPSmem::total);
+    else
+      run(fatc::fa_fwd_pp_kernel<false, true>, fatc::PPSmem::total);
   } else if (D == 64) {
     run(fatc::fa_fwd_tc_kernel<64, 2>, fatc::Smem<64, 2>::total);
   } else {
@@ -1079,14 +1158,18 @@ void flash_attn_bwd_tc_launch(torch::Tensor qkv, torch::Tensor dout, torch::Tens
   CUtensorMap mdq = make_tma_2d_f32(dq_acc.data_ptr(), C, static_cast<uint64_t>(B) * T, C, 32, 128);
   dim3 grid(T / 128, B * H);
   auto stream = at::cuda::getCurrentCUDAStream();
-  auto run = [&](auto kern, uint32_t smem) {
+  auto run = [&](auto kern, uint32_t smem, int parts) {
     C10_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
-    kern<<<grid, fatc::kBwdThreads, smem, stream>>>(
+    kern<<<grid, fatc::bwd_threads(parts), smem, stream>>>(
         mqkv, mdo, mdq, lse.data_ptr<float>(), delta.data_ptr<float>(),
         reinterpret_cast<__nv_bfloat16*>(dqkv.data_ptr()), H, T, static_cast<float>(scale), status.data_ptr<int>());
   };
-  if (D == 64) run(fatc::fa_bwd_tc_kernel<64, 2>, fatc::BwdSmem<64, 2>::total);
-  else run(fatc::fa_bwd_tc_kernel<128, 1>, fatc::BwdSmem<128, 1>::total);
+  // A/B switch for benchmarks: MNB_ATTN_BWD_PARTS=2 runs the 8-compute-warp kernel at D = 64
+  static const char* parts_env = std::getenv("MNB_ATTN_BWD_PARTS");
+  static const bool two_parts = parts_env != nullptr && parts_env[0] == '2';
+  if (D == 64 && !two_parts) run(fatc::fa_bwd_tc_kernel<64, 2, 4>, fatc::BwdSmem<64, 2>::total, 4);
+  else if (D == 64) run(fatc::fa_bwd_tc_kernel<64, 2, 2>, fatc::BwdSmem<64, 2>::total, 2);
+  else run(fatc::fa_bwd_tc_kernel<128, 1, 2>, fatc::BwdSmem<128, 1>::total, 2);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 

@@ -232,6 +232,20 @@ MNB_DEVICE void tmem_ld_32(uint32_t taddr, float* out) {
   for (int i = 0; i < 32; ++i) out[i] = __uint_as_float(r[i]);
 }
 
+// Load 16 consecutive fp32 columns of this thread's TMEM lane.
+MNB_DEVICE void tmem_ld_16(uint32_t taddr, float* out) {
+  uint32_t r[16];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
+      "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+  for (int i = 0; i < 16; ++i) out[i] = __uint_as_float(r[i]);
+}
+
 // 64 consecutive fp32 columns of this thread's TMEM lane with a single wait
 // (one load instruction instead of two dependent x32 round trips).
 MNB_DEVICE void tmem_ld_64(uint32_t taddr, float* out) {
@@ -295,8 +309,6 @@ __host__ __device__ constexpr uint32_t idesc_bf16(int m, int n, bool a_mn, bool 
 // ---------------------------------------------------------------------------
 // math
 // ---------------------------------------------------------------------------
-// Exact GELU, x * Phi(x) with Phi the standard normal CDF written through
-// erf; erff and expf are CUDA's own.
 // GELU with the exact (erf) definition, x * Phi(x).  erf is evaluated with
 // Abramowitz & Stegun, Handbook of Mathematical Functions, formula 7.1.26:
 //   erf(z) = 1 - (a1 t + a2 t^2 + a3 t^3 + a4 t^4 + a5 t^5) exp(-z^2),
@@ -329,6 +341,74 @@ MNB_DEVICE float normal_cdf_as(float x, float* e_out) {
 MNB_DEVICE float gelu_exact(float x) {
   float e;
   return x * normal_cdf_as(x, &e);
+}
+
+// Packed fp32 pairs: sm_100's f32x2 add / mul / fma do two lanes' worth of
+// fp32 math in one instruction (same IEEE rounding as two scalar ops).
+MNB_DEVICE uint64_t f2_bits(float2 a) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(a.x), "f"(a.y));
+  return r;
+}
+MNB_DEVICE float2 f2_of(uint64_t r) {
+  float2 a;
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(a.x), "=f"(a.y) : "l"(r));
+  return a;
+}
+MNB_DEVICE float2 add2(float2 a, float2 b) {
+  uint64_t d;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(f2_bits(a)), "l"(f2_bits(b)));
+  return f2_of(d);
+}
+MNB_DEVICE float2 mul2(float2 a, float2 b) {
+  uint64_t d;
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(f2_bits(a)), "l"(f2_bits(b)));
+  return f2_of(d);
+}
+MNB_DEVICE float2 fma2(float2 a, float2 b, float2 c) {
+  uint64_t d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(f2_bits(a)), "l"(f2_bits(b)), "l"(f2_bits(c)));
+  return f2_of(d);
+}
+MNB_DEVICE float2 sub2(float2 a, float2 b) {
+  uint64_t d;
+  asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(f2_bits(a)), "l"(f2_bits(b)));
+  return f2_of(d);
+}
+MNB_DEVICE float2 splat2(float a) { return make_float2(a, a); }
+// max of three floats in one instruction (sm_100)
+MNB_DEVICE float max3f(float a, float b, float c) {
+  float d;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
+}
+
+// normal_cdf_as on a pair, the polynomial and products in f32x2; the same
+// formula and rounding as the scalar version except that the polynomial's
+// sign is folded into its coefficients (exact).
+MNB_DEVICE float2 normal_cdf_as2(float2 x, float2* e_out) {
+  const float2 z = mul2(make_float2(fabsf(x.x), fabsf(x.y)), splat2(0.70710678118654752f));
+  const float2 d = fma2(splat2(0.3275911f), z, splat2(1.0f));
+  const float2 t = make_float2(rcp_approx(d.x), rcp_approx(d.y));
+  float2 q = fma2(t, splat2(-1.061405429f), splat2(1.453152027f));
+  q = fma2(t, q, splat2(-1.421413741f));
+  q = fma2(t, q, splat2(0.284496736f));
+  q = fma2(t, q, splat2(-0.254829592f));
+  const float2 negpoly = mul2(t, q);  // -(a1 t + ... + a5 t^5)
+  const float2 w = mul2(z, mul2(z, splat2(-1.4426950408889634f)));
+  const float2 e = make_float2(ex2_approx(w.x), ex2_approx(w.y));
+  const float2 erf_abs = fma2(negpoly, e, splat2(1.0f));
+  *e_out = e;
+  return fma2(erf_abs, make_float2(copysignf(0.5f, x.x), copysignf(0.5f, x.y)), splat2(0.5f));
+}
+MNB_DEVICE float2 gelu_exact2(float2 x) {
+  float2 e;
+  return mul2(x, normal_cdf_as2(x, &e));
+}
+MNB_DEVICE float2 gelu_grad2(float2 x) {
+  float2 e;
+  const float2 cdf = normal_cdf_as2(x, &e);
+  return fma2(mul2(x, splat2(0.3989422804014327f)), e, cdf);
 }
 // d/dx [x * Phi(x)] = Phi(x) + x * phi(x), phi(x) = exp(-x^2 / 2) / sqrt(2 pi).
 MNB_DEVICE float gelu_grad(float x) {

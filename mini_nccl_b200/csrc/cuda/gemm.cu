@@ -421,8 +421,9 @@ MNB_DEVICE void apply_inputs_fast(const GemmArgs& a, const EpiPrefetch& f, int k
       const int c = 32 * k + 2 * jp;
       const uint32_t word = ((c % vpl) / 2 == 0) ? f.bias.x : f.bias.y;
       const float2 b2 = unpack_bf16x2(__shfl_sync(0xffffffffu, word, c / vpl));
-      v[2 * jp] += b2.x;
-      v[2 * jp + 1] += b2.y;
+      const float2 r = add2(make_float2(v[2 * jp], v[2 * jp + 1]), b2);
+      v[2 * jp] = r.x;
+      v[2 * jp + 1] = r.y;
     }
   }
   if (a.epi & (kEpiResid | kEpiGeluGrad)) {
@@ -432,13 +433,10 @@ MNB_DEVICE void apply_inputs_fast(const GemmArgs& a, const EpiPrefetch& f, int k
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
         const float2 x = unpack_bf16x2(ws[j]);
-        if (a.epi & kEpiResid) {
-          v[8 * i + 2 * j] += x.x;
-          v[8 * i + 2 * j + 1] += x.y;
-        } else {
-          v[8 * i + 2 * j] *= gelu_grad(x.x);
-          v[8 * i + 2 * j + 1] *= gelu_grad(x.y);
-        }
+        const float2 cur = make_float2(v[8 * i + 2 * j], v[8 * i + 2 * j + 1]);
+        const float2 r = (a.epi & kEpiResid) ? add2(cur, x) : mul2(cur, gelu_grad2(x));
+        v[8 * i + 2 * j] = r.x;
+        v[8 * i + 2 * j + 1] = r.y;
       }
     }
   }
@@ -883,7 +881,11 @@ __global__ void __launch_bounds__(gemm_threads<FUSE>(), 1)
             if (gelu) {
               stage_row32(box_aux, lane, sub, v);  // pre-activation
 #pragma unroll
-              for (int i = 0; i < 32; ++i) v[i] = gelu_exact(v[i]);
+              for (int i = 0; i < 32; i += 2) {
+                const float2 g = gelu_exact2(make_float2(v[i], v[i + 1]));
+                v[i] = g.x;
+                v[i + 1] = g.y;
+              }
             }
             stage_row32(bo, lane, sub, v);
           }

@@ -87,14 +87,36 @@ def supports_gemm(x: torch.Tensor, w: torch.Tensor) -> bool:
     )
 
 
+# Split-K cost model: one 128 x BN x 64 k-block of MMAs on one SM at the
+# sustained bf16 rate, and the reduction pass reading every fp32 partial slice.
+_SUSTAINED_FLOPS = 1.36e15
+_HBM_BYTES_PER_S = 6.5e12
+
+
 def _splits_for(m: int, n: int, k: int) -> int:
-    """Split-K factor so small-output / long-K GEMMs still fill the machine."""
+    """Split-K factor for small-output / long-K GEMMs (the weight gradients).
+
+    The persistent kernel runs ``tiles * splits`` work units in waves of
+    NUM_SMS; the split minimising (waves x k-blocks per unit) plus the
+    reduction's reads of the ``splits`` fp32 slices wins.  Counting whole
+    waves matters: 54 output tiles in 3 splits are 162 units, two waves of
+    86 k-blocks, where 5 splits run two waves of 52.
+    """
     bn = 256 if n >= 256 else 128
     tiles = math.ceil(m / 128) * math.ceil(n / bn)
     k_blocks = math.ceil(k / 64)
     if tiles >= NUM_SMS or k_blocks < 16:
         return 1
-    return max(1, min(k_blocks // 8, math.ceil(NUM_SMS / tiles)))
+    kb_seconds = 128 * bn * 64 * 2 / (_SUSTAINED_FLOPS / NUM_SMS)
+    best, best_t = 1, float("inf")
+    for s in range(1, min(32, k_blocks // 4) + 1):
+        per = math.ceil(k_blocks / s)
+        s_eff = math.ceil(k_blocks / per)  # the kernel drops empty splits
+        waves = math.ceil(tiles * s_eff / NUM_SMS)
+        t = waves * per * kb_seconds + (s_eff * m * n * 4 / _HBM_BYTES_PER_S if s_eff > 1 else 0.0)
+        if t < best_t * (1 - 1e-6):
+            best, best_t = s_eff, t
+    return best
 
 
 def gemm(
