@@ -454,7 +454,7 @@ struct PPSmem {
 // kPoly: half of the softmax's exponentials as exp2_poly on the FMA pipe
 // (true), or all of them on MUFU (false).  kPacked: the row max with
 // three-input max and the scaling, row sums and O rescaling in f32x2 pairs
-// (half the instructions; same rounding), or all scalar (the A/B reference).
+// (fewer instructions, same rounding; measured no faster), or all scalar.
 template <bool kPoly, bool kPacked>
 __global__ void __launch_bounds__(kPPThreads, 1)
     fa_fwd_pp_kernel(const __grid_constant__ CUtensorMap map_qkv, __nv_bfloat16* __restrict__ o,
@@ -1120,15 +1120,17 @@ void flash_attn_fwd_tc(torch::Tensor qkv, torch::Tensor o, torch::Tensor lse, in
   // MNB_ATTN_POLY=1: half of the exponentials as exp2_poly (measured 12 %
   // slower at B16 H12 T1024 D64 than all on MUFU, so off by default)
   static const bool poly = std::getenv("MNB_ATTN_POLY") != nullptr;
-  static const bool scalar = std::getenv("MNB_ATTN_SCALAR") != nullptr;  // A/B switch: no f32x2 pairs
+  // MNB_ATTN_PACKED=1: f32x2 pairs in the softmax (measured 1-3 % slower than
+  // scalar at B16 H12 T1024 D64, so off by default)
+  static const bool packed = std::getenv("MNB_ATTN_PACKED") != nullptr;
   if (D == 64 && T % 256 == 0 && !single) {
     grid.x = T / 256;
     if (poly)
-      run(fatc::fa_fwd_pp_kernel<true, true>, fatc::PPSmem::total);
-    else if (scalar)
-      run(fatc::fa_fwd_pp_kernel<false, false>, fatc::PPSmem::total);
-    else
+      run(fatc::fa_fwd_pp_kernel<true, false>, fatc::PPSmem::total);
+    else if (packed)
       run(fatc::fa_fwd_pp_kernel<false, true>, fatc::PPSmem::total);
+    else
+      run(fatc::fa_fwd_pp_kernel<false, false>, fatc::PPSmem::total);
   } else if (D == 64) {
     run(fatc::fa_fwd_tc_kernel<64, 2>, fatc::Smem<64, 2>::total);
   } else {

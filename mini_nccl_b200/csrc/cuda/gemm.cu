@@ -97,6 +97,7 @@ struct GemmArgs {
   long long ldr;
   int epi;
   int tma_out;  // bf16 output (and GELU aux) written through shared memory + TMA store
+  int red_out;  // split-K: fp32 partial tiles added into one workspace by TMA reduce-add
   int* status;
   // fused collectives
   int rows_per_rank;                // M / world (RS: rows each rank owns; AG: rows of each shard)
@@ -305,6 +306,14 @@ MNB_DEVICE void epilogue_store(const GemmArgs& a, int row, int col0, float* v) {
 
 // Write 32 bf16 values (one row segment) as 16-byte chunks sub*4.. of a
 // 32-row x 128-byte box laid out in the 128-byte swizzle (conflict-free).
+// 32 floats -> row `row` of a 32-row x 128-byte fp32 staging box (128-byte swizzle)
+MNB_DEVICE void stage_row_f32(uint8_t* box, int row, const float* v) {
+#pragma unroll
+  for (int k = 0; k < 8; ++k)
+    *reinterpret_cast<float4*>(box + row * 128 + ((k ^ (row & 7)) * 16)) =
+        make_float4(v[4 * k], v[4 * k + 1], v[4 * k + 2], v[4 * k + 3]);
+}
+
 MNB_DEVICE void stage_row32(uint8_t* box, int row, int sub, const float* v) {
 #pragma unroll
   for (int k = 0; k < 4; ++k) {
@@ -897,6 +906,33 @@ __global__ void __launch_bounds__(gemm_threads<FUSE>(), 1)
             bulk_commit();
           }
         }
+      } else if (a.red_out) {
+        // split-K partial sums: 32 x 32 fp32 boxes -> staging -> TMA reduce-add
+        // into the one fp32 workspace (the adds run at L2; rows and columns
+        // past the matrix are clipped by the TMA unit)
+        uint8_t* box = staging + (warp - 2) * (S::boxes * 4096);
+        const int c_end = (half + 1) * (BN / 64);
+#pragma unroll 1
+        for (int c = half * (BN / 64); c < c_end; ++c) {
+          const int col0 = nb * BN + c * 32;
+          if (col0 >= a.N) break;
+          float v[32];
+          tmem_ld_32(lane_addr + c * 32, v);
+          if (c + 1 == c_end || col0 + 32 >= a.N) {
+            tc_fence_before();
+            mbar_arrive(tempty0 + 8 * acc);
+            released = true;
+          }
+          if (lane == 0) bulk_wait_read<0>();  // the box is free once the previous reduce has read it
+          __syncwarp();
+          stage_row_f32(box, lane, v);
+          asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+          __syncwarp();
+          if (lane == 0) {
+            tma_reduce_add_2d(&map_out, smem_u32(box), col0, mb * kBM + q * 32);
+            bulk_commit();
+          }
+        }
       } else {
 #pragma unroll 1
         for (int c = half * (BN / 64); c < (half + 1) * (BN / 64); ++c) {
@@ -1096,14 +1132,18 @@ void gemm(torch::Tensor a, torch::Tensor b, torch::Tensor out, bool a_mn, bool b
   args.k_blocks_per_split = per;
   args.splits = static_cast<int>(splits);
   if (splits > 1) {
-    TORCH_CHECK(workspace.has_value() && workspace->scalar_type() == at::kFloat &&
-                    workspace->numel() >= splits * static_cast<int64_t>(M) * N,
-                "split-K needs an fp32 workspace of splits*M*N");
+    // every split adds its partial tiles into one zeroed fp32 workspace (TMA
+    // reduce-add); a conversion pass writes the output
+    TORCH_CHECK(workspace.has_value() && workspace->scalar_type() == at::kFloat && workspace->is_contiguous() &&
+                    workspace->numel() >= static_cast<int64_t>(M) * N,
+                "split-K needs a contiguous fp32 workspace of M*N");
     TORCH_CHECK(!(args.epi & ~(kEpiAccum | kEpiOutF32)), "split-K supports plain/accumulate epilogues only");
+    TORCH_CHECK(N % 4 == 0, "split-K needs N % 4 == 0 (16-byte workspace rows)");
     args.out = workspace->data_ptr();
     args.ldo = N;
-    args.split_stride = static_cast<long long>(M) * N;
+    args.split_stride = 0;
     args.epi = kEpiOutF32;
+    args.red_out = 1;
   } else {
     args.out = out.data_ptr();
     args.ldo = out.stride(0);
@@ -1120,11 +1160,14 @@ void gemm(torch::Tensor a, torch::Tensor b, torch::Tensor out, bool a_mn, bool b
   // bf16 outputs without read-modify-write go through the TMA-store epilogue
   args.tma_out = (splits == 1 && !out_f32 && !(args.epi & kEpiAccum)) ? 1 : 0;
   CUtensorMap mo = ma, mx = ma;  // placeholders when unused (never dereferenced)
+  cudaStream_t stream = at::cuda::getCurrentCUDAStream();
   if (args.tma_out) {
     mo = make_tma_2d_bf16(out.data_ptr(), N, M, out.stride(0), 64, 32);
     if (args.epi & kEpiGelu) mx = make_tma_2d_bf16(aux->data_ptr(), N, M, args.ldaux, 64, 32);
+  } else if (args.red_out) {
+    mo = make_tma_2d_f32(workspace->data_ptr(), N, M, N, 32, 32);
+    C10_CUDA_CHECK(cudaMemsetAsync(workspace->data_ptr(), 0, static_cast<size_t>(M) * N * sizeof(float), stream));
   }
-  cudaStream_t stream = at::cuda::getCurrentCUDAStream();
 #define MNB_GEMM_CASE(BNV, AM, BMJ, ST)                                   \
   if (BN == BNV && a_mn == AM && b_mn == BMJ) {                            \
     launch_gemm<BNV, AM, BMJ, ST>(ma, mb, mo, mx, args, units, stream);    \
@@ -1161,7 +1204,7 @@ void gemm(torch::Tensor a, torch::Tensor b, torch::Tensor out, bool a_mn, bool b
     const int threads = 256;
     const int blocks = static_cast<int>(std::min<long long>((total4 + threads - 1) / threads, 148LL * 8));
     splitk_reduce_kernel<<<blocks, threads, 0, stream>>>(
-        reinterpret_cast<const float*>(workspace->data_ptr()), static_cast<int>(splits),
+        reinterpret_cast<const float*>(workspace->data_ptr()), 1,
         static_cast<long long>(M) * N, M, N, out.data_ptr(), out.stride(0), out_f32 ? 1 : 0,
         (epi & kEpiAccum) ? 1 : 0);
     C10_CUDA_KERNEL_LAUNCH_CHECK();

@@ -26,10 +26,13 @@ Replaces the reference's pinned-host staging path (mini_nccl/device.py:
    place; other tensors go through an NVLS staging buffer.
 
 Algorithm names: ``auto`` picks ``one_shot`` for small messages (one round of
-peer stores; lowest latency), ``nvls`` for sum reductions of fp32 / bf16 /
-fp16 from :data:`NVLS_MIN_BYTES` on (and always for tensors that live in NVLS
-memory), and ``two_shot`` (reduce-scatter + all-gather by peer stores) for
-the rest above :data:`ONE_SHOT_MAX_BYTES`.  ``ring``, ``tree``, ``halving``
+peer stores; lowest latency), ``nvls`` for sum all-reduces of fp32 / bf16 /
+fp16 from :data:`NVLS_MIN_BYTES` on at :data:`NVLS_MIN_WORLD` ranks or more
+(and always for tensors that live in NVLS memory), and ``two_shot``
+(reduce-scatter + all-gather by peer stores) for the rest above
+:data:`ONE_SHOT_MAX_BYTES`.  Reduce-scatter, all-gather and broadcast take
+the switch only for tensors already in multicast memory: on other tensors
+the staging copy leaves the direct peer-store kernels ahead.  ``ring``, ``tree``, ``halving``
 and ``naive`` run the reference's schedules step by step over peer memory
 (for parity and the narrow-wire precision study).  The cut-over sizes come
 from the measured sweep in ``results/`` (``benchmarks/bench_collectives.py``)
@@ -65,8 +68,10 @@ MAX_BLOCKS = int(os.environ.get("MINI_NCCL_DEVICE_BLOCKS", 255))
 BESIDE_BLOCKS = int(os.environ.get("MINI_NCCL_BESIDE_BLOCKS", 148))
 #: NVLS collectives on (where the hardware and driver support them).
 NVLS_ENABLED = os.environ.get("MINI_NCCL_NVLS", "1") != "0"
-#: From this many bytes on ``auto`` sends collectives through the switch ...
-NVLS_MIN_BYTES = int(os.environ.get("MINI_NCCL_NVLS_MIN_BYTES", 1 << 20))
+#: From this many bytes on ``auto`` sends all-reduces through the switch ...
+#: (W = 8 sweep, bf16: one-shot ahead at 1 MiB, 30.8 vs 26.6 GB/s busbw; NVLS
+#: ahead at 4 MiB, 99.8 vs 80.0)
+NVLS_MIN_BYTES = int(os.environ.get("MINI_NCCL_NVLS_MIN_BYTES", 2 << 20))
 #: ... on communicators of at least this many ranks.  With W ranks an NVLS
 #: all-reduce moves about (1 + 1/W) x the message per GPU each way against
 #: 2 (W-1)/W for two-shot: at W = 2 that is 1.5 vs 1 and the measured sweep
@@ -418,8 +423,11 @@ class DeviceComm:
             out.copy_(flat)
             return out.mul_(scale) if scale != 1.0 else out
         nbytes = flat.numel() * flat.element_size()
+        # auto: the switch only for an input already in multicast memory; on
+        # other tensors the staging copy makes the direct kernel faster (W = 8
+        # sweep: 488 vs 439 GB/s busbw at 1 GiB, ahead at every size)
         nvls = _pick(algorithm, self._nvls_sum_ok(flat, op) and (out.numel() * out.element_size()) % 16 == 0,
-                     self._nvls_preferred(nbytes) or self.impl.is_nvls(flat), "reduce_scatter")
+                     self.impl.is_nvls(flat), "reduce_scatter")
         if nvls:
             if not self.impl.is_nvls(flat):
                 self._ensure_nvls_staging(nbytes)
@@ -508,7 +516,8 @@ class DeviceComm:
             out.view(-1).copy_(shard.reshape(-1))
             return out
         nbytes = shard.numel() * shard.element_size()
-        nvls = _pick(algorithm, self.nvls and nbytes % 16 == 0, self._nvls_preferred(nbytes * W), "all_gather")
+        # auto: direct (W = 8 sweep: ahead of the switch path at every size)
+        nvls = _pick(algorithm, self.nvls and nbytes % 16 == 0, False, "all_gather")
         if nvls:
             self._ensure_nvls_staging(nbytes * W)
         else:
@@ -527,7 +536,8 @@ class DeviceComm:
         if self.world_size == 1:
             return tensor
         nbytes = tensor.numel() * tensor.element_size()
-        nvls = _pick(algorithm, self.nvls and nbytes % 16 == 0, self._nvls_preferred(nbytes), "broadcast")
+        # auto: direct (W = 8 sweep: ahead of the switch path at every size)
+        nvls = _pick(algorithm, self.nvls and nbytes % 16 == 0, False, "broadcast")
         if nvls:
             self._ensure_nvls_staging(nbytes)
         else:

@@ -98,7 +98,7 @@ def _splits_for(m: int, n: int, k: int) -> int:
 
     The persistent kernel runs ``tiles * splits`` work units in waves of
     NUM_SMS; the split minimising (waves x k-blocks per unit) plus the
-    reduction's reads of the ``splits`` fp32 slices wins.  Counting whole
+    partial tiles' fp32 traffic (reduce-adds into one workspace) wins.  Counting whole
     waves matters: 54 output tiles in 3 splits are 162 units, two waves of
     86 k-blocks, where 5 splits run two waves of 52.
     """
@@ -153,8 +153,8 @@ def gemm(
     if splits is None:
         splits = _splits_for(M, N, K) if (epi & ~EPI_ACCUM) == 0 and bias is None and resid is None else 1
     ws = None
-    if splits > 1:
-        ws = torch.empty(splits * M * N, dtype=torch.float32, device=a.device)
+    if splits > 1:  # the kernel zeroes it and adds every split's partial tiles into it
+        ws = torch.empty(M * N, dtype=torch.float32, device=a.device)
     ext().gemm(a, b, out, a_mn, b_mn, bias, aux, resid, epi, splits, ws, status_word(a.device))
     return out
 

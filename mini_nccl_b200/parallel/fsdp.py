@@ -48,6 +48,7 @@ changed between steps through :attr:`FullyShardedDataParallel.shard_optimizer`.
 
 from __future__ import annotations
 
+import os
 from collections.abc import Iterator
 
 import torch
@@ -58,6 +59,12 @@ from ..communicator import Communicator
 from .ddp import average_gradients
 
 _RELEASED = torch.empty(0)
+
+#: Flatten each unit's gradients into one of two alternating buffers bound to
+#: the NVLS multicast object, so the reduce-scatter (and fused AdamW) reads
+#: them in place through the switch: no zero fill of a fresh buffer and no
+#: copy into a staging buffer.  "0" flattens into ordinary device memory.
+FSDP_NVLS_GRADS = os.environ.get("MINI_NCCL_FSDP_NVLS_GRADS", "1") != "0"
 
 
 class _Unit:
@@ -143,15 +150,27 @@ class _Unit:
     def reduce_scatter_grads(self, grads: tuple[torch.Tensor | None, ...]) -> torch.Tensor:
         """Flatten the unit's gradients, keep this rank's averaged slice."""
         W = self.pg.world_size
-        if self.device.type == "cuda" and W > 1:
-            flat = self.pg.device_comm().scratch_zeros(self.padded_numel, self.dtype)
+        flat = self.owner._grad_buffer(self) if self.owner is not None else None
+        if flat is not None:  # multicast-bound, reused: zero only what no gradient covers
+            at = 0
+            for g, (_, _, _, n) in zip(grads, self.entries, strict=True):
+                if g is None:
+                    flat[at : at + n].zero_()
+                else:
+                    flat[at : at + n].copy_(g.reshape(-1))
+                at += n
+            if at < self.padded_numel:
+                flat[at:].zero_()
         else:
-            flat = torch.zeros(self.padded_numel, dtype=self.dtype, device=self.device)
-        at = 0
-        for g, (_, _, _, n) in zip(grads, self.entries, strict=True):
-            if g is not None:
-                flat[at : at + n].copy_(g.reshape(-1))
-            at += n
+            if self.device.type == "cuda" and W > 1:
+                flat = self.pg.device_comm().scratch_zeros(self.padded_numel, self.dtype)
+            else:
+                flat = torch.zeros(self.padded_numel, dtype=self.dtype, device=self.device)
+            at = 0
+            for g, (_, _, _, n) in zip(grads, self.entries, strict=True):
+                if g is not None:
+                    flat[at : at + n].copy_(g.reshape(-1))
+                at += n
         opt = self.owner.shard_optimizer if self.owner is not None else None
         if opt is not None:
             opt.step_unit(self, flat)
@@ -493,6 +512,28 @@ class FullyShardedDataParallel(nn.Module):
         self._side = None
         self._comm_stream = None
         self._bwd_prefetched: dict[int, torch.cuda.Event] = {}
+        # Two gradient buffers in NVLS memory, used by turns in unit order (the
+        # same on every rank).  Two, because a rank may flatten the next unit
+        # while a slower rank's switch reads of the previous one still run; the
+        # reduce-scatter of unit i+1 starts only once every rank has entered it,
+        # i.e. has finished unit i, so buffer i % 2 is free again by then.
+        self._grad_bufs: list[torch.Tensor] | None = None
+        self._grad_turn = 0
+        dev = self.units[0].device
+        if FSDP_NVLS_GRADS and dev.type == "cuda" and pg.world_size > 1:
+            dc = pg.device_comm()
+            if dc.nvls:
+                nbytes = max(u.padded_numel * u.shard.element_size() for u in self.units)
+                nbytes = -(-nbytes // 16) * 16  # any unit dtype views it whole
+                self._grad_bufs = [dc.symmetric_zeros(nbytes, torch.uint8, nvls=True) for _ in range(2)]
+
+    def _grad_buffer(self, unit: _Unit) -> torch.Tensor | None:
+        """The next NVLS gradient buffer, as ``unit.padded_numel`` of its dtype (or None)."""
+        if self._grad_bufs is None:
+            return None
+        buf = self._grad_bufs[self._grad_turn]
+        self._grad_turn ^= 1
+        return buf.view(unit.dtype)[: unit.padded_numel]
 
     # ---- prefetch (CUDA) -----------------------------------------------------------
 

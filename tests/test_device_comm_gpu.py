@@ -370,8 +370,15 @@ def _ddp_fused_optimizer(pg) -> str:
     # so a near-zero gradient whose sign flips under bf16 rounding (the fused
     # kernel does not round the reduced gradient to bf16) moves that element by
     # 2 lr: compare whole tensors by relative norm, not element by element.
+    # The key third of the QKV bias has an exactly zero gradient (softmax is
+    # invariant to a per-row constant), so its Adam steps follow rounding noise
+    # and it is left out.
+    C = 256
     for name, a in finals[0].items():
-        rel = ((a - finals[1][name]).norm() / (a.norm() + 1e-12)).item()
+        b = finals[1][name]
+        if name.endswith("qkv.bias"):
+            a, b = torch.cat([a[:C], a[2 * C:]]), torch.cat([b[:C], b[2 * C:]])
+        rel = ((a - b).norm() / (a.norm() + 1e-12)).item()
         assert rel <= 2e-2, (name, rel)
     flat = torch.cat([t.reshape(-1) for t in finals[1].values()])
     everyone = C.all_gather(pg, flat)

@@ -108,12 +108,17 @@ def test_gemm_epilogues():
     close(f32, a.float() @ b.float().t(), 1e-3)
 
 
-def test_gemm_split_k_accumulate():
-    gy, x = rnd(8192, 256, seed=12), rnd(8192, 192, seed=13)
-    dw = rnd(256, 192, seed=14)
+@pytest.mark.parametrize("M,N,splits", [(256, 192, 4), (200, 136, 3), (2304, 768, 8)])
+def test_gemm_split_k_accumulate(M, N, splits):
+    # split-K partial tiles are added into one fp32 workspace by TMA reduce-add;
+    # M and N off the tile grid exercise the clipped boxes
+    gy, x = rnd(8192, M, seed=12), rnd(8192, N, seed=13)
+    dw = rnd(M, N, seed=14)
     want = dw.float() + gy.float().t() @ x.float()
-    K.gemm(gy, x, dw, a_mn=True, b_mn=True, accumulate=True, splits=4)
+    K.gemm(gy, x, dw, a_mn=True, b_mn=True, accumulate=True, splits=splits)
     close(dw, want, 1e-2)
+    f32 = K.gemm(gy, x, a_mn=True, b_mn=True, out_dtype=torch.float32, splits=splits)
+    close(f32, gy.float().t() @ x.float(), 1e-3)
 
 
 @pytest.mark.parametrize("rows,C", [(1000, 768), (20000, 768), (5000, 256), (3000, 512), (3000, 1024),
