@@ -373,11 +373,11 @@ def _ddp_fused_optimizer(pg) -> str:
     # The key third of the QKV bias has an exactly zero gradient (softmax is
     # invariant to a per-row constant), so its Adam steps follow rounding noise
     # and it is left out.
-    C = 256
+    width = 256
     for name, a in finals[0].items():
         b = finals[1][name]
         if name.endswith("qkv.bias"):
-            a, b = torch.cat([a[:C], a[2 * C:]]), torch.cat([b[:C], b[2 * C:]])
+            a, b = torch.cat([a[:width], a[2 * width:]]), torch.cat([b[:width], b[2 * width:]])
         rel = ((a - b).norm() / (a.norm() + 1e-12)).item()
         assert rel <= 2e-2, (name, rel)
     flat = torch.cat([t.reshape(-1) for t in finals[1].values()])
