@@ -109,8 +109,10 @@ __global__ void __launch_bounds__(kThreads, D == 64 ? 2 : 1)
                  v_empty0 = k_empty0 + 8 * KV_STAGES;
 
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
-  const int qt = gridDim.x - 1 - blockIdx.x;  // longest causal rows first
-  const int bh = blockIdx.y;
+  // grid (B*H, query tiles), x fastest: every head's longest causal rows are
+  // launched before any head's shorter ones (longest work first over the whole grid)
+  const int qt = gridDim.y - 1 - blockIdx.y;
+  const int bh = blockIdx.x;
   const int b = bh / H, h = bh % H;
   const int q0 = qt * kQ;
   const int C = H * D;
@@ -479,8 +481,8 @@ __global__ void __launch_bounds__(kPPThreads, 1)
   auto v_empty = [&](int st) { return kv0 + 48 + 8 * st; };
 
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
-  const int pair = gridDim.x - 1 - blockIdx.x;  // longest causal rows first
-  const int bh = blockIdx.y;
+  const int pair = gridDim.y - 1 - blockIdx.y;  // longest causal rows of every head first
+  const int bh = blockIdx.x;
   const int b = bh / H, h = bh % H;
   const int q0 = pair * 256;
   const int C = H * D;
@@ -747,8 +749,10 @@ __global__ void __launch_bounds__(bwd_threads(PARTS), 1)
   const uint32_t stg_free0 = q_empty0 + 8 * STAGES, stg_full0 = stg_free0 + 16;  // [2] each, one per dQ staging box
 
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
-  const int j = blockIdx.x;  // key tile; j = 0 has the most query tiles, so it starts first
-  const int bh = blockIdx.y;
+  // grid (B*H, key tiles), x fastest: the key tiles with the most query tiles
+  // (j = 0) of every head are launched first
+  const int j = blockIdx.y;
+  const int bh = blockIdx.x;
   const int b = bh / H, h = bh % H;
   const int C = H * D;
   const int n_q = T / 128;
@@ -1108,7 +1112,7 @@ void flash_attn_fwd_tc(torch::Tensor qkv, torch::Tensor o, torch::Tensor lse, in
   TORCH_CHECK(D == 64 || D == 128, "tcgen05 attention supports head dim 64 or 128");
   c10::cuda::CUDAGuard g(qkv.device());
   CUtensorMap map = make_tma_2d_bf16(qkv.data_ptr(), C3, static_cast<uint64_t>(B) * T, C3, 64, 128);
-  dim3 grid((T + fatc::kQ - 1) / fatc::kQ, B * H);
+  dim3 grid(B * H, (T + fatc::kQ - 1) / fatc::kQ);
   auto stream = at::cuda::getCurrentCUDAStream();
   auto run = [&](auto kern, uint32_t smem) {
     C10_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
@@ -1124,7 +1128,7 @@ void flash_attn_fwd_tc(torch::Tensor qkv, torch::Tensor o, torch::Tensor lse, in
   // scalar at B16 H12 T1024 D64, so off by default)
   static const bool packed = std::getenv("MNB_ATTN_PACKED") != nullptr;
   if (D == 64 && T % 256 == 0 && !single) {
-    grid.x = T / 256;
+    grid.y = T / 256;
     if (poly)
       run(fatc::fa_fwd_pp_kernel<true, false>, fatc::PPSmem::total);
     else if (packed)
@@ -1158,7 +1162,7 @@ void flash_attn_bwd_tc_launch(torch::Tensor qkv, torch::Tensor dout, torch::Tens
   CUtensorMap mdo = make_tma_2d_bf16(dout.data_ptr(), C, static_cast<uint64_t>(B) * T, C, 64, 128);
   TORCH_CHECK(dq_acc.is_contiguous() && dq_acc.numel() == static_cast<int64_t>(B) * T * C, "dq_acc [B, T, C] fp32");
   CUtensorMap mdq = make_tma_2d_f32(dq_acc.data_ptr(), C, static_cast<uint64_t>(B) * T, C, 32, 128);
-  dim3 grid(T / 128, B * H);
+  dim3 grid(B * H, T / 128);
   auto stream = at::cuda::getCurrentCUDAStream();
   auto run = [&](auto kern, uint32_t smem, int parts) {
     C10_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
