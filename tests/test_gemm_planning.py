@@ -36,9 +36,11 @@ def test_qkv_weight_gradient_avoids_a_nearly_empty_second_wave() -> None:
     assert _kblock_time(2304, 768, 16384, _splits_for(2304, 768, 16384)) < _kblock_time(2304, 768, 16384, 3)
 
 
-@pytest.mark.parametrize("m,n,k", [(16384, 2304, 768), (16384, 768, 3072), (50304, 768, 16384),
-                                   (2304, 768, 512)])
+@pytest.mark.parametrize("m,n,k", [(16384, 2304, 768), (16384, 768, 3072), (16384, 768, 2304),
+                                   (16384, 768, 50304), (50304, 768, 16384), (2304, 768, 512)])
 def test_no_split_when_the_grid_is_full_or_k_is_short(m: int, n: int, k: int) -> None:
+    # a full grid stays unsplit even with a ragged last wave: the LM head's data
+    # gradient (16384 x 768 x 50304) measured slower in 5 splits than in one
     assert _splits_for(m, n, k) == 1
 
 
