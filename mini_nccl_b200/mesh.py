@@ -16,6 +16,7 @@ their own peer mappings and signal pads.
 
 from __future__ import annotations
 
+import math
 from collections.abc import Callable, Sequence
 
 import torch
@@ -28,16 +29,15 @@ class SubGroup:
 
     def __init__(self, parent: Communicator, global_ranks: Sequence[int], name: str = "") -> None:
         ranks = list(global_ranks)
-        if len(set(ranks)) != len(ranks):
-            raise ValueError(f"duplicate ranks in subgroup: {ranks}")
+        repeated = sorted({r for r in ranks if ranks.count(r) > 1})
+        if repeated:
+            raise ValueError(f"subgroup {ranks} names ranks {repeated} more than once (duplicate members)")
         if parent.rank not in ranks:
-            raise ValueError(
-                f"rank {parent.rank} is not a member of subgroup {ranks}; "
-                f"build it only on member ranks"
-            )
-        for r in ranks:
-            if not 0 <= r < parent.world_size:
-                raise ValueError(f"rank {r} is outside the parent group of {parent.world_size}")
+            raise ValueError(f"this process (rank {parent.rank}) is not a member of {ranks}: "
+                             "only the members construct a SubGroup")
+        outside = [r for r in ranks if not 0 <= r < parent.world_size]
+        if outside:
+            raise ValueError(f"ranks {outside} are outside the parent group of {parent.world_size}")
         self.parent = parent
         self.name = name
         #: Members in *parent* numbering (what ``SubGroup(parent, ranks)`` was given).
@@ -114,22 +114,18 @@ class ParallelMesh:
     def __init__(self, pg: Communicator, **dims: int) -> None:
         if not dims:
             raise ValueError("give at least one dimension, e.g. ParallelMesh(pg, tp=2)")
-        for name, size in dims.items():
-            if size < 1:
-                raise ValueError(f"dimension {name}={size} must be at least 1")
-        total = 1
-        for size in dims.values():
-            total *= size
-        if total != pg.world_size:
-            raise ValueError(f"mesh {dims} has {total} slots but the group has {pg.world_size} ranks")
+        too_small = {name: size for name, size in dims.items() if size < 1}
+        if too_small:
+            raise ValueError(f"every mesh dimension must be at least 1, got {too_small}")
+        slots = math.prod(dims.values())
+        if slots != pg.world_size:
+            raise ValueError(f"mesh {dims} has {slots} slots but the group has {pg.world_size} ranks")
         self.pg = pg
         self.dims = dict(dims)
         self.names = list(dims)
-        self.strides: dict[str, int] = {}
-        stride = 1
-        for name in reversed(self.names):
-            self.strides[name] = stride
-            stride *= self.dims[name]
+        sizes = list(dims.values())
+        # row-major: a dimension's stride is the product of the sizes after it
+        self.strides: dict[str, int] = {n: math.prod(sizes[i + 1:]) for i, n in enumerate(self.names)}
         self.coords = {n: (pg.rank // self.strides[n]) % self.dims[n] for n in self.names}
         self._groups: dict[str, SubGroup] = {}
 

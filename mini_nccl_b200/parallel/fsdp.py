@@ -48,6 +48,7 @@ changed between steps through :attr:`FullyShardedDataParallel.shard_optimizer`.
 
 from __future__ import annotations
 
+import contextlib
 import os
 from collections.abc import Iterator
 
@@ -380,6 +381,30 @@ class ShardAdamW:
             unit.shard.data.copy_(w)
 
 
+class _RngSnapshot:
+    """The generator states a unit's forward started from, for replaying it.
+
+    ``capture`` records the CPU generator and, for CUDA inputs, the
+    generator of that device; ``replaying()`` is a context in which both are
+    back at the recorded state and after which the caller's streams continue
+    exactly where they were (``fork_rng`` saves and restores them).
+    """
+
+    def __init__(self, device: torch.device) -> None:
+        self.cuda_device = device if device.type == "cuda" else None
+        self.cpu_state = torch.get_rng_state()
+        self.cuda_state = torch.cuda.get_rng_state(device) if self.cuda_device is not None else None
+
+    @contextlib.contextmanager
+    def replaying(self):
+        devices = [self.cuda_device] if self.cuda_device is not None else []
+        with torch.random.fork_rng(devices=devices, enabled=True):
+            torch.set_rng_state(self.cpu_state)
+            if self.cuda_device is not None:
+                torch.cuda.set_rng_state(self.cuda_state, self.cuda_device)
+            yield
+
+
 class _ShardedForward(torch.autograd.Function):
     """Unit forward with gathered parameters; backward recomputes (RNG rewound).
 
@@ -393,10 +418,7 @@ class _ShardedForward(torch.autograd.Function):
     def forward(ctx, unit: _Unit, shard: torch.Tensor, x: torch.Tensor):
         ctx.unit = unit
         ctx.save_for_backward(x, shard)
-        ctx.cpu_rng = torch.get_rng_state()
-        ctx.cuda_dev = x.device if x.is_cuda else None
-        if ctx.cuda_dev is not None:
-            ctx.cuda_rng = torch.cuda.get_rng_state(ctx.cuda_dev)
+        ctx.rng = _RngSnapshot(x.device)
         owner = unit.owner
         flat = owner._take_prefetched(unit) if owner is not None else None
         with torch.no_grad():
@@ -413,21 +435,18 @@ class _ShardedForward(torch.autograd.Function):
     def backward(ctx, grad_y: torch.Tensor):
         x, shard = ctx.saved_tensors
         unit: _Unit = ctx.unit
+        leaf = x.detach().requires_grad_(ctx.needs_input_grad[2])
+        wrt = ([leaf] if leaf.requires_grad else []) + list(unit.params)
         unit.materialize(shard)
         try:
-            devices = [] if ctx.cuda_dev is None else [ctx.cuda_dev]
-            x_in = x.detach().requires_grad_(True)
-            with torch.random.fork_rng(devices=devices, enabled=True):
-                torch.set_rng_state(ctx.cpu_rng)
-                if ctx.cuda_dev is not None:
-                    torch.cuda.set_rng_state(ctx.cuda_rng, ctx.cuda_dev)
-                with torch.enable_grad():
-                    y = unit.module(x_in)
-            grads = torch.autograd.grad(y, [x_in, *unit.params], grad_outputs=grad_y, allow_unused=True)
-            shard_grad = unit.reduce_scatter_grads(grads[1:])
+            with ctx.rng.replaying(), torch.enable_grad():
+                out = unit.module(leaf)
+            got = torch.autograd.grad(out, wrt, grad_outputs=grad_y, allow_unused=True)
+            dx = got[0] if leaf.requires_grad else None
+            shard_grad = unit.reduce_scatter_grads(got[len(wrt) - len(unit.params):])
         finally:
             unit.release()
-        return None, shard_grad, grads[0] if ctx.needs_input_grad[2] else None
+        return None, shard_grad, dx
 
 
 class _UnitWrapper(nn.Module):
