@@ -67,6 +67,7 @@
 #include <cstdlib>
 #include <mutex>
 #include <string>
+#include <type_traits>
 
 #include "common.cuh"
 #include "peer.cuh"
@@ -117,6 +118,7 @@ struct GemmArgs {
   int agw_parts;                            // parts per chunk (the unit of claimed work)
   int agw_pri_first, agw_pri_last;          // chunk range holding B (and its bias): gathered first
   uint32_t* agw_cnt;                        // [world * nch] per-chunk part counts, then the work counter
+  int agw_shallow;                          // 8 loads in flight per gather thread instead of 16 (A/B)
 };
 
 enum : int { kFuseNone = 0, kFuseRS = 1, kFuseAG = 2, kFuseAGW = 3 };
@@ -557,16 +559,22 @@ MNB_DEVICE void agw_gather(const GemmArgs& a, const PeerCtx& ctx, int gt) {
     const long long lo = min(units, part * per), hi = min(units, lo + per);
     const __nv_bfloat16* from = a.agw_src[src] + c0;
     __nv_bfloat16* to = a.agw_flat + static_cast<long long>(src) * a.agw_shard + c0;
-    constexpr int U = 8;
-    for (long long u0 = lo + gt; u0 < hi; u0 += U * kGatherThreads) {
-      uint4 v[U];
+    // U independent 16-byte peer loads in flight per thread: the gather is
+    // bound by NVLink load latency, not by issue (U = 16: 16 KB per CTA)
+    auto copy = [&](auto u_const) {
+      constexpr int U = decltype(u_const)::value;
+      for (long long u0 = lo + gt; u0 < hi; u0 += U * kGatherThreads) {
+        uint4 v[U];
 #pragma unroll
-      for (int j = 0; j < U; ++j)
-        if (u0 + j * kGatherThreads < hi) v[j] = ld_v4_cg_peer(from + 8 * (u0 + j * kGatherThreads));
+        for (int j = 0; j < U; ++j)
+          if (u0 + j * kGatherThreads < hi) v[j] = ld_v4_cg_peer(from + 8 * (u0 + j * kGatherThreads));
 #pragma unroll
-      for (int j = 0; j < U; ++j)
-        if (u0 + j * kGatherThreads < hi) st_v4(to + 8 * (u0 + j * kGatherThreads), v[j]);
-    }
+        for (int j = 0; j < U; ++j)
+          if (u0 + j * kGatherThreads < hi) st_v4(to + 8 * (u0 + j * kGatherThreads), v[j]);
+      }
+    };
+    if (a.agw_shallow) copy(std::integral_constant<int, 8>{});
+    else copy(std::integral_constant<int, 16>{});
     asm volatile("bar.sync 2, %0;" ::"n"(kGatherThreads) : "memory");  // part copied; agw_flag free again
     if (gt == 0) {
       __threadfence();
@@ -1397,6 +1405,8 @@ void gemm_agw(torch::Tensor x, torch::Tensor flat, int64_t w_off, int64_t N, c10
   args.agw_pri_first = chunk_of(w_off);
   args.agw_pri_last = chunk_of(w_off + N * K - 1);
   args.agw_cnt = reinterpret_cast<uint32_t*>(counters.data_ptr());
+  static const bool shallow = std::getenv("MNB_AGW_SHALLOW") != nullptr;  // A/B switch for benchmarks
+  args.agw_shallow = shallow ? 1 : 0;
   cudaStream_t stream = at::cuda::getCurrentCUDAStream();
   C10_CUDA_CHECK(cudaMemsetAsync(counters.data_ptr(), 0, (W * args.agw_nch + 1) * sizeof(uint32_t), stream));
   const int BN = N >= 256 ? 256 : 128;
