@@ -21,7 +21,9 @@ by a barrier and torch.cuda.synchronize() on both sides, max over ranks:
    are already resident on the device;
 2. ``e2e``: wall time of K steps through the public API where every step
    copies that step's inputs from pinned host memory and reads the loss back
-   to the host.
+   to the host.  The synthetic batches are made the way a data loader makes
+   them: batch i+1 is drawn on the CPU while step i runs on the GPU (two
+   pinned buffers per input), the same in every arm.
 
 ``--mode 3d`` runs BASELINE config 5: GPT 32 layers, d_model 4096, 32 heads,
 sequence 2048, on a tp x pp x dp mesh (N=8: 2 x 2 x 2; N=4: 2 x 2 x 1; N=2:
@@ -177,6 +179,36 @@ def batches_on_device(torch, n, B, dev, seed):
     return xs, ys
 
 
+class HostBatches:
+    """Random (x, y) token batches in pinned host memory, one step ahead.
+
+    ``current()`` is this step's pair; ``advance()`` (called once the step's
+    work is enqueued) draws the next pair on the CPU while the GPU runs.  Two
+    buffers per input: the pair being drawn was last copied to the device by
+    the previous step, whose result the caller has already read back.
+    """
+
+    def __init__(self, torch, rows: int, seq: int, vocab: int, seed: int) -> None:
+        self.torch = torch
+        self.vocab = vocab
+        self.gen = torch.Generator().manual_seed(seed)
+        self.bufs = [tuple(torch.empty((rows, seq), dtype=torch.int64).pin_memory() for _ in range(2))
+                     for _ in range(2)]
+        self.turn = 0
+        self._draw(0)
+
+    def _draw(self, k: int) -> None:
+        for t in self.bufs[k]:
+            self.torch.randint(0, self.vocab, t.shape, generator=self.gen, out=t)
+
+    def current(self):
+        return self.bufs[self.turn]
+
+    def advance(self) -> None:
+        self.turn ^= 1
+        self._draw(self.turn)
+
+
 def run_phases(torch, args, step_fn, barrier, reduce_max, dev, clocks: ClockSampler, e2e_step=None):
     """Warm-up, device-timed phase, optional e2e phase.  Returns (ms, e2e_ms, launches)."""
     from mini_nccl_b200.utils import launches
@@ -315,17 +347,16 @@ def run_ours_3d(args):
     def step(i):
         train(xs[i % 2], ys[i % 2])
 
-    hx = torch.empty((n_seq, SEQ), dtype=torch.int64).pin_memory()
-    hy = torch.empty((n_seq, SEQ), dtype=torch.int64).pin_memory()
-    gen = torch.Generator().manual_seed(77 + d)
+    host = HostBatches(torch, n_seq, SEQ, VOCAB, seed=77 + d)
     losses = []
 
     def e2e_step(i):
-        torch.randint(0, VOCAB, (n_seq, SEQ), generator=gen, out=hx)
-        torch.randint(0, VOCAB, (n_seq, SEQ), generator=gen, out=hy)
+        hx, hy = host.current()
         x = hx.to(dev, non_blocking=True) if first else None
         y = hy.to(dev, non_blocking=True) if last else None
-        losses.append(train(x, y))  # the pipeline returns the loss as a host float on the last stage
+        loss = train(x, y)  # the pipeline returns the loss as a host float on the last stage
+        host.advance()
+        losses.append(loss)
 
     def barrier():
         if world > 1:
@@ -404,14 +435,11 @@ def run_ours(args):
             opt.step()
         return loss
 
-    hx = torch.empty((B, SEQ), dtype=torch.int64).pin_memory()
-    hy = torch.empty((B, SEQ), dtype=torch.int64).pin_memory()
-    gen = torch.Generator().manual_seed(77 + rank)
+    host = HostBatches(torch, B, SEQ, VOCAB, seed=77 + rank)
     losses = []
 
     def e2e_step(i):
-        torch.randint(0, VOCAB, (B, SEQ), generator=gen, out=hx)
-        torch.randint(0, VOCAB, (B, SEQ), generator=gen, out=hy)
+        hx, hy = host.current()
         x = hx.to(dev, non_blocking=True)
         y = hy.to(dev, non_blocking=True)
         ddp.zero_grad()
@@ -420,6 +448,7 @@ def run_ours(args):
         ddp.sync()
         if opt is not None:
             opt.step()
+        host.advance()
         losses.append(loss.item())
 
     def barrier():
@@ -517,14 +546,13 @@ def run_reference(args):
     def step(i):
         return train(xs[i % 4], ys[i % 4])
 
-    hx = torch.empty((B, SEQ), dtype=torch.int64).pin_memory()
-    hy = torch.empty((B, SEQ), dtype=torch.int64).pin_memory()
-    gen = torch.Generator().manual_seed(77 + rank)
+    host = HostBatches(torch, B, SEQ, VOCAB, seed=77 + rank)
 
     def e2e_step(i):
-        torch.randint(0, VOCAB, (B, SEQ), generator=gen, out=hx)
-        torch.randint(0, VOCAB, (B, SEQ), generator=gen, out=hy)
-        train(hx.to(dev, non_blocking=True), hy.to(dev, non_blocking=True)).item()
+        hx, hy = host.current()
+        loss = train(hx.to(dev, non_blocking=True), hy.to(dev, non_blocking=True))
+        host.advance()
+        loss.item()
 
     def barrier():
         if pg is not None:
@@ -624,14 +652,13 @@ def run_torch(args):
     def step(i):
         return train(xs[i % 4], ys[i % 4])
 
-    hx = torch.empty((B, SEQ), dtype=torch.int64).pin_memory()
-    hy = torch.empty((B, SEQ), dtype=torch.int64).pin_memory()
-    gen = torch.Generator().manual_seed(77 + rank)
+    host = HostBatches(torch, B, SEQ, VOCAB, seed=77 + rank)
 
     def e2e_step(i):
-        torch.randint(0, VOCAB, (B, SEQ), generator=gen, out=hx)
-        torch.randint(0, VOCAB, (B, SEQ), generator=gen, out=hy)
-        train(hx.to(dev, non_blocking=True), hy.to(dev, non_blocking=True)).item()
+        hx, hy = host.current()
+        loss = train(hx.to(dev, non_blocking=True), hy.to(dev, non_blocking=True))
+        host.advance()
+        loss.item()
 
     def barrier():
         if world > 1:
@@ -864,16 +891,14 @@ def run_torch_3d(args):
     def step(i):
         train(xs[i % 2], ys[i % 2])
 
-    hx = torch.empty((n_seq, SEQ), dtype=torch.int64).pin_memory()
-    hy = torch.empty((n_seq, SEQ), dtype=torch.int64).pin_memory()
-    gen = torch.Generator().manual_seed(77 + d)
+    host = HostBatches(torch, n_seq, SEQ, VOCAB, seed=77 + d)
     final = [0.0]
 
     def e2e_step(i):
-        torch.randint(0, VOCAB, (n_seq, SEQ), generator=gen, out=hx)
-        torch.randint(0, VOCAB, (n_seq, SEQ), generator=gen, out=hy)
+        hx, hy = host.current()
         loss = train(hx.to(dev, non_blocking=True) if s == 0 else None,
                      hy.to(dev, non_blocking=True) if s == pp - 1 else None)
+        host.advance()
         if loss is not None:
             final[0] = float(loss.item())
 
