@@ -194,6 +194,27 @@ def test_flash_attention(B, T, H, D):
     close(qkv.grad, ref_in.grad, 3e-2)
 
 
+@pytest.mark.parametrize("rise", [0.0, 2.0, 8.0])
+def test_flash_attention_forward_with_scores_rising_along_the_keys(rise):
+    """Scores that grow tile after tile exercise the online softmax's rescaling:
+    every key tile raises the running maximum (rise=8: by ~11 log2 units per
+    tile; rise=2: by ~3; rise=0: ordinary scores), so the output accumulated
+    over earlier tiles is rescaled at each step."""
+    B, T, H, D = 2, 1024, 2, 64
+    C = H * D
+    g = torch.Generator(device="cpu").manual_seed(31)
+    q = torch.randn(B, T, H, D, generator=g) * 0.5 + 1.0
+    k = torch.randn(B, T, H, D, generator=g) * 0.5
+    k = k + rise * (torch.arange(T, dtype=torch.float32) / T).view(1, T, 1, 1)
+    v = torch.randn(B, T, H, D, generator=g)
+    qkv = torch.cat([t.reshape(B, T, C) for t in (q, k, v)], -1).to(DEV, torch.bfloat16)
+    y = K.FlashAttention.apply(qkv, H)
+    ref = qkv.float()
+    qr, kr, vr = (t.view(B, T, H, D).transpose(1, 2) for t in ref.split(C, -1))
+    yr = F.scaled_dot_product_attention(qr, kr, vr, is_causal=True).transpose(1, 2)
+    close(y, yr, 2e-2)
+
+
 def test_softmax_polynomial_exp2_against_exp2():
     """The FMA-pipe exp2 of the attention softmax stays within bf16's half-ulp of exp2."""
     x = torch.cat([torch.linspace(-126.0, 0.0, 1 << 20, device=DEV),
