@@ -151,7 +151,7 @@ class _Unit:
     def reduce_scatter_grads(self, grads: tuple[torch.Tensor | None, ...]) -> torch.Tensor:
         """Flatten the unit's gradients, keep this rank's averaged slice."""
         W = self.pg.world_size
-        flat = self.owner._grad_buffer(self) if self.owner is not None else None
+        flat = self.owner._grad_buffer(self) if self.owner is not None and W > 1 else None
         if flat is not None:  # multicast-bound, reused: zero only what no gradient covers
             at = 0
             for g, (_, _, _, n) in zip(grads, self.entries, strict=True):
