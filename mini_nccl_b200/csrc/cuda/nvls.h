@@ -62,6 +62,7 @@ class NvlsObject {
   CUmemGenericAllocationHandle mc_handle_ = 0;
   CUmemGenericAllocationHandle mem_handle_ = 0;
   bool have_mc_ = false, have_mem_ = false, added_ = false, bound_ = false, mapped_ = false;
+  bool uc_mapped_ = false, mc_mapped_ = false;
   int export_fd_ = -1;
   int listen_fd_ = -1;
   std::string sock_name_;

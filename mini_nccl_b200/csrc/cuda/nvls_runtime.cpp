@@ -265,11 +265,13 @@ void NvlsObject::bind_and_map() {
            "cuMemAddressReserve(unicast)");
   uc_ = reinterpret_cast<void*>(uc);
   cu_check(d.mem_map(uc, static_cast<size_t>(bytes_), 0, mem_handle_, 0), "cuMemMap(unicast)");
+  uc_mapped_ = true;
   cu_check(d.mem_set_access(uc, static_cast<size_t>(bytes_), &access, 1), "cuMemSetAccess(unicast)");
   cu_check(d.addr_reserve(&mc, static_cast<size_t>(bytes_), static_cast<size_t>(gran_), 0, 0),
            "cuMemAddressReserve(multicast)");
   mc_ = reinterpret_cast<void*>(mc);
   cu_check(d.mem_map(mc, static_cast<size_t>(bytes_), 0, mc_handle_, 0), "cuMemMap(multicast)");
+  mc_mapped_ = true;
   cu_check(d.mem_set_access(mc, static_cast<size_t>(bytes_), &access, 1), "cuMemSetAccess(multicast)");
   mapped_ = true;
   if (cudaMemset(uc_, 0, static_cast<size_t>(bytes_)) != cudaSuccess || cudaDeviceSynchronize() != cudaSuccess)
@@ -280,17 +282,19 @@ void NvlsObject::release() {
   const Driver& d = drv();
   if (d.mem_unmap == nullptr) return;
   const size_t n = static_cast<size_t>(bytes_);
+  // each address is unmapped on its own flag: a set-up that failed between the
+  // two mappings leaves one of them mapped
   if (mc_ != nullptr) {
-    if (mapped_) d.mem_unmap(reinterpret_cast<CUdeviceptr>(mc_), n);
+    if (mc_mapped_) d.mem_unmap(reinterpret_cast<CUdeviceptr>(mc_), n);
     d.addr_free(reinterpret_cast<CUdeviceptr>(mc_), n);
     mc_ = nullptr;
   }
   if (uc_ != nullptr) {
-    if (mapped_) d.mem_unmap(reinterpret_cast<CUdeviceptr>(uc_), n);
+    if (uc_mapped_) d.mem_unmap(reinterpret_cast<CUdeviceptr>(uc_), n);
     d.addr_free(reinterpret_cast<CUdeviceptr>(uc_), n);
     uc_ = nullptr;
   }
-  mapped_ = false;
+  uc_mapped_ = mc_mapped_ = mapped_ = false;
   if (bound_) {
     CUdevice dev = 0;
     if (d.device_get(&dev, device_) == CUDA_SUCCESS) d.mc_unbind(mc_handle_, dev, 0, n);
