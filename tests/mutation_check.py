@@ -163,6 +163,16 @@ MUTATIONS: list[Mutation] = [
       "            with torch.cuda.stream(side):\n",
       ["tests/test_stream_order_gpu.py::test_fsdp_side_and_comm_streams_wait_for_their_producers"],
       "a unit's gradient reduce-scatter may read gradients backward has not written yet", needs_gpu=True),
+    M("splitk-ignores-partial-waves", "mini_nccl_b200/ops/kernels.py",
+      "        waves = math.ceil(tiles * s_eff / NUM_SMS)\n",
+      "        waves = tiles * s_eff / NUM_SMS\n",
+      ["tests/test_gemm_planning.py"],
+      "the split-K plan counts fractional waves, so a nearly empty last wave looks free"),
+    M("host-batches-single-buffer", "bench.py",
+      "        self.turn ^= 1\n",
+      "        self.turn ^= 0\n",
+      ["tests/test_bench_host_batches.py"],
+      "the next batch is drawn into the buffer whose copy the current step just enqueued"),
     M("control-docstring", "mini_nccl_b200/collectives.py",
       "    \"\"\"Deterministic contiguous split; the first ``n % parts`` pieces get one extra.\"\"\"\n",
       "    \"\"\"Deterministic contiguous split (the first n % parts pieces get one extra).\"\"\"\n",
