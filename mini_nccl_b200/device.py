@@ -256,10 +256,6 @@ class DeviceComm:
     def _nvls_sum_ok(self, tensor: torch.Tensor, op: str) -> bool:
         return self.nvls and op == "sum" and tensor.dtype in _NVLS_DTYPES
 
-    def _nvls_preferred(self, nbytes: int) -> bool:
-        """Whether ``auto`` should use the switch for a message of ``nbytes``."""
-        return self.world_size >= NVLS_MIN_WORLD and nbytes >= NVLS_MIN_BYTES
-
     def scratch_zeros(self, numel: int, dtype: torch.dtype) -> torch.Tensor:
         """A zeroed tensor inside the staging buffer's tail is not safe to hand out
         (collectives reuse it), so scratch is ordinary device memory."""
@@ -375,10 +371,8 @@ class DeviceComm:
         # the switch reads the tensor's own type: a narrower wire needs the peer kernels
         nvls_ok = self._nvls_sum_ok(tensor, op) and not (wire_bf16 and tensor.dtype != torch.bfloat16)
         if algorithm == "auto":
-            if nvls_ok and (self._nvls_preferred(nbytes) or self.impl.is_nvls(tensor)):
-                algorithm = "nvls"
-            else:
-                algorithm = "one_shot" if nbytes <= ONE_SHOT_MAX_BYTES else "two_shot"
+            algorithm = auto_all_reduce_algorithm(nbytes, self.world_size, nvls_ok,
+                                                  nvls_ok and self.impl.is_nvls(tensor))
         if algorithm == "nvls" and not nvls_ok:
             raise ValueError(f"nvls all-reduce needs NVLS ({self.nvls_reason or 'available'}), op='sum', "
                              f"an fp32 / bf16 / fp16 tensor and no narrower wire type")
@@ -721,6 +715,19 @@ class DeviceComm:
                 except Exception:  # the host communicator is gone: release anyway
                     pass
             self.impl.close()
+
+
+def auto_all_reduce_algorithm(nbytes: int, world: int, nvls_ok: bool, in_multicast_memory: bool) -> str:
+    """What ``all_reduce(algorithm="auto")`` runs for a message of ``nbytes``.
+
+    The switch (``nvls``) for a sum it can do on a tensor already bound to the
+    multicast object, or from :data:`NVLS_MIN_BYTES` on at
+    :data:`NVLS_MIN_WORLD` ranks or more; otherwise one round of peer stores
+    up to :data:`ONE_SHOT_MAX_BYTES` and the two-shot kernel above it.
+    """
+    if nvls_ok and (in_multicast_memory or (world >= NVLS_MIN_WORLD and nbytes >= NVLS_MIN_BYTES)):
+        return "nvls"
+    return "one_shot" if nbytes <= ONE_SHOT_MAX_BYTES else "two_shot"
 
 
 def _pick(algorithm: str, eligible: bool, preferred: bool, op: str) -> bool:

@@ -35,3 +35,22 @@ def test_ring_schedule_visits_each_foreign_block_once_per_phase() -> None:
         assert {s[4] for s in reduce} == {1} and {s[4] for s in gather} == {2}
         assert len({s[1] for s in reduce}) == W - 1 and len({s[1] for s in gather}) == W - 1
         assert sum(s[3] for s in reduce) < n and sum(s[3] for s in gather) < n
+
+
+def test_auto_all_reduce_follows_the_measured_cut_overs() -> None:
+    from mini_nccl_b200.device import NVLS_MIN_BYTES, ONE_SHOT_MAX_BYTES, auto_all_reduce_algorithm
+
+    KiB, MiB = 1 << 10, 1 << 20
+    # two ranks: the switch moves more bytes per GPU than the peer kernels
+    assert auto_all_reduce_algorithm(64 * KiB, 2, True, False) == "one_shot"
+    assert auto_all_reduce_algorithm(ONE_SHOT_MAX_BYTES, 2, True, False) == "one_shot"
+    assert auto_all_reduce_algorithm(ONE_SHOT_MAX_BYTES + 16, 2, True, False) == "two_shot"
+    assert auto_all_reduce_algorithm(256 * MiB, 2, True, False) == "two_shot"
+    # eight ranks: one-shot below NVLS_MIN_BYTES, the switch from there on
+    assert auto_all_reduce_algorithm(1 * MiB, 8, True, False) == "one_shot"
+    assert auto_all_reduce_algorithm(NVLS_MIN_BYTES, 8, True, False) == "nvls"
+    assert auto_all_reduce_algorithm(1 << 30, 8, True, False) == "nvls"
+    # no usable switch path: peer kernels at every size
+    assert auto_all_reduce_algorithm(1 << 30, 8, False, False) == "two_shot"
+    # a tensor bound to the multicast object is reduced in place at any size
+    assert auto_all_reduce_algorithm(4 * KiB, 2, True, True) == "nvls"
