@@ -97,8 +97,8 @@ MUTATIONS: list[Mutation] = [
       ["tests/test_ddp.py::test_a_dtype_change_starts_a_new_bucket"],
       "buckets follow registration order, so the first bucket to fill is reduced last"),
     M("fsdp-rng-not-replayed", "mini_nccl_b200/parallel/fsdp.py",
-      "                torch.set_rng_state(ctx.cpu_rng)\n",
-      "                pass\n",
+      "            torch.set_rng_state(self.cpu_state)\n",
+      "            pass\n",
       ["tests/test_fsdp.py::test_recompute_replays_randomness"],
       "the recompute draws a fresh dropout mask"),
     M("fsdp-sum-not-mean", "mini_nccl_b200/parallel/fsdp.py",
@@ -128,8 +128,8 @@ MUTATIONS: list[Mutation] = [
       ["tests/test_pipeline.py::test_1f1b_bounds_in_flight_microbatches"],
       "1F1B holds one microbatch more than W - s in flight"),
     M("mesh-first-dim-fastest", "mini_nccl_b200/mesh.py",
-      "        for name in reversed(self.names):\n            self.strides[name] = stride\n",
-      "        for name in self.names:\n            self.strides[name] = stride\n",
+      "math.prod(sizes[i + 1:])",
+      "math.prod(sizes[:i])",
       ["tests/test_mesh.py::test_mesh_layout_last_dimension_fastest"],
       "the rank layout no longer matches the documented last-dimension-fastest order"),
     M("recorder-seq-frozen", "mini_nccl_b200/recorder.py",
