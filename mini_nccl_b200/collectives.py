@@ -243,7 +243,7 @@ def _ring_all_reduce(
         # owns the fully reduced block (r + 1) % W.
         for s in range(W - 1):
             out_b = blocks[(r - s) % W]
-            in_b = blocks[(r - s - 1) % W]
+            in_b = blocks[(r - s) % W]
             if wire_dtype is None:
                 pg.send_recv_sliced(
                     out_b, right, landing, left, slices,
