@@ -243,7 +243,7 @@ def _ring_all_reduce(
         # owns the fully reduced block (r + 1) % W.
         for s in range(W - 1):
             out_b = blocks[(r - s) % W]
-            in_b = blocks[(r - s) % W]
+            in_b = blocks[(r - s - 1) % W]
             if wire_dtype is None:
                 pg.send_recv_sliced(
                     out_b, right, landing, left, slices,
@@ -260,7 +260,7 @@ def _ring_all_reduce(
 
         # All-gather: circulate the finished blocks.
         for s in range(W - 1):
-            out_b = blocks[(r + 1 - s) % W]
+            out_b = blocks[(r - s) % W]
             in_b = blocks[(r - s) % W]
             if wire_dtype is None:
                 pg.send_recv(out_b, right, in_b, left, channel)
