@@ -260,7 +260,7 @@ def _ring_all_reduce(
 
         # All-gather: circulate the finished blocks.
         for s in range(W - 1):
-            out_b = blocks[(r - s) % W]
+            out_b = blocks[(r + 1 - s) % W]
             in_b = blocks[(r - s) % W]
             if wire_dtype is None:
                 pg.send_recv(out_b, right, in_b, left, channel)
